@@ -1,0 +1,446 @@
+"""Benchmark of the fused render + L1/SSIM loss step (forward and backward) on B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+One step = depth order -> projection/binning -> blend -> fused L1+SSIM loss and gradient ->
+reverse blend -> chain rule to the Gaussian parameters (+ one NCCL all-reduce of the gradients
+when N > 1).  Default workload: "dynamic128" (16 frames of 128x128, 32768 Gaussians with
+velocities, SH degree 1, one camera per frame on an arc, gradients summed over frames).  With N
+GPUs every rank renders 16 more frames of the same arc (weak scaling) against the same Gaussian set.
+
+Prints one JSON line (rank 0).  Metric: Mpix/s (rendered pixels per second, all ranks).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "Mpix/s fwd+bwd render+SSIM at 1/2/4/8 B200; % HBM roofline; vs ref CPU"
+UNIT = "Mpix/s"
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 1024 * 1024
+
+# Algorithmic bytes of one raster launch (see DESIGN.md "raster roofline"):
+#   backward: per (tile, Gaussian) pair an 8 B key + a 48 B projected record read and a 40 B
+#   gradient record read-modify-written (80 B); per pixel 4 B transmittance + 4 B state + 12 B
+#   image gradient read.   forward: per pair key + record (56 B); per pixel 24 B written.
+BWD_BYTES_PER_PAIR, BWD_BYTES_PER_PIXEL = 136, 20
+FWD_BYTES_PER_PAIR, FWD_BYTES_PER_PIXEL = 56, 24
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", default="dynamic128")
+    ap.add_argument("--scale", type=float, default=1.0, help="Gaussian-count scale (1 = full workload)")
+    ap.add_argument("--image-scale", type=float, default=1.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--stages", action="store_true", help="print per-stage times to stderr")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------------------------
+# workloads
+
+
+def make_workload(name: str, rank: int, world: int, scale: float, image_scale: float):
+    from dynaworld_b200 import synthetic as syn
+    from dynaworld_b200.distributed import shard_views
+
+    if name == "dynamic128":
+        return syn.dynamic128(scale=scale, image_scale=image_scale, frames=16, frame_offset=16 * rank,
+                              total_frames=16 * world), "weak"
+    full = syn.WORKLOADS[name](scale=scale, image_scale=image_scale)
+    shared = full.views_per_set >= full.n_views
+    sh = shard_views(full.n_views, world, rank, full.views_per_set, shared_set=shared)
+    return full.views(sh.start, sh.stop), ("strong" if world > 1 else "weak")
+
+
+def workload_config(name, wl, world, scaling):
+    return {
+        "workload": f"{name}: {wl.n_views * world if scaling == 'weak' else wl.n_views} views/frames at "
+                    f"{wl.height}x{wl.width}, {wl.n_gaussians} Gaussians per set, SH degree {wl.sh_degree}"
+                    + (", velocities" if wl.velocity is not None else ""),
+        "views_per_gpu": wl.n_views,
+        "gaussians": wl.n_gaussians,
+        "height": wl.height,
+        "width": wl.width,
+        "sh_degree": wl.sh_degree,
+        "loss": "standard_gs: 0.8*L1 + 0.2*(1-SSIM)/2, 11x11 box window (reference losses.py)",
+        "renderer": "exact (dense.py semantics), tile 16, alpha cutoff 2^-25",
+        "parallelism": f"dp{world} over views, NCCL all-reduce of Gaussian gradients" if world > 1 else "single GPU",
+        "l2": "flushed between timed steps (256 MiB write outside the timed events)",
+    }
+
+
+# ---------------------------------------------------------------------------------------------
+# the step
+
+
+class Step:
+    """One render + loss forward/backward of a workload resident on the device."""
+
+    def __init__(self, wl, device, world):
+        from dynaworld_b200.config import B200RendererConfig
+
+        self.wl = wl
+        self.dev = device
+        self.world = world
+        self.cfg = B200RendererConfig()
+        self.params = {k: getattr(wl, k).to(device).contiguous().requires_grad_(True)
+                       for k in ("means", "log_scales", "quats", "opacity_logits", "sh")}
+        if wl.velocity is not None:
+            self.params["velocity"] = wl.velocity.to(device).contiguous().requires_grad_(True)
+        self.intr = torch.stack([wl.fx, wl.fy, wl.cx, wl.cy], -1).to(device).contiguous()
+        self.c2w = wl.camera_to_world.to(device).contiguous()
+        self.times = wl.times.to(device).contiguous()
+        self.target = wl.target.to(device).contiguous()
+
+    def run(self, params=None, intr=None, c2w=None, times=None, target=None):
+        from dynaworld_b200.distributed import allreduce_gradients
+        from dynaworld_b200.losses import reconstruction_loss_per_image
+        from dynaworld_b200.renderer import render_b200
+
+        p = params or self.params
+        for v in p.values():
+            v.grad = None
+        image, _alpha, _ = render_b200(
+            p["means"], p["log_scales"], p["quats"], p["opacity_logits"], p["sh"],
+            intrinsics=self.intr if intr is None else intr, camera_to_world=self.c2w if c2w is None else c2w,
+            height=self.wl.height, width=self.wl.width, velocity=p.get("velocity"),
+            times=self.times if times is None else times, views_per_set=self.wl.views_per_set, config=self.cfg,
+        )
+        loss = reconstruction_loss_per_image(image, self.target if target is None else target)
+        loss.sum().backward()
+        if self.world > 1:
+            allreduce_gradients([v.grad for v in p.values()])
+        return loss
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks
+
+
+class ClockSampler:
+    """nvidia-smi samples of the local GPU while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU port (the oracle's restatement of the reference's dense renderer + loss)
+
+
+def cpu_sample_time(wl, window: int, frame: int = 0, reps: int = 1):
+    """Seconds for one fwd+bwd of the reference algorithm (dense render of every Gaussian at every
+    pixel + standard_gs loss) on a window x window crop of one frame, on this host's cores."""
+    from oracle import splat_oracle as so
+
+    W0 = (wl.width - window) // 2
+    H0 = (wl.height - window) // 2
+    sl = slice(frame, frame + 1)
+    times = []
+    for _ in range(reps):
+        leaves = {k: getattr(wl, k)[0 if wl.views_per_set >= wl.n_views else frame // wl.views_per_set][None]
+                  .clone().requires_grad_(True) for k in ("means", "log_scales", "quats", "opacity_logits", "sh")}
+        vel = None
+        if wl.velocity is not None:
+            vel = wl.velocity[0][None].clone().requires_grad_(True)
+        t0 = time.perf_counter()
+        raw = so.RawGaussians(leaves["means"], leaves["log_scales"], leaves["quats"], leaves["opacity_logits"],
+                              leaves["sh"], vel)
+        m, s, q, o, rgb = so.activate(raw, wl.times[sl], wl.camera_to_world[sl], 1)
+        key = so.camera_depth_fp32(m.detach(), wl.camera_to_world[sl])
+        img, _, _ = so.render_dense(m, s, q, o, rgb, window, window, wl.fx[sl], wl.fy[sl], wl.cx[sl], wl.cy[sl],
+                                    wl.camera_to_world[sl], sort_key=key, x0=W0, y0=H0)
+        tgt = wl.target[sl][:, :, H0:H0 + window, W0:W0 + window]
+        so.reconstruction_loss_per_image(img, tgt).sum().backward()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times)
+
+
+def cpu_baseline(wl, budget_s: float = 15.0):
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    t8 = cpu_sample_time(wl, 8)
+    per_px = t8 / 64.0
+    window = int(max(8, min(64, math.sqrt(budget_s / 2.0 / max(per_px, 1e-9)))))
+    t = cpu_sample_time(wl, window, reps=2)
+    return {
+        "value": (window * window) / t / 1e6,
+        "unit": UNIT,
+        "cores": cores,
+        "kind": "port",
+        "sample": f"{window}x{window} centre window of frame 0 ({wl.n_gaussians} Gaussians, all blended at every "
+                  f"pixel as dense.py does), fwd+bwd with the standard_gs loss, median of 2",
+    }
+
+
+def reference_arm(args, rank, world):
+    """--impl reference: the reference's CPU algorithm (oracle port of dense.py + losses.py)."""
+    if rank != 0:
+        return 0
+    wl, scaling = make_workload(args.workload, 0, 1, args.scale, args.image_scale)
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    per_px = cpu_sample_time(wl, 8) / 64.0
+    steps = max(1, args.steps)
+    budget = 120.0
+    window = int(max(4, min(64, math.sqrt(budget / (steps + args.warmup) / max(per_px, 1e-9)))))
+    for _ in range(args.warmup):
+        cpu_sample_time(wl, window, frame=0)
+    total = 0.0
+    for k in range(steps):
+        total += cpu_sample_time(wl, window, frame=k % wl.n_views)
+    value = steps * window * window / total / 1e6
+    sample = (f"{window}x{window} centre window of one frame per step ({wl.n_gaussians} Gaussians, dense "
+              f"all-pairs blend + standard_gs loss, fwd+bwd), frames cycled")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / steps, "higher_is_better": True,
+        "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args.workload, wl, 1, scaling),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------------------------
+# main GPU arm
+
+
+def hbm_peak():
+    try:
+        p = json.loads(PEAKS.read_text())
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def main():
+    args = parse_args()
+    rank, local_rank, world = (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+                               int(os.environ.get("WORLD_SIZE", 1)))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+
+    from dynaworld_b200 import _lib, build
+    from dynaworld_b200 import render as R
+
+    build.build()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    L = _lib.load()
+    wl, scaling = make_workload(args.workload, rank, world, args.scale, args.image_scale)
+    step = Step(wl, dev, world)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step.run()
+    barrier()
+
+    # ---- timed region: inputs resident in HBM ----
+    R.STAGE_EVENTS = []
+    sampler = ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ else local_rank)
+    sampler.start()
+    launches0 = L.gsb_kernel_launches()
+    evs = []
+    barrier()
+    for _ in range(args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step.run()
+        b.record()
+        evs.append((a, b))
+    barrier()
+    launches = L.gsb_kernel_launches() - launches0
+    clocks = sampler.stop()
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    local_total = sum(step_ms)
+    stage_ms: dict[str, list[float]] = {}
+    for name, a, b in R.STAGE_EVENTS:
+        stage_ms.setdefault(name, []).append(a.elapsed_time(b))
+    R.STAGE_EVENTS = None
+    n_pairs = int(getattr(step, "last_pairs", 0))
+
+    t = torch.tensor([local_total], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    pixels_per_step = wl.n_views * wl.height * wl.width * world
+    value = pixels_per_step * args.steps / (total_ms / 1e3) / 1e6
+
+    # pair count of the workload (for the roofline), from one more forward
+    from dynaworld_b200.render import SceneSpec, ViewSpec, forward_stages
+
+    sspec = SceneSpec(wl.n_sets, wl.n_gaussians, True, wl.sh_degree, wl.velocity is not None, True)
+    vspec = ViewSpec(wl.n_views, wl.views_per_set, wl.height, wl.width)
+    tens = {"means": step.params["means"].detach(), "scales": step.params["log_scales"].detach(),
+            "quats": step.params["quats"].detach(),
+            "opacities": step.params["opacity_logits"].detach().reshape(wl.n_sets, wl.n_gaussians),
+            "colors": step.params["sh"].detach(),
+            "velocity": step.params["velocity"].detach() if "velocity" in step.params else None,
+            "intrinsics": step.intr, "camera_to_world": step.c2w, "times": step.times}
+    _, _, _, fstate = forward_stages(sspec, vspec, step.cfg, 1e-4, tens)
+    n_pairs = fstate.n_pairs
+    del fstate
+
+    # ---- end to end: host buffers in, loss out, through the public API ----
+    e2e = None
+    if not args.no_e2e:
+        host = {k: v.detach().cpu().pin_memory() for k, v in step.params.items()}
+        h_intr, h_c2w = step.intr.cpu().pin_memory(), step.c2w.cpu().pin_memory()
+        h_times, h_target = step.times.cpu().pin_memory(), step.target.cpu().pin_memory()
+        h2d = sum(v.numel() * v.element_size() for v in host.values()) + sum(
+            v.numel() * v.element_size() for v in (h_intr, h_c2w, h_times, h_target))
+        d2h = wl.n_views * 4
+
+        def e2e_step():
+            p = {k: v.to(dev, non_blocking=True).requires_grad_(True) for k, v in host.items()}
+            loss = step.run(p, h_intr.to(dev, non_blocking=True), h_c2w.to(dev, non_blocking=True),
+                            h_times.to(dev, non_blocking=True), h_target.to(dev, non_blocking=True))
+            return loss.detach().cpu()
+
+        for _ in range(max(2, args.warmup)):
+            e2e_step()
+        barrier()
+        e_evs = []
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            e2e_step()
+            b.record()
+            e_evs.append((a, b))
+        barrier()
+        et = torch.tensor([sum(a.elapsed_time(b) for a, b in e_evs)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e2e = {"value": pixels_per_step * args.steps / (float(et.item()) / 1e3) / 1e6, "unit": UNIT,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+
+    # ---- roofline of the dominant kernel ----
+    means = {k: sum(v) / len(v) for k, v in stage_ms.items()}
+    dominant = max(("raster_bwd", "raster_fwd"), key=lambda k: means.get(k, 0.0))
+    px = wl.n_views * wl.height * wl.width
+    if dominant == "raster_bwd":
+        alg_bytes = BWD_BYTES_PER_PAIR * n_pairs + BWD_BYTES_PER_PIXEL * px
+    else:
+        alg_bytes = FWD_BYTES_PER_PAIR * n_pairs + FWD_BYTES_PER_PIXEL * px
+    peak, peak_kind = hbm_peak()
+    dur_s = means[dominant] / 1e3
+    achieved = alg_bytes / dur_s / 1e9
+    roofline = {"bound": "hbm", "kernel": f"{dominant} (gsb_{dominant})", "achieved": achieved, "peak": peak,
+                "unit": "GB/s", "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+                "bytes_per_launch": int(alg_bytes), "pairs": int(n_pairs), "pixels": int(px),
+                "launch_ms": means[dominant],
+                "note": "raster is FP32/SFU-issue bound (records re-read from L2); see profiles/ for ncu counters"}
+    stage_share = {k: round(v / sum(means.values()), 4) for k, v in means.items()} if means else {}
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline(wl)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args.workload, wl, world, scaling),
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
+            "gpu_launches": int(launches), "stage_ms": {k: round(v, 4) for k, v in means.items()},
+            "stage_share": stage_share,
+        }
+        print(json.dumps(line), flush=True)
+        if args.stages:
+            print(json.dumps(means, indent=1), file=sys.stderr)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,345 @@
+// extern "C" entry points of libgsb200.so (declared in include/gsb200.h).
+#include <atomic>
+#include <cmath>
+#include <cstring>
+
+#include "gsb_common.cuh"
+#include "gsb_internal.h"
+
+namespace gsb {
+
+static std::atomic<unsigned long long> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int bits_for(uint64_t count) {
+  int b = 0;
+  while ((uint64_t(1) << b) < count) ++b;
+  return b;
+}
+
+RenderConsts make_consts(const gsb_views& v, const gsb_options& o) {
+  RenderConsts rc{};
+  rc.tile = o.tile_size;
+  rc.tiles_x = (v.width + o.tile_size - 1) / o.tile_size;
+  rc.tiles_y = (v.height + o.tile_size - 1) / o.tile_size;
+  rc.n_tiles = rc.tiles_x * rc.tiles_y;
+  rc.compat = (o.flags & GSB_RENDER_TILED_COMPAT) != 0;
+  rc.depth = (o.flags & GSB_RENDER_DEPTH) != 0;
+  rc.ellipse = (o.flags & GSB_RENDER_NO_ELLIPSE) == 0;
+  rc.near_plane = o.near_plane;
+  rc.alpha_clamp = o.alpha_clamp;
+  rc.alpha_cutoff = rc.compat ? 0.0f : o.alpha_cutoff;
+  rc.t_threshold = rc.compat ? 0.0f : o.transmittance_threshold;
+  rc.eps = o.eps;
+  rc.pixel_center = o.pixel_center;
+  for (int k = 0; k < 3; ++k) rc.bg[k] = o.background[k];
+  rc.bound_scale = o.bound_scale;
+  rc.tiled_threshold = o.tiled_alpha_threshold;
+  volatile float one = 1.0f;
+  rc.f0 = one + o.eps;  // fl32(1 + eps)
+  rc.log2_f0 = rc.compat ? 0.0f : float(std::log2(double(rc.f0)));
+  return rc;
+}
+
+static cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+static gsb_status launch_status() { return cudaGetLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA; }
+
+static gsb_status check_views(const gsb_views* v) {
+  if (!v || !v->intrinsics || !v->camera_to_world) return GSB_ERR_ARG;
+  if (v->n_views <= 0 || v->height <= 0 || v->width <= 0 || v->views_per_set <= 0) return GSB_ERR_SHAPE;
+  return GSB_OK;
+}
+
+static gsb_status check_scene(const gsb_scene* s, const gsb_views* v) {
+  if (!s || !s->means || !s->scales || !s->quats || !s->opacities || !s->colors) return GSB_ERR_ARG;
+  if ((s->flags & GSB_SCENE_VELOCITY) && !s->velocity) return GSB_ERR_ARG;
+  if (s->n_sets <= 0 || s->n_gaussians <= 0) return GSB_ERR_SHAPE;
+  if ((v->n_views - 1) / v->views_per_set >= s->n_sets) return GSB_ERR_SHAPE;
+  if ((s->flags & GSB_SCENE_RAW) && (s->sh_degree < 0 || s->sh_degree > 3)) return GSB_ERR_ARG;
+  if (uint64_t(v->n_views) * uint64_t(s->n_gaussians) >= (uint64_t(1) << 30)) return GSB_ERR_SHAPE;
+  return GSB_OK;
+}
+
+static gsb_status check_opts(const gsb_options* o) {
+  if (!o) return GSB_ERR_ARG;
+  if (o->tile_size != 8 && o->tile_size != 16) return GSB_ERR_ARG;
+  if (!(o->near_plane > 0.0f)) return GSB_ERR_ARG;
+  if (!(o->alpha_cutoff >= 0.0f) || !(o->transmittance_threshold >= 0.0f) || !(o->eps >= 0.0f)) return GSB_ERR_ARG;
+  return GSB_OK;
+}
+
+static int32_t* begin_status(void* ws, cudaStream_t st) {
+  auto* h = static_cast<WorkspaceHeader*>(ws);
+  cudaMemsetAsync(h, 0, 8, st);
+  return &h->status;
+}
+
+}  // namespace gsb
+
+using namespace gsb;
+
+extern "C" {
+
+GSB_API const char* gsb_version(void) { return "gsb200 1.0 sm_100a"; }
+
+GSB_API uint64_t gsb_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+GSB_API const char* gsb_status_string(int s) {
+  switch (s) {
+    case GSB_OK: return "ok";
+    case GSB_ERR_SHAPE: return "inconsistent or unsupported sizes";
+    case GSB_ERR_WORKSPACE: return "workspace too small";
+    case GSB_ERR_KEY_OVERFLOW: return "too many (tile, Gaussian) pairs (limit 2^30 per call)";
+    case GSB_ERR_NONFINITE: return "non-finite values";
+    case GSB_ERR_TIMEOUT: return "a bounded device-side wait gave up";
+    case GSB_ERR_CUDA: return "CUDA runtime error";
+    case GSB_ERR_ARG: return "invalid argument";
+    default: return "unknown status";
+  }
+}
+
+GSB_API gsb_status gsb_read_status(const void* workspace, int* status_out, void* stream) {
+  if (!workspace || !status_out) return GSB_ERR_ARG;
+  int32_t v[2] = {0, 0};
+  if (cudaMemcpyAsync(v, workspace, 8, cudaMemcpyDeviceToHost, as_stream(stream))) return GSB_ERR_CUDA;
+  if (cudaStreamSynchronize(as_stream(stream))) return GSB_ERR_CUDA;
+  *status_out = v[0];
+  return GSB_OK;
+}
+
+// ---- stage 1 ---------------------------------------------------------------------------------
+
+static size_t depth_ws(int32_t B, int32_t G) {
+  const uint32_t n = uint32_t(size_t(B) * G);
+  const int kb = B > 1 ? 8 : 4;
+  Carver c(nullptr, 0);
+  c.take<WorkspaceHeader>(1);
+  c.take<char>(size_t(n) * kb);  // keys
+  c.take<uint32_t>(n);           // values
+  c.take<char>(size_t(n) * kb);  // sorted keys
+  c.take<uint32_t>(n);           // sorted values
+  c.take<char>(radix_sort_workspace(n, kb, 1));
+  return c.used;
+}
+
+GSB_API size_t gsb_depth_order_workspace(const gsb_scene* scene, const gsb_views* views) {
+  if (!scene || !views) return 0;
+  return depth_ws(views->n_views, scene->n_gaussians);
+}
+
+GSB_API gsb_status gsb_depth_order(const gsb_scene* scene, const gsb_views* views, int32_t* sorted_ids,
+                                   int32_t* rank_of, void* workspace, size_t workspace_bytes, void* stream) {
+  gsb_status s;
+  if ((s = check_views(views)) != GSB_OK) return s;
+  if ((s = check_scene(scene, views)) != GSB_OK) return s;
+  if (!sorted_ids || !rank_of || !workspace) return GSB_ERR_ARG;
+  const int32_t B = views->n_views, G = scene->n_gaussians;
+  if (workspace_bytes < depth_ws(B, G)) return GSB_ERR_WORKSPACE;
+  cudaStream_t st = as_stream(stream);
+  const uint32_t n = uint32_t(size_t(B) * G);
+  const int kb = B > 1 ? 8 : 4;
+  Carver c(workspace, workspace_bytes);
+  c.take<WorkspaceHeader>(1);
+  void* keys = c.take<char>(size_t(n) * kb);
+  uint32_t* vals = c.take<uint32_t>(n);
+  void* skeys = c.take<char>(size_t(n) * kb);
+  uint32_t* svals = c.take<uint32_t>(n);
+  const size_t sws = radix_sort_workspace(n, kb, 1);
+  void* sort_ws = c.take<char>(sws);
+  int32_t* status = begin_status(workspace, st);
+  if ((s = launch_depth_keys(*scene, *views, kb == 8 ? static_cast<uint64_t*>(keys) : nullptr,
+                             kb == 4 ? static_cast<uint32_t*>(keys) : nullptr, vals, st)) != GSB_OK)
+    return s;
+  const int bit_hi = 32 + (B > 1 ? bits_for(uint64_t(B)) : 0);
+  if ((s = radix_sort(keys, skeys, vals, svals, n, kb, 0, bit_hi, sort_ws, sws, st, status)) != GSB_OK) return s;
+  return launch_invert_order(svals, B, G, sorted_ids, rank_of, st);
+}
+
+// ---- stage 2 ---------------------------------------------------------------------------------
+
+static size_t preprocess_ws(int32_t B, int32_t G) {
+  const uint32_t n = uint32_t(size_t(B) * G);
+  Carver c(nullptr, 0);
+  c.take<WorkspaceHeader>(1);
+  c.take<uint32_t>(n);
+  c.take<char>(exclusive_scan_workspace(n));
+  return c.used;
+}
+
+GSB_API size_t gsb_preprocess_workspace(const gsb_views* views, int32_t n_gaussians) {
+  if (!views) return 0;
+  return preprocess_ws(views->n_views, n_gaussians);
+}
+
+GSB_API gsb_status gsb_preprocess_fwd(const gsb_scene* scene, const gsb_views* views, const gsb_options* opts,
+                                      const int32_t* rank_of, float* records, int32_t* tile_rects,
+                                      uint32_t* pair_offsets, float* cov2d_out, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  gsb_status s;
+  if ((s = check_views(views)) != GSB_OK) return s;
+  if ((s = check_scene(scene, views)) != GSB_OK) return s;
+  if ((s = check_opts(opts)) != GSB_OK) return s;
+  if (!rank_of || !records || !tile_rects || !pair_offsets || !workspace) return GSB_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(records) % 16 || reinterpret_cast<uintptr_t>(tile_rects) % 16) return GSB_ERR_ARG;
+  const int32_t B = views->n_views, G = scene->n_gaussians;
+  if (workspace_bytes < preprocess_ws(B, G)) return GSB_ERR_WORKSPACE;
+  cudaStream_t st = as_stream(stream);
+  const uint32_t n = uint32_t(size_t(B) * G);
+  Carver c(workspace, workspace_bytes);
+  c.take<WorkspaceHeader>(1);
+  uint32_t* counts = c.take<uint32_t>(n);
+  const size_t scan_bytes = exclusive_scan_workspace(n);
+  void* scan_ws = c.take<char>(scan_bytes);
+  int32_t* status = begin_status(workspace, st);
+  const RenderConsts rc = make_consts(*views, *opts);
+  if ((s = launch_preprocess_fwd(*scene, *views, rc, rank_of, records, reinterpret_cast<int4*>(tile_rects), counts,
+                                 cov2d_out, st)) != GSB_OK)
+    return s;
+  return exclusive_scan(counts, n, pair_offsets, scan_ws, scan_bytes, st, status);
+}
+
+// ---- stage 3 ---------------------------------------------------------------------------------
+
+static size_t bin_ws(uint32_t n_pairs) {
+  Carver c(nullptr, 0);
+  c.take<WorkspaceHeader>(1);
+  c.take<uint64_t>(n_pairs);
+  c.take<char>(radix_sort_workspace(n_pairs, 8, 0));
+  return c.used;
+}
+
+GSB_API size_t gsb_bin_workspace(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians,
+                                 uint32_t n_pairs) {
+  (void)views;
+  (void)opts;
+  (void)n_gaussians;
+  return bin_ws(n_pairs);
+}
+
+GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians, const float* records,
+                           const int32_t* tile_rects, const uint32_t* pair_offsets, uint32_t n_pairs,
+                           uint64_t* sorted_keys, uint32_t* tile_ranges, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  gsb_status s;
+  if ((s = check_views(views)) != GSB_OK) return s;
+  if ((s = check_opts(opts)) != GSB_OK) return s;
+  if (n_gaussians <= 0) return GSB_ERR_SHAPE;
+  if (!records || !tile_rects || !pair_offsets || !tile_ranges || !workspace) return GSB_ERR_ARG;
+  if (n_pairs > 0 && !sorted_keys) return GSB_ERR_ARG;
+  if (n_pairs >= (1u << 30)) return GSB_ERR_KEY_OVERFLOW;
+  if (workspace_bytes < bin_ws(n_pairs)) return GSB_ERR_WORKSPACE;
+  cudaStream_t st = as_stream(stream);
+  const RenderConsts rc = make_consts(*views, *opts);
+  const int32_t B = views->n_views;
+  Carver c(workspace, workspace_bytes);
+  c.take<WorkspaceHeader>(1);
+  uint64_t* keys = c.take<uint64_t>(n_pairs);
+  const size_t sws = radix_sort_workspace(n_pairs, 8, 0);
+  void* sort_ws = c.take<char>(sws);
+  int32_t* status = begin_status(workspace, st);
+  if (n_pairs > 0) {
+    if ((s = launch_emit(B, n_gaussians, rc, views->height, views->width, records,
+                         reinterpret_cast<const int4*>(tile_rects), pair_offsets, n_pairs, keys, status, st)) != GSB_OK)
+      return s;
+    const int bits = bits_for(uint64_t(B) * uint64_t(rc.n_tiles));
+    if ((s = radix_sort(keys, sorted_keys, nullptr, nullptr, n_pairs, 8, 32, 32 + bits, sort_ws, sws, st, status)) !=
+        GSB_OK)
+      return s;
+  }
+  return launch_tile_ranges(sorted_keys, n_pairs, tile_ranges, size_t(B) * rc.n_tiles, st);
+}
+
+// ---- stages 4 and 6 --------------------------------------------------------------------------
+
+GSB_API gsb_status gsb_raster_fwd(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians,
+                                  const float* records, const uint64_t* sorted_keys, const uint32_t* tile_ranges,
+                                  float* image, float* alpha, float* depth, float* pixel_t, uint32_t* pixel_state,
+                                  void* stream) {
+  gsb_status s;
+  if ((s = check_views(views)) != GSB_OK) return s;
+  if ((s = check_opts(opts)) != GSB_OK) return s;
+  if (n_gaussians <= 0) return GSB_ERR_SHAPE;
+  if (!records || !tile_ranges || !image || !pixel_t || !pixel_state) return GSB_ERR_ARG;
+  RasterArgs a{};
+  a.B = views->n_views, a.G = n_gaussians, a.H = views->height, a.W = views->width;
+  a.rc = make_consts(*views, *opts);
+  a.records = records, a.keys = sorted_keys, a.ranges = tile_ranges;
+  a.image = image, a.alpha = alpha, a.depth = (opts->flags & GSB_RENDER_DEPTH) ? depth : nullptr;
+  a.pixel_t = pixel_t, a.pixel_state = pixel_state;
+  if (views->n_views > 65535) return GSB_ERR_SHAPE;
+  return launch_raster_fwd(a, as_stream(stream));
+}
+
+GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians,
+                                  const float* records, const uint64_t* sorted_keys, const uint32_t* tile_ranges,
+                                  const float* pixel_t, const uint32_t* pixel_state, const float* d_image,
+                                  const float* d_alpha, const float* d_depth, const float* view_scale, float* grad2d,
+                                  void* stream) {
+  gsb_status s;
+  if ((s = check_views(views)) != GSB_OK) return s;
+  if ((s = check_opts(opts)) != GSB_OK) return s;
+  if (n_gaussians <= 0) return GSB_ERR_SHAPE;
+  if (!records || !tile_ranges || !pixel_t || !pixel_state || !d_image || !grad2d) return GSB_ERR_ARG;
+  RasterArgs a{};
+  a.B = views->n_views, a.G = n_gaussians, a.H = views->height, a.W = views->width;
+  a.rc = make_consts(*views, *opts);
+  a.records = records, a.keys = sorted_keys, a.ranges = tile_ranges;
+  a.pixel_t = const_cast<float*>(pixel_t), a.pixel_state = const_cast<uint32_t*>(pixel_state);
+  a.d_image = d_image, a.d_alpha = d_alpha, a.d_depth = d_depth, a.view_scale = view_scale, a.grad2d = grad2d;
+  if (views->n_views > 65535) return GSB_ERR_SHAPE;
+  return launch_raster_bwd(a, as_stream(stream));
+}
+
+// ---- stage 5 ---------------------------------------------------------------------------------
+
+GSB_API size_t gsb_loss_workspace(int32_t n_images) { return loss_workspace(n_images); }
+
+GSB_API gsb_status gsb_loss_fwd_bwd(const gsb_loss_options* lopts, int32_t n_images, int32_t channels, int32_t height,
+                                    int32_t width, const float* pred, const float* target, float* loss, float* dpred,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (!lopts) return GSB_ERR_ARG;
+  return loss_fwd_bwd(*lopts, n_images, channels, height, width, pred, target, loss, dpred, workspace,
+                      workspace_bytes, as_stream(stream));
+}
+
+GSB_API gsb_status gsb_scale_planes(const float* in, const float* scale, float* out, int32_t n_images,
+                                    int64_t plane_elems, void* stream) {
+  return scale_planes(in, scale, out, n_images, plane_elems, as_stream(stream));
+}
+
+// ---- stage 7 ---------------------------------------------------------------------------------
+
+GSB_API gsb_status gsb_preprocess_bwd(const gsb_scene* scene, const gsb_views* views, const gsb_options* opts,
+                                      const int32_t* rank_of, const float* grad2d, gsb_scene_grads* grads,
+                                      void* stream) {
+  gsb_status s;
+  if ((s = check_views(views)) != GSB_OK) return s;
+  if ((s = check_scene(scene, views)) != GSB_OK) return s;
+  if ((s = check_opts(opts)) != GSB_OK) return s;
+  if (!rank_of || !grad2d || !grads) return GSB_ERR_ARG;
+  const RenderConsts rc = make_consts(*views, *opts);
+  return launch_preprocess_bwd(*scene, *views, rc, rank_of, grad2d, *grads, as_stream(stream));
+}
+
+// ---- utility ---------------------------------------------------------------------------------
+
+GSB_API size_t gsb_radix_sort_workspace(uint32_t n, int key_bytes, int with_values) {
+  return align_up(sizeof(WorkspaceHeader)) + radix_sort_workspace(n, key_bytes, with_values);
+}
+
+GSB_API gsb_status gsb_radix_sort(const void* keys_in, void* keys_out, const uint32_t* values_in, uint32_t* values_out,
+                                  uint32_t n, int key_bytes, int bit_lo, int bit_hi, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (n > 0 && (!keys_in || !keys_out)) return GSB_ERR_ARG;
+  if (!workspace) return GSB_ERR_ARG;
+  const size_t need = gsb_radix_sort_workspace(n, key_bytes, values_in != nullptr);
+  if (workspace_bytes < need) return GSB_ERR_WORKSPACE;
+  cudaStream_t st = as_stream(stream);
+  int32_t* status = begin_status(workspace, st);
+  char* inner = static_cast<char*>(workspace) + align_up(sizeof(WorkspaceHeader));
+  return radix_sort(keys_in, keys_out, values_in, values_out, n, key_bytes, bit_lo, bit_hi, inner,
+                    workspace_bytes - align_up(sizeof(WorkspaceHeader)), st, status);
+}
+
+}  // extern "C"

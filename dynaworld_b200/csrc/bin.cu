@@ -1,0 +1,80 @@
+// Binning: one 64-bit key per (view, tile, Gaussian) pair, stable radix sort by (view, tile), and
+// the [start, end) run of every tile.
+//
+// Restates build_tile_assignments (src/train/renderers/tiled.py:31-71): the reference lists
+// (tile, Gaussian) pairs and stable-argsorts them by tile (:59), with Gaussians already in depth
+// order (renderers/common.py:191), so each tile's list is in depth order.  Here the pairs are
+// emitted in (view, depth rank) order with the rank in the key's low 32 bits, and only the
+// (view, tile) bits are sorted -- the stability of the LSD sort keeps depth order within a tile.
+#include "gsb_common.cuh"
+#include "gsb_internal.h"
+#include "tiles.cuh"
+
+namespace gsb {
+
+__global__ void __launch_bounds__(256) emit_keys_kernel(int32_t n_views, int32_t G, RenderConsts rc, int H, int W,
+                                                        const float* __restrict__ records,
+                                                        const int4* __restrict__ rects,
+                                                        const uint32_t* __restrict__ offsets, uint32_t n_pairs,
+                                                        uint64_t* __restrict__ keys, int32_t* __restrict__ status) {
+  const size_t total = size_t(n_views) * G;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+    const uint32_t start = offsets[i];
+    const uint32_t end = offsets[i + 1];
+    if (start == end) continue;
+    const uint32_t b = uint32_t(i / G);
+    const uint32_t r = uint32_t(i - size_t(b) * G);
+    const int4 rc4 = rects[i];
+    const uint64_t view_base = uint64_t(b) * rc.n_tiles;
+    uint32_t k = start;
+    if (!rc.compat && rc.ellipse) {
+      const float4 r0 = reinterpret_cast<const float4*>(records)[i * 3 + 0];
+      const float4 r1 = reinterpret_cast<const float4*>(records)[i * 3 + 1];
+      TileRect rect;
+      ExactShape es;
+      exact_rect(r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, rc.alpha_cutoff, H, W, rc.pixel_center, rc.tile, &rect, &es);
+      for (int ty = rc4.y; ty <= rc4.w; ++ty)
+        for (int tx = rc4.x; tx <= rc4.z; ++tx) {
+          if (!exact_tile_hit(es, tx, ty, rc.tile, H, W, rc.pixel_center)) continue;
+          if (k < end && k < n_pairs) keys[k] = ((view_base + uint64_t(ty) * rc.tiles_x + tx) << 32) | r;
+          ++k;
+        }
+    } else {
+      for (int ty = rc4.y; ty <= rc4.w; ++ty)
+        for (int tx = rc4.x; tx <= rc4.z; ++tx) {
+          if (k < end && k < n_pairs) keys[k] = ((view_base + uint64_t(ty) * rc.tiles_x + tx) << 32) | r;
+          ++k;
+        }
+    }
+    if (k != end) record_error(status, GSB_ERR_KEY_OVERFLOW, int(i));
+  }
+}
+
+__global__ void tile_ranges_kernel(const uint64_t* __restrict__ keys, uint32_t n, uint32_t* __restrict__ ranges) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const uint32_t t = uint32_t(keys[i] >> 32);
+    if (i == 0 || uint32_t(keys[i - 1] >> 32) != t) ranges[size_t(t) * 2] = i;
+    if (i + 1 == n || uint32_t(keys[i + 1] >> 32) != t) ranges[size_t(t) * 2 + 1] = i + 1;
+  }
+}
+
+gsb_status launch_emit(int32_t B, int32_t G, const RenderConsts& rc, int H, int W, const float* records,
+                       const int4* rects, const uint32_t* offsets, uint32_t n_pairs, uint64_t* keys, int32_t* status,
+                       cudaStream_t st) {
+  const size_t n = size_t(B) * G;
+  const int grid = int(std::min<size_t>((n + 255) / 256, size_t(148) * 32));
+  note_launch();
+  emit_keys_kernel<<<grid, 256, 0, st>>>(B, G, rc, H, W, records, rects, offsets, n_pairs, keys, status);
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
+gsb_status launch_tile_ranges(const uint64_t* keys, uint32_t n, uint32_t* ranges, size_t n_ranges, cudaStream_t st) {
+  if (cudaMemsetAsync(ranges, 0, n_ranges * 2 * sizeof(uint32_t), st)) return GSB_ERR_CUDA;
+  if (n == 0) return GSB_OK;
+  const int grid = int(std::min<uint32_t>((n + 255) / 256, 148u * 32u));
+  note_launch();
+  tile_ranges_kernel<<<grid, 256, 0, st>>>(keys, n, ranges);
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
+}  // namespace gsb

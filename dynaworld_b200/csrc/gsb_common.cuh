@@ -1,0 +1,91 @@
+// Shared device helpers of libgsb200 (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gsb200.h"
+
+namespace gsb {
+
+// Every workspace starts with this header; kernels record the first error in `status`.
+struct WorkspaceHeader {
+  int32_t status;
+  int32_t detail;
+  uint32_t pad[62];
+};
+static_assert(sizeof(WorkspaceHeader) == 256, "header is 256 bytes");
+
+constexpr size_t kAlign = 256;
+__host__ __device__ inline size_t align_up(size_t x, size_t a = kAlign) { return (x + a - 1) / a * a; }
+
+// Bump allocator over a caller-owned workspace (host side; no device allocation).
+struct Carver {
+  char* base;
+  size_t used;
+  size_t cap;
+  explicit Carver(void* p, size_t c) : base(static_cast<char*>(p)), used(0), cap(c) {}
+  template <typename T>
+  T* take(size_t count) {
+    size_t off = align_up(used);
+    used = off + align_up(count * sizeof(T));
+    return (base && used <= cap) ? reinterpret_cast<T*>(base + off) : nullptr;
+  }
+  bool ok() const { return used <= cap; }
+};
+
+__device__ inline void record_error(int32_t* status, int code, int detail = 0) {
+  if (status && atomicCAS(status, 0, code) == 0) status[1] = detail;
+}
+
+// IEEE-754 float -> uint32 whose unsigned order is the float order; -0 == +0, NaN last.
+__device__ __host__ inline uint32_t float_sort_key(float f) {
+  uint32_t u;
+#ifdef __CUDA_ARCH__
+  u = __float_as_uint(f);
+#else
+  memcpy(&u, &f, 4);
+#endif
+  if ((u & 0x7fffffffu) == 0u) u = 0u;                      // -0 -> +0
+  if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) u = 0x7fc00000u;  // NaN
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// log2(fl32(1 + 1e-6)) = log2(1 + 2^-20): the per-Gaussian transmittance growth of dense.py:225.
+constexpr double kLog2F0 = 1.3757959012e-06;
+
+struct Intrinsics {
+  float fx, fy, cx, cy;
+};
+
+// Camera of one view, as read from device arrays.
+struct Camera {
+  float R[9];  // camera_to_world rotation, row-major: R[j*3+k] = c2w[j][k]
+  float t[3];  // camera centre (world)
+  Intrinsics k;
+};
+
+__device__ inline Camera load_camera(const float* intr, const float* c2w, int b) {
+  Camera c;
+  const float* m = c2w + b * 16;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) c.R[j * 3 + k] = m[j * 4 + k];
+    c.t[j] = m[j * 4 + 3];
+  }
+  c.k.fx = intr[b * 4 + 0];
+  c.k.fy = intr[b * 4 + 1];
+  c.k.cx = intr[b * 4 + 2];
+  c.k.cy = intr[b * 4 + 3];
+  return c;
+}
+
+// Camera-space coordinate k of world point m: fma(d2,R2k, fma(d1,R1k, d0*R0k)), d = fl32(m - t).
+// Same rounding as the reference's float32 (m - t) @ R (common.py:39-51) on FMA CPUs, so depth
+// keys, and hence the sort order, agree bit for bit.
+__device__ inline float cam_coord(const float d[3], const float R[9], int k) {
+  return __fmaf_rn(d[2], R[6 + k], __fmaf_rn(d[1], R[3 + k], __fmul_rn(d[0], R[k])));
+}
+
+}  // namespace gsb

@@ -1,0 +1,89 @@
+// Internal (host-side) interfaces between the translation units of libgsb200.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "gsb200.h"
+
+namespace gsb {
+
+// Counts kernel launches made by this library (diagnostic; read by gsb_kernel_launches()).
+void note_launch();
+
+// Radix sort (sort.cu).
+size_t radix_sort_workspace(uint32_t n, int key_bytes, int with_values);
+gsb_status radix_sort(const void* keys_in, void* keys_out, const uint32_t* vals_in, uint32_t* vals_out, uint32_t n,
+                      int key_bytes, int bit_lo, int bit_hi, void* ws, size_t ws_bytes, cudaStream_t stream,
+                      int32_t* status);
+
+// Exclusive scan: offsets[0..n) and offsets[n] = total (sort.cu).
+size_t exclusive_scan_workspace(uint32_t n);
+gsb_status exclusive_scan(const uint32_t* counts, uint32_t n, uint32_t* offsets, void* scratch, size_t scratch_bytes,
+                          cudaStream_t stream, int32_t* status);
+
+// Values derived from gsb_options once per call.
+struct RenderConsts {
+  int tile;
+  int tiles_x, tiles_y, n_tiles;
+  bool compat;
+  bool depth;
+  bool ellipse;
+  float near_plane, alpha_clamp, alpha_cutoff, t_threshold, eps, pixel_center;
+  float bg[3];
+  float bound_scale, tiled_threshold;
+  float f0;      // fl32(1 + eps), or 1 in compat mode (tile-local products)
+  float log2_f0; // log2(f0) for the rank factors (0 in compat mode)
+};
+
+RenderConsts make_consts(const gsb_views& v, const gsb_options& o);
+int bits_for(uint64_t count);  // smallest b with 2^b >= count (0 for count <= 1)
+
+// Raster stage arguments (raster.cu).
+struct RasterArgs {
+  int B, G, H, W;
+  RenderConsts rc;
+  const float* records;
+  const uint64_t* keys;
+  const uint32_t* ranges;
+  float* image;
+  float* alpha;
+  float* depth;
+  float* pixel_t;
+  uint32_t* pixel_state;
+  const float* d_image;
+  const float* d_alpha;
+  const float* d_depth;
+  const float* view_scale;
+  float* grad2d;
+};
+gsb_status launch_raster_fwd(const RasterArgs& a, cudaStream_t st);
+gsb_status launch_raster_bwd(const RasterArgs& a, cudaStream_t st);
+
+// Preprocess (preprocess.cu).
+gsb_status launch_depth_keys(const gsb_scene& sc, const gsb_views& vw, uint64_t* keys64, uint32_t* keys32,
+                             uint32_t* vals, cudaStream_t st);
+gsb_status launch_invert_order(const uint32_t* sorted_vals, int32_t B, int32_t G, int32_t* sorted_ids,
+                               int32_t* rank_of, cudaStream_t st);
+gsb_status launch_preprocess_fwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
+                                 const int32_t* rank_of, float* records, int4* rects, uint32_t* counts, float* cov,
+                                 cudaStream_t st);
+gsb_status launch_preprocess_bwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
+                                 const int32_t* rank_of, const float* grad2d, const gsb_scene_grads& gr,
+                                 cudaStream_t st);
+
+// Binning (bin.cu).
+gsb_status launch_emit(int32_t B, int32_t G, const RenderConsts& rc, int H, int W, const float* records,
+                       const int4* rects, const uint32_t* offsets, uint32_t n_pairs, uint64_t* keys, int32_t* status,
+                       cudaStream_t st);
+gsb_status launch_tile_ranges(const uint64_t* keys, uint32_t n, uint32_t* ranges, size_t n_ranges, cudaStream_t st);
+
+// Loss (loss.cu).
+size_t loss_workspace(int32_t n_images);
+gsb_status loss_fwd_bwd(const gsb_loss_options& o, int32_t B, int32_t C, int32_t H, int32_t W, const float* pred,
+                        const float* target, float* loss, float* dpred, void* ws, size_t ws_bytes, cudaStream_t st);
+gsb_status scale_planes(const float* in, const float* scale, float* out, int32_t B, int64_t per, cudaStream_t st);
+
+}  // namespace gsb

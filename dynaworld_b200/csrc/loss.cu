@@ -1,0 +1,352 @@
+// Fused reconstruction loss: value per image and d loss / d prediction in one pass.
+//
+// Restates reconstruction_loss_per_image (src/train/losses.py:58-85) with standard_gs =
+// l1_weight * mean|pred - target| + dssim_weight * (1 - SSIM)/2, where SSIM (losses.py:21-44) is
+// the per-image mean of the SSIM map built from reflect-padded 11x11 box means (losses.py:13-18,
+// avg_pool2d after F.pad(mode="reflect")), C1 = 1e-4, C2 = 9e-4, clamped to [-1, 1].
+//
+// One CTA per 32x32 output tile of one image plane.  The five window means are separable sums
+// over a shared-memory copy of the (reflected) input; the SSIM gradient needs the adjoint of the
+// window operator, which for reflect padding folds the zero-padded window sums at the mirrored
+// positions -q and 2(N-1)-q back onto q:
+//   (W^T g)(q) = sum_{m in {q, -q, 2(N-1)-q} valid} sum_k w_k g(m + k)   (g = 0 off the image).
+// The kernel assumes the final clamp of the SSIM mean is inactive; a finishing kernel computes the
+// per-image loss and a fix-up kernel rewrites the gradient of any image whose mean left [-1, 1].
+#include <cmath>
+
+#include "gsb_common.cuh"
+#include "gsb_internal.h"
+
+namespace gsb {
+
+constexpr int kLossTile = 32;
+constexpr int kLossThreads = 256;
+
+struct LossArgs {
+  int B, C, H, W;
+  int type;  // 0 standard_gs, 1 l1, 2 mse, 3 l1_mse
+  float c1, c2;
+  float c_l1, c_mse, c_ssim;  // gradient coefficients (already divided by C*H*W)
+  float w[16];                // window taps, w[k + half]
+  const float* pred;
+  const float* target;
+  float* dpred;
+  double* acc;  // [B, 3]: sum |d|, sum d^2, sum ssim
+};
+
+__device__ __forceinline__ int reflect_idx(int i, int n) {
+  i = i < 0 ? -i : i;
+  i = i >= n ? 2 * (n - 1) - i : i;
+  return min(max(i, 0), n - 1);
+}
+
+template <int HW>
+__global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
+  constexpr int R = kLossTile + 4 * HW;  // input rows/cols held
+  constexpr int M = kLossTile + 2 * HW;  // window-mean rows/cols computed
+  extern __shared__ float smem[];
+  float* xs = smem;                 // [R][R]
+  float* ys = xs + R * R;           // [R][R]
+  float* hs = ys + R * R;           // [5][R][M]
+  float* gm = hs + 5 * R * M;       // [3][M][M]
+  float* ha = gm + 3 * M * M;       // [3][M][kLossTile]
+  __shared__ double s_red[3][kLossThreads / 32];
+
+  const int plane = blockIdx.z, b = plane / a.C;
+  const int x0 = blockIdx.x * kLossTile, y0 = blockIdx.y * kLossTile;
+  const int H = a.H, W = a.W;
+  const size_t poff = size_t(plane) * H * W;
+  const bool ssim = a.type == 0;
+  const int tid = threadIdx.x;
+
+  for (int i = tid; i < R * R; i += kLossThreads) {
+    const int r = i / R, c = i - r * R;
+    const int gy = reflect_idx(y0 - 2 * HW + r, H), gx = reflect_idx(x0 - 2 * HW + c, W);
+    xs[i] = a.pred[poff + size_t(gy) * W + gx];
+    ys[i] = a.target[poff + size_t(gy) * W + gx];
+  }
+  __syncthreads();
+
+  double sum_s = 0.0;
+  if (ssim) {
+    // horizontal window sums for input rows r in [0,R), mean columns c in [0,M)
+    for (int i = tid; i < R * M; i += kLossThreads) {
+      const int r = i / M, c = i - r * M;
+      float s0 = 0, s1 = 0, s2 = 0, s3 = 0, s4 = 0;
+#pragma unroll
+      for (int k = -HW; k <= HW; ++k) {
+        const float wk = a.w[k + HW];
+        const float x = xs[r * R + c + HW + k], y = ys[r * R + c + HW + k];
+        s0 = fmaf(wk, x, s0);
+        s1 = fmaf(wk, y, s1);
+        s2 = fmaf(wk, x * x, s2);
+        s3 = fmaf(wk, y * y, s3);
+        s4 = fmaf(wk, x * y, s4);
+      }
+      hs[0 * R * M + i] = s0;
+      hs[1 * R * M + i] = s1;
+      hs[2 * R * M + i] = s2;
+      hs[3 * R * M + i] = s3;
+      hs[4 * R * M + i] = s4;
+    }
+    __syncthreads();
+    // vertical sums -> SSIM map and its derivatives w.r.t. the three prediction moments
+    for (int i = tid; i < M * M; i += kLossThreads) {
+      const int r = i / M, c = i - r * M;
+      const int gy = y0 - HW + r, gx = x0 - HW + c;
+      float d_mx = 0.0f, d_mxx = 0.0f, d_mxy = 0.0f;
+      if (gy >= 0 && gy < H && gx >= 0 && gx < W) {
+        float m[5] = {0, 0, 0, 0, 0};
+#pragma unroll
+        for (int k = -HW; k <= HW; ++k) {
+          const float wk = a.w[k + HW];
+          const int row = (r + HW + k) * M + c;
+#pragma unroll
+          for (int q = 0; q < 5; ++q) m[q] = fmaf(wk, hs[q * R * M + row], m[q]);
+        }
+        const float mux = m[0], muy = m[1];
+        const float mux2 = mux * mux, muy2 = muy * muy, muxy = mux * muy;
+        const float sxx = m[2] - mux2, syy = m[3] - muy2, sxy = m[4] - muxy;
+        const float A1 = 2.0f * muxy + a.c1, A2 = 2.0f * sxy + a.c2;
+        const float B1 = mux2 + muy2 + a.c1, B2 = sxx + syy + a.c2;
+        const float Draw = B1 * B2;
+        const float Dc = fmaxf(Draw, 1e-12f);
+        const float s = (A1 * A2) / Dc;
+        const float dsdD = Draw >= 1e-12f ? -s / Dc : 0.0f;
+        const float ds_mu = (2.0f * muy * A2) / Dc + dsdD * (2.0f * mux * B2);  // explicit mu_x
+        const float ds_sxx = dsdD * B1;
+        const float ds_sxy = 2.0f * A1 / Dc;
+        d_mx = ds_mu - 2.0f * mux * ds_sxx - muy * ds_sxy;
+        d_mxx = ds_sxx;
+        d_mxy = ds_sxy;
+        if (r >= HW && r < HW + kLossTile && c >= HW && c < HW + kLossTile) sum_s += double(s);
+      }
+      gm[0 * M * M + i] = d_mx;
+      gm[1 * M * M + i] = d_mxx;
+      gm[2 * M * M + i] = d_mxy;
+    }
+    __syncthreads();
+    // horizontal adjoint: rows r in [0,M), output columns cq in [0,kLossTile)
+    for (int i = tid; i < M * kLossTile; i += kLossThreads) {
+      const int r = i / kLossTile, cq = i - r * kLossTile;
+      const int qx = x0 + cq;
+      float acc0 = 0, acc1 = 0, acc2 = 0;
+      if (qx < W) {
+        const int ms[3] = {qx, (qx >= 1 && qx <= HW) ? -qx : INT32_MIN,
+                           (qx >= W - 1 - HW && qx <= W - 2) ? 2 * (W - 1) - qx : INT32_MIN};
+#pragma unroll
+        for (int t = 0; t < 3; ++t) {
+          if (ms[t] == INT32_MIN) continue;
+#pragma unroll
+          for (int k = -HW; k <= HW; ++k) {
+            const int gi = ms[t] + k;
+            if (gi < 0 || gi >= W) continue;
+            const int col = gi - x0 + HW;
+            const float wk = a.w[k + HW];
+            acc0 = fmaf(wk, gm[0 * M * M + r * M + col], acc0);
+            acc1 = fmaf(wk, gm[1 * M * M + r * M + col], acc1);
+            acc2 = fmaf(wk, gm[2 * M * M + r * M + col], acc2);
+          }
+        }
+      }
+      ha[0 * M * kLossTile + i] = acc0;
+      ha[1 * M * kLossTile + i] = acc1;
+      ha[2 * M * kLossTile + i] = acc2;
+    }
+    __syncthreads();
+  }
+
+  // vertical adjoint + gradient + L1/L2 sums over the output tile
+  double sum_l1 = 0.0, sum_l2 = 0.0;
+  for (int i = tid; i < kLossTile * kLossTile; i += kLossThreads) {
+    const int rq = i / kLossTile, cq = i - rq * kLossTile;
+    const int qy = y0 + rq, qx = x0 + cq;
+    if (qy >= H || qx >= W) continue;
+    const float x = xs[(rq + 2 * HW) * R + cq + 2 * HW];
+    const float y = ys[(rq + 2 * HW) * R + cq + 2 * HW];
+    const float d = x - y;
+    sum_l1 += double(fabsf(d));
+    sum_l2 += double(d * d);
+    if (!a.dpred) continue;
+    const float sgn = d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f);
+    float grad = a.c_l1 * sgn + a.c_mse * 2.0f * d;
+    if (ssim) {
+      float v0 = 0, v1 = 0, v2 = 0;
+      const int ms[3] = {qy, (qy >= 1 && qy <= HW) ? -qy : INT32_MIN,
+                         (qy >= H - 1 - HW && qy <= H - 2) ? 2 * (H - 1) - qy : INT32_MIN};
+#pragma unroll
+      for (int t = 0; t < 3; ++t) {
+        if (ms[t] == INT32_MIN) continue;
+#pragma unroll
+        for (int k = -HW; k <= HW; ++k) {
+          const int gi = ms[t] + k;
+          if (gi < 0 || gi >= H) continue;
+          const int row = gi - y0 + HW;
+          const float wk = a.w[k + HW];
+          v0 = fmaf(wk, ha[0 * M * kLossTile + row * kLossTile + cq], v0);
+          v1 = fmaf(wk, ha[1 * M * kLossTile + row * kLossTile + cq], v1);
+          v2 = fmaf(wk, ha[2 * M * kLossTile + row * kLossTile + cq], v2);
+        }
+      }
+      grad += a.c_ssim * (v0 + 2.0f * x * v1 + y * v2);
+    }
+    a.dpred[poff + size_t(qy) * W + qx] = grad;
+  }
+  // block reduction of the three sums, one double atomic per quantity
+  const int lane = tid & 31, warp = tid >> 5;
+  double v[3] = {sum_l1, sum_l2, sum_s};
+#pragma unroll
+  for (int q = 0; q < 3; ++q) {
+    for (int o = 16; o > 0; o >>= 1) v[q] += __shfl_down_sync(0xffffffffu, v[q], o);
+    if (lane == 0) s_red[q][warp] = v[q];
+  }
+  __syncthreads();
+  if (tid < 3) {
+    double t = 0.0;
+    for (int w = 0; w < kLossThreads / 32; ++w) t += s_red[tid][w];
+    atomicAdd(a.acc + b * 3 + tid, t);
+  }
+}
+
+struct LossFinish {
+  int B;
+  int type;
+  double n;  // C*H*W
+  float l1_weight, dssim_weight, mse_weight;
+  int dssim_half;
+};
+
+__global__ void loss_finish_kernel(LossFinish f, const double* __restrict__ acc, float* __restrict__ loss,
+                                   int32_t* __restrict__ clamp_hit) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= f.B) return;
+  const double l1 = acc[b * 3 + 0] / f.n, mse = acc[b * 3 + 1] / f.n, s = acc[b * 3 + 2] / f.n;
+  const float l1f = float(l1), msef = float(mse);
+  float out;
+  int hit = 0;
+  switch (f.type) {
+    case 1: out = l1f; break;
+    case 2: out = msef; break;
+    case 3: out = f.l1_weight * l1f + f.mse_weight * msef; break;
+    default: {
+      const float sf = float(s);
+      const float sc = fminf(fmaxf(sf, -1.0f), 1.0f);
+      hit = (sf >= -1.0f && sf <= 1.0f) ? 0 : 1;
+      out = f.l1_weight * l1f + f.dssim_weight * ((1.0f - sc) * (f.dssim_half ? 0.5f : 1.0f));
+    }
+  }
+  loss[b] = out;
+  clamp_hit[b] = hit;
+}
+
+// Gradient of an image whose SSIM mean was clamped: the SSIM term contributes nothing.
+__global__ void loss_fixup_kernel(int B, int C, int H, int W, float c_l1, const int32_t* __restrict__ clamp_hit,
+                                  const float* __restrict__ pred, const float* __restrict__ target,
+                                  float* __restrict__ dpred) {
+  const size_t per = size_t(C) * H * W;
+  const size_t total = per * B;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+    if (!clamp_hit[i / per]) continue;
+    const float d = pred[i] - target[i];
+    dpred[i] = c_l1 * (d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f));
+  }
+}
+
+__global__ void scale_planes_kernel(const float* __restrict__ in, const float* __restrict__ scale,
+                                    float* __restrict__ out, int32_t B, int64_t per) {
+  const int64_t total = per * B;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x)
+    out[i] = in[i] * scale[i / per];
+}
+
+// ---- host ------------------------------------------------------------------------------------
+
+size_t loss_workspace(int32_t n_images) {
+  Carver c(nullptr, 0);
+  c.take<WorkspaceHeader>(1);
+  c.take<double>(size_t(n_images) * 3);
+  c.take<int32_t>(n_images);
+  return c.used;
+}
+
+template <int HW>
+static gsb_status launch_loss_t(const LossArgs& a, cudaStream_t st) {
+  constexpr int R = kLossTile + 4 * HW, M = kLossTile + 2 * HW;
+  const size_t smem = sizeof(float) * (2 * R * R + 5 * R * M + 3 * M * M + 3 * M * kLossTile);
+  if (cudaFuncSetAttribute(loss_kernel<HW>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)))
+    return GSB_ERR_CUDA;
+  const dim3 grid((a.W + kLossTile - 1) / kLossTile, (a.H + kLossTile - 1) / kLossTile, a.B * a.C);
+  note_launch();
+  loss_kernel<HW><<<grid, kLossThreads, smem, st>>>(a);
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
+gsb_status loss_fwd_bwd(const gsb_loss_options& o, int32_t B, int32_t C, int32_t H, int32_t W, const float* pred,
+                        const float* target, float* loss, float* dpred, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (!pred || !target || !loss) return GSB_ERR_ARG;
+  if (B <= 0 || C <= 0 || H <= 0 || W <= 0) return GSB_ERR_SHAPE;
+  if (o.type < 0 || o.type > 3) return GSB_ERR_ARG;
+  const int ws_size = o.window_size;
+  const int half = ws_size / 2;
+  if (o.type == 0) {
+    if (ws_size < 3 || ws_size > 15 || (ws_size % 2) == 0) return GSB_ERR_ARG;
+    if (half >= H || half >= W) return GSB_ERR_SHAPE;  // reflect padding needs pad < size
+  }
+  Carver c(ws, ws_bytes);
+  c.take<WorkspaceHeader>(1);
+  double* acc = c.take<double>(size_t(B) * 3);
+  int32_t* hit = c.take<int32_t>(B);
+  if (!c.ok() || !ws) return GSB_ERR_WORKSPACE;
+  if (cudaMemsetAsync(acc, 0, size_t(B) * 3 * sizeof(double), st)) return GSB_ERR_CUDA;
+
+  const double n = double(C) * H * W;
+  LossArgs a{};
+  a.B = B, a.C = C, a.H = H, a.W = W, a.type = o.type, a.c1 = o.c1, a.c2 = o.c2;
+  a.c_l1 = (o.type == 0 || o.type == 3) ? float(o.l1_weight / n) : (o.type == 1 ? float(1.0 / n) : 0.0f);
+  a.c_mse = o.type == 3 ? float(o.mse_weight / n) : (o.type == 2 ? float(1.0 / n) : 0.0f);
+  a.c_ssim = o.type == 0 ? float(-o.dssim_weight * (o.dssim_half ? 0.5 : 1.0) / n) : 0.0f;
+  if (o.type == 0) {
+    if (o.window == 1) {
+      double sum = 0.0, t[16];
+      for (int k = -half; k <= half; ++k) sum += t[k + half] = std::exp(-(double(k) * k) / (2.0 * o.sigma * o.sigma));
+      for (int k = 0; k < ws_size; ++k) a.w[k] = float(t[k] / sum);
+    } else {
+      for (int k = 0; k < ws_size; ++k) a.w[k] = 1.0f / float(ws_size);
+    }
+  }
+  a.pred = pred, a.target = target, a.dpred = dpred, a.acc = acc;
+  gsb_status s;
+  switch (o.type == 0 ? half : 0) {
+    case 0: s = launch_loss_t<0>(a, st); break;
+    case 1: s = launch_loss_t<1>(a, st); break;
+    case 2: s = launch_loss_t<2>(a, st); break;
+    case 3: s = launch_loss_t<3>(a, st); break;
+    case 4: s = launch_loss_t<4>(a, st); break;
+    case 5: s = launch_loss_t<5>(a, st); break;
+    case 6: s = launch_loss_t<6>(a, st); break;
+    default: s = launch_loss_t<7>(a, st); break;
+  }
+  if (s != GSB_OK) return s;
+  LossFinish f{B, o.type, n, o.l1_weight, o.dssim_weight, o.mse_weight, o.dssim_half};
+  note_launch();
+  loss_finish_kernel<<<(B + 127) / 128, 128, 0, st>>>(f, acc, loss, hit);
+  if (dpred && o.type == 0) {
+    const size_t total = size_t(B) * C * H * W;
+    const int grid = int(std::min<size_t>((total + 255) / 256, 148u * 16u));
+    note_launch();
+    loss_fixup_kernel<<<grid, 256, 0, st>>>(B, C, H, W, a.c_l1, hit, pred, target, dpred);
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
+gsb_status scale_planes(const float* in, const float* scale, float* out, int32_t B, int64_t per, cudaStream_t st) {
+  if (!in || !scale || !out || B < 0 || per < 0) return GSB_ERR_ARG;
+  const int64_t total = per * B;
+  if (total == 0) return GSB_OK;
+  const int grid = int(std::min<int64_t>((total + 255) / 256, 148 * 16));
+  note_launch();
+  scale_planes_kernel<<<grid, 256, 0, st>>>(in, scale, out, B, per);
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
+}  // namespace gsb

@@ -1,0 +1,562 @@
+// Preprocess: depth keys, projection (+ activation, SH, time offset), tile bounds and counts,
+// and the chain rule back to the scene parameters.
+//
+// Forward restates the reference's project_gaussians_2d_batch (src/train/renderers/common.py:
+// 149-231): quaternion -> rotation (:169-179), Sigma = (R S)(R S)^T (:181-187), world -> camera
+// (:39-51), near-plane mask keeping the depth slot with opacity 0 (:197-203), EWA Jacobian
+// (:210-214), +0.3 low-pass (:216-218), det clamp 1e-6 and inverse (:220-225), means2D (:227-229).
+// One thread per (view, Gaussian); outputs go to the Gaussian's depth-rank slot so that the
+// binning and raster stages read them in depth order.
+#include "gsb_common.cuh"
+#include "gsb_internal.h"
+#include "tiles.cuh"
+
+namespace gsb {
+
+// ---- real spherical harmonics (degree <= 3), standard 3DGS sign convention -------------------
+// Constants: sqrt((2l+1)/(4 pi) (l-m)!/(l+m)!) with the sqrt(2) of the real basis folded in.
+constexpr float kC0 = 0.28209479177387814f;   // 1 / (2 sqrt(pi))
+constexpr float kC1 = 0.4886025119029199f;    // sqrt(3 / (4 pi))
+constexpr float kC2a = 1.0925484305920792f;   // sqrt(15 / pi) / 2
+constexpr float kC2b = 0.31539156525252005f;  // sqrt(5 / pi) / 4
+constexpr float kC2c = 0.5462742152960396f;   // sqrt(15 / pi) / 4
+constexpr float kC3a = 0.5900435899266435f;   // sqrt(35 / (2 pi)) / 4
+constexpr float kC3b = 2.890611442640554f;    // sqrt(105 / pi) / 2
+constexpr float kC3c = 0.4570457994644658f;   // sqrt(21 / (2 pi)) / 4
+constexpr float kC3d = 0.3731763325901154f;   // sqrt(7 / pi) / 4
+constexpr float kC3e = 1.445305721320277f;    // sqrt(105 / pi) / 4
+
+template <int K>
+__device__ inline void sh_basis(float x, float y, float z, float* Y) {
+  Y[0] = kC0;
+  if (K > 1) {
+    Y[1] = -kC1 * y;
+    Y[2] = kC1 * z;
+    Y[3] = -kC1 * x;
+  }
+  if (K > 4) {
+    const float xx = x * x, yy = y * y, zz = z * z;
+    Y[4] = kC2a * x * y;
+    Y[5] = -kC2a * y * z;
+    Y[6] = kC2b * (2.0f * zz - xx - yy);
+    Y[7] = -kC2a * x * z;
+    Y[8] = kC2c * (xx - yy);
+    if (K > 9) {
+      Y[9] = -kC3a * y * (3.0f * xx - yy);
+      Y[10] = kC3b * x * y * z;
+      Y[11] = -kC3c * y * (4.0f * zz - xx - yy);
+      Y[12] = kC3d * z * (2.0f * zz - 3.0f * xx - 3.0f * yy);
+      Y[13] = -kC3c * x * (4.0f * zz - xx - yy);
+      Y[14] = kC3e * z * (xx - yy);
+      Y[15] = -kC3a * x * (xx - 3.0f * yy);
+    }
+  }
+}
+
+// d Y_k / d(x, y, z) for k < K.
+template <int K>
+__device__ inline void sh_basis_grad(float x, float y, float z, float (*dY)[3]) {
+  dY[0][0] = dY[0][1] = dY[0][2] = 0.0f;
+  if (K > 1) {
+    dY[1][0] = 0.0f, dY[1][1] = -kC1, dY[1][2] = 0.0f;
+    dY[2][0] = 0.0f, dY[2][1] = 0.0f, dY[2][2] = kC1;
+    dY[3][0] = -kC1, dY[3][1] = 0.0f, dY[3][2] = 0.0f;
+  }
+  if (K > 4) {
+    const float xx = x * x, yy = y * y, zz = z * z;
+    dY[4][0] = kC2a * y, dY[4][1] = kC2a * x, dY[4][2] = 0.0f;
+    dY[5][0] = 0.0f, dY[5][1] = -kC2a * z, dY[5][2] = -kC2a * y;
+    dY[6][0] = -2.0f * kC2b * x, dY[6][1] = -2.0f * kC2b * y, dY[6][2] = 4.0f * kC2b * z;
+    dY[7][0] = -kC2a * z, dY[7][1] = 0.0f, dY[7][2] = -kC2a * x;
+    dY[8][0] = 2.0f * kC2c * x, dY[8][1] = -2.0f * kC2c * y, dY[8][2] = 0.0f;
+    if (K > 9) {
+      dY[9][0] = -kC3a * 6.0f * x * y, dY[9][1] = -kC3a * (3.0f * xx - 3.0f * yy), dY[9][2] = 0.0f;
+      dY[10][0] = kC3b * y * z, dY[10][1] = kC3b * x * z, dY[10][2] = kC3b * x * y;
+      dY[11][0] = kC3c * 2.0f * x * y, dY[11][1] = -kC3c * (4.0f * zz - xx - 3.0f * yy), dY[11][2] = -kC3c * 8.0f * y * z;
+      dY[12][0] = -kC3d * 6.0f * x * z, dY[12][1] = -kC3d * 6.0f * y * z,
+      dY[12][2] = kC3d * (6.0f * zz - 3.0f * xx - 3.0f * yy);
+      dY[13][0] = -kC3c * (4.0f * zz - 3.0f * xx - yy), dY[13][1] = kC3c * 2.0f * x * y, dY[13][2] = -kC3c * 8.0f * x * z;
+      dY[14][0] = kC3e * 2.0f * x * z, dY[14][1] = -kC3e * 2.0f * y * z, dY[14][2] = kC3e * (xx - yy);
+      dY[15][0] = -kC3a * (3.0f * xx - 3.0f * yy), dY[15][1] = kC3a * 6.0f * x * y, dY[15][2] = 0.0f;
+    }
+  }
+}
+
+// ---- parameter loading -----------------------------------------------------------------------
+
+struct GaussParams {
+  float m[3];    // means at the view's time
+  float s[3];    // linear scales
+  float q[4];    // quaternion used by the rotation formula
+  float qn_inv;  // raw mode: 1/|q_raw| (for the normalisation backward)
+  float o;       // opacity
+};
+
+__device__ inline GaussParams load_params(const gsb_scene& sc, size_t pg, float t) {
+  GaussParams p;
+  const bool raw = sc.flags & GSB_SCENE_RAW;
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    float m = sc.means[pg * 3 + k];
+    if (sc.flags & GSB_SCENE_VELOCITY) m = __fadd_rn(m, __fmul_rn(t, sc.velocity[pg * 3 + k]));
+    p.m[k] = m;
+    const float s = sc.scales[pg * 3 + k];
+    p.s[k] = raw ? expf(s) : s;
+  }
+  const float4 q4 = reinterpret_cast<const float4*>(sc.quats)[pg];
+  p.q[0] = q4.x, p.q[1] = q4.y, p.q[2] = q4.z, p.q[3] = q4.w;
+  p.qn_inv = 1.0f;
+  if (raw) {
+    const float n = sqrtf(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
+    p.qn_inv = 1.0f / n;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) p.q[k] *= p.qn_inv;
+  }
+  const float o = sc.opacities[pg];
+  p.o = raw ? 1.0f / (1.0f + expf(-o)) : o;
+  return p;
+}
+
+// Rotation of common.py:169-179 (q = r, i, j, k; not renormalised).
+__device__ inline void quat_rot(const float q[4], float R[9]) {
+  const float r = q[0], i = q[1], j = q[2], k = q[3];
+  R[0] = 1.0f - 2.0f * (j * j + k * k);
+  R[1] = 2.0f * (i * j - r * k);
+  R[2] = 2.0f * (i * k + r * j);
+  R[3] = 2.0f * (i * j + r * k);
+  R[4] = 1.0f - 2.0f * (i * i + k * k);
+  R[5] = 2.0f * (j * k - r * i);
+  R[6] = 2.0f * (i * k - r * j);
+  R[7] = 2.0f * (j * k + r * i);
+  R[8] = 1.0f - 2.0f * (i * i + j * j);
+}
+
+// Everything the forward computes for one (view, Gaussian); the backward recomputes it.
+struct Proj {
+  bool front;
+  float d[3];          // mean_t - camera centre (world)
+  float x, y, z;       // camera coordinates
+  float zs, xp, yp;    // z_safe, x_project, y_project
+  float Rq[9];         // Gaussian rotation
+  float M[9];          // Rq diag(s)
+  float cc[9];         // camera-space covariance
+  float J00, J02, J11, J12;
+  float c00, c01, c11; // 2-D covariance incl. the 0.3 low-pass
+  float det_raw, det;
+  float A, B, C;
+  float mx, my;
+  float o_eff;
+};
+
+__device__ inline void project(const GaussParams& p, const Camera& cam, float near_plane, Proj& P) {
+#pragma unroll
+  for (int k = 0; k < 3; ++k) P.d[k] = __fsub_rn(p.m[k], cam.t[k]);
+  P.x = cam_coord(P.d, cam.R, 0);
+  P.y = cam_coord(P.d, cam.R, 1);
+  P.z = cam_coord(P.d, cam.R, 2);
+  quat_rot(p.q, P.Rq);
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int j = 0; j < 3; ++j) P.M[i * 3 + j] = P.Rq[i * 3 + j] * p.s[j];
+  float S[9];
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      S[i * 3 + k] = P.M[i * 3 + 0] * P.M[k * 3 + 0] + P.M[i * 3 + 1] * P.M[k * 3 + 1] + P.M[i * 3 + 2] * P.M[k * 3 + 2];
+  // cc = Rcw^T S Rcw, Rcw[j][k] = cam.R[j*3+k]
+  float T1[9];
+#pragma unroll
+  for (int j = 0; j < 3; ++j)
+#pragma unroll
+    for (int b = 0; b < 3; ++b)
+      T1[j * 3 + b] = S[j * 3 + 0] * cam.R[0 * 3 + b] + S[j * 3 + 1] * cam.R[1 * 3 + b] + S[j * 3 + 2] * cam.R[2 * 3 + b];
+#pragma unroll
+  for (int a = 0; a < 3; ++a)
+#pragma unroll
+    for (int b = 0; b < 3; ++b)
+      P.cc[a * 3 + b] = cam.R[0 * 3 + a] * T1[0 * 3 + b] + cam.R[1 * 3 + a] * T1[1 * 3 + b] + cam.R[2 * 3 + a] * T1[2 * 3 + b];
+  P.front = P.z > near_plane;
+  P.zs = P.front ? fmaxf(P.z, near_plane) : 1.0f;
+  P.xp = P.front ? P.x : 0.0f;
+  P.yp = P.front ? P.y : 0.0f;
+  P.o_eff = p.o * (P.front ? 1.0f : 0.0f);
+  const float fx = cam.k.fx, fy = cam.k.fy;
+  const float zs2 = P.zs * P.zs;
+  P.J00 = fx / P.zs;
+  P.J02 = -(fx * P.xp) / zs2;
+  P.J11 = fy / P.zs;
+  P.J12 = -(fy * P.yp) / zs2;
+  const float* c = P.cc;
+  P.c00 = P.J00 * P.J00 * c[0] + 2.0f * P.J00 * P.J02 * c[2] + P.J02 * P.J02 * c[8] + 0.3f;
+  P.c11 = P.J11 * P.J11 * c[4] + 2.0f * P.J11 * P.J12 * c[5] + P.J12 * P.J12 * c[8] + 0.3f;
+  P.c01 = P.J00 * P.J11 * c[1] + P.J00 * P.J12 * c[2] + P.J02 * P.J11 * c[5] + P.J02 * P.J12 * c[8];
+  P.det_raw = P.c00 * P.c11 - P.c01 * P.c01;
+  P.det = fmaxf(P.det_raw, 1e-6f);
+  P.A = P.c11 / P.det;
+  P.C = P.c00 / P.det;
+  const float inv01 = -P.c01 / P.det;
+  P.B = inv01 + inv01;
+  P.mx = __fadd_rn(__fdiv_rn(__fmul_rn(fx, P.xp), P.zs), cam.k.cx);
+  P.my = __fadd_rn(__fdiv_rn(__fmul_rn(fy, P.yp), P.zs), cam.k.cy);
+}
+
+template <int K>
+__device__ inline void eval_color(const gsb_scene& sc, size_t pg, const float d[3], bool clamp, float rgb[3]) {
+  const float inv = rsqrtf(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
+  float Y[K];
+  sh_basis<K>(d[0] * inv, d[1] * inv, d[2] * inv, Y);
+  const float* sh = sc.colors + pg * size_t(K) * 3;
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    float v = 0.5f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) v += Y[k] * sh[k * 3 + c];
+    rgb[c] = clamp ? fmaxf(v, 0.0f) : v;
+  }
+}
+
+__device__ inline void load_color(const gsb_scene& sc, size_t pg, const float d[3], float rgb[3]) {
+  if (!(sc.flags & GSB_SCENE_RAW)) {
+    rgb[0] = sc.colors[pg * 3 + 0], rgb[1] = sc.colors[pg * 3 + 1], rgb[2] = sc.colors[pg * 3 + 2];
+    return;
+  }
+  const bool clamp = sc.flags & GSB_SCENE_SH_CLAMP;
+  switch (sc.sh_degree) {
+    case 0: eval_color<1>(sc, pg, d, clamp, rgb); break;
+    case 1: eval_color<4>(sc, pg, d, clamp, rgb); break;
+    case 2: eval_color<9>(sc, pg, d, clamp, rgb); break;
+    default: eval_color<16>(sc, pg, d, clamp, rgb); break;
+  }
+}
+
+// ---- stage 1 kernels: depth keys and inverse permutation -------------------------------------
+
+__global__ void depth_key_kernel(gsb_scene sc, gsb_views vw, uint64_t* __restrict__ keys64,
+                                 uint32_t* __restrict__ keys32, uint32_t* __restrict__ vals) {
+  const size_t G = sc.n_gaussians;
+  const size_t total = size_t(vw.n_views) * G;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+    const int b = int(i / G);
+    const size_t g = i - size_t(b) * G;
+    const size_t pg = size_t(b / vw.views_per_set) * G + g;
+    const float t = vw.times ? vw.times[b] : 0.0f;
+    const float* c2w = vw.camera_to_world + b * 16;
+    float d[3], R[9];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      float m = sc.means[pg * 3 + k];
+      if (sc.flags & GSB_SCENE_VELOCITY) m = __fadd_rn(m, __fmul_rn(t, sc.velocity[pg * 3 + k]));
+      d[k] = __fsub_rn(m, c2w[k * 4 + 3]);
+#pragma unroll
+      for (int j = 0; j < 3; ++j) R[k * 3 + j] = c2w[k * 4 + j];
+    }
+    const uint32_t key = float_sort_key(cam_coord(d, R, 2));
+    if (keys64) keys64[i] = (uint64_t(b) << 32) | key;
+    else keys32[i] = key;
+    vals[i] = uint32_t(g);
+  }
+}
+
+__global__ void invert_order_kernel(const uint32_t* __restrict__ sorted_vals, int32_t n_views, int32_t G,
+                                    int32_t* __restrict__ sorted_ids, int32_t* __restrict__ rank_of) {
+  const size_t total = size_t(n_views) * G;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+    const size_t b = i / G;
+    const int32_t r = int32_t(i - b * G);
+    const int32_t g = int32_t(sorted_vals[i]);
+    sorted_ids[i] = g;
+    rank_of[b * G + g] = r;
+  }
+}
+
+// ---- stage 2: projection + bounds ------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) preprocess_fwd_kernel(gsb_scene sc, gsb_views vw, RenderConsts rc,
+                                                             const int32_t* __restrict__ rank_of,
+                                                             float* __restrict__ records, int4* __restrict__ rects,
+                                                             uint32_t* __restrict__ counts, float* __restrict__ cov_out) {
+  const size_t G = sc.n_gaussians;
+  const size_t total = size_t(vw.n_views) * G;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+    const int b = int(i / G);
+    const size_t g = i - size_t(b) * G;
+    const size_t pg = size_t(b / vw.views_per_set) * G + g;
+    const float t = vw.times ? vw.times[b] : 0.0f;
+    const Camera cam = load_camera(vw.intrinsics, vw.camera_to_world, b);
+    const GaussParams p = load_params(sc, pg, t);
+    Proj P;
+    project(p, cam, rc.near_plane, P);
+    float rgb[3];
+    load_color(sc, pg, P.d, rgb);
+
+    TileRect rect;
+    float tau_f;
+    uint32_t count = 0;
+    if (rc.compat) {
+      rect = compat_rect(P.mx, P.my, P.c00, P.c11, P.o_eff, rc.bound_scale, rc.tiled_threshold, vw.height, vw.width,
+                         rc.tile);
+      count = rect.count();
+      tau_f = __int_as_float(0x7f800000);  // +inf: every listed pair is blended
+    } else {
+      ExactShape es;
+      if (exact_rect(P.mx, P.my, P.A, P.B, P.C, P.o_eff, rc.alpha_cutoff, vw.height, vw.width, rc.pixel_center,
+                     rc.tile, &rect, &es)) {
+        if (rc.ellipse) {
+          for (int ty = rect.ty0; ty <= rect.ty1; ++ty)
+            for (int tx = rect.tx0; tx <= rect.tx1; ++tx)
+              count += exact_tile_hit(es, tx, ty, rc.tile, vw.height, vw.width, rc.pixel_center) ? 1u : 0u;
+        } else {
+          count = rect.count();
+        }
+        tau_f = __double2float_ru(es.thresh);
+      } else {
+        tau_f = -1.0f;  // never blended
+      }
+    }
+    const size_t slot = size_t(b) * G + size_t(rank_of[i]);
+    float4* rec = reinterpret_cast<float4*>(records + slot * GSB_RECORD_FLOATS);
+    rec[0] = make_float4(P.mx, P.my, P.A, P.B);
+    rec[1] = make_float4(P.C, P.o_eff, P.z, tau_f);
+    rec[2] = make_float4(rgb[0], rgb[1], rgb[2], 0.0f);
+    rects[slot] = make_int4(rect.tx0, rect.ty0, rect.tx1, rect.ty1);
+    counts[slot] = count;
+    if (cov_out) {
+      cov_out[slot * 3 + 0] = P.c00;
+      cov_out[slot * 3 + 1] = P.c01;
+      cov_out[slot * 3 + 2] = P.c11;
+    }
+  }
+}
+
+// ---- stage 7: backward -----------------------------------------------------------------------
+
+// d loss / d quaternion components (r, i, j, k) from d loss / d R of quat_rot.
+__device__ inline void quat_rot_vjp(const float q[4], const float G[9], float dq[4]) {
+  const float r = q[0], i = q[1], j = q[2], k = q[3];
+  dq[0] = 2.0f * (-k * G[1] + j * G[2] + k * G[3] - i * G[5] - j * G[6] + i * G[7]);
+  dq[1] = 2.0f * (j * G[1] + k * G[2] + j * G[3] - 2.0f * i * G[4] - r * G[5] + k * G[6] + r * G[7] - 2.0f * i * G[8]);
+  dq[2] = 2.0f * (-2.0f * j * G[0] + i * G[1] + r * G[2] + i * G[3] + k * G[5] - r * G[6] + k * G[7] - 2.0f * j * G[8]);
+  dq[3] = 2.0f * (-2.0f * k * G[0] - r * G[1] + i * G[2] + r * G[3] - 2.0f * k * G[4] + j * G[5] + i * G[6] + j * G[7]);
+}
+
+template <int K>  // K = SH coefficients per channel (1, 4, 9, 16) or 0 for plain rgb
+__global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_views vw, RenderConsts rc,
+                                                             const int32_t* __restrict__ rank_of,
+                                                             const float* __restrict__ grad2d, gsb_scene_grads gr) {
+  const size_t G = sc.n_gaussians;
+  const size_t total = size_t(sc.n_sets) * G;
+  const bool raw = sc.flags & GSB_SCENE_RAW;
+  const bool vel = sc.flags & GSB_SCENE_VELOCITY;
+  const bool clamp_sh = sc.flags & GSB_SCENE_SH_CLAMP;
+  constexpr int KC = K > 0 ? K : 1;
+  for (size_t pg = blockIdx.x * size_t(blockDim.x) + threadIdx.x; pg < total; pg += size_t(gridDim.x) * blockDim.x) {
+    const int s = int(pg / G);
+    const size_t g = pg - size_t(s) * G;
+    float am[3] = {0, 0, 0}, av[3] = {0, 0, 0}, as[3] = {0, 0, 0}, aq[4] = {0, 0, 0, 0}, ao = 0.0f;
+    float acol[KC * 3];
+#pragma unroll
+    for (int k = 0; k < KC * 3; ++k) acol[k] = 0.0f;
+    const int b0 = s * vw.views_per_set;
+    const int b1 = min(b0 + vw.views_per_set, vw.n_views);
+    for (int b = b0; b < b1; ++b) {
+      const size_t slot = size_t(b) * G + size_t(rank_of[size_t(b) * G + g]);
+      const float* g2 = grad2d + slot * GSB_GRAD2D_FLOATS;
+      float dmx = g2[0], dmy = g2[1], dA = g2[2], dB = g2[3], dC = g2[4], dO = g2[5];
+      const float dcol[3] = {g2[6], g2[7], g2[8]};
+      const float dzo = g2[9];
+      const float t = vw.times ? vw.times[b] : 0.0f;
+      const Camera cam = load_camera(vw.intrinsics, vw.camera_to_world, b);
+      const GaussParams p = load_params(sc, pg, t);
+      Proj P;
+      project(p, cam, rc.near_plane, P);
+      if (!P.front) continue;  // opacity * 0: no gradient reaches this Gaussian from this view
+      float dmt[3] = {0.0f, 0.0f, 0.0f};
+
+      // colour
+      if (K == 0) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c) acol[c] += dcol[c];
+      } else {
+        const float n2 = P.d[0] * P.d[0] + P.d[1] * P.d[1] + P.d[2] * P.d[2];
+        const float inv = rsqrtf(n2);
+        const float dir[3] = {P.d[0] * inv, P.d[1] * inv, P.d[2] * inv};
+        float Y[KC];
+        sh_basis<KC>(dir[0], dir[1], dir[2], Y);
+        const float* sh = sc.colors + pg * size_t(KC) * 3;
+        float dc[3];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          float v = 0.5f;
+#pragma unroll
+          for (int k = 0; k < KC; ++k) v += Y[k] * sh[k * 3 + c];
+          dc[c] = (clamp_sh && !(v >= 0.0f)) ? 0.0f : dcol[c];
+        }
+#pragma unroll
+        for (int k = 0; k < KC; ++k)
+#pragma unroll
+          for (int c = 0; c < 3; ++c) acol[k * 3 + c] += dc[c] * Y[k];
+        if (KC > 1) {
+          float dY[KC][3];
+          sh_basis_grad<KC>(dir[0], dir[1], dir[2], dY);
+          float ddir[3] = {0.0f, 0.0f, 0.0f};
+#pragma unroll
+          for (int k = 1; k < KC; ++k) {
+            const float w = dc[0] * sh[k * 3 + 0] + dc[1] * sh[k * 3 + 1] + dc[2] * sh[k * 3 + 2];
+            ddir[0] += w * dY[k][0];
+            ddir[1] += w * dY[k][1];
+            ddir[2] += w * dY[k][2];
+          }
+          const float dd = dir[0] * ddir[0] + dir[1] * ddir[1] + dir[2] * ddir[2];
+#pragma unroll
+          for (int k = 0; k < 3; ++k) dmt[k] += (ddir[k] - dir[k] * dd) * inv;
+        }
+      }
+
+      // inverse covariance -> covariance
+      const float det = P.det;
+      const float ddet = (P.det_raw >= 1e-6f) ? -(dA * P.A + dB * P.B + dC * P.C) / det : 0.0f;
+      const float g00 = dC / det + ddet * P.c11;
+      const float g11 = dA / det + ddet * P.c00;
+      const float g01 = -2.0f * dB / det - 2.0f * ddet * P.c01;  // total over the two off-diagonals
+      // covariance = J cc J^T, J rows u = (J00, 0, J02), v = (0, J11, J12)
+      const float u[3] = {P.J00, 0.0f, P.J02}, v[3] = {0.0f, P.J11, P.J12};
+      float cu[3], cv[3];
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        cu[a] = P.cc[a * 3 + 0] * u[0] + P.cc[a * 3 + 1] * u[1] + P.cc[a * 3 + 2] * u[2];
+        cv[a] = P.cc[a * 3 + 0] * v[0] + P.cc[a * 3 + 1] * v[1] + P.cc[a * 3 + 2] * v[2];
+      }
+      const float du0 = 2.0f * g00 * cu[0] + g01 * cv[0];
+      const float du2 = 2.0f * g00 * cu[2] + g01 * cv[2];
+      const float dv1 = 2.0f * g11 * cv[1] + g01 * cu[1];
+      const float dv2 = 2.0f * g11 * cv[2] + g01 * cu[2];
+      float dcc[9];
+#pragma unroll
+      for (int a = 0; a < 3; ++a)
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+          dcc[a * 3 + c] = g00 * u[a] * u[c] + g11 * v[a] * v[c] + 0.5f * g01 * (u[a] * v[c] + v[a] * u[c]);
+      // Jacobian and means2D -> camera coordinates
+      const float fx = cam.k.fx, fy = cam.k.fy, zs = P.zs;
+      const float izs = 1.0f / zs, izs2 = izs * izs, izs3 = izs2 * izs;
+      const float dxp = du2 * (-fx * izs2) + dmx * fx * izs;
+      const float dyp = dv2 * (-fy * izs2) + dmy * fy * izs;
+      const float dzs = du0 * (-fx * izs2) + du2 * (2.0f * fx * P.xp * izs3) + dv1 * (-fy * izs2) +
+                        dv2 * (2.0f * fy * P.yp * izs3) + dmx * (-fx * P.xp * izs2) + dmy * (-fy * P.yp * izs2);
+      const float dmc[3] = {dxp, dyp, dzs + dzo};
+      // camera -> world: mc = Rcw^T d, cc = Rcw^T S Rcw
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+        dmt[j] += cam.R[j * 3 + 0] * dmc[0] + cam.R[j * 3 + 1] * dmc[1] + cam.R[j * 3 + 2] * dmc[2];
+      float T2[9], dS[9];
+#pragma unroll
+      for (int a = 0; a < 3; ++a)
+#pragma unroll
+        for (int k = 0; k < 3; ++k)
+          T2[a * 3 + k] = dcc[a * 3 + 0] * cam.R[k * 3 + 0] + dcc[a * 3 + 1] * cam.R[k * 3 + 1] + dcc[a * 3 + 2] * cam.R[k * 3 + 2];
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+#pragma unroll
+        for (int k = 0; k < 3; ++k)
+          dS[j * 3 + k] = cam.R[j * 3 + 0] * T2[0 * 3 + k] + cam.R[j * 3 + 1] * T2[1 * 3 + k] + cam.R[j * 3 + 2] * T2[2 * 3 + k];
+      // S = M M^T -> dM = (dS + dS^T) M
+      float dRq[9];
+      float dsv[3] = {0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          float dm = 0.0f;
+#pragma unroll
+          for (int k = 0; k < 3; ++k) dm += (dS[i * 3 + k] + dS[k * 3 + i]) * P.M[k * 3 + j];
+          dRq[i * 3 + j] = dm * p.s[j];
+          dsv[j] += dm * P.Rq[i * 3 + j];
+        }
+      float dq[4];
+      quat_rot_vjp(p.q, dRq, dq);
+      if (raw) {
+        const float dot = p.q[0] * dq[0] + p.q[1] * dq[1] + p.q[2] * dq[2] + p.q[3] * dq[3];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) aq[k] += (dq[k] - p.q[k] * dot) * p.qn_inv;
+#pragma unroll
+        for (int k = 0; k < 3; ++k) as[k] += dsv[k] * p.s[k];
+        ao += dO * p.o * (1.0f - p.o);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) aq[k] += dq[k];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) as[k] += dsv[k];
+        ao += dO;
+      }
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        am[k] += dmt[k];
+        av[k] += t * dmt[k];
+      }
+    }
+    if (gr.means)
+      for (int k = 0; k < 3; ++k) gr.means[pg * 3 + k] = am[k];
+    if (gr.scales)
+      for (int k = 0; k < 3; ++k) gr.scales[pg * 3 + k] = as[k];
+    if (gr.quats)
+      for (int k = 0; k < 4; ++k) gr.quats[pg * 4 + k] = aq[k];
+    if (gr.opacities) gr.opacities[pg] = ao;
+    if (gr.colors)
+      for (int k = 0; k < KC * 3; ++k) gr.colors[pg * KC * 3 + k] = acol[k];
+    if (gr.velocity && vel)
+      for (int k = 0; k < 3; ++k) gr.velocity[pg * 3 + k] = av[k];
+  }
+}
+
+// ---- host launchers --------------------------------------------------------------------------
+
+static int grid_for(size_t n, int threads) {
+  const size_t blocks = (n + threads - 1) / threads;
+  return int(std::min<size_t>(blocks, size_t(148) * 64));
+}
+
+gsb_status launch_depth_keys(const gsb_scene& sc, const gsb_views& vw, uint64_t* keys64, uint32_t* keys32,
+                             uint32_t* vals, cudaStream_t st) {
+  const size_t n = size_t(vw.n_views) * sc.n_gaussians;
+  note_launch();
+  depth_key_kernel<<<grid_for(n, 256), 256, 0, st>>>(sc, vw, keys64, keys32, vals);
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
+gsb_status launch_invert_order(const uint32_t* sorted_vals, int32_t B, int32_t G, int32_t* sorted_ids,
+                               int32_t* rank_of, cudaStream_t st) {
+  note_launch();
+  invert_order_kernel<<<grid_for(size_t(B) * G, 256), 256, 0, st>>>(sorted_vals, B, G, sorted_ids, rank_of);
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
+gsb_status launch_preprocess_fwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
+                                 const int32_t* rank_of, float* records, int4* rects, uint32_t* counts, float* cov,
+                                 cudaStream_t st) {
+  const size_t n = size_t(vw.n_views) * sc.n_gaussians;
+  note_launch();
+  preprocess_fwd_kernel<<<grid_for(n, 256), 256, 0, st>>>(sc, vw, rc, rank_of, records, rects, counts, cov);
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
+gsb_status launch_preprocess_bwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
+                                 const int32_t* rank_of, const float* grad2d, const gsb_scene_grads& gr,
+                                 cudaStream_t st) {
+  const size_t n = size_t(sc.n_sets) * sc.n_gaussians;
+  const int grid = grid_for(n, 128);
+  const bool raw = sc.flags & GSB_SCENE_RAW;
+  const int deg = raw ? sc.sh_degree : -1;
+  switch (deg) {
+    case -1: { note_launch(); preprocess_bwd_kernel<0><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); } break;
+    case 0: { note_launch(); preprocess_bwd_kernel<1><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); } break;
+    case 1: { note_launch(); preprocess_bwd_kernel<4><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); } break;
+    case 2: { note_launch(); preprocess_bwd_kernel<9><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); } break;
+    case 3: { note_launch(); preprocess_bwd_kernel<16><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); } break;
+    default: return GSB_ERR_ARG;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
+}  // namespace gsb

@@ -1,0 +1,389 @@
+// Hand-written LSD radix sort (one-sweep: one read and one write of the keys per 8-bit digit,
+// partition prefixes by decoupled look-back) and a three-phase exclusive prefix scan.
+//
+// Look-back waits are bounded: a partition that waits more than kSpinLimit polls records
+// GSB_ERR_TIMEOUT in the workspace status word and carries on with the prefix it has, so a bug
+// can corrupt the output but never hangs the GPU.  Partitions take their index from an atomic
+// counter in start order, so a partition only ever waits on partitions that are already running.
+#include <cstring>
+
+#include "gsb_common.cuh"
+#include "gsb_internal.h"
+
+namespace gsb {
+
+constexpr int kSortThreads = 256;
+constexpr int kSortWarps = kSortThreads / 32;
+constexpr uint32_t kFlagAgg = 1u << 30;
+constexpr uint32_t kFlagIncl = 2u << 30;
+constexpr uint32_t kCountMask = (1u << 30) - 1u;
+constexpr int kSpinLimit = 1 << 22;
+
+template <typename K>
+struct SortTraits;
+template <>
+struct SortTraits<uint32_t> {
+  static constexpr int kItems = 16;
+};
+template <>
+struct SortTraits<uint64_t> {
+  static constexpr int kItems = 12;
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// Histograms of every pass's digit, all passes in one read of the keys.
+template <typename K>
+__global__ void __launch_bounds__(kSortThreads) radix_hist_kernel(const K* __restrict__ keys, uint32_t n,
+                                                                  int bit_lo, int bit_hi, int passes,
+                                                                  uint32_t* __restrict__ hist) {
+  __shared__ uint32_t s_hist[8][256];
+  for (int i = threadIdx.x; i < passes * 256; i += blockDim.x) s_hist[i / 256][i % 256] = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t base = blockIdx.x * blockDim.x; base < n; base += stride) {
+    const uint32_t i = base + threadIdx.x;
+    const bool valid = i < n;
+    const K k = valid ? keys[i] : K(0);
+    for (int p = 0; p < passes; ++p) {
+      const int shift = bit_lo + 8 * p;
+      const int nbits = min(8, bit_hi - shift);
+      const uint32_t d = valid ? uint32_t((k >> shift) & K((1u << nbits) - 1u)) : 0xffffffffu;
+      const uint32_t peers = __match_any_sync(0xffffffffu, d);
+      if (valid && lane == __ffs(peers) - 1) atomicAdd(&s_hist[p][d], __popc(peers));
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < passes * 256; i += blockDim.x) {
+    const uint32_t c = s_hist[i / 256][i % 256];
+    if (c) atomicAdd(&hist[i], c);
+  }
+}
+
+// Exclusive scan of 256 values held one per thread (blockDim == 256); returns the total too.
+__device__ __forceinline__ uint32_t block_excl_scan_256(uint32_t v, uint32_t* s_tmp, uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_tmp[warp] = x;
+  __syncthreads();
+  uint32_t warp_base = 0, all = 0;
+  for (int w = 0; w < kSortWarps; ++w) {
+    const uint32_t t = s_tmp[w];
+    if (w < warp) warp_base += t;
+    all += t;
+  }
+  __syncthreads();
+  if (total) *total = all;
+  return warp_base + x - v;
+}
+
+template <typename K, bool kVals>
+__global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
+    const K* __restrict__ keys_in, K* __restrict__ keys_out, const uint32_t* __restrict__ vals_in,
+    uint32_t* __restrict__ vals_out, uint32_t n, int shift, int nbits, const uint32_t* __restrict__ hist,
+    uint32_t* __restrict__ lookback, uint32_t* __restrict__ part_counter, int32_t* __restrict__ status) {
+  constexpr int kItems = SortTraits<K>::kItems;
+  constexpr uint32_t kPart = kSortThreads * kItems;
+  __shared__ uint32_t s_part;
+  __shared__ uint32_t s_warp_hist[kSortWarps][256];
+  __shared__ uint32_t s_base[256];
+  __shared__ uint32_t s_tmp[kSortWarps];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) s_part = atomicAdd(part_counter, 1u);
+  for (int w = 0; w < kSortWarps; ++w) s_warp_hist[w][tid] = 0;
+  __syncthreads();
+  const uint32_t part = s_part;
+  const uint32_t mask = (1u << nbits) - 1u;
+
+  // Warp-striped load: warp w owns keys [part*kPart + w*32*kItems, +32*kItems), item j of lane l
+  // is key base + 32*j + l, so (j, lane) order is input order: the ranking below is stable.
+  const uint32_t base = part * kPart + warp * 32 * kItems + lane;
+  K k[kItems];
+  uint32_t v[kItems];
+  uint32_t rank[kItems];
+  uint32_t dig[kItems];
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const uint32_t idx = base + 32 * j;
+    const bool valid = idx < n;
+    k[j] = valid ? keys_in[idx] : K(0);
+    if (kVals) v[j] = valid ? vals_in[idx] : 0u;
+    dig[j] = valid ? uint32_t((k[j] >> shift) & K(mask)) : 0xffffffffu;
+  }
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const uint32_t d = dig[j];
+    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    uint32_t cnt = 0;
+    if (d != 0xffffffffu) cnt = s_warp_hist[warp][d];
+    __syncwarp();
+    if (d != 0xffffffffu) {
+      rank[j] = cnt + __popc(peers & lanemask_lt());
+      if (lane == 31 - __clz(peers)) s_warp_hist[warp][d] = cnt + __popc(peers);
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+
+  // Per digit (one per thread): exclusive prefix over warps, partition total.
+  uint32_t total = 0;
+  for (int w = 0; w < kSortWarps; ++w) {
+    const uint32_t c = s_warp_hist[w][tid];
+    s_warp_hist[w][tid] = total;
+    total += c;
+  }
+  // Publish this partition's digit count, then look back for the exclusive prefix.
+  uint32_t* my = lookback + size_t(part) * 256 + tid;
+  if (part == 0) {
+    st_release_u32(my, kFlagIncl | total);
+  } else {
+    st_release_u32(my, kFlagAgg | total);
+  }
+  uint32_t excl = 0;
+  if (part > 0) {
+    int64_t p = int64_t(part) - 1;
+    int spins = 0;
+    while (p >= 0) {
+      const uint32_t w = ld_acquire_u32(lookback + size_t(p) * 256 + tid);
+      const uint32_t flag = w & ~kCountMask;
+      if (flag == 0u) {
+        if (++spins > kSpinLimit) {
+          record_error(status, GSB_ERR_TIMEOUT, int(part));
+          break;
+        }
+        continue;
+      }
+      excl += w & kCountMask;
+      if (flag == kFlagIncl) break;
+      --p;
+    }
+    st_release_u32(my, kFlagIncl | ((excl + total) & kCountMask));
+  }
+  const uint32_t digit_start = block_excl_scan_256(hist[tid], s_tmp, nullptr);
+  s_base[tid] = digit_start + excl;
+  __syncthreads();
+
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const uint32_t d = dig[j];
+    if (d == 0xffffffffu) continue;
+    const uint32_t pos = s_base[d] + s_warp_hist[warp][d] + rank[j];
+    keys_out[pos] = k[j];
+    if (kVals) vals_out[pos] = v[j];
+  }
+}
+
+// ---- host driver ---------------------------------------------------------------------------
+
+static uint32_t parts_for(uint32_t n, int key_bytes) {
+  const uint32_t part = kSortThreads * (key_bytes == 8 ? SortTraits<uint64_t>::kItems : SortTraits<uint32_t>::kItems);
+  return (n + part - 1) / part;
+}
+
+size_t radix_sort_workspace(uint32_t n, int key_bytes, int with_values) {
+  const int passes = 8;  // worst case (64-bit keys)
+  const uint32_t parts = parts_for(n, key_bytes);
+  Carver c(nullptr, 0);
+  c.take<WorkspaceHeader>(1);
+  c.take<uint32_t>(size_t(passes) * 256);          // histograms
+  c.take<uint32_t>(size_t(passes));                // partition counters
+  c.take<uint32_t>(size_t(passes) * parts * 256);  // look-back
+  c.take<char>(size_t(n) * key_bytes);             // ping-pong keys
+  if (with_values) c.take<uint32_t>(n);            // ping-pong values
+  return c.used;
+}
+
+template <typename K>
+static gsb_status radix_sort_t(const K* keys_in, K* keys_out, const uint32_t* vals_in, uint32_t* vals_out,
+                               uint32_t n, int bit_lo, int bit_hi, void* ws, size_t ws_bytes,
+                               cudaStream_t stream, int32_t* status) {
+  const int passes = (bit_hi - bit_lo + 7) / 8;
+  const bool with_vals = vals_in != nullptr;
+  if (n == 0) return GSB_OK;
+  if (passes <= 0) {
+    if (cudaMemcpyAsync(keys_out, keys_in, size_t(n) * sizeof(K), cudaMemcpyDeviceToDevice, stream)) return GSB_ERR_CUDA;
+    if (with_vals && cudaMemcpyAsync(vals_out, vals_in, size_t(n) * 4, cudaMemcpyDeviceToDevice, stream)) return GSB_ERR_CUDA;
+    return GSB_OK;
+  }
+  const uint32_t parts = parts_for(n, sizeof(K));
+  Carver c(ws, ws_bytes);
+  c.take<WorkspaceHeader>(1);
+  uint32_t* hist = c.take<uint32_t>(size_t(8) * 256);
+  uint32_t* counters = c.take<uint32_t>(8);
+  uint32_t* lookback = c.take<uint32_t>(size_t(8) * parts * 256);
+  K* alt_keys = reinterpret_cast<K*>(c.take<char>(size_t(n) * sizeof(K)));
+  uint32_t* alt_vals = with_vals ? c.take<uint32_t>(n) : nullptr;
+  if (!c.ok()) return GSB_ERR_WORKSPACE;
+  // hist, counters and look-back are contiguous after the header: one memset clears them.
+  const size_t clear_bytes = reinterpret_cast<char*>(lookback + size_t(8) * parts * 256) - reinterpret_cast<char*>(hist);
+  if (cudaMemsetAsync(hist, 0, clear_bytes, stream)) return GSB_ERR_CUDA;
+
+  const int hist_blocks = int(std::min<uint32_t>((n + kSortThreads - 1) / kSortThreads, 148u * 8u));
+  note_launch();
+  radix_hist_kernel<K><<<hist_blocks, kSortThreads, 0, stream>>>(keys_in, n, bit_lo, bit_hi, passes, hist);
+  const K* src_k = keys_in;
+  const uint32_t* src_v = vals_in;
+  for (int p = 0; p < passes; ++p) {
+    const bool to_out = ((passes - 1 - p) % 2) == 0;
+    K* dst_k = to_out ? keys_out : alt_keys;
+    uint32_t* dst_v = with_vals ? (to_out ? vals_out : alt_vals) : nullptr;
+    const int shift = bit_lo + 8 * p;
+    const int nbits = std::min(8, bit_hi - shift);
+    if (with_vals) {
+      note_launch();
+      onesweep_kernel<K, true><<<parts, kSortThreads, 0, stream>>>(src_k, dst_k, src_v, dst_v, n, shift, nbits,
+                                                                    hist + 256 * p, lookback + size_t(p) * parts * 256,
+                                                                    counters + p, status);
+    } else {
+      note_launch();
+      onesweep_kernel<K, false><<<parts, kSortThreads, 0, stream>>>(src_k, dst_k, nullptr, nullptr, n, shift, nbits,
+                                                                     hist + 256 * p, lookback + size_t(p) * parts * 256,
+                                                                     counters + p, status);
+    }
+    src_k = dst_k;
+    src_v = dst_v;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
+gsb_status radix_sort(const void* keys_in, void* keys_out, const uint32_t* vals_in, uint32_t* vals_out, uint32_t n,
+                      int key_bytes, int bit_lo, int bit_hi, void* ws, size_t ws_bytes, cudaStream_t stream,
+                      int32_t* status) {
+  if (n >= (1u << 30)) return GSB_ERR_KEY_OVERFLOW;
+  if (bit_lo < 0 || bit_hi > key_bytes * 8 || bit_hi < bit_lo) return GSB_ERR_ARG;
+  if ((vals_in == nullptr) != (vals_out == nullptr)) return GSB_ERR_ARG;
+  if (key_bytes == 4)
+    return radix_sort_t<uint32_t>(static_cast<const uint32_t*>(keys_in), static_cast<uint32_t*>(keys_out), vals_in,
+                                  vals_out, n, bit_lo, bit_hi, ws, ws_bytes, stream, status);
+  if (key_bytes == 8)
+    return radix_sort_t<uint64_t>(static_cast<const uint64_t*>(keys_in), static_cast<uint64_t*>(keys_out), vals_in,
+                                  vals_out, n, bit_lo, bit_hi, ws, ws_bytes, stream, status);
+  return GSB_ERR_ARG;
+}
+
+// ---- exclusive prefix scan of uint32 counts (three phases, no inter-block waits) -------------
+
+constexpr int kScanThreads = 256;
+constexpr int kScanItems = 16;
+constexpr uint32_t kScanTile = kScanThreads * kScanItems;
+
+__global__ void __launch_bounds__(kScanThreads) scan_reduce_kernel(const uint32_t* __restrict__ in, uint32_t n,
+                                                                    unsigned long long* __restrict__ block_sums) {
+  __shared__ unsigned long long s[kScanThreads / 32];
+  const uint32_t base = blockIdx.x * kScanTile;
+  unsigned long long acc = 0;
+  for (int j = 0; j < kScanItems; ++j) {
+    const uint32_t i = base + j * kScanThreads + threadIdx.x;
+    if (i < n) acc += in[i];
+  }
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long t = 0;
+    for (int w = 0; w < kScanThreads / 32; ++w) t += s[w];
+    block_sums[blockIdx.x] = t;
+  }
+}
+
+// One block: exclusive scan of the block sums in place; writes the grand total.
+__global__ void __launch_bounds__(1024) scan_blocksums_kernel(unsigned long long* __restrict__ sums, uint32_t nb,
+                                                                uint32_t* __restrict__ total_out,
+                                                                int32_t* __restrict__ status) {
+  __shared__ unsigned long long s_w[32];
+  __shared__ unsigned long long s_carry;
+  if (threadIdx.x == 0) s_carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (uint32_t base = 0; base < nb; base += blockDim.x) {
+    const uint32_t i = base + threadIdx.x;
+    const unsigned long long v = i < nb ? sums[i] : 0ull;
+    unsigned long long x = v;
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned long long y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) s_w[warp] = x;
+    __syncthreads();
+    unsigned long long wb = 0, all = 0;
+    for (int w = 0; w < int(blockDim.x / 32); ++w) {
+      if (w < warp) wb += s_w[w];
+      all += s_w[w];
+    }
+    const unsigned long long carry = s_carry;
+    if (i < nb) sums[i] = carry + wb + x - v;
+    __syncthreads();
+    if (threadIdx.x == 0) s_carry = carry + all;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const unsigned long long t = s_carry;
+    if (t >= (1ull << 30)) record_error(status, GSB_ERR_KEY_OVERFLOW, 0);
+    *total_out = uint32_t(t >= 0xffffffffull ? 0xffffffffull : t);
+  }
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const uint32_t* __restrict__ in, uint32_t n,
+                                                                   const unsigned long long* __restrict__ block_off,
+                                                                   uint32_t* __restrict__ out) {
+  __shared__ uint32_t s_tmp[kScanThreads / 32];
+  // Blocked per-thread ranges keep the scan order: thread t owns items [t*kItems, (t+1)*kItems).
+  const uint32_t base = blockIdx.x * kScanTile + threadIdx.x * kScanItems;
+  uint32_t x[kScanItems];
+  uint32_t sum = 0;
+#pragma unroll
+  for (int j = 0; j < kScanItems; ++j) {
+    const uint32_t i = base + j;
+    x[j] = i < n ? in[i] : 0u;
+    sum += x[j];
+  }
+  const uint32_t before = block_excl_scan_256(sum, s_tmp, nullptr);
+  uint32_t run = uint32_t(block_off[blockIdx.x]) + before;
+#pragma unroll
+  for (int j = 0; j < kScanItems; ++j) {
+    const uint32_t i = base + j;
+    if (i < n) out[i] = run;
+    run += x[j];
+  }
+}
+
+size_t exclusive_scan_workspace(uint32_t n) {
+  const uint32_t nb = (n + kScanTile - 1) / kScanTile;
+  return align_up(size_t(nb + 1) * sizeof(unsigned long long));
+}
+
+gsb_status exclusive_scan(const uint32_t* counts, uint32_t n, uint32_t* offsets, void* scratch, size_t scratch_bytes,
+                          cudaStream_t stream, int32_t* status) {
+  const uint32_t nb = (n + kScanTile - 1) / kScanTile;
+  if (scratch_bytes < exclusive_scan_workspace(n)) return GSB_ERR_WORKSPACE;
+  auto* sums = static_cast<unsigned long long*>(scratch);
+  if (n == 0) return cudaMemsetAsync(offsets, 0, 4, stream) ? GSB_ERR_CUDA : GSB_OK;
+  note_launch();
+  scan_reduce_kernel<<<nb, kScanThreads, 0, stream>>>(counts, n, sums);
+  note_launch();
+  scan_blocksums_kernel<<<1, 1024, 0, stream>>>(sums, nb, offsets + n, status);
+  note_launch();
+  scan_apply_kernel<<<nb, kScanThreads, 0, stream>>>(counts, n, sums, offsets);
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
+}  // namespace gsb

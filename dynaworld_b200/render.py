@@ -1,0 +1,267 @@
+"""Render pipeline over the C ABI, and its torch.autograd wrapper.
+
+Forward: depth order -> projection/bounds/pair offsets -> (one host read of the pair count) ->
+pair keys + radix sort + tile ranges -> blend.  Backward: reverse blend -> chain rule to the scene
+parameters.  Every stage is a libgsb200 kernel; torch only allocates memory and supplies the
+stream.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .config import B200RendererConfig
+
+MIN_RENDER_DEPTH = 1e-4  # src/train/renderers/common.py:3
+
+# Optional stage timing: when set to a list, every C-ABI stage call appends
+# (stage name, start event, end event), both recorded on the launching stream.
+STAGE_EVENTS: list | None = None
+
+
+class _stage:
+    """Brackets one C-ABI call with CUDA events when STAGE_EVENTS is enabled."""
+
+    def __init__(self, name: str):
+        self.name = name
+        self.ev = None
+
+    def __enter__(self):
+        if STAGE_EVENTS is not None:
+            self.ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            self.ev[0].record()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ev is not None:
+            self.ev[1].record()
+            STAGE_EVENTS.append((self.name, *self.ev))
+        return False
+
+
+@dataclass
+class SceneSpec:
+    """Non-tensor description of a scene (Gaussian parameter sets)."""
+
+    n_sets: int
+    n_gaussians: int
+    raw: bool
+    sh_degree: int
+    velocity: bool
+    sh_clamp: bool
+
+
+@dataclass
+class ViewSpec:
+    n_views: int
+    views_per_set: int
+    height: int
+    width: int
+
+
+@dataclass
+class FrameState:
+    """What the backward needs from the forward (all device tensors)."""
+
+    rank_of: torch.Tensor
+    records: torch.Tensor
+    keys: torch.Tensor
+    ranges: torch.Tensor
+    pixel_t: torch.Tensor
+    pixel_state: torch.Tensor
+    n_pairs: int
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ws(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def _f32(t: torch.Tensor | None) -> torch.Tensor | None:
+    if t is None:
+        return None
+    return t.detach().to(dtype=torch.float32).contiguous()
+
+
+def scene_struct(spec: SceneSpec, means, scales, quats, opacities, colors, velocity) -> _lib.Scene:
+    s = _lib.Scene()
+    s.n_sets = spec.n_sets
+    s.n_gaussians = spec.n_gaussians
+    s.sh_degree = spec.sh_degree
+    flags = 0
+    if spec.raw:
+        flags |= _lib.SCENE_RAW
+        if spec.sh_clamp:
+            flags |= _lib.SCENE_SH_CLAMP
+    if spec.velocity:
+        flags |= _lib.SCENE_VELOCITY
+    s.flags = flags
+    s.means, s.scales, s.quats = means.data_ptr(), scales.data_ptr(), quats.data_ptr()
+    s.opacities, s.colors = opacities.data_ptr(), colors.data_ptr()
+    s.velocity = velocity.data_ptr() if velocity is not None else None
+    return s
+
+
+def views_struct(spec: ViewSpec, intrinsics, camera_to_world, times) -> _lib.Views:
+    v = _lib.Views()
+    v.n_views, v.views_per_set, v.height, v.width = spec.n_views, spec.views_per_set, spec.height, spec.width
+    v.intrinsics = intrinsics.data_ptr()
+    v.camera_to_world = camera_to_world.data_ptr()
+    v.times = times.data_ptr() if times is not None else None
+    return v
+
+
+def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, near_plane: float,
+                   tensors: dict) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None, FrameState]:
+    L = _lib.lib()
+    dev = tensors["means"].device
+    st = _stream(dev)
+    B, G, H, W = vspec.n_views, sspec.n_gaussians, vspec.height, vspec.width
+    scene = scene_struct(sspec, tensors["means"], tensors["scales"], tensors["quats"], tensors["opacities"],
+                         tensors["colors"], tensors.get("velocity"))
+    views = views_struct(vspec, tensors["intrinsics"], tensors["camera_to_world"], tensors.get("times"))
+    opts = cfg.options(near_plane)
+
+    sorted_ids = torch.empty(B * G, dtype=torch.int32, device=dev)
+    rank_of = torch.empty(B * G, dtype=torch.int32, device=dev)
+    ws1 = _ws(L.gsb_depth_order_workspace(scene, views), dev)
+    with _stage("depth_order"):
+        _lib.check("gsb_depth_order", L.gsb_depth_order(scene, views, sorted_ids.data_ptr(), rank_of.data_ptr(),
+                                                        ws1.data_ptr(), ws1.numel(), st))
+    records = torch.empty(B * G * _lib.RECORD_FLOATS, dtype=torch.float32, device=dev)
+    rects = torch.empty(B * G * 4, dtype=torch.int32, device=dev)
+    offsets = torch.empty(B * G + 1, dtype=torch.int32, device=dev)
+    ws2 = _ws(L.gsb_preprocess_workspace(views, G), dev)
+    with _stage("preprocess_fwd"):
+        _lib.check("gsb_preprocess_fwd", L.gsb_preprocess_fwd(scene, views, opts, rank_of.data_ptr(),
+                                                              records.data_ptr(), rects.data_ptr(),
+                                                              offsets.data_ptr(), None, ws2.data_ptr(), ws2.numel(),
+                                                              st))
+    # The one host synchronisation of the forward: pair count plus the device status words.
+    head = torch.cat([offsets[-1:], ws1.view(torch.int32)[:1], ws2.view(torch.int32)[:1]]).cpu().tolist()
+    n_pairs = head[0] & 0xFFFFFFFF
+    for name, code in (("gsb_depth_order", head[1]), ("gsb_preprocess_fwd", head[2])):
+        _lib.check(name, code)
+    n_tiles = -(-H // cfg.tile_size) * -(-W // cfg.tile_size)
+    keys = torch.empty(max(n_pairs, 1), dtype=torch.int64, device=dev)
+    ranges = torch.empty(B * n_tiles * 2, dtype=torch.int32, device=dev)
+    ws3 = _ws(L.gsb_bin_workspace(views, opts, G, n_pairs), dev)
+    with _stage("bin"):
+        _lib.check("gsb_bin", L.gsb_bin(views, opts, G, records.data_ptr(), rects.data_ptr(), offsets.data_ptr(),
+                                        n_pairs, keys.data_ptr(), ranges.data_ptr(), ws3.data_ptr(), ws3.numel(), st))
+    image = torch.empty(B, 3, H, W, dtype=torch.float32, device=dev)
+    alpha = torch.empty(B, H, W, dtype=torch.float32, device=dev)
+    depth = torch.empty(B, H, W, dtype=torch.float32, device=dev) if cfg.depth else None
+    pixel_t = torch.empty(B, H, W, dtype=torch.float32, device=dev)
+    pixel_state = torch.empty(B, H, W, dtype=torch.int32, device=dev)
+    with _stage("raster_fwd"):
+        _lib.check("gsb_raster_fwd", L.gsb_raster_fwd(views, opts, G, records.data_ptr(), keys.data_ptr(),
+                                                      ranges.data_ptr(), image.data_ptr(), alpha.data_ptr(),
+                                                      _lib.ptr(depth), pixel_t.data_ptr(), pixel_state.data_ptr(),
+                                                      st))
+    if cfg.check_status:
+        _lib.check("gsb_bin", int(ws3.view(torch.int32)[0].item()))
+    state = FrameState(rank_of, records, keys, ranges, pixel_t, pixel_state, n_pairs)
+    return image, alpha, depth, state
+
+
+def backward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, near_plane: float, tensors: dict,
+                    state: FrameState, d_image: torch.Tensor, d_alpha: torch.Tensor | None,
+                    d_depth: torch.Tensor | None, view_scale: torch.Tensor | None = None) -> dict:
+    L = _lib.lib()
+    dev = tensors["means"].device
+    st = _stream(dev)
+    B, G = vspec.n_views, sspec.n_gaussians
+    scene = scene_struct(sspec, tensors["means"], tensors["scales"], tensors["quats"], tensors["opacities"],
+                         tensors["colors"], tensors.get("velocity"))
+    views = views_struct(vspec, tensors["intrinsics"], tensors["camera_to_world"], tensors.get("times"))
+    opts = cfg.options(near_plane)
+    grad2d = torch.empty(B * G * _lib.GRAD2D_FLOATS, dtype=torch.float32, device=dev)
+    with _stage("raster_bwd"):
+        _lib.check("gsb_raster_bwd", L.gsb_raster_bwd(views, opts, G, state.records.data_ptr(),
+                                                      state.keys.data_ptr(), state.ranges.data_ptr(),
+                                                      state.pixel_t.data_ptr(), state.pixel_state.data_ptr(),
+                                                      d_image.data_ptr(), _lib.ptr(d_alpha), _lib.ptr(d_depth),
+                                                      _lib.ptr(view_scale), grad2d.data_ptr(), st))
+    out = {k: torch.empty_like(tensors[k]) for k in ("means", "scales", "quats", "opacities", "colors")}
+    if sspec.velocity:
+        out["velocity"] = torch.empty_like(tensors["velocity"])
+    g = _lib.SceneGrads()
+    g.means, g.scales, g.quats = out["means"].data_ptr(), out["scales"].data_ptr(), out["quats"].data_ptr()
+    g.opacities, g.colors = out["opacities"].data_ptr(), out["colors"].data_ptr()
+    g.velocity = out["velocity"].data_ptr() if "velocity" in out else None
+    with _stage("preprocess_bwd"):
+        _lib.check("gsb_preprocess_bwd", L.gsb_preprocess_bwd(scene, views, opts, state.rank_of.data_ptr(),
+                                                              grad2d.data_ptr(), g, st))
+    return out
+
+
+_PARAM_NAMES = ("means", "scales", "quats", "opacities", "colors", "velocity")
+
+
+class _RenderFunction(torch.autograd.Function):
+    """(image [B,3,H,W], alpha [B,H,W], depth [B,H,W]) of the scene; gradients flow to the six
+    scene tensors.  Camera tensors get no gradient (the forward refuses cameras that need one)."""
+
+    @staticmethod
+    def forward(ctx, sspec, vspec, cfg, near_plane, means, scales, quats, opacities, colors, velocity, intrinsics,
+                camera_to_world, times):
+        tensors = {
+            "means": _f32(means), "scales": _f32(scales), "quats": _f32(quats), "opacities": _f32(opacities),
+            "colors": _f32(colors), "velocity": _f32(velocity), "intrinsics": _f32(intrinsics),
+            "camera_to_world": _f32(camera_to_world), "times": _f32(times),
+        }
+        image, alpha, depth, state = forward_stages(sspec, vspec, cfg, near_plane, tensors)
+        ctx.sspec, ctx.vspec, ctx.cfg, ctx.near_plane = sspec, vspec, cfg, near_plane
+        ctx.tensors = tensors
+        ctx.state = state
+        ctx.shapes = [None if t is None else (t.shape, t.dtype) for t in (means, scales, quats, opacities, colors,
+                                                                          velocity)]
+        if depth is None:
+            depth = image.new_zeros(0)
+            ctx.mark_non_differentiable(depth)
+        return image, alpha, depth
+
+    @staticmethod
+    def backward(ctx, d_image, d_alpha, d_depth):
+        vspec = ctx.vspec
+        B, H, W = vspec.n_views, vspec.height, vspec.width
+        t = ctx.tensors
+        if d_image is None:
+            d_image = torch.zeros(B, 3, H, W, dtype=torch.float32, device=t["means"].device)
+        d_image = d_image.to(torch.float32).contiguous()
+        d_alpha = None if d_alpha is None else d_alpha.to(torch.float32).contiguous()
+        d_depth = None if (d_depth is None or d_depth.numel() == 0) else d_depth.to(torch.float32).contiguous()
+        grads = backward_stages(ctx.sspec, vspec, ctx.cfg, ctx.near_plane, t, ctx.state, d_image, d_alpha, d_depth)
+        out = []
+        for name, shp in zip(_PARAM_NAMES, ctx.shapes):
+            if shp is None or name not in grads:
+                out.append(None)
+            else:
+                out.append(grads[name].reshape(shp[0]).to(shp[1]))
+        ctx.state = None
+        return (None, None, None, None, *out, None, None, None)
+
+
+def _check_cameras_no_grad(*tensors):
+    for t in tensors:
+        if isinstance(t, torch.Tensor) and t.requires_grad:
+            raise NotImplementedError(
+                "the b200 renderer does not differentiate camera parameters (intrinsics / camera_to_world / "
+                "times); detach them or use the dense renderer for camera optimisation."
+            )
+
+
+def render_scene(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, near_plane: float, *, means, scales,
+                 quats, opacities, colors, velocity, intrinsics, camera_to_world, times):
+    """Autograd entry used by every public render function."""
+    if not means.is_cuda:
+        raise RuntimeError("the b200 renderer runs on CUDA devices only (got a tensor on %s)" % means.device)
+    _check_cameras_no_grad(intrinsics, camera_to_world, times)
+    return _RenderFunction.apply(sspec, vspec, cfg, float(near_plane), means, scales, quats, opacities, colors,
+                                 velocity, intrinsics, camera_to_world, times)

@@ -1,0 +1,165 @@
+"""Public render functions.
+
+* ``render_b200_3dgs_batch`` / ``render_b200_3dgs``: drop-ins for the reference's backend entry
+  points (``render_pytorch_3dgs_batch``, src/train/renderers/dense.py:170-236, and
+  ``render_fast_mac_3dgs[_batch]``, src/train/renderers/fast_mac.py:216-309): activated per-frame
+  Gaussians [K,G,C], one camera per frame, image [K,3,H,W] (or [3,H,W]).
+* ``render_b200``: raw parameters (means, log-scales, quaternions, opacity logits, SH, optional
+  velocity with per-view times) shared by groups of views; returns image, alpha and depth.
+"""
+from __future__ import annotations
+
+import torch
+
+from .config import B200RendererConfig
+from .render import MIN_RENDER_DEPTH, SceneSpec, ViewSpec, render_scene
+
+
+def _per_view(value, K: int, device) -> torch.Tensor:
+    if torch.is_tensor(value):
+        v = value.detach().to(device=device, dtype=torch.float32)
+        return v.expand(K) if v.ndim == 0 else v.reshape(K)
+    return torch.full((K,), float(value), device=device, dtype=torch.float32)
+
+
+def _intrinsics(fx, fy, cx, cy, K, device) -> torch.Tensor:
+    return torch.stack([_per_view(v, K, device) for v in (fx, fy, cx, cy)], dim=-1).contiguous()
+
+
+def _check_projection(projection_mode: str, cameras) -> None:
+    """Pinhole projection only.  ``camera_model`` with all-pinhole cameras is the same projection
+    (src/train/renderers/projection.py delegates it to common.py); other lens models are not
+    implemented by this renderer and are refused."""
+    if projection_mode == "legacy_pinhole":
+        return
+    if projection_mode != "camera_model":
+        raise ValueError(f"Unknown projection_mode: {projection_mode}")
+    cams = list(cameras) if isinstance(cameras, (list, tuple)) else ([cameras] if cameras is not None else [])
+    if not cams:
+        raise ValueError("camera_model projection requires CameraSpec values.")
+    lens = sorted({getattr(c, "lens_model", "pinhole") for c in cams})
+    if lens != ["pinhole"]:
+        raise NotImplementedError(f"the b200 renderer supports pinhole cameras only (lens models: {lens}).")
+
+
+def render_b200_3dgs_batch(
+    means3d: torch.Tensor,
+    scales: torch.Tensor,
+    quats: torch.Tensor,
+    opacities: torch.Tensor,
+    rgbs: torch.Tensor,
+    height: int,
+    width: int,
+    fx,
+    fy,
+    cx,
+    cy,
+    *,
+    cameras=None,
+    projection_mode: str = "legacy_pinhole",
+    camera_to_world: torch.Tensor | None = None,
+    near_plane: float = MIN_RENDER_DEPTH,
+    config: B200RendererConfig | None = None,
+) -> torch.Tensor:
+    """[K,G,3] means, [K,G,3] scales, [K,G,4] quaternions, [K,G,1] opacities, [K,G,3] rgbs and
+    per-frame intrinsics / camera_to_world [K,4,4] -> image [K,3,H,W] in [0,1]."""
+    _check_projection(projection_mode, cameras)
+    config = config or B200RendererConfig()
+    K, G = int(means3d.shape[0]), int(means3d.shape[1])
+    dev = means3d.device
+    intr = _intrinsics(fx, fy, cx, cy, K, dev)
+    if camera_to_world is None:
+        c2w = torch.eye(4, device=dev, dtype=torch.float32).expand(K, 4, 4).contiguous()
+    else:
+        c2w = camera_to_world.to(device=dev, dtype=torch.float32)
+        c2w = (c2w.unsqueeze(0).expand(K, 4, 4) if c2w.ndim == 2 else c2w).contiguous()
+    sspec = SceneSpec(n_sets=K, n_gaussians=G, raw=False, sh_degree=0, velocity=False, sh_clamp=False)
+    vspec = ViewSpec(n_views=K, views_per_set=1, height=int(height), width=int(width))
+    image, _alpha, _depth = render_scene(
+        sspec, vspec, config, near_plane, means=means3d, scales=scales, quats=quats,
+        opacities=opacities.reshape(K, G), colors=rgbs, velocity=None, intrinsics=intr, camera_to_world=c2w,
+        times=None,
+    )
+    return image
+
+
+def render_b200_3dgs(
+    means3d: torch.Tensor,
+    scales: torch.Tensor,
+    quats: torch.Tensor,
+    opacities: torch.Tensor,
+    rgbs: torch.Tensor,
+    height: int,
+    width: int,
+    fx,
+    fy,
+    cx,
+    cy,
+    *,
+    camera=None,
+    projection_mode: str = "legacy_pinhole",
+    camera_to_world: torch.Tensor | None = None,
+    near_plane: float = MIN_RENDER_DEPTH,
+    config: B200RendererConfig | None = None,
+) -> torch.Tensor:
+    """Single frame: [G,*] Gaussians -> image [3,H,W] (render_pytorch_3dgs, dense.py:105-167)."""
+    c2w = None if camera_to_world is None else camera_to_world.reshape(1, 4, 4)
+    return render_b200_3dgs_batch(
+        means3d.unsqueeze(0), scales.unsqueeze(0), quats.unsqueeze(0), opacities.reshape(1, -1, 1),
+        rgbs.unsqueeze(0), height, width, fx, fy, cx, cy, cameras=[camera] if camera is not None else None,
+        projection_mode=projection_mode, camera_to_world=c2w, near_plane=near_plane, config=config,
+    )[0]
+
+
+def render_b200(
+    means: torch.Tensor,
+    log_scales: torch.Tensor,
+    quats: torch.Tensor,
+    opacity_logits: torch.Tensor,
+    sh: torch.Tensor,
+    *,
+    intrinsics: torch.Tensor,
+    camera_to_world: torch.Tensor,
+    height: int,
+    width: int,
+    velocity: torch.Tensor | None = None,
+    times: torch.Tensor | None = None,
+    views_per_set: int | None = None,
+    near_plane: float = MIN_RENDER_DEPTH,
+    config: B200RendererConfig | None = None,
+):
+    """Raw-parameter render.
+
+    means/log_scales [S,G,3] (or [G,3]), quats [S,G,4] (normalised here), opacity_logits [S,G,1]
+    or [S,G], sh [S,G,(d+1)^2,3] (rgb = SH(view dir) + 0.5), velocity [S,G,3] with times [B]
+    (means_t = means + t * velocity).  View b uses set b // views_per_set (default: all views
+    share set 0 when S == 1, else B // S views per set).  intrinsics [B,4] = fx, fy, cx, cy;
+    camera_to_world [B,4,4].  Returns image [B,3,H,W], alpha [B,H,W] (sum of blend weights) and
+    depth [B,H,W] (sum of weight * camera z; None unless ``config.depth``).
+    """
+    config = config or B200RendererConfig()
+    if means.ndim == 2:
+        means, log_scales, quats = means.unsqueeze(0), log_scales.unsqueeze(0), quats.unsqueeze(0)
+        opacity_logits, sh = opacity_logits.unsqueeze(0), sh.unsqueeze(0)
+        velocity = None if velocity is None else velocity.unsqueeze(0)
+    S, G = int(means.shape[0]), int(means.shape[1])
+    B = int(camera_to_world.shape[0])
+    k = int(sh.shape[-2])
+    degree = {1: 0, 4: 1, 9: 2, 16: 3}.get(k)
+    if degree is None:
+        raise ValueError(f"sh must have 1, 4, 9 or 16 coefficients per channel, got {k}")
+    if views_per_set is None:
+        views_per_set = B if S == 1 else B // S
+    if views_per_set <= 0 or (B - 1) // views_per_set >= S:
+        raise ValueError(f"{B} views with views_per_set={views_per_set} need more than {S} sets")
+    if velocity is not None and times is None:
+        raise ValueError("velocity needs per-view times")
+    sspec = SceneSpec(n_sets=S, n_gaussians=G, raw=True, sh_degree=degree, velocity=velocity is not None,
+                      sh_clamp=config.sh_clamp)
+    vspec = ViewSpec(n_views=B, views_per_set=views_per_set, height=int(height), width=int(width))
+    image, alpha, depth = render_scene(
+        sspec, vspec, config, near_plane, means=means, scales=log_scales, quats=quats,
+        opacities=opacity_logits.reshape(S, G), colors=sh, velocity=velocity,
+        intrinsics=intrinsics.reshape(B, 4), camera_to_world=camera_to_world, times=times,
+    )
+    return image, alpha, (depth if config.depth else None)

@@ -1,0 +1,224 @@
+/*
+ * gsb200.h -- C ABI of libgsb200.so, the B200 (sm_100a) Gaussian-splat render + L1/SSIM loss.
+ *
+ * Plain C: device pointers, sizes and a cudaStream_t passed as void*.  No torch types.
+ * Every entry point is stream-ordered, allocates nothing (the caller owns all device memory,
+ * workspaces included) and returns a gsb_status.  Status codes never trap the device: kernels
+ * that can fail record a code in the caller's workspace, read back by gsb_read_status().
+ *
+ * The stages replace the reference's Python render path (nbardy/dynaworld, src/train):
+ *
+ *   gsb_depth_order      <- the stable argsort by camera z of
+ *                           renderers/common.py:190-195 (project_gaussians_2d_batch)
+ *   gsb_preprocess_fwd   <- renderers/common.py:149-231 (projection, EWA covariance,
+ *                           near-plane mask) plus raw-parameter activation / SH / time offset
+ *                           (the model head of gs_models/blocks.py:172-186), and the per-Gaussian
+ *                           tile bounds of renderers/tiled.py:7-28
+ *   gsb_bin              <- renderers/tiled.py:31-71 (build_tile_assignments: tile lists in
+ *                           (tile, depth) order)
+ *   gsb_raster_fwd       <- renderers/dense.py:208-236 (render_pytorch_3dgs_batch blend) and
+ *                           renderers/tiled.py:162-198 (tile-local variant)
+ *   gsb_raster_bwd,
+ *   gsb_preprocess_bwd   <- torch autograd through the two above (dense.py / common.py)
+ *   gsb_loss_fwd_bwd     <- losses.py:13-85 (reconstruction_loss_per_image, standard_gs)
+ *   gsb_scale_planes     <- the upstream-gradient product autograd applies to the loss
+ *
+ * The Metal scaffold of the reference exposes the same split as a torch op pair
+ * (third_party/fast-mac-gsplat-scaffold/csrc/bindings.cpp:44-52).
+ */
+#ifndef GSB200_H
+#define GSB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GSB_API __attribute__((visibility("default")))
+
+typedef enum gsb_status {
+  GSB_OK = 0,
+  GSB_ERR_SHAPE = 1,        /* inconsistent or unsupported sizes */
+  GSB_ERR_WORKSPACE = 2,    /* workspace too small: the needed size was written back */
+  GSB_ERR_KEY_OVERFLOW = 3, /* more (tile, Gaussian) pairs than the 2^30 a call supports */
+  GSB_ERR_NONFINITE = 4,    /* non-finite projected values were counted (see gsb_read_status) */
+  GSB_ERR_TIMEOUT = 5,      /* a bounded device-side wait gave up */
+  GSB_ERR_CUDA = 6,         /* a CUDA runtime call failed (launch error etc.) */
+  GSB_ERR_ARG = 7           /* NULL pointer or bad option value */
+} gsb_status;
+
+/* Scene flags (gsb_scene.flags). */
+#define GSB_SCENE_RAW 0x1u      /* scales are log-scales, quats are normalised, opacities are
+                                   logits, colors are SH coefficients (else: activated values as
+                                   the reference's render call takes them) */
+#define GSB_SCENE_VELOCITY 0x2u /* means_t = means + t_view * velocity */
+#define GSB_SCENE_SH_CLAMP 0x4u /* rgb = max(SH(dir) + 0.5, 0) (raw mode only) */
+
+/* Render flags (gsb_options.flags). */
+#define GSB_RENDER_TILED_COMPAT 0x1u /* tiled.py bounds (bound_scale, 1/255 threshold) and
+                                        tile-local (1+eps) products, no cutoff, no early stop */
+#define GSB_RENDER_DEPTH 0x2u        /* write depth = sum_i w_i z_i */
+#define GSB_RENDER_NO_ELLIPSE 0x4u   /* exact mode: keep every tile of the bounding box */
+
+/* Gaussians: n_sets sets of n_gaussians each; view b draws on set b / views_per_set. */
+typedef struct gsb_scene {
+  int32_t n_sets;
+  int32_t n_gaussians;
+  int32_t sh_degree;      /* raw mode: 0..3; activated mode: ignored (colors are rgb) */
+  uint32_t flags;         /* GSB_SCENE_* */
+  const float* means;     /* [S,G,3] */
+  const float* scales;    /* [S,G,3] linear (activated) or log-scales (raw) */
+  const float* quats;     /* [S,G,4] (r,i,j,k); raw mode normalises them */
+  const float* opacities; /* [S,G]   opacity in [0,1] (activated) or logits (raw) */
+  const float* colors;    /* [S,G,3] rgb (activated) or SH [S,G,(d+1)^2,3] (raw) */
+  const float* velocity;  /* [S,G,3] with GSB_SCENE_VELOCITY, else NULL */
+} gsb_scene;
+
+/* Views (cameras). */
+typedef struct gsb_views {
+  int32_t n_views;
+  int32_t views_per_set;
+  int32_t height;
+  int32_t width;
+  const float* intrinsics;      /* [B,4] fx, fy, cx, cy (device) */
+  const float* camera_to_world; /* [B,4,4] row-major, camera +z is the optical axis (device) */
+  const float* times;           /* [B] or NULL (device) */
+} gsb_views;
+
+typedef struct gsb_options {
+  int32_t tile_size;              /* 8 or 16 */
+  uint32_t flags;                 /* GSB_RENDER_* */
+  float near_plane;               /* reference default 1e-4 (common.py:3) */
+  float alpha_clamp;              /* 0.99 (dense.py:220) */
+  float alpha_cutoff;             /* exact mode: pairs with alpha below it count as alpha 0 */
+  float transmittance_threshold;  /* exact mode: a pixel stops once T falls below it */
+  float eps;                      /* 1e-6 (dense.py:225) */
+  float pixel_center;             /* 0.0 (common.py:13-19) */
+  float background[3];            /* (1,1,1) (dense.py:231) */
+  float bound_scale;              /* tiled compat: 3.0 (tiled.py:7) */
+  float tiled_alpha_threshold;    /* tiled compat: 1/255 (tiled.py:7) */
+} gsb_options;
+
+/* Gradients of the scene parameters (device, shapes as gsb_scene; NULL entries are skipped). */
+typedef struct gsb_scene_grads {
+  float* means;
+  float* scales;
+  float* quats;
+  float* opacities;
+  float* colors;
+  float* velocity;
+} gsb_scene_grads;
+
+typedef struct gsb_loss_options {
+  int32_t type;          /* 0 standard_gs, 1 l1, 2 mse, 3 l1_mse */
+  int32_t window_size;   /* odd, 3..31; reference 11 */
+  int32_t window;        /* 0 box (reference), 1 gaussian */
+  int32_t dssim_half;    /* 1: (1-SSIM)/2 as the reference, 0: (1-SSIM) */
+  float l1_weight;       /* 0.8 */
+  float dssim_weight;    /* 0.2 */
+  float mse_weight;      /* 0.2 */
+  float c1;              /* 1e-4 */
+  float c2;              /* 9e-4 */
+  float sigma;           /* gaussian window sigma, 1.5 */
+} gsb_loss_options;
+
+/* Size of one projected record (floats), of one 2-D gradient record (floats), and of the
+   per-pixel state the backward reads. */
+#define GSB_RECORD_FLOATS 12
+#define GSB_GRAD2D_FLOATS 10
+
+/* ---- library ------------------------------------------------------------------------------ */
+GSB_API const char* gsb_version(void);
+/* Number of kernels this library has launched in this process (all devices, all threads). */
+GSB_API uint64_t gsb_kernel_launches(void);
+GSB_API const char* gsb_status_string(int status);
+/* Reads the device status word of a workspace (after the stream is synchronised by the caller).
+   Returns GSB_OK or the first error recorded by a kernel using that workspace. */
+GSB_API gsb_status gsb_read_status(const void* workspace, int* status_out, void* stream);
+
+/* ---- stage 1: per-view stable depth order (common.py:190-195) ----------------------------- */
+GSB_API size_t gsb_depth_order_workspace(const gsb_scene* scene, const gsb_views* views);
+/* sorted_ids[b*G + r] = index of the r-th nearest Gaussian of view b (ties by index);
+   rank_of[b*G + g] = its inverse. */
+GSB_API gsb_status gsb_depth_order(const gsb_scene* scene, const gsb_views* views,
+                                   int32_t* sorted_ids, int32_t* rank_of,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- stage 2: projection in depth order, tile bounds, pair count prefix ------------------- */
+GSB_API size_t gsb_preprocess_workspace(const gsb_views* views, int32_t n_gaussians);
+/* records[(b*G + r)*12 ..] = mx, my, A, B, C, opacity, z, tau, r, g, b, 0 for the r-th nearest
+   Gaussian of view b (A, B, C: inv_cov00, inv_cov01+inv_cov10, inv_cov11; tau: the q above
+   which alpha < alpha_cutoff).  tile_rects[(b*G + r)*4 ..] = tx0, ty0, tx1, ty1 (inclusive;
+   empty when tx0 > tx1).  pair_offsets[B*G + 1]: exclusive prefix of the per-Gaussian pair
+   counts; pair_offsets[B*G] is the total (<= 2^30, else GSB_ERR_KEY_OVERFLOW at gsb_bin).
+   cov2d_out ([B*G*3] c00, c01, c11 in depth order) may be NULL. */
+GSB_API gsb_status gsb_preprocess_fwd(const gsb_scene* scene, const gsb_views* views,
+                                      const gsb_options* opts, const int32_t* rank_of,
+                                      float* records, int32_t* tile_rects, uint32_t* pair_offsets,
+                                      float* cov2d_out, void* workspace, size_t workspace_bytes,
+                                      void* stream);
+
+/* ---- stage 3: pair keys, radix sort by (view, tile), tile ranges (tiled.py:31-71) ---------- */
+GSB_API size_t gsb_bin_workspace(const gsb_views* views, const gsb_options* opts,
+                                 int32_t n_gaussians, uint32_t n_pairs);
+/* sorted_keys[n_pairs]: ((view*n_tiles + tile) << 32) | depth_rank, ascending.
+   tile_ranges[B*n_tiles*2]: [start, end) of each tile's run in sorted_keys. */
+GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians,
+                           const float* records, const int32_t* tile_rects,
+                           const uint32_t* pair_offsets, uint32_t n_pairs,
+                           uint64_t* sorted_keys, uint32_t* tile_ranges,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- stage 4: front-to-back blend (dense.py:208-236) -------------------------------------- */
+/* image [B,3,H,W] (clamped), alpha [B,H,W] = sum of weights, depth [B,H,W] or NULL,
+   pixel_t [B,H,W] and pixel_state [B,H,W]: the per-pixel state gsb_raster_bwd needs. */
+GSB_API gsb_status gsb_raster_fwd(const gsb_views* views, const gsb_options* opts,
+                                  int32_t n_gaussians, const float* records,
+                                  const uint64_t* sorted_keys, const uint32_t* tile_ranges,
+                                  float* image, float* alpha, float* depth,
+                                  float* pixel_t, uint32_t* pixel_state, void* stream);
+
+/* ---- stage 5: fused L1 + SSIM loss and its gradient (losses.py:13-85) --------------------- */
+GSB_API size_t gsb_loss_workspace(int32_t n_images);
+/* loss[B]; dpred (may be NULL): d loss[b] / d pred for a unit upstream gradient. */
+GSB_API gsb_status gsb_loss_fwd_bwd(const gsb_loss_options* lopts, int32_t n_images,
+                                    int32_t channels, int32_t height, int32_t width,
+                                    const float* pred, const float* target, float* loss,
+                                    float* dpred, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+/* out[b, ...] = scale[b] * in[b, ...] for n_images planes of plane_elems floats (in == out ok). */
+GSB_API gsb_status gsb_scale_planes(const float* in, const float* scale, float* out,
+                                    int32_t n_images, int64_t plane_elems, void* stream);
+
+/* ---- stage 6: reverse blend, per-(view, Gaussian) 2-D gradients --------------------------- */
+/* grad2d[(b*G + r)*10 ..] = dL/d(mx, my, A, B, C, opacity, r, g, b, z) of the r-th nearest
+   Gaussian of view b; zeroed by the call.  d_alpha, d_depth, view_scale may be NULL. */
+GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opts,
+                                  int32_t n_gaussians, const float* records,
+                                  const uint64_t* sorted_keys, const uint32_t* tile_ranges,
+                                  const float* pixel_t, const uint32_t* pixel_state,
+                                  const float* d_image, const float* d_alpha,
+                                  const float* d_depth, const float* view_scale,
+                                  float* grad2d, void* stream);
+
+/* ---- stage 7: chain rule to the scene parameters (common.py:149-231 backward) ------------- */
+/* Gradients are summed over the views that share a set and overwrite the outputs. */
+GSB_API gsb_status gsb_preprocess_bwd(const gsb_scene* scene, const gsb_views* views,
+                                      const gsb_options* opts, const int32_t* rank_of,
+                                      const float* grad2d, gsb_scene_grads* grads, void* stream);
+
+/* ---- utility: the library's radix sort on its own (tests, benchmarks) --------------------- */
+GSB_API size_t gsb_radix_sort_workspace(uint32_t n, int key_bytes, int with_values);
+/* Stable LSD sort of n keys by bits [bit_lo, bit_hi); keys are uint32 (key_bytes 4) or uint64
+   (key_bytes 8); values (uint32) may be NULL. Input buffers are left unchanged. */
+GSB_API gsb_status gsb_radix_sort(const void* keys_in, void* keys_out, const uint32_t* values_in,
+                                  uint32_t* values_out, uint32_t n, int key_bytes, int bit_lo,
+                                  int bit_hi, void* workspace, size_t workspace_bytes,
+                                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GSB200_H */

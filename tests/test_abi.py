@@ -1,0 +1,76 @@
+"""libgsb200.so loads and exports every entry point include/gsb200.h declares (no GPU needed)."""
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+from dynaworld_b200 import _lib, build
+
+HEADER = ROOT / "include" / "gsb200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"GSB_API\s+[\w\s\*]+?\b(gsb_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    assert "gsb_raster_fwd" in names and "gsb_preprocess_bwd" in names and len(names) >= 15
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [n for n in declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_bindings_cover_the_header():
+    assert set(declared_symbols()) == set(_lib.SIGNATURES)
+
+
+def test_version_and_status_strings(lib):
+    assert b"sm_100a" in lib.gsb_version()
+    for code in range(8):
+        assert lib.gsb_status_string(code)
+
+
+def test_struct_sizes_match_header():
+    # 4 ints + 6 pointers; 4 ints + 3 pointers; 2 ints + 13 floats (incl. background[3])
+    assert ctypes.sizeof(_lib.Scene) == 16 + 6 * 8
+    assert ctypes.sizeof(_lib.Views) == 16 + 3 * 8
+    assert ctypes.sizeof(_lib.Options) == 8 + 11 * 4
+    assert ctypes.sizeof(_lib.LossOptions) == 16 + 6 * 4
+
+
+def test_argument_errors_return_codes_without_touching_a_gpu(lib):
+    """Invalid arguments are rejected on the host with a status, before any CUDA call."""
+    v = _lib.Views()
+    assert lib.gsb_depth_order(None, None, None, None, None, 0, None) == 7  # GSB_ERR_ARG
+    assert lib.gsb_raster_fwd(ctypes.byref(v), None, 1, None, None, None, None, None, None, None, None, None) == 7
+    o = _lib.Options()
+    o.tile_size = 12
+    v.intrinsics = v.camera_to_world = 16
+    v.n_views = v.height = v.width = v.views_per_set = 1
+    assert lib.gsb_raster_fwd(ctypes.byref(v), ctypes.byref(o), 1, 16, 16, 16, 16, 16, 16, 16, 16, None) == 7
+    lo = _lib.LossOptions()
+    lo.type = 0
+    lo.window_size = 4  # even window
+    assert lib.gsb_loss_fwd_bwd(ctypes.byref(lo), 1, 3, 16, 16, 16, 16, 16, None, 16, 4096, None) == 7
+
+
+def test_workspace_queries_are_host_only(lib):
+    s, v = _lib.Scene(), _lib.Views()
+    s.n_gaussians = 1000
+    v.n_views = 4
+    assert lib.gsb_depth_order_workspace(ctypes.byref(s), ctypes.byref(v)) > 4 * 1000 * 16
+    assert lib.gsb_preprocess_workspace(ctypes.byref(v), 1000) >= 4 * 1000 * 4
+    assert lib.gsb_bin_workspace(ctypes.byref(v), None, 1000, 5000) >= 5000 * 16
+    assert lib.gsb_radix_sort_workspace(10000, 8, 1) > 10000 * 12
+    assert lib.gsb_loss_workspace(8) >= 256 + 8 * 24

@@ -1,0 +1,198 @@
+"""CUDA render + loss against the reference's outputs (golden fixtures) and the oracle.
+
+Tolerances (the BASELINE parity bar): image and alpha within 1e-4 absolute; gradients within
+1e-3 of each tensor's largest magnitude (max |g - g_ref| <= 1e-3 * max |g_ref|); tile lists and
+sorted key order bit-exact.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN_CASES, grad_close, load_golden
+from dynaworld_b200 import synthetic
+from dynaworld_b200.config import B200RendererConfig
+from dynaworld_b200.renderer import render_b200_3dgs, render_b200_3dgs_batch
+from gpu_helpers import DEV, keys_np, records_np, render_raw, sorted_ids_from_rank, stages
+from oracle import splat_oracle as so
+from oracle import tiles_oracle as to
+
+pytestmark = pytest.mark.gpu
+
+IMAGE_TOL = 1e-4
+GRAD_REL = 1e-3
+
+
+@pytest.mark.parametrize("case", GOLDEN_CASES)
+def test_depth_order_bit_exact(case):
+    g = load_golden(case)
+    wl = g.workload()
+    _, _, _, st = stages(wl)
+    ids = sorted_ids_from_rank(st.rank_of, wl.n_views, wl.n_gaussians)
+    np.testing.assert_array_equal(ids, g["ref_depth_order"])
+
+
+@pytest.mark.parametrize("case", GOLDEN_CASES)
+def test_projected_records_match_reference(case):
+    g = load_golden(case)
+    wl = g.workload()
+    _, _, _, st = stages(wl)
+    rec = records_np(st, wl.n_views, wl.n_gaussians)
+    m2, inv = g["ref_means2d"], g["ref_inv_cov"]
+    np.testing.assert_allclose(rec[..., 0:2], m2, rtol=1e-5, atol=1e-3)
+    scale = np.abs(inv).max()
+    np.testing.assert_allclose(rec[..., 2], inv[..., 0, 0], rtol=1e-4, atol=1e-6 * scale)
+    np.testing.assert_allclose(rec[..., 3], inv[..., 0, 1] + inv[..., 1, 0], rtol=1e-4, atol=1e-6 * scale)
+    np.testing.assert_allclose(rec[..., 4], inv[..., 1, 1], rtol=1e-4, atol=1e-6 * scale)
+    np.testing.assert_allclose(rec[..., 5], g["ref_proj_opacity"][..., 0], rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(rec[..., 8:11], g["ref_proj_rgb"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("case", GOLDEN_CASES)
+@pytest.mark.parametrize("ellipse", [True, False])
+def test_exact_mode_lists_bit_exact(case, ellipse):
+    """Pair keys from the GPU equal the numpy restatement of the exact-mode rule applied to the
+    GPU's own projected records (same float64 operation order)."""
+    g = load_golden(case)
+    wl = g.workload()
+    cfg = B200RendererConfig(ellipse_culling=ellipse)
+    _, _, _, st = stages(wl, cfg)
+    rec = records_np(st, wl.n_views, wl.n_gaussians)
+    per_view = []
+    for b in range(wl.n_views):
+        r = rec[b]
+        per_view.append(to.exact_pairs_one_view(r[:, 0], r[:, 1], r[:, 2], r[:, 3], r[:, 4], r[:, 5], wl.height,
+                                                wl.width, 16, np.float32(cfg.alpha_cutoff), ellipse_test=ellipse))
+    ref = to.sort_pairs(per_view, to.n_tiles_for(wl.height, wl.width, 16))
+    np.testing.assert_array_equal(keys_np(st), ref)
+
+
+@pytest.mark.parametrize("case", GOLDEN_CASES)
+@pytest.mark.parametrize("tile", [8, 16])
+def test_tiled_compat_lists_match_reference(case, tile):
+    """tiled_compat mode reproduces tiled.py's tile lists and their order exactly."""
+    g = load_golden(case)
+    wl = g.workload()
+    _, _, _, st = stages(wl, B200RendererConfig(mode="tiled_compat", tile_size=tile))
+    k = keys_np(st)
+    n_tiles = to.n_tiles_for(wl.height, wl.width, tile)
+    view_tile = (k >> np.uint64(32)).astype(np.int64)
+    rank = (k & np.uint64(0xFFFFFFFF)).astype(np.int64)
+    np.testing.assert_array_equal(view_tile // n_tiles, g[f"ref_tiled{tile}_view"])
+    np.testing.assert_array_equal(view_tile % n_tiles, g[f"ref_tiled{tile}_tile"])
+    np.testing.assert_array_equal(rank, g[f"ref_tiled{tile}_rank"])
+
+
+@pytest.mark.parametrize("case", GOLDEN_CASES)
+def test_image_loss_and_gradients_match_reference(case):
+    g = load_golden(case)
+    wl = g.workload()
+    out = render_raw(wl)
+    err = (out["image"] - g.t("ref_image")).abs().max().item()
+    assert err <= IMAGE_TOL, f"image max abs err {err:.3e}"
+    torch.testing.assert_close(out["loss"], g.t("ref_loss"), rtol=1e-4, atol=2e-6)
+    for k in ("means", "log_scales", "quats", "opacity_logits", "sh") + (("velocity",) if wl.velocity is not None
+                                                                          else ()):
+        ok, e, s = grad_close(out[f"grad_{k}"], g.t(f"ref_grad_{k}"), GRAD_REL)
+        assert ok, f"{case} {k}: max err {e:.3e} vs scale {s:.3e}"
+
+
+@pytest.mark.parametrize("case", ["static64", "dynamic128_small", "edge"])
+def test_alpha_and_depth_match_oracle(case):
+    g = load_golden(case)
+    wl = g.workload()
+    out = render_raw(wl, B200RendererConfig(depth=True), grads=False, loss=False)
+    raw = so.RawGaussians(*(t.double() for t in (wl.means, wl.log_scales, wl.quats, wl.opacity_logits, wl.sh)),
+                          None if wl.velocity is None else wl.velocity.double())
+    m, s, q, o, rgb = so.activate(raw, wl.times.double(), wl.camera_to_world, wl.views_per_set)
+    img, alpha, depth = so.render_dense(m, s, q, o, rgb, wl.height, wl.width, wl.fx, wl.fy, wl.cx, wl.cy,
+                                        wl.camera_to_world, sort_key=so.camera_depth_fp32(m.float(),
+                                                                                           wl.camera_to_world))
+    assert (out["alpha"].double() - alpha).abs().max().item() <= IMAGE_TOL
+    assert (out["depth"].double() - depth).abs().max().item() <= IMAGE_TOL * max(1.0, depth.abs().max().item())
+
+
+@pytest.mark.parametrize("case", ["static64", "dynamic128_small", "multiview384_small"])
+def test_dropin_activated_batch_api(case):
+    """render_b200_3dgs_batch takes the reference's activated [K,G,C] payload (dense.py:170)."""
+    g = load_golden(case)
+    wl = g.workload()
+    act = {k: g.t(f"ref_act_{k}", DEV).requires_grad_(True) for k in ("xyz", "scales", "quats", "opacities",
+                                                                        "rgbs")}
+    img = render_b200_3dgs_batch(act["xyz"], act["scales"], act["quats"], act["opacities"], act["rgbs"],
+                                 wl.height, wl.width, wl.fx.to(DEV), wl.fy.to(DEV), wl.cx.to(DEV), wl.cy.to(DEV),
+                                 camera_to_world=wl.camera_to_world.to(DEV))
+    assert (img.detach().cpu() - g.t("ref_image")).abs().max().item() <= IMAGE_TOL
+    from dynaworld_b200.losses import reconstruction_loss_per_image
+
+    reconstruction_loss_per_image(img, wl.target.to(DEV)).sum().backward()
+    for k, v in act.items():
+        ok, e, s = grad_close(v.grad, g.t(f"ref_grad_act_{k}"), GRAD_REL)
+        assert ok, f"{case} {k}: {e:.3e} vs {s:.3e}"
+
+
+def test_dropin_single_frame_api():
+    g = load_golden("static64")
+    a = {k: g.t(f"ref_act_{k}", DEV)[0] for k in ("xyz", "scales", "quats", "opacities", "rgbs")}
+    img = render_b200_3dgs(a["xyz"], a["scales"], a["quats"], a["opacities"], a["rgbs"], 64, 64, 64.0, 64.0, 32.0,
+                           32.0, camera_to_world=torch.eye(4, device=DEV))
+    assert img.shape == (3, 64, 64)
+    assert (img.cpu() - g.t("ref_image")[0]).abs().max().item() <= IMAGE_TOL
+
+
+@pytest.mark.parametrize("tile", [8, 16])
+@pytest.mark.parametrize("case", ["static64", "dynamic128_small", "edge"])
+def test_tiled_compat_image_matches_reference_tiled(case, tile):
+    g = load_golden(case)
+    wl = g.workload()
+    out = render_raw(wl, B200RendererConfig(mode="tiled_compat", tile_size=tile), grads=False, loss=False)
+    err = (out["image"] - g.t(f"ref_tiled{tile}_image")).abs().max().item()
+    assert err <= IMAGE_TOL, f"{err:.3e}"
+
+
+def test_full_size_dynamic128_window():
+    """G=32768 at 128x128: frame 5's 32x32 window against the reference's dense render of it."""
+    g = load_golden("dynamic128_crop")
+    wl = synthetic.dynamic128().views(5, 6)
+    from tests.golden.make_golden import workload_arrays  # noqa: F401  (checksum layout)
+
+    for k, v in workload_arrays(wl).items():
+        assert float(v.double().sum()) == pytest.approx(float(g[f"checksum_{k}"]), rel=1e-12, abs=1e-9), k
+    out = render_raw(wl, grads=False, loss=False)
+    x0, y0, w, h = (int(v) for v in g["crop"])
+    err = (out["image"][:, :, y0:y0 + h, x0:x0 + w] - g.t("ref_image")).abs().max().item()
+    assert err <= IMAGE_TOL, f"{err:.3e}"
+
+
+def test_forward_is_deterministic_and_backward_is_stable():
+    wl = load_golden("dynamic128_small").workload()
+    a = render_raw(wl)
+    b = render_raw(wl)
+    assert torch.equal(a["image"], b["image"])
+    for k in ("means", "sh"):
+        ok, e, s = grad_close(a[f"grad_{k}"], b[f"grad_{k}"], 1e-5)
+        assert ok, (k, e, s)
+
+
+def test_empty_and_invisible_scenes():
+    """All Gaussians behind the camera: white image, zero alpha, zero gradients (no pairs)."""
+    wl = synthetic.static64(scale=0.01)
+    wl.means[..., 2] = -5.0
+    out = render_raw(wl)
+    assert torch.all(out["image"] == 1.0) and torch.all(out["alpha"] == 0.0)
+    for k in ("means", "log_scales", "quats", "opacity_logits", "sh"):
+        assert torch.all(out[f"grad_{k}"] == 0.0)
+
+
+def test_ragged_image_sizes():
+    """Images that are not a multiple of the tile: matches the dense oracle on every pixel."""
+    wl = synthetic.static64(scale=0.25)
+    for H, W in [(37, 45), (16, 17), (9, 70)]:
+        wl2 = synthetic.Workload(**{**wl.__dict__, "height": H, "width": W,
+                                    "target": torch.rand(1, 3, H, W, generator=torch.Generator().manual_seed(H))})
+        out = render_raw(wl2, grads=False, loss=False)
+        raw = so.RawGaussians(wl.means.double(), wl.log_scales.double(), wl.quats.double(),
+                              wl.opacity_logits.double(), wl.sh.double(), None)
+        m, s, q, o, rgb = so.activate(raw, wl.times.double(), wl.camera_to_world, 1)
+        img, _, _ = so.render_dense(m, s, q, o, rgb, H, W, wl.fx, wl.fy, wl.cx, wl.cy, wl.camera_to_world,
+                                    sort_key=so.camera_depth_fp32(m.float(), wl.camera_to_world))
+        assert (out["image"].double() - img).abs().max().item() <= IMAGE_TOL

@@ -1,0 +1,117 @@
+"""Host-side logic: configs, dispatch, argument checks, synthetic workloads (CPU only)."""
+import pytest
+import torch
+
+from dynaworld_b200 import rendering, synthetic
+from dynaworld_b200.config import EXACT_ALPHA_CUTOFF, B200RendererConfig, LossConfig
+from dynaworld_b200.losses import reconstruction_loss_per_image
+from dynaworld_b200.renderer import render_b200, render_b200_3dgs_batch
+
+
+def test_from_mapping_contract():
+    cfg = B200RendererConfig.from_mapping(None, fallback_tile_size=8, fallback_alpha_threshold=1 / 255)
+    assert cfg.tile_size == 16 and cfg.mode == "exact" and cfg.alpha_cutoff == EXACT_ALPHA_CUTOFF
+    assert cfg.tiled_alpha_threshold == pytest.approx(1 / 255)
+    compat = B200RendererConfig.from_mapping({"mode": "tiled_compat"}, fallback_tile_size=8,
+                                             fallback_alpha_threshold=0.01)
+    assert compat.tile_size == 8 and compat.tiled_alpha_threshold == 0.01
+    with pytest.raises(ValueError):
+        B200RendererConfig.from_mapping({"background": [1, 1]}, fallback_tile_size=8, fallback_alpha_threshold=0.1)
+    with pytest.raises(ValueError):
+        B200RendererConfig(mode="fast")
+    with pytest.raises(ValueError):
+        B200RendererConfig(tile_size=32)
+
+
+def test_exact_cutoff_is_the_float32_identity_boundary():
+    a = torch.tensor([EXACT_ALPHA_CUTOFF], dtype=torch.float32)
+    assert (1.0 - a).item() == 1.0
+    b = torch.tensor([EXACT_ALPHA_CUTOFF], dtype=torch.float32).nextafter(torch.tensor(1.0))
+    assert (1.0 - b).item() < 1.0
+
+
+def test_options_struct():
+    o = B200RendererConfig(mode="tiled_compat", depth=True).options(0.05)
+    assert o.flags & 1 and o.flags & 2 and o.near_plane == pytest.approx(0.05)
+
+
+def test_loss_config():
+    c = LossConfig.from_mapping({"type": "L1"})
+    assert c.type == "l1" and c.options().type == 1
+    with pytest.raises(ValueError):
+        LossConfig.from_mapping({"type": "huber"})
+    with pytest.raises(ValueError):
+        LossConfig.from_mapping({"ssim_window": "tri"})
+
+
+def test_pick_renderer_mode():
+    assert rendering.pick_renderer_mode("b200", 1, 1, 1, 0) == "b200"
+    assert rendering.pick_renderer_mode("auto", 1, 1, 1, 0) == "b200"
+    with pytest.raises(ValueError):
+        rendering.pick_renderer_mode("dense", 1, 1, 1, 0)
+    with pytest.raises(ValueError):
+        rendering.pick_renderer_mode("nope", 1, 1, 1, 0)
+
+
+class _Cam:
+    def __init__(self, lens="pinhole"):
+        self.fx, self.fy, self.cx, self.cy = 10.0, 10.0, 4.0, 4.0
+        self.camera_to_world = torch.eye(4)
+        self.lens_model = lens
+
+
+def test_projection_mode_resolution():
+    assert rendering.resolve_camera_projection_mode([_Cam()], "auto") == "legacy_pinhole"
+    assert rendering.resolve_camera_projection_mode([_Cam("opencv_fisheye")], "auto") == "camera_model"
+    with pytest.raises(ValueError):
+        rendering.resolve_camera_projection_mode([_Cam("opencv_fisheye")], "legacy_pinhole")
+    with pytest.raises(ValueError):
+        rendering.resolve_camera_projection_mode([_Cam()], "orthographic")
+
+
+def test_camera_for_viewport():
+    c = rendering.camera_for_viewport(_Cam(), 8, 8, 16, 32)
+    assert (c.fx, c.fy, c.cx, c.cy) == (40.0, 20.0, 16.0, 8.0)
+    with pytest.raises(ValueError):
+        rendering.camera_for_viewport(_Cam(), 0, 8, 16, 16)
+
+
+def test_cpu_tensors_fail_loudly():
+    """No CPU fallback: the product path refuses CPU tensors."""
+    wl = synthetic.static64(scale=0.01)
+    K, G = 1, wl.n_gaussians
+    with pytest.raises(RuntimeError, match="CUDA"):
+        render_b200_3dgs_batch(torch.zeros(K, G, 3), torch.ones(K, G, 3), torch.ones(K, G, 4), torch.ones(K, G, 1),
+                               torch.ones(K, G, 3), 8, 8, 8.0, 8.0, 4.0, 4.0)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        render_b200(wl.means, wl.log_scales, wl.quats, wl.opacity_logits, wl.sh,
+                    intrinsics=torch.tensor([[64.0, 64, 32, 32]]), camera_to_world=torch.eye(4)[None],
+                    height=64, width=64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        reconstruction_loss_per_image(torch.zeros(1, 3, 16, 16), torch.zeros(1, 3, 16, 16))
+
+
+def test_non_pinhole_lenses_are_refused():
+    with pytest.raises(NotImplementedError):
+        render_b200_3dgs_batch(torch.zeros(1, 2, 3), torch.ones(1, 2, 3), torch.ones(1, 2, 4), torch.ones(1, 2, 1),
+                               torch.ones(1, 2, 3), 8, 8, 8.0, 8.0, 4.0, 4.0, cameras=[_Cam("radial_tangential")],
+                               projection_mode="camera_model")
+
+
+@pytest.mark.parametrize("name", sorted(synthetic.WORKLOADS))
+def test_synthetic_workloads_small(name):
+    wl = synthetic.WORKLOADS[name](scale=0.002, image_scale=0.05)
+    assert wl.means.shape[-1] == 3 and wl.target.shape[0] == wl.n_views
+    assert wl.camera_to_world.shape == (wl.n_views, 4, 4)
+    assert (wl.n_views - 1) // wl.views_per_set < wl.n_sets
+    assert torch.isfinite(wl.means).all()
+
+
+def test_synthetic_shapes_full_size_metadata():
+    wl = synthetic.dynamic128()
+    assert wl.n_views == 16 and wl.n_gaussians == 32768 and wl.height == 128 and wl.sh_degree == 1
+    assert wl.times[-1].item() == pytest.approx(1.0)
+    cont = synthetic.dynamic128(frames=2, frame_offset=14, total_frames=16)
+    torch.testing.assert_close(cont.camera_to_world, wl.camera_to_world[14:16])
+    torch.testing.assert_close(cont.target, wl.target[14:16])
+    torch.testing.assert_close(cont.times, wl.times[14:16])
