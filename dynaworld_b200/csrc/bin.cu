@@ -50,9 +50,11 @@ __global__ void __launch_bounds__(256) emit_keys_kernel(int32_t n_views, int32_t
   }
 }
 
-__global__ void tile_ranges_kernel(const uint64_t* __restrict__ keys, uint32_t n, uint32_t* __restrict__ ranges) {
+__global__ void tile_ranges_kernel(const uint64_t* __restrict__ keys, uint32_t n, uint32_t* __restrict__ ranges,
+                                   size_t n_ranges) {
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const uint32_t t = uint32_t(keys[i] >> 32);
+    if (t >= n_ranges) continue;
     if (i == 0 || uint32_t(keys[i - 1] >> 32) != t) ranges[size_t(t) * 2] = i;
     if (i + 1 == n || uint32_t(keys[i + 1] >> 32) != t) ranges[size_t(t) * 2 + 1] = i + 1;
   }
@@ -73,7 +75,7 @@ gsb_status launch_tile_ranges(const uint64_t* keys, uint32_t n, uint32_t* ranges
   if (n == 0) return GSB_OK;
   const int grid = int(std::min<uint32_t>((n + 255) / 256, 148u * 32u));
   note_launch();
-  tile_ranges_kernel<<<grid, 256, 0, st>>>(keys, n, ranges);
+  tile_ranges_kernel<<<grid, 256, 0, st>>>(keys, n, ranges, n_ranges);
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 

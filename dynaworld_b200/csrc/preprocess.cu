@@ -267,7 +267,7 @@ __global__ void invert_order_kernel(const uint32_t* __restrict__ sorted_vals, in
     const int32_t r = int32_t(i - b * G);
     const int32_t g = int32_t(sorted_vals[i]);
     sorted_ids[i] = g;
-    rank_of[b * G + g] = r;
+    if (g >= 0 && g < G) rank_of[b * G + g] = r;
   }
 }
 

@@ -48,7 +48,7 @@ __device__ __forceinline__ void pixel_of(int tid, int& lx, int& ly) {
 __device__ __forceinline__ void load_entry(const RasterArgs& a, const float* recs, uint32_t idx, uint32_t end,
                                            int slot, float4* s_geo, float4* s_cot, float4* s_col, float* s_skip,
                                            uint32_t* s_rank) {
-  const uint32_t r = uint32_t(a.keys[idx]);
+  const uint32_t r = min(uint32_t(a.keys[idx]), uint32_t(a.G - 1));  // ranks are < G for valid keys
   const uint32_t rn = (idx + 1 < end) ? uint32_t(a.keys[idx + 1]) : r + 1u;
   const float4* rec = reinterpret_cast<const float4*>(recs + size_t(r) * GSB_RECORD_FLOATS);
   const float4 r0 = __ldg(rec + 0), r1 = __ldg(rec + 1), r2 = __ldg(rec + 2);

@@ -187,6 +187,10 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
     const uint32_t d = dig[j];
     if (d == 0xffffffffu) continue;
     const uint32_t pos = s_base[d] + s_warp_hist[warp][d] + rank[j];
+    if (pos >= n) {  // only after a timed-out look-back: never write outside the output
+      record_error(status, GSB_ERR_TIMEOUT, int(part));
+      continue;
+    }
     keys_out[pos] = k[j];
     if (kVals) vals_out[pos] = v[j];
   }

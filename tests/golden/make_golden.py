@@ -91,7 +91,13 @@ def render_case(R, wl: syn.Workload, crop=None, with_grads=True, tiles=(8, 16)) 
             out[f"grad_{k}"] = v.grad
         if vel is not None:
             out["grad_velocity"] = vel.grad
-        for k, v in act.items():
+        # gradients w.r.t. the reference render call's own inputs: activated tensors as independent
+        # leaves (rgb no longer depends on xyz through the SH view direction)
+        leaves = {k: v.detach().clone().requires_grad_(True) for k, v in act.items()}
+        img2 = R["dense"](leaves["xyz"], leaves["scales"], leaves["quats"], leaves["opacities"], leaves["rgbs"], H, W,
+                          wl.fx, wl.fy, cx, cy, camera_to_world=wl.camera_to_world)
+        R["loss"](img2, target, LOSS_CFG).sum().backward()
+        for k, v in leaves.items():
             out[f"grad_act_{k}"] = v.grad
     # projection internals of the reference, in its depth order
     with torch.no_grad():

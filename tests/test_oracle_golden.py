@@ -141,3 +141,19 @@ def test_culled_tiled_compat_matches_reference_tiled():
         img, *_ = co.blend_culled_view(m2, inv3, op, rgb, None, rpt, H, W, tile, alpha_cutoff=0.0,
                                        transmittance_threshold=0.0, eps_mode="tile_local")
         assert (img.float() - g.t(f"ref_tiled{tile}_image")[0]).abs().max().item() < 2e-6
+
+
+@pytest.mark.parametrize("case", ["static64", "dynamic128_small", "multiview384_small"])
+def test_activated_input_gradients_match_reference(case):
+    """Gradients w.r.t. the reference render call's own inputs (xyz, scales, quats, opacities, rgbs)."""
+    g = load_golden(case)
+    wl = g.workload()
+    act = {k: g.t(f"ref_act_{k}").double().requires_grad_(True) for k in ("xyz", "scales", "quats", "opacities",
+                                                                            "rgbs")}
+    key = so.camera_depth_fp32(act["xyz"].float(), wl.camera_to_world)
+    img, _, _ = so.render_dense(act["xyz"], act["scales"], act["quats"], act["opacities"], act["rgbs"], wl.height,
+                                wl.width, wl.fx, wl.fy, wl.cx, wl.cy, wl.camera_to_world, sort_key=key)
+    so.reconstruction_loss_per_image(img, wl.target.double()).sum().backward()
+    for k, v in act.items():
+        ok, err, scale = grad_close(v.grad, g.t(f"ref_grad_act_{k}"))
+        assert ok, f"{k}: {err:.3e} vs {scale:.3e}"
