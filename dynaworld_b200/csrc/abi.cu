@@ -37,7 +37,8 @@ RenderConsts make_consts(const gsb_views& v, const gsb_options& o) {
   rc.tiled_threshold = o.tiled_alpha_threshold;
   volatile float one = 1.0f;
   rc.f0 = one + o.eps;  // fl32(1 + eps)
-  rc.log2_f0 = rc.compat ? 0.0f : float(std::log2(double(rc.f0)));
+  // T_i = F0^pos_i * S_i in both modes; pos is the depth rank (exact) or the list index (compat)
+  rc.log2_f0 = float(std::log2(double(rc.f0)));
   return rc;
 }
 

@@ -34,8 +34,8 @@ struct RenderConsts {
   float near_plane, alpha_clamp, alpha_cutoff, t_threshold, eps, pixel_center;
   float bg[3];
   float bound_scale, tiled_threshold;
-  float f0;      // fl32(1 + eps), or 1 in compat mode (tile-local products)
-  float log2_f0; // log2(f0) for the rank factors (0 in compat mode)
+  float f0;      // fl32(1 + eps): the transmittance factor of an alpha-0 pair
+  float log2_f0; // log2(f0): T_i = F0^pos_i * S_i (pos = depth rank, or list index in compat mode)
 };
 
 RenderConsts make_consts(const gsb_views& v, const gsb_options& o);

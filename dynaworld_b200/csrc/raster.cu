@@ -2,123 +2,159 @@
 //
 // One CTA per (view, tile), one thread per pixel (16x16 tile: 8 warps, each an 8x4 pixel block).
 // The tile's list (sorted pair keys, low 32 bits = depth rank) is consumed in batches of one entry
-// per thread: each thread gathers one projected record into shared memory, then every thread
-// walks the batch for its pixel.
+// per thread: each thread gathers one projected record into shared memory and marks which warp
+// blocks the Gaussian's ellipse box reaches; each warp then compacts the batch to the entries that
+// reach its block and walks only those.
 //
 // Semantics of the reference's dense blend (src/train/renderers/dense.py:208-233):
 //   alpha_i = clamp(o_i exp(min(power_i, 0)), 0, alpha_clamp)     (dense.py:217-220)
 //   T_i     = prod_{j<i} fl32(fl32(1 - alpha_j) + eps)  over ALL Gaussians of the view in depth
-//             order (dense.py:222-228); a Gaussian absent from the tile list contributes
-//             F0 = fl32(1 + eps), restored here from depth ranks:
-//             T before entry 0 = F0^rank0, T after entry i *= f_i * F0^(rank_{i+1} - rank_i - 1)
+//             order (dense.py:222-228); a Gaussian that does not touch the pixel contributes
+//             F0 = fl32(1 + eps) (exactly so when its alpha <= 2^-25).
 //   out     = clamp(sum w c + (1 - clamp(sum w, 0, 1)) bg, 0, 1), w = T alpha (dense.py:229-233)
-// Pairs with alpha < alpha_cutoff count as alpha = 0 (exact for alpha <= 2^-25, where
-// fl32(1 - alpha) == 1); a pixel stops once T < transmittance_threshold.  In tiled-compat mode
-// F0 = 1 between entries (tile-local products, tiled.py:176-185), nothing is skipped and nothing
-// stops.
+// With pos_i the depth rank of entry i (exact mode) or its index in the tile list (tiled-compat
+// mode, tile-local products as tiled.py:176-185):
+//   T_i = F0^pos_i * S_i,   S_i = prod_{blended j < i} f_j / F0,
+// so entries a pixel skips leave S unchanged and cost nothing.  A pair is skipped when its alpha
+// is below alpha_cutoff, or when q exceeds the Gaussian's threshold (alpha < max(cutoff, 2^-25));
+// a pixel stops once T falls below the transmittance threshold.
 #include "gsb_common.cuh"
 #include "gsb_internal.h"
 
 namespace gsb {
 
-
 constexpr uint32_t kCountBits = 28;
 constexpr uint32_t kCountMask = (1u << kCountBits) - 1u;
 
-// q = A dx^2 + B dx dy + C dy^2 with a fixed rounding sequence (forward and backward must agree).
+// q = A dx^2 + B dx dy + C dy^2 with a fixed rounding sequence (forward and backward agree).
 __device__ __forceinline__ float pair_q(float A, float B, float C, float dx, float dy) {
   const float t0 = __fmul_rn(__fmul_rn(A, dx), dx);
   const float t1 = __fmaf_rn(__fmul_rn(B, dx), dy, t0);
   return __fmaf_rn(__fmul_rn(C, dy), dy, t1);
 }
 
+// Pixel of thread tid: warp w covers the 8x4 block (w % (TILE/8), w / (TILE/8)).
 template <int TILE>
 __device__ __forceinline__ void pixel_of(int tid, int& lx, int& ly) {
   const int lane = tid & 31, warp = tid >> 5;
-  if (TILE == 16) {
-    lx = (warp & 1) * 8 + (lane & 7);
-    ly = (warp >> 1) * 4 + (lane >> 3);
-  } else {
-    lx = lane & 7;
-    ly = warp * 4 + (lane >> 3);
-  }
+  constexpr int BX = TILE / 8;
+  lx = (warp % BX) * 8 + (lane & 7);
+  ly = (warp / BX) * 4 + (lane >> 3);
 }
 
-// Loads list entry idx of [start, end) into shared slot `slot`.
-__device__ __forceinline__ void load_entry(const RasterArgs& a, const float* recs, uint32_t idx, uint32_t end,
-                                           int slot, float4* s_geo, float4* s_cot, float4* s_col, float* s_skip,
-                                           uint32_t* s_rank) {
+struct Batch {
+  float4* geo;    // mx, my, A, B
+  float4* cot;    // C, opacity, tau, F0^pos
+  float4* col;    // r, g, b, z
+  uint32_t* rank; // depth rank (gradient slot)
+  uint32_t* mask; // warp blocks the entry's box reaches
+};
+
+// Loads list entry idx of the tile (list index li) into slot `slot` and marks the warp blocks of
+// the tile that the ellipse box {q <= tau} reaches (conservative).
+template <int TILE>
+__device__ __forceinline__ void load_entry(const RasterArgs& a, const float* recs, uint32_t idx, uint32_t li,
+                                           int slot, int tile_x0, int tile_y0, const Batch& s) {
+  constexpr int NW = TILE * TILE / 32, BX = TILE / 8;
   const uint32_t r = min(uint32_t(a.keys[idx]), uint32_t(a.G - 1));  // ranks are < G for valid keys
-  const uint32_t rn = (idx + 1 < end) ? uint32_t(a.keys[idx + 1]) : r + 1u;
   const float4* rec = reinterpret_cast<const float4*>(recs + size_t(r) * GSB_RECORD_FLOATS);
   const float4 r0 = __ldg(rec + 0), r1 = __ldg(rec + 1), r2 = __ldg(rec + 2);
-  float E = 1.0f, Es = a.rc.f0;
-  if (a.rc.log2_f0 != 0.0f) {
-    E = exp2f(float(rn - r - 1u) * a.rc.log2_f0);
-    Es = exp2f(float(rn - r) * a.rc.log2_f0);
+  const float pos = a.rc.compat ? float(li) : float(r);
+  const float pw = a.rc.log2_f0 != 0.0f ? exp2f(pos * a.rc.log2_f0) : 1.0f;
+  s.geo[slot] = r0;
+  s.cot[slot] = make_float4(r1.x, r1.y, r1.w, pw);
+  s.col[slot] = make_float4(r2.x, r2.y, r2.z, r1.z);
+  s.rank[slot] = r;
+  // box of the ellipse q <= tau: half extents sqrt(tau (A^-1)_ii), (A^-1)_00 = C/det
+  const float A = r0.z, B = r0.w, C = r1.x, tau = r1.w;
+  uint32_t m = 0;
+  if (tau >= 0.0f) {
+    const float det = A * C - 0.25f * B * B;
+    float ex, ey;
+    if (det > 0.0f && isfinite(tau)) {
+      ex = sqrtf(tau * C / det) * 1.0001f + 0.01f;
+      ey = sqrtf(tau * A / det) * 1.0001f + 0.01f;
+    } else {
+      ex = ey = __int_as_float(0x7f800000);
+    }
+    const float pc = a.rc.pixel_center;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float bx0 = float(tile_x0 + (w % BX) * 8) + pc, by0 = float(tile_y0 + (w / BX) * 4) + pc;
+      const bool hit = (r0.x + ex >= bx0) && (r0.x - ex <= bx0 + 7.0f) && (r0.y + ey >= by0) &&
+                       (r0.y - ey <= by0 + 3.0f);
+      m |= hit ? (1u << w) : 0u;
+    }
   }
-  s_geo[slot] = r0;
-  s_cot[slot] = make_float4(r1.x, r1.y, r1.w, E);
-  s_col[slot] = make_float4(r2.x, r2.y, r2.z, r1.z);
-  s_skip[slot] = Es;
-  if (s_rank) s_rank[slot] = r;
+  s.mask[slot] = m;
+}
+
+// Compacts the batch's entries that reach this warp's block into list[0..count), in list order.
+__device__ __forceinline__ int compact_warp(const uint32_t* mask, int nb, int warp, int lane, uint16_t* list) {
+  int count = 0;
+  for (int c = 0; c < nb; c += 32) {
+    const int slot = c + lane;
+    const bool keep = slot < nb && ((mask[slot] >> warp) & 1u);
+    const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+    if (keep) list[count + __popc(bal & ((1u << lane) - 1u))] = uint16_t(slot);
+    count += __popc(bal);
+  }
+  __syncwarp();
+  return count;
 }
 
 template <int TILE>
 __global__ void __launch_bounds__(TILE* TILE) raster_fwd_kernel(RasterArgs a) {
-  constexpr int NT = TILE * TILE;
-  __shared__ float4 s_geo[NT];  // mx, my, A, B
-  __shared__ float4 s_cot[NT];  // C, opacity, tau, E
-  __shared__ float4 s_col[NT];  // r, g, b, z
-  __shared__ float s_skip[NT];  // F0 * E: the factor of a skipped pair
-  __shared__ float s_t0;
+  constexpr int NT = TILE * TILE, NW = NT / 32;
+  __shared__ float4 s_geo[NT], s_cot[NT], s_col[NT];
+  __shared__ uint32_t s_rank[NT], s_mask[NT];
+  __shared__ uint16_t s_list[NW][NT];
+  const Batch sb{s_geo, s_cot, s_col, s_rank, s_mask};
   const RenderConsts& rc = a.rc;
   const int tile = blockIdx.x, view = blockIdx.y;
-  const int tx = tile % rc.tiles_x, ty = tile / rc.tiles_x;
-  const int tid = threadIdx.x;
+  const int tile_x0 = (tile % rc.tiles_x) * TILE, tile_y0 = (tile / rc.tiles_x) * TILE;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int lx, ly;
   pixel_of<TILE>(tid, lx, ly);
-  const int px = tx * TILE + lx, py = ty * TILE + ly;
+  const int px = tile_x0 + lx, py = tile_y0 + ly;
   const bool inside = px < a.W && py < a.H;
   const float fx = float(px) + rc.pixel_center, fy = float(py) + rc.pixel_center;
   const size_t rb = (size_t(view) * rc.n_tiles + tile) * 2;
   const uint32_t start = a.ranges[rb], end = a.ranges[rb + 1];
   const float* recs = a.records + size_t(view) * a.G * GSB_RECORD_FLOATS;
+  const float inv_f0 = 1.0f / rc.f0;
 
-  float T = 1.0f, C0 = 0.0f, C1 = 0.0f, C2 = 0.0f, Ws = 0.0f, D = 0.0f;
+  float S = 1.0f, C0 = 0.0f, C1 = 0.0f, C2 = 0.0f, Ws = 0.0f, D = 0.0f;
   uint32_t n_proc = end - start;
   bool done = !inside;
   for (uint32_t b0 = start; b0 < end; b0 += NT) {
     if (__syncthreads_and(done)) break;
-    const uint32_t idx = b0 + tid;
-    if (idx < end) load_entry(a, recs, idx, end, tid, s_geo, s_cot, s_col, s_skip, nullptr);
-    if (idx == start) s_t0 = rc.log2_f0 != 0.0f ? exp2f(float(uint32_t(a.keys[start])) * rc.log2_f0) : 1.0f;
-    __syncthreads();
-    if (b0 == start) T = s_t0;
-    if (done) continue;
     const int nb = min(NT, int(end - b0));
-    for (int j = 0; j < nb; ++j) {
+    if (tid < nb) load_entry<TILE>(a, recs, b0 + tid, b0 + tid - start, tid, tile_x0, tile_y0, sb);
+    __syncthreads();
+    const int cnt = compact_warp(s_mask, nb, warp, lane, s_list[warp]);
+    if (done) continue;
+    for (int i = 0; i < cnt; ++i) {
+      const int j = s_list[warp][i];
       const float4 g = s_geo[j];
       const float4 ct = s_cot[j];
       const float dx = __fsub_rn(fx, g.x), dy = __fsub_rn(fy, g.y);
       const float q = pair_q(g.z, g.w, ct.x, dx, dy);
-      float fac = s_skip[j];
-      if (q <= ct.z) {
-        const float e = __expf(fminf(-0.5f * q, 0.0f));
-        const float alpha = fminf(fmaxf(ct.y * e, 0.0f), rc.alpha_clamp);
-        if (alpha >= rc.alpha_cutoff) {
-          const float4 c = s_col[j];
-          const float w = T * alpha;
-          C0 = fmaf(w, c.x, C0);
-          C1 = fmaf(w, c.y, C1);
-          C2 = fmaf(w, c.z, C2);
-          Ws += w;
-          D = fmaf(w, c.w, D);
-          fac = __fmul_rn(__fadd_rn(__fsub_rn(1.0f, alpha), rc.eps), ct.w);
-        }
-      }
-      T = __fmul_rn(T, fac);
-      if (T < rc.t_threshold) {
+      if (!(q <= ct.z)) continue;
+      const float e = __expf(fminf(-0.5f * q, 0.0f));
+      const float alpha = fminf(fmaxf(ct.y * e, 0.0f), rc.alpha_clamp);
+      if (!(alpha >= rc.alpha_cutoff)) continue;
+      const float4 c = s_col[j];
+      const float T = S * ct.w;
+      const float w = T * alpha;
+      C0 = fmaf(w, c.x, C0);
+      C1 = fmaf(w, c.y, C1);
+      C2 = fmaf(w, c.z, C2);
+      Ws += w;
+      D = fmaf(w, c.w, D);
+      const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
+      S = S * (f * inv_f0);
+      if (T * f < rc.t_threshold) {  // T after this entry
         done = true;
         n_proc = b0 - start + uint32_t(j) + 1u;
         break;
@@ -141,7 +177,7 @@ __global__ void __launch_bounds__(TILE* TILE) raster_fwd_kernel(RasterArgs a) {
   }
   if (a.alpha) a.alpha[pix] = Ws;
   if (a.depth) a.depth[pix] = D;
-  a.pixel_t[pix] = T;
+  a.pixel_t[pix] = S;  // normalised transmittance after the last blended entry
   a.pixel_state[pix] = min(n_proc, kCountMask) | (mask << kCountBits);
 }
 
@@ -180,34 +216,34 @@ __device__ __forceinline__ float warp_sum16(float v[16], int lane) {
 
 template <int TILE>
 __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
-  constexpr int NT = TILE * TILE;
-  __shared__ float4 s_geo[NT];
-  __shared__ float4 s_cot[NT];
-  __shared__ float4 s_col[NT];
-  __shared__ float s_skip[NT];
-  __shared__ uint32_t s_rank[NT];
-  __shared__ uint32_t s_red[NT / 32];
+  constexpr int NT = TILE * TILE, NW = NT / 32;
+  __shared__ float4 s_geo[NT], s_cot[NT], s_col[NT];
+  __shared__ uint32_t s_rank[NT], s_mask[NT];
+  __shared__ uint16_t s_list[NW][NT];
+  __shared__ uint32_t s_red[NW];
+  const Batch sb{s_geo, s_cot, s_col, s_rank, s_mask};
   const RenderConsts& rc = a.rc;
   const int tile = blockIdx.x, view = blockIdx.y;
-  const int tx = tile % rc.tiles_x, ty = tile / rc.tiles_x;
+  const int tile_x0 = (tile % rc.tiles_x) * TILE, tile_y0 = (tile / rc.tiles_x) * TILE;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int lx, ly;
   pixel_of<TILE>(tid, lx, ly);
-  const int px = tx * TILE + lx, py = ty * TILE + ly;
+  const int px = tile_x0 + lx, py = tile_y0 + ly;
   const bool inside = px < a.W && py < a.H;
   const float fx = float(px) + rc.pixel_center, fy = float(py) + rc.pixel_center;
   const size_t rb = (size_t(view) * rc.n_tiles + tile) * 2;
   const uint32_t start = a.ranges[rb], end = a.ranges[rb + 1];
   const float* recs = a.records + size_t(view) * a.G * GSB_RECORD_FLOATS;
   float* g2 = a.grad2d + size_t(view) * a.G * GSB_GRAD2D_FLOATS;
+  const float inv_f0 = 1.0f / rc.f0;
 
   const size_t HW = size_t(a.H) * a.W;
   const size_t poff = size_t(py) * a.W + px;
   const size_t pix = size_t(view) * HW + poff;
-  float T = 0.0f, g0 = 0.0f, g1 = 0.0f, g2c = 0.0f, gW = 0.0f, gD = 0.0f;
+  float S = 0.0f, g0 = 0.0f, g1 = 0.0f, g2c = 0.0f, gW = 0.0f, gD = 0.0f;
   uint32_t n_proc = 0;
   if (inside) {
-    T = a.pixel_t[pix];
+    S = a.pixel_t[pix];
     const uint32_t st = a.pixel_state[pix];
     n_proc = st & kCountMask;
     const uint32_t mask = st >> kCountBits;
@@ -225,16 +261,18 @@ __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
   __syncthreads();
   uint32_t max_n = 0;
 #pragma unroll
-  for (int w = 0; w < NT / 32; ++w) max_n = max(max_n, s_red[w]);
+  for (int w = 0; w < NW; ++w) max_n = max(max_n, s_red[w]);
 
   float R0 = 0.0f, R1 = 0.0f, R2 = 0.0f, RW = 0.0f, RD = 0.0f;
   for (int64_t be = max_n; be > 0; be -= NT) {
     const uint32_t bs = uint32_t(be > NT ? be - NT : 0);
     const int nb = int(be - bs);
     __syncthreads();
-    if (tid < nb) load_entry(a, recs, start + bs + tid, end, tid, s_geo, s_cot, s_col, s_skip, s_rank);
+    if (tid < nb) load_entry<TILE>(a, recs, start + bs + tid, bs + tid, tid, tile_x0, tile_y0, sb);
     __syncthreads();
-    for (int j = nb - 1; j >= 0; --j) {
+    const int cnt = compact_warp(s_mask, nb, warp, lane, s_list[warp]);
+    for (int i = cnt - 1; i >= 0; --i) {
+      const int j = s_list[warp][i];
       float v[16];
 #pragma unroll
       for (int k = 0; k < 16; ++k) v[k] = 0.0f;
@@ -244,45 +282,39 @@ __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
         const float4 ct = s_cot[j];
         const float dx = __fsub_rn(fx, g.x), dy = __fsub_rn(fy, g.y);
         const float q = pair_q(g.z, g.w, ct.x, dx, dy);
-        float fac = s_skip[j];
-        float alpha = 0.0f, e = 0.0f;
-        bool hit = false;
         if (q <= ct.z) {
-          e = __expf(fminf(-0.5f * q, 0.0f));
-          alpha = fminf(fmaxf(ct.y * e, 0.0f), rc.alpha_clamp);
-          if (alpha >= rc.alpha_cutoff) {
-            hit = true;
-            fac = __fmul_rn(__fadd_rn(__fsub_rn(1.0f, alpha), rc.eps), ct.w);
-          }
-        }
-        T = __fdiv_rn(T, fac);  // T before this entry
-        if (hit) {
-          const float4 c = s_col[j];
-          const float w = T * alpha;
-          const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
-          const float dldw = g0 * c.x + g1 * c.y + g2c * c.z + gW + gD * c.w;
-          const float dlda = T * dldw - (g0 * R0 + g1 * R1 + g2c * R2 + gW * RW + gD * RD) / f;
-          R0 = fmaf(w, c.x, R0);
-          R1 = fmaf(w, c.y, R1);
-          R2 = fmaf(w, c.z, R2);
-          RW += w;
-          RD = fmaf(w, c.w, RD);
+          const float e = __expf(fminf(-0.5f * q, 0.0f));
           const float araw = ct.y * e;
-          const float dlr = (araw >= 0.0f && araw <= rc.alpha_clamp) ? dlda : 0.0f;
-          const float power = -0.5f * q;
-          const float pmask = power < 0.0f ? 1.0f : (power == 0.0f ? 0.5f : 0.0f);
-          const float dpow = dlr * araw * pmask;
-          v[0] = dpow * (g.z * dx + 0.5f * g.w * dy);
-          v[1] = dpow * (ct.x * dy + 0.5f * g.w * dx);
-          v[2] = -0.5f * dpow * dx * dx;
-          v[3] = -0.5f * dpow * dx * dy;
-          v[4] = -0.5f * dpow * dy * dy;
-          v[5] = dlr * e;
-          v[6] = g0 * w;
-          v[7] = g1 * w;
-          v[8] = g2c * w;
-          v[9] = gD * w;
-          contrib = true;
+          const float alpha = fminf(fmaxf(araw, 0.0f), rc.alpha_clamp);
+          if (alpha >= rc.alpha_cutoff) {
+            const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
+            S = __fdividef(S, f * inv_f0);  // S before this entry
+            const float T = S * ct.w;
+            const float4 c = s_col[j];
+            const float w = T * alpha;
+            const float dldw = g0 * c.x + g1 * c.y + g2c * c.z + gW + gD * c.w;
+            const float dlda = T * dldw - __fdividef(g0 * R0 + g1 * R1 + g2c * R2 + gW * RW + gD * RD, f);
+            R0 = fmaf(w, c.x, R0);
+            R1 = fmaf(w, c.y, R1);
+            R2 = fmaf(w, c.z, R2);
+            RW += w;
+            RD = fmaf(w, c.w, RD);
+            const float dlr = (araw >= 0.0f && araw <= rc.alpha_clamp) ? dlda : 0.0f;
+            const float power = -0.5f * q;
+            const float pmask = power < 0.0f ? 1.0f : (power == 0.0f ? 0.5f : 0.0f);
+            const float dpow = dlr * araw * pmask;
+            v[0] = dpow * (g.z * dx + 0.5f * g.w * dy);
+            v[1] = dpow * (ct.x * dy + 0.5f * g.w * dx);
+            v[2] = -0.5f * dpow * dx * dx;
+            v[3] = -0.5f * dpow * dx * dy;
+            v[4] = -0.5f * dpow * dy * dy;
+            v[5] = dlr * e;
+            v[6] = g0 * w;
+            v[7] = g1 * w;
+            v[8] = g2c * w;
+            v[9] = gD * w;
+            contrib = true;
+          }
         }
       }
       if (__any_sync(0xffffffffu, contrib)) {
