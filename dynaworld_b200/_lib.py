@@ -83,6 +83,8 @@ SIGNATURES = {
     "gsb_loss_workspace": (C.c_size_t, [C.c_int32]),
     "gsb_loss_fwd_bwd": (C.c_int, [P(LossOptions), C.c_int32, C.c_int32, C.c_int32, C.c_int32, vp, vp, vp, vp, vp,
                                    C.c_size_t, vp]),
+    "gsb_loss_fwd_bwd_noalloc": (C.c_int, [P(LossOptions), C.c_int32, C.c_int32, C.c_int32, C.c_int32, vp, vp, vp,
+                                           vp, vp]),
     "gsb_scale_planes": (C.c_int, [vp, vp, vp, C.c_int32, C.c_int64, vp]),
     "gsb_raster_bwd": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "gsb_preprocess_bwd": (C.c_int, [P(Scene), P(Views), P(Options), vp, vp, P(SceneGrads), vp]),

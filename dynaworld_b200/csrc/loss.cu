@@ -13,6 +13,7 @@
 // The kernel assumes the final clamp of the SSIM mean is inactive; a finishing kernel computes the
 // per-image loss and a fix-up kernel rewrites the gradient of any image whose mean left [-1, 1].
 #include <cmath>
+#include <mutex>
 
 #include "gsb_common.cuh"
 #include "gsb_internal.h"
@@ -349,4 +350,61 @@ gsb_status scale_planes(const float* in, const float* scale, float* out, int32_t
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 
+// ---- allocation-free loss entry ----------------------------------------------------------------
+//
+// gsb_loss_fwd_bwd needs a small device workspace (three double sums and one flag per image) that
+// its caller allocates.  Some callers have no way to allocate device memory: a plugin or binding
+// that is handed its input and output buffers by a host framework which owns the device allocator
+// and offers no call to obtain more.  For them gsb_loss_fwd_bwd_noalloc keeps that workspace in the
+// fixed array below, which is part of the library image: every GPU that loads the library holds it
+// (about 112 KiB) until the process exits.  Host code cannot use the array's name as a device
+// address (on the host it names a stand-in, not device memory), so the entry point looks the
+// address up once per device with cudaGetSymbolAddress, with that device current, and caches it.
+
+constexpr int32_t kNoAllocMaxImages = GSB_LOSS_NOALLOC_MAX_IMAGES;
+constexpr size_t kNoAllocAlign = 256;
+constexpr size_t noalloc_round(size_t x) { return (x + kNoAllocAlign - 1) / kNoAllocAlign * kNoAllocAlign; }
+// Same carving as loss_workspace(): header, per-image double sums, per-image clamp flags.
+constexpr size_t kNoAllocBytes = noalloc_round(sizeof(WorkspaceHeader)) +
+                                 noalloc_round(size_t(kNoAllocMaxImages) * 3 * sizeof(double)) +
+                                 noalloc_round(size_t(kNoAllocMaxImages) * sizeof(int32_t));
+
+static __device__ __align__(256) unsigned char g_loss_scratch[kNoAllocBytes];
+
+constexpr int kNoAllocMaxDevices = 128;
+static std::mutex g_loss_scratch_mu;
+static void* g_loss_scratch_addr[kNoAllocMaxDevices] = {};
+
+// Device address of g_loss_scratch on the current device (looked up on first use per device).
+static gsb_status loss_scratch_address(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return GSB_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_loss_scratch_mu);
+  if (g_loss_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_loss_scratch);
+    if (e != cudaSuccess || p == nullptr) return GSB_ERR_CUDA;
+    g_loss_scratch_addr[dev] = p;
+  }
+  *out = g_loss_scratch_addr[dev];
+  return GSB_OK;
+}
+
 }  // namespace gsb
+
+extern "C" GSB_API gsb_status gsb_loss_fwd_bwd_noalloc(const gsb_loss_options* lopts, int32_t n_images,
+                                                       int32_t channels, int32_t height, int32_t width,
+                                                       const float* pred, const float* target, float* loss,
+                                                       float* dpred, void* stream) {
+  using namespace gsb;
+  if (!lopts) return GSB_ERR_ARG;
+  if (n_images <= 0 || n_images > kNoAllocMaxImages) return GSB_ERR_SHAPE;  // scratch holds at most this many
+  if (loss_workspace(n_images) > kNoAllocBytes) return GSB_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  const gsb_status s = loss_scratch_address(&scratch);
+  if (s != GSB_OK) return s;
+  // loss_fwd_bwd clears the per-image sums before its kernels run, so nothing carries over
+  // from the previous call that used the array.
+  return loss_fwd_bwd(*lopts, n_images, channels, height, width, pred, target, loss, dpred, scratch, kNoAllocBytes,
+                      static_cast<cudaStream_t>(stream));
+}

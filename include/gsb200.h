@@ -188,6 +188,22 @@ GSB_API gsb_status gsb_loss_fwd_bwd(const gsb_loss_options* lopts, int32_t n_ima
                                     const float* pred, const float* target, float* loss,
                                     float* dpred, void* workspace, size_t workspace_bytes,
                                     void* stream);
+/* Allocation-free variant of gsb_loss_fwd_bwd.  No counterpart in the reference: it exists for
+   callers that cannot allocate device memory at all -- typically a plugin or language binding
+   that is handed its input and output buffers by a host framework owning the device allocator.
+   Same results as gsb_loss_fwd_bwd; its scratch (three double sums and one flag per image) is a
+   fixed array inside the library, about 112 KiB, held by every GPU that loads the library until
+   the process exits.  Limit: n_images <= GSB_LOSS_NOALLOC_MAX_IMAGES, larger batches return
+   GSB_ERR_SHAPE before anything is launched.  The first call on each device looks up the array's
+   device address with that device current and caches it: make that first call before any stream
+   capture.  Every call uses the same array; each call clears the sums it needs, but calls that
+   overlap on the GPU (several streams or host threads at once) race on it and give wrong results,
+   so order them on one stream. */
+#define GSB_LOSS_NOALLOC_MAX_IMAGES 4096
+GSB_API gsb_status gsb_loss_fwd_bwd_noalloc(const gsb_loss_options* lopts, int32_t n_images,
+                                            int32_t channels, int32_t height, int32_t width,
+                                            const float* pred, const float* target, float* loss,
+                                            float* dpred, void* stream);
 /* out[b, ...] = scale[b] * in[b, ...] for n_images planes of plane_elems floats (in == out ok). */
 GSB_API gsb_status gsb_scale_planes(const float* in, const float* scale, float* out,
                                     int32_t n_images, int64_t plane_elems, void* stream);
