@@ -1,10 +1,9 @@
 // Raster: per-tile front-to-back blend and its reverse-order backward.
 //
-// One CTA per (view, tile), one thread per pixel (16x16 tile: 8 warps, each an 8x4 pixel block).
-// The tile's list (sorted pair keys, low 32 bits = depth rank) is consumed in batches of one entry
-// per thread: each thread gathers one projected record into shared memory and marks which warp
-// blocks the Gaussian's ellipse box reaches; each warp then compacts the batch to the entries that
-// reach its block and walks only those.
+// One CTA per (view, tile) of 16x16 pixels, one thread per pixel; each warp owns an 8x4 pixel block
+// and works independently of the other warps (no CTA barrier): it streams the tile's sorted list in
+// chunks of 32 entries (one gather per lane; the 8 warps of a tile read the same records, so all but
+// the first read hit L1), keeps the entries whose ellipse box reaches its block, and walks those.
 //
 // Semantics of the reference's dense blend (src/train/renderers/dense.py:208-233):
 //   alpha_i = clamp(o_i exp(min(power_i, 0)), 0, alpha_clamp)     (dense.py:217-220)
@@ -25,6 +24,7 @@ namespace gsb {
 
 constexpr uint32_t kCountBits = 28;
 constexpr uint32_t kCountMask = (1u << kCountBits) - 1u;
+constexpr uint32_t kFull = 0xffffffffu;
 
 // q = A dx^2 + B dx dy + C dy^2 with a fixed rounding sequence (forward and backward agree).
 __device__ __forceinline__ float pair_q(float A, float B, float C, float dx, float dy) {
@@ -33,133 +33,101 @@ __device__ __forceinline__ float pair_q(float A, float B, float C, float dx, flo
   return __fmaf_rn(__fmul_rn(C, dy), dy, t1);
 }
 
-// Pixel of thread tid: warp w covers the 8x4 block (w % (TILE/8), w / (TILE/8)).
+// Pixel block of warp w inside a TILE x TILE tile: 8 wide, 4 high.
 template <int TILE>
-__device__ __forceinline__ void pixel_of(int tid, int& lx, int& ly) {
-  const int lane = tid & 31, warp = tid >> 5;
+__device__ __forceinline__ void block_of(int warp, int& bx, int& by) {
   constexpr int BX = TILE / 8;
-  lx = (warp % BX) * 8 + (lane & 7);
-  ly = (warp / BX) * 4 + (lane >> 3);
+  bx = (warp % BX) * 8;
+  by = (warp / BX) * 4;
 }
 
-struct Batch {
-  float4* geo;    // mx, my, A, B
-  float4* cot;    // C, opacity, tau, F0^pos
-  float4* col;    // r, g, b, z
-  uint32_t* rank; // depth rank (gradient slot)
-  uint32_t* mask; // warp blocks the entry's box reaches
+struct WarpSlots {
+  float4* geo;     // mx, my, A, B
+  float4* cot;     // C, opacity, tau, F0^pos
+  float4* col;     // r, g, b, z
+  uint32_t* rank;  // depth rank (gradient slot)
 };
 
-// Loads list entry idx of the tile (list index li) into slot `slot` and marks the warp blocks of
-// the tile that the ellipse box {q <= tau} reaches (conservative).
-template <int TILE>
-__device__ __forceinline__ void load_entry(const RasterArgs& a, const float* recs, uint32_t idx, uint32_t li,
-                                           int slot, int tile_x0, int tile_y0, const Batch& s) {
-  constexpr int NW = TILE * TILE / 32, BX = TILE / 8;
+// Lane loads list entry idx (list index li) into its warp slot and returns whether the Gaussian's
+// ellipse box {q <= tau} reaches the warp's pixel block [bx0, bx0+7] x [by0, by0+3] (pixel
+// centres; conservative).
+__device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* recs, uint32_t idx, uint32_t li,
+                                           float bx0, float by0, const WarpSlots& s, int lane) {
   const uint32_t r = min(uint32_t(a.keys[idx]), uint32_t(a.G - 1));  // ranks are < G for valid keys
   const float4* rec = reinterpret_cast<const float4*>(recs + size_t(r) * GSB_RECORD_FLOATS);
   const float4 r0 = __ldg(rec + 0), r1 = __ldg(rec + 1), r2 = __ldg(rec + 2);
   const float pos = a.rc.compat ? float(li) : float(r);
-  const float pw = a.rc.log2_f0 != 0.0f ? exp2f(pos * a.rc.log2_f0) : 1.0f;
-  s.geo[slot] = r0;
-  s.cot[slot] = make_float4(r1.x, r1.y, r1.w, pw);
-  s.col[slot] = make_float4(r2.x, r2.y, r2.z, r1.z);
-  s.rank[slot] = r;
-  // box of the ellipse q <= tau: half extents sqrt(tau (A^-1)_ii), (A^-1)_00 = C/det
+  const float pw = exp2f(pos * a.rc.log2_f0);
+  s.geo[lane] = r0;
+  s.cot[lane] = make_float4(r1.x, r1.y, r1.w, pw);
+  s.col[lane] = make_float4(r2.x, r2.y, r2.z, r1.z);
+  if (s.rank) s.rank[lane] = r;
   const float A = r0.z, B = r0.w, C = r1.x, tau = r1.w;
-  uint32_t m = 0;
-  if (tau >= 0.0f) {
-    const float det = A * C - 0.25f * B * B;
-    float ex, ey;
-    if (det > 0.0f && isfinite(tau)) {
-      ex = sqrtf(tau * C / det) * 1.0001f + 0.01f;
-      ey = sqrtf(tau * A / det) * 1.0001f + 0.01f;
-    } else {
-      ex = ey = __int_as_float(0x7f800000);
-    }
-    const float pc = a.rc.pixel_center;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      const float bx0 = float(tile_x0 + (w % BX) * 8) + pc, by0 = float(tile_y0 + (w / BX) * 4) + pc;
-      const bool hit = (r0.x + ex >= bx0) && (r0.x - ex <= bx0 + 7.0f) && (r0.y + ey >= by0) &&
-                       (r0.y - ey <= by0 + 3.0f);
-      m |= hit ? (1u << w) : 0u;
-    }
-  }
-  s.mask[slot] = m;
-}
-
-// Compacts the batch's entries that reach this warp's block into list[0..count), in list order.
-__device__ __forceinline__ int compact_warp(const uint32_t* mask, int nb, int warp, int lane, uint16_t* list) {
-  int count = 0;
-  for (int c = 0; c < nb; c += 32) {
-    const int slot = c + lane;
-    const bool keep = slot < nb && ((mask[slot] >> warp) & 1u);
-    const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-    if (keep) list[count + __popc(bal & ((1u << lane) - 1u))] = uint16_t(slot);
-    count += __popc(bal);
-  }
-  __syncwarp();
-  return count;
+  if (!(tau >= 0.0f)) return false;
+  const float det = A * C - 0.25f * B * B;
+  if (!(det > 0.0f) || !isfinite(tau)) return true;
+  // half extents of the ellipse: sqrt(tau (A^-1)_ii), (A^-1)_00 = C/det, (A^-1)_11 = A/det
+  const float ex = sqrtf(tau * C / det) * 1.0001f + 0.01f;
+  const float ey = sqrtf(tau * A / det) * 1.0001f + 0.01f;
+  return (r0.x + ex >= bx0) && (r0.x - ex <= bx0 + 7.0f) && (r0.y + ey >= by0) && (r0.y - ey <= by0 + 3.0f);
 }
 
 template <int TILE>
 __global__ void __launch_bounds__(TILE* TILE) raster_fwd_kernel(RasterArgs a) {
-  constexpr int NT = TILE * TILE, NW = NT / 32;
-  __shared__ float4 s_geo[NT], s_cot[NT], s_col[NT];
-  __shared__ uint32_t s_rank[NT], s_mask[NT];
-  __shared__ uint16_t s_list[NW][NT];
-  const Batch sb{s_geo, s_cot, s_col, s_rank, s_mask};
+  constexpr int NW = TILE * TILE / 32;
+  __shared__ float4 s_geo[NW][32], s_cot[NW][32], s_col[NW][32];
   const RenderConsts& rc = a.rc;
   const int tile = blockIdx.x, view = blockIdx.y;
-  const int tile_x0 = (tile % rc.tiles_x) * TILE, tile_y0 = (tile / rc.tiles_x) * TILE;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  int lx, ly;
-  pixel_of<TILE>(tid, lx, ly);
-  const int px = tile_x0 + lx, py = tile_y0 + ly;
+  int bx, by;
+  block_of<TILE>(warp, bx, by);
+  const int px = (tile % rc.tiles_x) * TILE + bx + (lane & 7);
+  const int py = (tile / rc.tiles_x) * TILE + by + (lane >> 3);
+  const float bx0 = float(px - (lane & 7)) + rc.pixel_center, by0 = float(py - (lane >> 3)) + rc.pixel_center;
   const bool inside = px < a.W && py < a.H;
   const float fx = float(px) + rc.pixel_center, fy = float(py) + rc.pixel_center;
   const size_t rb = (size_t(view) * rc.n_tiles + tile) * 2;
   const uint32_t start = a.ranges[rb], end = a.ranges[rb + 1];
   const float* recs = a.records + size_t(view) * a.G * GSB_RECORD_FLOATS;
   const float inv_f0 = 1.0f / rc.f0;
+  const WarpSlots ws{s_geo[warp], s_cot[warp], s_col[warp], nullptr};
 
   float S = 1.0f, C0 = 0.0f, C1 = 0.0f, C2 = 0.0f, Ws = 0.0f, D = 0.0f;
   uint32_t n_proc = end - start;
   bool done = !inside;
-  for (uint32_t b0 = start; b0 < end; b0 += NT) {
-    if (__syncthreads_and(done)) break;
-    const int nb = min(NT, int(end - b0));
-    if (tid < nb) load_entry<TILE>(a, recs, b0 + tid, b0 + tid - start, tid, tile_x0, tile_y0, sb);
-    __syncthreads();
-    const int cnt = compact_warp(s_mask, nb, warp, lane, s_list[warp]);
-    if (done) continue;
-    for (int i = 0; i < cnt; ++i) {
-      const int j = s_list[warp][i];
-      const float4 g = s_geo[j];
-      const float4 ct = s_cot[j];
+  for (uint32_t c = start; c < end; c += 32) {
+    if (__all_sync(kFull, done)) break;
+    const uint32_t idx = c + lane;
+    const bool keep = idx < end && load_entry(a, recs, idx, idx - start, bx0, by0, ws, lane);
+    uint32_t m = __ballot_sync(kFull, keep);
+    __syncwarp();
+    while (m && !done) {
+      const int j = __ffs(m) - 1;
+      m &= m - 1;
+      const float4 g = s_geo[warp][j];
+      const float4 ct = s_cot[warp][j];
       const float dx = __fsub_rn(fx, g.x), dy = __fsub_rn(fy, g.y);
       const float q = pair_q(g.z, g.w, ct.x, dx, dy);
       if (!(q <= ct.z)) continue;
       const float e = __expf(fminf(-0.5f * q, 0.0f));
       const float alpha = fminf(fmaxf(ct.y * e, 0.0f), rc.alpha_clamp);
       if (!(alpha >= rc.alpha_cutoff)) continue;
-      const float4 c = s_col[j];
+      const float4 col = s_col[warp][j];
       const float T = S * ct.w;
       const float w = T * alpha;
-      C0 = fmaf(w, c.x, C0);
-      C1 = fmaf(w, c.y, C1);
-      C2 = fmaf(w, c.z, C2);
+      C0 = fmaf(w, col.x, C0);
+      C1 = fmaf(w, col.y, C1);
+      C2 = fmaf(w, col.z, C2);
       Ws += w;
-      D = fmaf(w, c.w, D);
+      D = fmaf(w, col.w, D);
       const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
       S = S * (f * inv_f0);
       if (T * f < rc.t_threshold) {  // T after this entry
         done = true;
-        n_proc = b0 - start + uint32_t(j) + 1u;
-        break;
+        n_proc = c - start + uint32_t(j) + 1u;
       }
     }
+    __syncwarp();  // slots are rewritten by the next chunk
   }
   if (!inside) return;
   const size_t HW = size_t(a.H) * a.W;
@@ -167,11 +135,11 @@ __global__ void __launch_bounds__(TILE* TILE) raster_fwd_kernel(RasterArgs a) {
   const size_t pix = size_t(view) * HW + poff;
   const float wc = fminf(fmaxf(Ws, 0.0f), 1.0f);
   const float one_m = __fsub_rn(1.0f, wc);
-  const float col[3] = {C0, C1, C2};
+  const float cc[3] = {C0, C1, C2};
   uint32_t mask = (Ws >= 0.0f && Ws <= 1.0f) ? 8u : 0u;
 #pragma unroll
   for (int ch = 0; ch < 3; ++ch) {
-    const float pre = __fadd_rn(col[ch], __fmul_rn(one_m, rc.bg[ch]));
+    const float pre = __fadd_rn(cc[ch], __fmul_rn(one_m, rc.bg[ch]));
     if (pre >= 0.0f && pre <= 1.0f) mask |= 1u << ch;
     a.image[(size_t(view) * 3 + ch) * HW + poff] = fminf(fmaxf(pre, 0.0f), 1.0f);
   }
@@ -181,54 +149,59 @@ __global__ void __launch_bounds__(TILE* TILE) raster_fwd_kernel(RasterArgs a) {
   a.pixel_state[pix] = min(n_proc, kCountMask) | (mask << kCountBits);
 }
 
-// Sum of each of 16 per-lane values over the warp; afterwards lane l holds the total of value
-// l >> 1.  Recursive halving: 8 + 4 + 2 + 1 + 1 shuffles instead of 16 * 5.
-__device__ __forceinline__ float warp_sum16(float v[16], int lane) {
+// Warp sum of 10 per-lane values (v[10], v[11] are padding).  Afterwards lane l holds the total of
+// value 6*b4 + 3*b3 + (2*b2 + b1) (b = bits of l) when 2*b2 + b1 < 3; 13 shuffles.
+__device__ __forceinline__ float warp_sum10(float v[12], int lane, int* index) {
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
+  for (int k = 0; k < 6; ++k) {
     const bool up = lane & 16;
-    const float send = up ? v[k] : v[k + 8];
-    const float keep = up ? v[k + 8] : v[k];
-    v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    const float send = up ? v[k] : v[k + 6];
+    const float keep = up ? v[k + 6] : v[k];
+    v[k] = keep + __shfl_xor_sync(kFull, send, 16);
   }
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < 3; ++k) {
     const bool up = lane & 8;
-    const float send = up ? v[k] : v[k + 4];
-    const float keep = up ? v[k + 4] : v[k];
-    v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    const float send = up ? v[k] : v[k + 3];
+    const float keep = up ? v[k + 3] : v[k];
+    v[k] = keep + __shfl_xor_sync(kFull, send, 8);
   }
+  v[3] = 0.0f;
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     const bool up = lane & 4;
     const float send = up ? v[k] : v[k + 2];
     const float keep = up ? v[k + 2] : v[k];
-    v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    v[k] = keep + __shfl_xor_sync(kFull, send, 4);
   }
   {
     const bool up = lane & 2;
     const float send = up ? v[0] : v[1];
     const float keep = up ? v[1] : v[0];
-    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    v[0] = keep + __shfl_xor_sync(kFull, send, 2);
   }
-  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+  const int sub = ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+  *index = sub < 3 ? ((lane >> 4) & 1) * 6 + ((lane >> 3) & 1) * 3 + sub : 99;
+  return v[0] + __shfl_xor_sync(kFull, v[0], 1);
 }
+
+// Lanes contributing to one entry at or below this count add their own values atomically; above
+// it the warp reduces first.
+constexpr int kSparseContributors = 4;
 
 template <int TILE>
 __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
-  constexpr int NT = TILE * TILE, NW = NT / 32;
-  __shared__ float4 s_geo[NT], s_cot[NT], s_col[NT];
-  __shared__ uint32_t s_rank[NT], s_mask[NT];
-  __shared__ uint16_t s_list[NW][NT];
-  __shared__ uint32_t s_red[NW];
-  const Batch sb{s_geo, s_cot, s_col, s_rank, s_mask};
+  constexpr int NW = TILE * TILE / 32;
+  __shared__ float4 s_geo[NW][32], s_cot[NW][32], s_col[NW][32];
+  __shared__ uint32_t s_rank[NW][32];
   const RenderConsts& rc = a.rc;
   const int tile = blockIdx.x, view = blockIdx.y;
-  const int tile_x0 = (tile % rc.tiles_x) * TILE, tile_y0 = (tile / rc.tiles_x) * TILE;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  int lx, ly;
-  pixel_of<TILE>(tid, lx, ly);
-  const int px = tile_x0 + lx, py = tile_y0 + ly;
+  int bx, by;
+  block_of<TILE>(warp, bx, by);
+  const int px = (tile % rc.tiles_x) * TILE + bx + (lane & 7);
+  const int py = (tile / rc.tiles_x) * TILE + by + (lane >> 3);
+  const float bx0 = float(px - (lane & 7)) + rc.pixel_center, by0 = float(py - (lane >> 3)) + rc.pixel_center;
   const bool inside = px < a.W && py < a.H;
   const float fx = float(px) + rc.pixel_center, fy = float(py) + rc.pixel_center;
   const size_t rb = (size_t(view) * rc.n_tiles + tile) * 2;
@@ -236,6 +209,7 @@ __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
   const float* recs = a.records + size_t(view) * a.G * GSB_RECORD_FLOATS;
   float* g2 = a.grad2d + size_t(view) * a.G * GSB_GRAD2D_FLOATS;
   const float inv_f0 = 1.0f / rc.f0;
+  const WarpSlots ws{s_geo[warp], s_cot[warp], s_col[warp], s_rank[warp]};
 
   const size_t HW = size_t(a.H) * a.W;
   const size_t poff = size_t(py) * a.W + px;
@@ -256,30 +230,24 @@ __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
     if (a.d_alpha) gW += a.d_alpha[pix];
     if (a.d_depth) gD = a.d_depth[pix];
   }
-  const uint32_t wmax = __reduce_max_sync(0xffffffffu, n_proc);
-  if (lane == 0) s_red[warp] = wmax;
-  __syncthreads();
-  uint32_t max_n = 0;
-#pragma unroll
-  for (int w = 0; w < NW; ++w) max_n = max(max_n, s_red[w]);
+  const uint32_t wmax = __reduce_max_sync(kFull, n_proc);  // list prefix this warp has to revisit
 
   float R0 = 0.0f, R1 = 0.0f, R2 = 0.0f, RW = 0.0f, RD = 0.0f;
-  for (int64_t be = max_n; be > 0; be -= NT) {
-    const uint32_t bs = uint32_t(be > NT ? be - NT : 0);
-    const int nb = int(be - bs);
-    __syncthreads();
-    if (tid < nb) load_entry<TILE>(a, recs, start + bs + tid, bs + tid, tid, tile_x0, tile_y0, sb);
-    __syncthreads();
-    const int cnt = compact_warp(s_mask, nb, warp, lane, s_list[warp]);
-    for (int i = cnt - 1; i >= 0; --i) {
-      const int j = s_list[warp][i];
-      float v[16];
+  for (int64_t cb = wmax ? int64_t((wmax - 1) / 32) * 32 : -32; cb >= 0; cb -= 32) {
+    const uint32_t li = uint32_t(cb) + lane;
+    const bool keep = li < wmax && load_entry(a, recs, start + li, li, bx0, by0, ws, lane);
+    uint32_t m = __ballot_sync(kFull, keep);
+    __syncwarp();
+    while (m) {
+      const int j = 31 - __clz(m);
+      m &= ~(1u << j);
+      float v[12];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) v[k] = 0.0f;
+      for (int k = 0; k < 12; ++k) v[k] = 0.0f;
       bool contrib = false;
-      if (bs + uint32_t(j) < n_proc) {
-        const float4 g = s_geo[j];
-        const float4 ct = s_cot[j];
+      if (uint32_t(cb) + uint32_t(j) < n_proc) {
+        const float4 g = s_geo[warp][j];
+        const float4 ct = s_cot[warp][j];
         const float dx = __fsub_rn(fx, g.x), dy = __fsub_rn(fy, g.y);
         const float q = pair_q(g.z, g.w, ct.x, dx, dy);
         if (q <= ct.z) {
@@ -290,24 +258,25 @@ __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
             const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
             S = __fdividef(S, f * inv_f0);  // S before this entry
             const float T = S * ct.w;
-            const float4 c = s_col[j];
+            const float4 col = s_col[warp][j];
             const float w = T * alpha;
-            const float dldw = g0 * c.x + g1 * c.y + g2c * c.z + gW + gD * c.w;
+            const float dldw = g0 * col.x + g1 * col.y + g2c * col.z + gW + gD * col.w;
             const float dlda = T * dldw - __fdividef(g0 * R0 + g1 * R1 + g2c * R2 + gW * RW + gD * RD, f);
-            R0 = fmaf(w, c.x, R0);
-            R1 = fmaf(w, c.y, R1);
-            R2 = fmaf(w, c.z, R2);
+            R0 = fmaf(w, col.x, R0);
+            R1 = fmaf(w, col.y, R1);
+            R2 = fmaf(w, col.z, R2);
             RW += w;
-            RD = fmaf(w, c.w, RD);
+            RD = fmaf(w, col.w, RD);
             const float dlr = (araw >= 0.0f && araw <= rc.alpha_clamp) ? dlda : 0.0f;
             const float power = -0.5f * q;
             const float pmask = power < 0.0f ? 1.0f : (power == 0.0f ? 0.5f : 0.0f);
             const float dpow = dlr * araw * pmask;
-            v[0] = dpow * (g.z * dx + 0.5f * g.w * dy);
-            v[1] = dpow * (ct.x * dy + 0.5f * g.w * dx);
-            v[2] = -0.5f * dpow * dx * dx;
-            v[3] = -0.5f * dpow * dx * dy;
-            v[4] = -0.5f * dpow * dy * dy;
+            const float u = dpow * dx, t = dpow * dy;
+            v[0] = g.z * u + 0.5f * g.w * t;
+            v[1] = ct.x * t + 0.5f * g.w * u;
+            v[2] = -0.5f * u * dx;
+            v[3] = -0.5f * u * dy;
+            v[4] = -0.5f * t * dy;
             v[5] = dlr * e;
             v[6] = g0 * w;
             v[7] = g1 * w;
@@ -317,13 +286,22 @@ __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
           }
         }
       }
-      if (__any_sync(0xffffffffu, contrib)) {
-        const float s = warp_sum16(v, lane);
-        const int k = lane >> 1;
-        if ((lane & 1) == 0 && k < GSB_GRAD2D_FLOATS && s != 0.0f)
-          atomicAdd(g2 + size_t(s_rank[j]) * GSB_GRAD2D_FLOATS + k, s);
+      const uint32_t cm = __ballot_sync(kFull, contrib);
+      if (cm == 0u) continue;
+      float* dst = g2 + size_t(s_rank[warp][j]) * GSB_GRAD2D_FLOATS;
+      if (__popc(cm) <= kSparseContributors) {
+        if (contrib) {
+#pragma unroll
+          for (int k = 0; k < GSB_GRAD2D_FLOATS; ++k)
+            if (v[k] != 0.0f) atomicAdd(dst + k, v[k]);
+        }
+      } else {
+        int k;
+        const float s = warp_sum10(v, lane, &k);
+        if ((lane & 1) == 0 && k < GSB_GRAD2D_FLOATS && s != 0.0f) atomicAdd(dst + k, s);
       }
     }
+    __syncwarp();  // slots are rewritten by the next chunk
   }
 }
 
