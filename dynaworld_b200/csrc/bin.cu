@@ -30,15 +30,17 @@ __global__ void __launch_bounds__(256) emit_keys_kernel(int32_t n_views, int32_t
     if (!rc.compat && rc.ellipse) {
       const float4 r0 = reinterpret_cast<const float4*>(records)[i * 3 + 0];
       const float4 r1 = reinterpret_cast<const float4*>(records)[i * 3 + 1];
-      TileRect rect;
       ExactShape es;
-      exact_rect(r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, rc.alpha_cutoff, H, W, rc.pixel_center, rc.tile, &rect, &es);
-      for (int ty = rc4.y; ty <= rc4.w; ++ty)
-        for (int tx = rc4.x; tx <= rc4.z; ++tx) {
-          if (!exact_tile_hit(es, tx, ty, rc.tile, H, W, rc.pixel_center)) continue;
-          if (k < end && k < n_pairs) keys[k] = ((view_base + uint64_t(ty) * rc.tiles_x + tx) << 32) | r;
-          ++k;
+      if (exact_shape(r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, rc.alpha_cutoff, H, W, rc.pixel_center, &es)) {
+        for (int ty = rc4.y; ty <= rc4.w; ++ty) {
+          int tx0, tx1;
+          if (!exact_row(es, ty, rc.tile, rc.pixel_center, &tx0, &tx1)) continue;
+          for (int tx = tx0; tx <= tx1; ++tx) {
+            if (k < end && k < n_pairs) keys[k] = ((view_base + uint64_t(ty) * rc.tiles_x + tx) << 32) | r;
+            ++k;
+          }
         }
+      }
     } else {
       for (int ty = rc4.y; ty <= rc4.w; ++ty)
         for (int tx = rc4.x; tx <= rc4.z; ++tx) {

@@ -301,16 +301,19 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(gsb_scene sc, gsb_v
       tau_f = __int_as_float(0x7f800000);  // +inf: every listed pair is blended
     } else {
       ExactShape es;
-      if (exact_rect(P.mx, P.my, P.A, P.B, P.C, P.o_eff, rc.alpha_cutoff, vw.height, vw.width, rc.pixel_center,
-                     rc.tile, &rect, &es)) {
+      rect = TileRect{1, 1, 0, 0};
+      if (exact_shape(P.mx, P.my, P.A, P.B, P.C, P.o_eff, rc.alpha_cutoff, vw.height, vw.width, rc.pixel_center,
+                      &es)) {
+        rect = exact_rect_of(es, rc.tile);
         if (rc.ellipse) {
-          for (int ty = rect.ty0; ty <= rect.ty1; ++ty)
-            for (int tx = rect.tx0; tx <= rect.tx1; ++tx)
-              count += exact_tile_hit(es, tx, ty, rc.tile, vw.height, vw.width, rc.pixel_center) ? 1u : 0u;
+          for (int ty = rect.ty0; ty <= rect.ty1; ++ty) {
+            int tx0, tx1;
+            if (exact_row(es, ty, rc.tile, rc.pixel_center, &tx0, &tx1)) count += uint32_t(tx1 - tx0 + 1);
+          }
         } else {
           count = rect.count();
         }
-        tau_f = __double2float_ru(es.thresh);
+        tau_f = __double2float_ru(es.L);
       } else {
         tau_f = -1.0f;  // never blended
       }

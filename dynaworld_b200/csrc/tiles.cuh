@@ -1,11 +1,12 @@
 // Tile bounds of one projected Gaussian.  Used by both the pair count (preprocess) and the pair
 // emission (bin), so the two always agree on the tile set.
 //
-// exact mode: every tile whose pixel-centre rectangle contains a point with
-//   opacity * exp(-q/2) >= alpha_cutoff,   q = A dx^2 + B dx dy + C dy^2,
-// i.e. min over the rectangle of q <= tau = 2 ln(opacity / alpha_cutoff), with a small relative
-// and absolute slack.  Double precision, each operation rounded separately (explicit __d*_rn), so
-// the float64 numpy restatement reproduces the lists bit for bit.
+// exact mode: the tiles holding a pixel centre with q = A dx^2 + B dx dy + C dy^2 <= L, where
+// L = tau (1 + rel) + abs and tau = 2 ln(opacity / alpha_cutoff) (alpha >= cutoff <=> q <= tau).
+// Per tile row, the ellipse restricted to the row's band of pixel-centre rows projects onto an
+// x-interval [xl, xr] (a convex set's projection); the row's tiles are those holding a pixel
+// column centre inside it.  O(rows) per Gaussian.  Double precision, every operation rounded
+// separately (explicit __d*_rn), so the float64 numpy restatement gives the same lists bit for bit.
 //
 // tiled_compat mode: compute_gaussian_bounds + build_tile_assignments of the reference
 // (src/train/renderers/tiled.py:7-45), float32 with torch's operation order.
@@ -25,8 +26,10 @@ struct TileRect {
 
 struct ExactShape {
   double mx, my, a, b, c;  // record values widened to double
-  double tau;              // 2 ln(o / cutoff)
-  double thresh;           // tau * (1 + rel) + abs
+  double det;              // a c - b^2 / 4
+  double L;                // ellipse level: tau (1 + rel) + abs
+  double ex, ey;           // half extents sqrt(L c / det), sqrt(L a / det)
+  int px0, px1, py0, py1;  // pixel rectangle (inclusive), clipped to the image
 };
 
 __device__ inline double dmul(double x, double y) { return __dmul_rn(x, y); }
@@ -34,69 +37,62 @@ __device__ inline double dadd(double x, double y) { return __dadd_rn(x, y); }
 __device__ inline double dsub(double x, double y) { return __dsub_rn(x, y); }
 __device__ inline double ddiv(double x, double y) { return __ddiv_rn(x, y); }
 
-// Returns false when the Gaussian touches no pixel.
-__device__ inline bool exact_rect(float mxf, float myf, float af, float bf, float cf, float of, float cutoff, int H,
-                                  int W, float pc, int tile, TileRect* rect, ExactShape* sh) {
-  rect->tx0 = 1;
-  rect->tx1 = 0;
-  rect->ty0 = 1;
-  rect->ty1 = 0;
+// Returns false when the Gaussian reaches no pixel centre.
+__device__ inline bool exact_shape(float mxf, float myf, float af, float bf, float cf, float of, float cutoff, int H,
+                                   int W, float pc, ExactShape* s) {
   const double o = of, cut = cutoff;
   if (!(o > cut)) return false;
   const double a = af, b = bf, c = cf, mx = mxf, my = myf;
   const double tau = dmul(2.0, log(ddiv(o, cut)));
   const double det = dsub(dmul(a, c), dmul(dmul(0.25, b), b));
   if (!(det > 0.0) || !(a > 0.0) || !(c > 0.0)) return false;
-  const double ex = dadd(dmul(__dsqrt_rn(dmul(tau, ddiv(c, det))), 1.0 + kExactRelMargin), kExactAbsMargin);
-  const double ey = dadd(dmul(__dsqrt_rn(dmul(tau, ddiv(a, det))), 1.0 + kExactRelMargin), kExactAbsMargin);
+  const double L = dadd(dmul(tau, 1.0 + kExactRelMargin), kExactAbsMargin);
+  const double ex = __dsqrt_rn(dmul(L, ddiv(c, det)));
+  const double ey = __dsqrt_rn(dmul(L, ddiv(a, det)));
   const double dpc = pc;
   const double px0 = fmax(ceil(dsub(dsub(mx, ex), dpc)), 0.0);
   const double px1 = fmin(floor(dsub(dadd(mx, ex), dpc)), double(W - 1));
   const double py0 = fmax(ceil(dsub(dsub(my, ey), dpc)), 0.0);
   const double py1 = fmin(floor(dsub(dadd(my, ey), dpc)), double(H - 1));
   if (!(px0 <= px1) || !(py0 <= py1) || !isfinite(mx) || !isfinite(my)) return false;
-  rect->tx0 = int(px0) / tile;
-  rect->tx1 = int(px1) / tile;
-  rect->ty0 = int(py0) / tile;
-  rect->ty1 = int(py1) / tile;
-  sh->mx = mx;
-  sh->my = my;
-  sh->a = a;
-  sh->b = b;
-  sh->c = c;
-  sh->tau = tau;
-  sh->thresh = dadd(dmul(tau, 1.0 + kExactRelMargin), kExactAbsMargin);
+  s->mx = mx, s->my = my, s->a = a, s->b = b, s->c = c, s->det = det, s->L = L, s->ex = ex, s->ey = ey;
+  s->px0 = int(px0), s->px1 = int(px1), s->py0 = int(py0), s->py1 = int(py1);
   return true;
 }
 
-__device__ inline double quad_at(const ExactShape& s, double dx, double dy) {
-  return dadd(dmul(dmul(s.a, dx), dx), dadd(dmul(dmul(s.b, dx), dy), dmul(dmul(s.c, dy), dy)));
+// x offset of the ellipse boundary at row offset u: (-(b u) -/+ sqrt(4 a L - 4 det u^2)) / (2 a).
+__device__ inline double ellipse_x(const ExactShape& s, double u, bool right) {
+  const double disc = fmax(dsub(dmul(dmul(4.0, s.a), s.L), dmul(dmul(4.0, s.det), dmul(u, u))), 0.0);
+  const double r = __dsqrt_rn(disc);
+  const double nb = -dmul(s.b, u);
+  return ddiv(right ? dadd(nb, r) : dsub(nb, r), dmul(2.0, s.a));
 }
 
-// Minimum of q over the pixel-centre box [X0,X1] x [Y0,Y1] compared with the threshold.
-__device__ inline bool exact_tile_hit(const ExactShape& s, int tx, int ty, int tile, int H, int W, float pc) {
+// Tile-column range [tx0, tx1] of tile row ty (false if the row has no tile).
+__device__ inline bool exact_row(const ExactShape& s, int ty, int tile, float pc, int* tx0, int* tx1) {
   const double dpc = pc;
-  const double X0 = dadd(double(max(tx * tile, 0)), dpc);
-  const double X1 = dadd(double(min(tx * tile + tile - 1, W - 1)), dpc);
-  const double Y0 = dadd(double(max(ty * tile, 0)), dpc);
-  const double Y1 = dadd(double(min(ty * tile + tile - 1, H - 1)), dpc);
-  if (X0 <= s.mx && s.mx <= X1 && Y0 <= s.my && s.my <= Y1) return true;  // min is 0
-  double q = 1.0 / 0.0;
-  // edges x = X0, X1: minimise over dy
-  for (int e = 0; e < 2; ++e) {
-    const double dx = dsub(e ? X1 : X0, s.mx);
-    const double t = ddiv(-dmul(s.b, dx), dmul(2.0, s.c));
-    const double dy = fmin(fmax(t, dsub(Y0, s.my)), dsub(Y1, s.my));
-    q = fmin(q, quad_at(s, dx, dy));
-  }
-  // edges y = Y0, Y1: minimise over dx
-  for (int e = 0; e < 2; ++e) {
-    const double dy = dsub(e ? Y1 : Y0, s.my);
-    const double t = ddiv(-dmul(s.b, dy), dmul(2.0, s.a));
-    const double dx = fmin(fmax(t, dsub(X0, s.mx)), dsub(X1, s.mx));
-    q = fmin(q, quad_at(s, dx, dy));
-  }
-  return q <= s.thresh;
+  const double Y0 = dadd(double(max(ty * tile, s.py0)), dpc);
+  const double Y1 = dadd(double(min(ty * tile + tile - 1, s.py1)), dpc);
+  const double u0 = fmax(dsub(Y0, s.my), -s.ey);
+  const double u1 = fmin(dsub(Y1, s.my), s.ey);
+  if (!(u0 <= u1)) return false;
+  // leftmost point of the ellipse at u = b ex / (2c), rightmost at -b ex / (2c)
+  const double ul = ddiv(dmul(s.b, s.ex), dmul(2.0, s.c));
+  const double ur = -ul;
+  const double xl = (u0 <= ul && ul <= u1) ? -s.ex : fmin(ellipse_x(s, u0, false), ellipse_x(s, u1, false));
+  const double xr = (u0 <= ur && ur <= u1) ? s.ex : fmax(ellipse_x(s, u0, true), ellipse_x(s, u1, true));
+  const double qx0 = fmax(ceil(dsub(dadd(s.mx, xl), dpc)), double(s.px0));
+  const double qx1 = fmin(floor(dsub(dadd(s.mx, xr), dpc)), double(s.px1));
+  if (!(qx0 <= qx1)) return false;
+  *tx0 = int(qx0) / tile;
+  *tx1 = int(qx1) / tile;
+  return true;
+}
+
+__device__ inline TileRect exact_rect_of(const ExactShape& s, int tile) {
+  TileRect r;
+  r.tx0 = s.px0 / tile, r.tx1 = s.px1 / tile, r.ty0 = s.py0 / tile, r.ty1 = s.py1 / tile;
+  return r;
 }
 
 // tiled.py:7-28 then :31-41, float32.  logf is formed in double and rounded once.

@@ -11,11 +11,11 @@ Two bound rules:
   ordered by (tile, depth rank) -- the stable argsort of tiled.py:59 applied
   to Gaussians already in depth order (common.py:191).
 * ``exact`` is this library's rule for dense-equivalent rendering: every
-  tile whose pixel-centre rectangle holds a point with
-  opacity * exp(-q/2) >= alpha_cutoff, i.e. min over the rectangle of
-  q = d^T inv_cov d <= tau = 2 ln(opacity / alpha_cutoff).  Computed in
-  float64 with the operation order of the CUDA preprocess so that both give
-  the same lists bit for bit.
+  tile holding a pixel centre with opacity * exp(-q/2) >= alpha_cutoff, i.e.
+  q = d^T inv_cov d <= tau = 2 ln(opacity / alpha_cutoff) (plus slack),
+  found row by row from the ellipse's x-interval over each tile row.
+  Computed in float64 with the operation order of the CUDA preprocess so
+  that both give the same lists bit for bit.
 
 Keys: one 64-bit key per (view, tile, Gaussian) pair,
 ``(view * n_tiles + tile) << 32 | depth_rank``; the sorted order is the key
@@ -77,70 +77,70 @@ def tile_rects_from_pixel_bounds(min_x, max_x, min_y, max_y, valid, tile_size):
     return tx0, tx1, ty0, ty1, count
 
 
-def _exact_min_q(a, b, c, mx, my, X0, X1, Y0, Y1):
-    """Minimum of q = a dx^2 + b dx dy + c dy^2 over the box [X0,X1] x [Y0,Y1] (float64).
-
-    dx = x - mx, dy = y - my.  Zero if the mean lies in the box, else the
-    least of the four edge minima (1-D quadratic minimiser clamped to the
-    edge).  Same operation order as the CUDA kernel.
-    """
-    inside = (X0 <= mx) & (mx <= X1) & (Y0 <= my) & (my <= Y1)
-
-    def edge_x(xe, lo, hi):  # x fixed, minimise over dy in [lo-my, hi-my]
-        dx = xe - mx
-        t = -(b * dx) / (2.0 * c)
-        dy = np.minimum(np.maximum(t, lo - my), hi - my)
-        return (a * dx) * dx + ((b * dx) * dy + (c * dy) * dy)
-
-    def edge_y(ye, lo, hi):  # y fixed, minimise over dx
-        dy = ye - my
-        t = -(b * dy) / (2.0 * a)
-        dx = np.minimum(np.maximum(t, lo - mx), hi - mx)
-        return (a * dx) * dx + ((b * dx) * dy + (c * dy) * dy)
-
-    q = np.minimum(
-        np.minimum(edge_x(X0, Y0, Y1), edge_x(X1, Y0, Y1)),
-        np.minimum(edge_y(Y0, X0, X1), edge_y(Y1, X0, X1)),
-    )
-    return np.where(inside, 0.0, q)
+def _ellipse_x(a, b, det, L, u, right):
+    """x offset of the ellipse boundary at row offset u: (-(b u) -/+ sqrt(4 a L - 4 det u^2)) / (2 a)."""
+    disc = max((4.0 * a) * L - (4.0 * det) * (u * u), 0.0)
+    r = math.sqrt(disc)
+    nb = -(b * u)
+    return ((nb + r) if right else (nb - r)) / (2.0 * a)
 
 
 def exact_pairs_one_view(mx, my, a, b, c, o, H, W, tile_size, alpha_cutoff, pixel_center=0.0, ellipse_test=True):
     """Exact-mode tile lists for one view; inputs are float32 per-Gaussian records in rank order.
 
-    a = inv_cov00, b = inv_cov01 + inv_cov10, c = inv_cov11.
+    a = inv_cov00, b = inv_cov01 + inv_cov10, c = inv_cov11.  A tile is listed when it holds a
+    pixel centre with q <= L, L = tau (1 + rel) + abs, tau = 2 ln(o / cutoff): per tile row, the
+    ellipse restricted to the row band projects onto an x-interval; the row's tiles are those
+    holding a pixel-column centre in it (``ellipse_test=False`` keeps the whole bounding box).
+    Float64, one rounding per operation, in the order of the CUDA preprocess (tiles.cuh).
     Returns (tile_ids, ranks) of every pair, ordered by (rank, tile).
     """
-    mx, my, a, b, c, o = (np.asarray(v, dtype=np.float32).astype(np.float64) for v in (mx, my, a, b, c, o))
-    G = mx.shape[0]
+    f64 = lambda v: np.asarray(v, dtype=np.float32).astype(np.float64)  # noqa: E731
+    mx, my, a, b, c, o = (f64(v) for v in (mx, my, a, b, c, o))
+    cut = float(np.float32(alpha_cutoff))
     tiles_x = (W + tile_size - 1) // tile_size
-    with np.errstate(divide="ignore", invalid="ignore"):
-        vis = o > alpha_cutoff
-        tau = np.where(vis, 2.0 * np.log(np.where(vis, o, 1.0) / alpha_cutoff), 0.0)
-        det = a * c - (0.25 * b) * b
-        ok = vis & (det > 0) & (a > 0) & (c > 0)
-        # extents of {d : q(d) <= tau}: sqrt(tau * (A^-1)_ii), (A^-1)_00 = c/det.
-        ex = np.sqrt(np.where(ok, tau * (c / det), 0.0)) * (1.0 + EXACT_REL_MARGIN) + EXACT_ABS_MARGIN
-        ey = np.sqrt(np.where(ok, tau * (a / det), 0.0)) * (1.0 + EXACT_REL_MARGIN) + EXACT_ABS_MARGIN
-    px0 = np.maximum(np.ceil(mx - ex - pixel_center), 0.0)
-    px1 = np.minimum(np.floor(mx + ex - pixel_center), W - 1.0)
-    py0 = np.maximum(np.ceil(my - ey - pixel_center), 0.0)
-    py1 = np.minimum(np.floor(my + ey - pixel_center), H - 1.0)
-    ok = ok & (px0 <= px1) & (py0 <= py1) & np.isfinite(mx) & np.isfinite(my)
+    pc = float(pixel_center)
     tiles, ranks = [], []
-    for g in np.nonzero(ok)[0]:
-        tx0, tx1 = int(px0[g]) // tile_size, int(px1[g]) // tile_size
-        ty0, ty1 = int(py0[g]) // tile_size, int(py1[g]) // tile_size
-        for ty in range(ty0, ty1 + 1):
+    for g in range(mx.shape[0]):
+        if not (o[g] > cut):
+            continue
+        A, Bq, Cq, MX, MY = float(a[g]), float(b[g]), float(c[g]), float(mx[g]), float(my[g])
+        tau = 2.0 * math.log(float(o[g]) / cut)
+        det = A * Cq - (0.25 * Bq) * Bq
+        if not (det > 0.0 and A > 0.0 and Cq > 0.0):
+            continue
+        L = tau * (1.0 + EXACT_REL_MARGIN) + EXACT_ABS_MARGIN
+        ex = math.sqrt(L * (Cq / det))
+        ey = math.sqrt(L * (A / det))
+        px0 = max(math.ceil((MX - ex) - pc), 0.0)
+        px1 = min(math.floor((MX + ex) - pc), W - 1.0)
+        py0 = max(math.ceil((MY - ey) - pc), 0.0)
+        py1 = min(math.floor((MY + ey) - pc), H - 1.0)
+        if not (px0 <= px1 and py0 <= py1 and math.isfinite(MX) and math.isfinite(MY)):
+            continue
+        px0, px1, py0, py1 = int(px0), int(px1), int(py0), int(py1)
+        for ty in range(py0 // tile_size, py1 // tile_size + 1):
+            if ellipse_test:
+                Y0 = float(max(ty * tile_size, py0)) + pc
+                Y1 = float(min(ty * tile_size + tile_size - 1, py1)) + pc
+                u0 = max(Y0 - MY, -ey)
+                u1 = min(Y1 - MY, ey)
+                if not (u0 <= u1):
+                    continue
+                ul = (Bq * ex) / (2.0 * Cq)
+                ur = -ul
+                xl = -ex if (u0 <= ul <= u1) else min(_ellipse_x(A, Bq, det, L, u0, False),
+                                                      _ellipse_x(A, Bq, det, L, u1, False))
+                xr = ex if (u0 <= ur <= u1) else max(_ellipse_x(A, Bq, det, L, u0, True),
+                                                     _ellipse_x(A, Bq, det, L, u1, True))
+                qx0 = max(math.ceil((MX + xl) - pc), float(px0))
+                qx1 = min(math.floor((MX + xr) - pc), float(px1))
+                if not (qx0 <= qx1):
+                    continue
+                tx0, tx1 = int(qx0) // tile_size, int(qx1) // tile_size
+            else:
+                tx0, tx1 = px0 // tile_size, px1 // tile_size
             for tx in range(tx0, tx1 + 1):
-                if ellipse_test:
-                    X0 = max(tx * tile_size, 0) + pixel_center
-                    X1 = min(tx * tile_size + tile_size - 1, W - 1) + pixel_center
-                    Y0 = max(ty * tile_size, 0) + pixel_center
-                    Y1 = min(ty * tile_size + tile_size - 1, H - 1) + pixel_center
-                    q = _exact_min_q(a[g], b[g], c[g], mx[g], my[g], X0, X1, Y0, Y1)
-                    if not (q <= tau[g] * (1.0 + EXACT_REL_MARGIN) + EXACT_ABS_MARGIN):
-                        continue
                 tiles.append(ty * tiles_x + tx)
                 ranks.append(g)
     return np.asarray(tiles, dtype=np.int64), np.asarray(ranks, dtype=np.int64)
