@@ -56,6 +56,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--stages", action="store_true", help="print per-stage times to stderr")
+    ap.add_argument("--tile", type=int, default=None, help="tile size (8 or 16; default: the renderer's)")
     return ap.parse_args()
 
 
@@ -100,13 +101,13 @@ def workload_config(name, wl, world, scaling):
 class Step:
     """One render + loss forward/backward of a workload resident on the device."""
 
-    def __init__(self, wl, device, world):
+    def __init__(self, wl, device, world, tile=None):
         from dynaworld_b200.config import B200RendererConfig
 
         self.wl = wl
         self.dev = device
         self.world = world
-        self.cfg = B200RendererConfig()
+        self.cfg = B200RendererConfig() if tile is None else B200RendererConfig(tile_size=tile)
         self.params = {k: getattr(wl, k).to(device).contiguous().requires_grad_(True)
                        for k in ("means", "log_scales", "quats", "opacity_logits", "sh")}
         if wl.velocity is not None:
@@ -309,7 +310,7 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     L = _lib.load()
     wl, scaling = make_workload(args.workload, rank, world, args.scale, args.image_scale)
-    step = Step(wl, dev, world)
+    step = Step(wl, dev, world, args.tile)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
 
     def barrier():
