@@ -78,15 +78,16 @@ SIGNATURES = {
     "gsb_preprocess_workspace": (C.c_size_t, [P(Views), C.c_int32]),
     "gsb_preprocess_fwd": (C.c_int, [P(Scene), P(Views), P(Options), vp, vp, vp, vp, vp, vp, C.c_size_t, vp]),
     "gsb_bin_workspace": (C.c_size_t, [P(Views), P(Options), C.c_int32, C.c_uint32]),
-    "gsb_bin": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, C.c_uint32, vp, vp, vp, C.c_size_t, vp]),
-    "gsb_raster_fwd": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "gsb_bin": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, C.c_uint32, vp, vp, vp, vp, C.c_size_t,
+                          vp]),
+    "gsb_raster_fwd": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "gsb_loss_workspace": (C.c_size_t, [C.c_int32]),
     "gsb_loss_fwd_bwd": (C.c_int, [P(LossOptions), C.c_int32, C.c_int32, C.c_int32, C.c_int32, vp, vp, vp, vp, vp,
                                    C.c_size_t, vp]),
     "gsb_loss_fwd_bwd_noalloc": (C.c_int, [P(LossOptions), C.c_int32, C.c_int32, C.c_int32, C.c_int32, vp, vp, vp,
                                            vp, vp]),
     "gsb_scale_planes": (C.c_int, [vp, vp, vp, C.c_int32, C.c_int64, vp]),
-    "gsb_raster_bwd": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "gsb_raster_bwd": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "gsb_preprocess_bwd": (C.c_int, [P(Scene), P(Views), P(Options), vp, vp, P(SceneGrads), vp]),
     "gsb_radix_sort_workspace": (C.c_size_t, [C.c_uint32, C.c_int, C.c_int]),
     "gsb_radix_sort": (C.c_int, [vp, vp, vp, vp, C.c_uint32, C.c_int, C.c_int, C.c_int, vp, C.c_size_t, vp]),

@@ -44,8 +44,6 @@ RenderConsts make_consts(const gsb_views& v, const gsb_options& o) {
 
 static cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
-static gsb_status launch_status() { return cudaGetLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA; }
-
 static gsb_status check_views(const gsb_views* v) {
   if (!v || !v->intrinsics || !v->camera_to_world) return GSB_ERR_ARG;
   if (v->n_views <= 0 || v->height <= 0 || v->width <= 0 || v->views_per_set <= 0) return GSB_ERR_SHAPE;
@@ -202,26 +200,36 @@ GSB_API gsb_status gsb_preprocess_fwd(const gsb_scene* scene, const gsb_views* v
 
 // ---- stage 3 ---------------------------------------------------------------------------------
 
-static size_t bin_ws(uint32_t n_pairs) {
+static size_t bin_ws(uint32_t n_pairs, size_t n_tiles_total) {
+  const uint32_t nt = uint32_t(n_tiles_total);
   Carver c(nullptr, 0);
   c.take<WorkspaceHeader>(1);
   c.take<uint64_t>(n_pairs);
   c.take<char>(radix_sort_workspace(n_pairs, 8, 0));
+  c.take<uint32_t>(nt);  // order keys
+  c.take<uint32_t>(nt);  // order values
+  c.take<uint32_t>(nt);  // sorted order keys
+  c.take<char>(radix_sort_workspace(nt, 4, 1));
   return c.used;
+}
+
+static size_t n_tiles_total(const gsb_views* views, const gsb_options* opts) {
+  if (!views || !opts || opts->tile_size <= 0) return 0;
+  const size_t tx = (size_t(views->width) + opts->tile_size - 1) / opts->tile_size;
+  const size_t ty = (size_t(views->height) + opts->tile_size - 1) / opts->tile_size;
+  return size_t(views->n_views) * tx * ty;
 }
 
 GSB_API size_t gsb_bin_workspace(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians,
                                  uint32_t n_pairs) {
-  (void)views;
-  (void)opts;
   (void)n_gaussians;
-  return bin_ws(n_pairs);
+  return bin_ws(n_pairs, n_tiles_total(views, opts));
 }
 
 GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians, const float* records,
                            const int32_t* tile_rects, const uint32_t* pair_offsets, uint32_t n_pairs,
-                           uint64_t* sorted_keys, uint32_t* tile_ranges, void* workspace, size_t workspace_bytes,
-                           void* stream) {
+                           uint64_t* sorted_keys, uint32_t* tile_ranges, uint32_t* tile_order, void* workspace,
+                           size_t workspace_bytes, void* stream) {
   gsb_status s;
   if ((s = check_views(views)) != GSB_OK) return s;
   if ((s = check_opts(opts)) != GSB_OK) return s;
@@ -229,7 +237,9 @@ GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int3
   if (!records || !tile_rects || !pair_offsets || !tile_ranges || !workspace) return GSB_ERR_ARG;
   if (n_pairs > 0 && !sorted_keys) return GSB_ERR_ARG;
   if (n_pairs >= (1u << 30)) return GSB_ERR_KEY_OVERFLOW;
-  if (workspace_bytes < bin_ws(n_pairs)) return GSB_ERR_WORKSPACE;
+  const size_t NT = n_tiles_total(views, opts);
+  if (NT >= (size_t(1) << 30)) return GSB_ERR_SHAPE;
+  if (workspace_bytes < bin_ws(n_pairs, NT)) return GSB_ERR_WORKSPACE;
   cudaStream_t st = as_stream(stream);
   const RenderConsts rc = make_consts(*views, *opts);
   const int32_t B = views->n_views;
@@ -238,6 +248,11 @@ GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int3
   uint64_t* keys = c.take<uint64_t>(n_pairs);
   const size_t sws = radix_sort_workspace(n_pairs, 8, 0);
   void* sort_ws = c.take<char>(sws);
+  uint32_t* okeys = c.take<uint32_t>(NT);
+  uint32_t* ovals = c.take<uint32_t>(NT);
+  uint32_t* okeys_sorted = c.take<uint32_t>(NT);
+  const size_t ows = radix_sort_workspace(uint32_t(NT), 4, 1);
+  void* order_ws = c.take<char>(ows);
   int32_t* status = begin_status(workspace, st);
   if (n_pairs > 0) {
     if ((s = launch_emit(B, n_gaussians, rc, views->height, views->width, records,
@@ -248,15 +263,19 @@ GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int3
         GSB_OK)
       return s;
   }
-  return launch_tile_ranges(sorted_keys, n_pairs, tile_ranges, size_t(B) * rc.n_tiles, st);
+  if ((s = launch_tile_ranges(sorted_keys, n_pairs, tile_ranges, size_t(B) * rc.n_tiles, st)) != GSB_OK) return s;
+  if (!tile_order) return GSB_OK;
+  // launch order: tiles by descending list length (16-bit key: length / 16, saturated)
+  if ((s = launch_tile_order_keys(tile_ranges, uint32_t(NT), okeys, ovals, st)) != GSB_OK) return s;
+  return radix_sort(okeys, okeys_sorted, ovals, tile_order, uint32_t(NT), 4, 0, 16, order_ws, ows, st, status);
 }
 
 // ---- stages 4 and 6 --------------------------------------------------------------------------
 
 GSB_API gsb_status gsb_raster_fwd(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians,
                                   const float* records, const uint64_t* sorted_keys, const uint32_t* tile_ranges,
-                                  float* image, float* alpha, float* depth, float* pixel_t, uint32_t* pixel_state,
-                                  void* stream) {
+                                  const uint32_t* tile_order, float* image, float* alpha, float* depth,
+                                  float* pixel_t, uint32_t* pixel_state, void* stream) {
   gsb_status s;
   if ((s = check_views(views)) != GSB_OK) return s;
   if ((s = check_opts(opts)) != GSB_OK) return s;
@@ -265,7 +284,7 @@ GSB_API gsb_status gsb_raster_fwd(const gsb_views* views, const gsb_options* opt
   RasterArgs a{};
   a.B = views->n_views, a.G = n_gaussians, a.H = views->height, a.W = views->width;
   a.rc = make_consts(*views, *opts);
-  a.records = records, a.keys = sorted_keys, a.ranges = tile_ranges;
+  a.records = records, a.keys = sorted_keys, a.ranges = tile_ranges, a.order = tile_order;
   a.image = image, a.alpha = alpha, a.depth = (opts->flags & GSB_RENDER_DEPTH) ? depth : nullptr;
   a.pixel_t = pixel_t, a.pixel_state = pixel_state;
   if (views->n_views > 65535) return GSB_ERR_SHAPE;
@@ -274,7 +293,8 @@ GSB_API gsb_status gsb_raster_fwd(const gsb_views* views, const gsb_options* opt
 
 GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians,
                                   const float* records, const uint64_t* sorted_keys, const uint32_t* tile_ranges,
-                                  const float* pixel_t, const uint32_t* pixel_state, const float* d_image,
+                                  const uint32_t* tile_order, const float* pixel_t, const uint32_t* pixel_state,
+                                  const float* d_image,
                                   const float* d_alpha, const float* d_depth, const float* view_scale, float* grad2d,
                                   void* stream) {
   gsb_status s;
@@ -285,7 +305,7 @@ GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opt
   RasterArgs a{};
   a.B = views->n_views, a.G = n_gaussians, a.H = views->height, a.W = views->width;
   a.rc = make_consts(*views, *opts);
-  a.records = records, a.keys = sorted_keys, a.ranges = tile_ranges;
+  a.records = records, a.keys = sorted_keys, a.ranges = tile_ranges, a.order = tile_order;
   a.pixel_t = const_cast<float*>(pixel_t), a.pixel_state = const_cast<uint32_t*>(pixel_state);
   a.d_image = d_image, a.d_alpha = d_alpha, a.d_depth = d_depth, a.view_scale = view_scale, a.grad2d = grad2d;
   if (views->n_views > 65535) return GSB_ERR_SHAPE;

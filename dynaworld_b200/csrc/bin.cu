@@ -62,6 +62,25 @@ __global__ void tile_ranges_kernel(const uint64_t* __restrict__ keys, uint32_t n
   }
 }
 
+// Sort key of a tile's launch slot: longer lists first (length / 16, saturated to 16 bits).
+__global__ void tile_order_keys_kernel(const uint32_t* __restrict__ ranges, uint32_t n, uint32_t* __restrict__ keys,
+                                       uint32_t* __restrict__ vals) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const uint32_t len = ranges[size_t(i) * 2 + 1] - ranges[size_t(i) * 2];
+    keys[i] = 0xFFFFu - min(len >> 4, 0xFFFFu);
+    vals[i] = i;
+  }
+}
+
+gsb_status launch_tile_order_keys(const uint32_t* ranges, uint32_t n, uint32_t* keys, uint32_t* vals,
+                                  cudaStream_t st) {
+  if (n == 0) return GSB_OK;
+  const int grid = int(std::min<uint32_t>((n + 255) / 256, 148u * 16u));
+  note_launch();
+  tile_order_keys_kernel<<<grid, 256, 0, st>>>(ranges, n, keys, vals);
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
 gsb_status launch_emit(int32_t B, int32_t G, const RenderConsts& rc, int H, int W, const float* records,
                        const int4* rects, const uint32_t* offsets, uint32_t n_pairs, uint64_t* keys, int32_t* status,
                        cudaStream_t st) {

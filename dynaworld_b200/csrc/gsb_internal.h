@@ -48,6 +48,7 @@ struct RasterArgs {
   const float* records;
   const uint64_t* keys;
   const uint32_t* ranges;
+  const uint32_t* order;  // launch order of view*n_tiles + tile, or NULL
   float* image;
   float* alpha;
   float* depth;
@@ -79,6 +80,8 @@ gsb_status launch_emit(int32_t B, int32_t G, const RenderConsts& rc, int H, int 
                        const int4* rects, const uint32_t* offsets, uint32_t n_pairs, uint64_t* keys, int32_t* status,
                        cudaStream_t st);
 gsb_status launch_tile_ranges(const uint64_t* keys, uint32_t n, uint32_t* ranges, size_t n_ranges, cudaStream_t st);
+gsb_status launch_tile_order_keys(const uint32_t* ranges, uint32_t n_tiles_total, uint32_t* keys, uint32_t* vals,
+                                  cudaStream_t st);
 
 // Loss (loss.cu).
 size_t loss_workspace(int32_t n_images);

@@ -77,7 +77,9 @@ __global__ void __launch_bounds__(TILE* TILE) raster_fwd_kernel(RasterArgs a) {
   constexpr int NW = TILE * TILE / 32;
   __shared__ float4 s_geo[NW][32], s_cot[NW][32], s_col[NW][32];
   const RenderConsts& rc = a.rc;
-  const int tile = blockIdx.x, view = blockIdx.y;
+  const uint32_t slot = blockIdx.y * uint32_t(rc.n_tiles) + blockIdx.x;
+  const uint32_t vt = a.order ? a.order[slot] : slot;  // heaviest tiles first
+  const int view = int(vt / uint32_t(rc.n_tiles)), tile = int(vt % uint32_t(rc.n_tiles));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int bx, by;
   block_of<TILE>(warp, bx, by);
@@ -189,13 +191,15 @@ __device__ __forceinline__ float warp_sum10(float v[12], int lane, int* index) {
 // it the warp reduces first.
 constexpr int kSparseContributors = 4;
 
-template <int TILE>
+template <int TILE, bool DEPTH>  // DEPTH: a depth gradient is given
 __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
   constexpr int NW = TILE * TILE / 32;
   __shared__ float4 s_geo[NW][32], s_cot[NW][32], s_col[NW][32];
   __shared__ uint32_t s_rank[NW][32];
   const RenderConsts& rc = a.rc;
-  const int tile = blockIdx.x, view = blockIdx.y;
+  const uint32_t slot = blockIdx.y * uint32_t(rc.n_tiles) + blockIdx.x;
+  const uint32_t vt = a.order ? a.order[slot] : slot;  // heaviest tiles first
+  const int view = int(vt / uint32_t(rc.n_tiles)), tile = int(vt % uint32_t(rc.n_tiles));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int bx, by;
   block_of<TILE>(warp, bx, by);
@@ -205,10 +209,9 @@ __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
   const bool inside = px < a.W && py < a.H;
   const float fx = float(px) + rc.pixel_center, fy = float(py) + rc.pixel_center;
   const size_t rb = (size_t(view) * rc.n_tiles + tile) * 2;
-  const uint32_t start = a.ranges[rb], end = a.ranges[rb + 1];
+  const uint32_t start = a.ranges[rb];
   const float* recs = a.records + size_t(view) * a.G * GSB_RECORD_FLOATS;
   float* g2 = a.grad2d + size_t(view) * a.G * GSB_GRAD2D_FLOATS;
-  const float inv_f0 = 1.0f / rc.f0;
   const WarpSlots ws{s_geo[warp], s_cot[warp], s_col[warp], s_rank[warp]};
 
   const size_t HW = size_t(a.H) * a.W;
@@ -256,17 +259,23 @@ __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
           const float alpha = fminf(fmaxf(araw, 0.0f), rc.alpha_clamp);
           if (alpha >= rc.alpha_cutoff) {
             const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
-            S = __fdividef(S, f * inv_f0);  // S before this entry
+            const float rf = __fdividef(1.0f, f);
+            S = S * (rc.f0 * rf);  // S before this entry: S_after / (f / F0)
             const float T = S * ct.w;
             const float4 col = s_col[warp][j];
             const float w = T * alpha;
-            const float dldw = g0 * col.x + g1 * col.y + g2c * col.z + gW + gD * col.w;
-            const float dlda = T * dldw - __fdividef(g0 * R0 + g1 * R1 + g2c * R2 + gW * RW + gD * RD, f);
+            float dldw = g0 * col.x + g1 * col.y + g2c * col.z + gW;
+            float rsum = g0 * R0 + g1 * R1 + g2c * R2 + gW * RW;
+            if (DEPTH) {
+              dldw = fmaf(gD, col.w, dldw);
+              rsum = fmaf(gD, RD, rsum);
+              RD = fmaf(w, col.w, RD);
+            }
+            const float dlda = T * dldw - rsum * rf;
             R0 = fmaf(w, col.x, R0);
             R1 = fmaf(w, col.y, R1);
             R2 = fmaf(w, col.z, R2);
             RW += w;
-            RD = fmaf(w, col.w, RD);
             const float dlr = (araw >= 0.0f && araw <= rc.alpha_clamp) ? dlda : 0.0f;
             const float power = -0.5f * q;
             const float pmask = power < 0.0f ? 1.0f : (power == 0.0f ? 0.5f : 0.0f);
@@ -281,7 +290,7 @@ __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
             v[6] = g0 * w;
             v[7] = g1 * w;
             v[8] = g2c * w;
-            v[9] = gD * w;
+            v[9] = DEPTH ? gD * w : 0.0f;
             contrib = true;
           }
         }
@@ -316,8 +325,11 @@ gsb_status launch_raster_fwd(const RasterArgs& a, cudaStream_t st) {
 gsb_status launch_raster_bwd(const RasterArgs& a, cudaStream_t st) {
   if (cudaMemsetAsync(a.grad2d, 0, size_t(a.B) * a.G * GSB_GRAD2D_FLOATS * sizeof(float), st)) return GSB_ERR_CUDA;
   const dim3 grid(a.rc.n_tiles, a.B);
-  if (a.rc.tile == 16) { note_launch(); raster_bwd_kernel<16><<<grid, 256, 0, st>>>(a); }
-  else if (a.rc.tile == 8) { note_launch(); raster_bwd_kernel<8><<<grid, 64, 0, st>>>(a); }
+  const bool depth = a.d_depth != nullptr;
+  if (a.rc.tile == 16 && depth) { note_launch(); raster_bwd_kernel<16, true><<<grid, 256, 0, st>>>(a); }
+  else if (a.rc.tile == 16) { note_launch(); raster_bwd_kernel<16, false><<<grid, 256, 0, st>>>(a); }
+  else if (a.rc.tile == 8 && depth) { note_launch(); raster_bwd_kernel<8, true><<<grid, 64, 0, st>>>(a); }
+  else if (a.rc.tile == 8) { note_launch(); raster_bwd_kernel<8, false><<<grid, 64, 0, st>>>(a); }
   else return GSB_ERR_ARG;
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }

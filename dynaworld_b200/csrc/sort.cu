@@ -105,7 +105,10 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
   __shared__ uint32_t s_part;
   __shared__ uint32_t s_warp_hist[kSortWarps][256];
   __shared__ uint32_t s_base[256];
+  __shared__ uint32_t s_local[256];
   __shared__ uint32_t s_tmp[kSortWarps];
+  __shared__ K s_keys[kPart];
+  __shared__ uint32_t s_vals[kVals ? kPart : 1];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) s_part = atomicAdd(part_counter, 1u);
@@ -178,21 +181,32 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
     }
     st_release_u32(my, kFlagIncl | ((excl + total) & kCountMask));
   }
+  // Digit runs of this partition: local start of each digit, global start of its run.
+  s_local[tid] = block_excl_scan_256(total, s_tmp, nullptr);
   const uint32_t digit_start = block_excl_scan_256(hist[tid], s_tmp, nullptr);
   s_base[tid] = digit_start + excl;
   __syncthreads();
-
+  // Stage the partition in (digit, input) order, then write each digit's run contiguously.
 #pragma unroll
   for (int j = 0; j < kItems; ++j) {
     const uint32_t d = dig[j];
     if (d == 0xffffffffu) continue;
-    const uint32_t pos = s_base[d] + s_warp_hist[warp][d] + rank[j];
+    const uint32_t lpos = s_local[d] + s_warp_hist[warp][d] + rank[j];
+    s_keys[lpos] = k[j];
+    if (kVals) s_vals[lpos] = v[j];
+  }
+  __syncthreads();
+  const uint32_t n_valid = min(kPart, n - part * kPart);
+  for (uint32_t i = tid; i < n_valid; i += kSortThreads) {
+    const K key = s_keys[i];
+    const uint32_t d = uint32_t((key >> shift) & K(mask));
+    const uint32_t pos = s_base[d] + (i - s_local[d]);
     if (pos >= n) {  // only after a timed-out look-back: never write outside the output
       record_error(status, GSB_ERR_TIMEOUT, int(part));
       continue;
     }
-    keys_out[pos] = k[j];
-    if (kVals) vals_out[pos] = v[j];
+    keys_out[pos] = key;
+    if (kVals) vals_out[pos] = s_vals[i];
   }
 }
 

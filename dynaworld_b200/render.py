@@ -69,6 +69,7 @@ class FrameState:
     records: torch.Tensor
     keys: torch.Tensor
     ranges: torch.Tensor
+    order: torch.Tensor
     pixel_t: torch.Tensor
     pixel_state: torch.Tensor
     n_pairs: int
@@ -150,10 +151,12 @@ def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, n
     n_tiles = -(-H // cfg.tile_size) * -(-W // cfg.tile_size)
     keys = torch.empty(max(n_pairs, 1), dtype=torch.int64, device=dev)
     ranges = torch.empty(B * n_tiles * 2, dtype=torch.int32, device=dev)
+    order = torch.empty(B * n_tiles, dtype=torch.int32, device=dev)
     ws3 = _ws(L.gsb_bin_workspace(views, opts, G, n_pairs), dev)
     with _stage("bin"):
         _lib.check("gsb_bin", L.gsb_bin(views, opts, G, records.data_ptr(), rects.data_ptr(), offsets.data_ptr(),
-                                        n_pairs, keys.data_ptr(), ranges.data_ptr(), ws3.data_ptr(), ws3.numel(), st))
+                                        n_pairs, keys.data_ptr(), ranges.data_ptr(), order.data_ptr(), ws3.data_ptr(),
+                                        ws3.numel(), st))
     image = torch.empty(B, 3, H, W, dtype=torch.float32, device=dev)
     alpha = torch.empty(B, H, W, dtype=torch.float32, device=dev)
     depth = torch.empty(B, H, W, dtype=torch.float32, device=dev) if cfg.depth else None
@@ -161,12 +164,13 @@ def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, n
     pixel_state = torch.empty(B, H, W, dtype=torch.int32, device=dev)
     with _stage("raster_fwd"):
         _lib.check("gsb_raster_fwd", L.gsb_raster_fwd(views, opts, G, records.data_ptr(), keys.data_ptr(),
-                                                      ranges.data_ptr(), image.data_ptr(), alpha.data_ptr(),
+                                                      ranges.data_ptr(), order.data_ptr(), image.data_ptr(),
+                                                      alpha.data_ptr(),
                                                       _lib.ptr(depth), pixel_t.data_ptr(), pixel_state.data_ptr(),
                                                       st))
     if cfg.check_status:
         _lib.check("gsb_bin", int(ws3.view(torch.int32)[0].item()))
-    state = FrameState(rank_of, records, keys, ranges, pixel_t, pixel_state, n_pairs)
+    state = FrameState(rank_of, records, keys, ranges, order, pixel_t, pixel_state, n_pairs)
     return image, alpha, depth, state
 
 
@@ -185,6 +189,7 @@ def backward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, 
     with _stage("raster_bwd"):
         _lib.check("gsb_raster_bwd", L.gsb_raster_bwd(views, opts, G, state.records.data_ptr(),
                                                       state.keys.data_ptr(), state.ranges.data_ptr(),
+                                                      state.order.data_ptr(),
                                                       state.pixel_t.data_ptr(), state.pixel_state.data_ptr(),
                                                       d_image.data_ptr(), _lib.ptr(d_alpha), _lib.ptr(d_depth),
                                                       _lib.ptr(view_scale), grad2d.data_ptr(), st))

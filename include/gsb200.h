@@ -164,19 +164,23 @@ GSB_API gsb_status gsb_preprocess_fwd(const gsb_scene* scene, const gsb_views* v
 GSB_API size_t gsb_bin_workspace(const gsb_views* views, const gsb_options* opts,
                                  int32_t n_gaussians, uint32_t n_pairs);
 /* sorted_keys[n_pairs]: ((view*n_tiles + tile) << 32) | depth_rank, ascending.
-   tile_ranges[B*n_tiles*2]: [start, end) of each tile's run in sorted_keys. */
+   tile_ranges[B*n_tiles*2]: [start, end) of each tile's run in sorted_keys.
+   tile_order[B*n_tiles] (may be NULL): view*n_tiles + tile, longest lists first -- the launch
+   order the raster stages use so that the heaviest tiles do not finish last. */
 GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians,
                            const float* records, const int32_t* tile_rects,
                            const uint32_t* pair_offsets, uint32_t n_pairs,
-                           uint64_t* sorted_keys, uint32_t* tile_ranges,
+                           uint64_t* sorted_keys, uint32_t* tile_ranges, uint32_t* tile_order,
                            void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- stage 4: front-to-back blend (dense.py:208-236) -------------------------------------- */
 /* image [B,3,H,W] (clamped), alpha [B,H,W] = sum of weights, depth [B,H,W] or NULL,
-   pixel_t [B,H,W] and pixel_state [B,H,W]: the per-pixel state gsb_raster_bwd needs. */
+   pixel_t [B,H,W] and pixel_state [B,H,W]: the per-pixel state gsb_raster_bwd needs.
+   tile_order: gsb_bin's launch order, or NULL for (view, tile) order. */
 GSB_API gsb_status gsb_raster_fwd(const gsb_views* views, const gsb_options* opts,
                                   int32_t n_gaussians, const float* records,
                                   const uint64_t* sorted_keys, const uint32_t* tile_ranges,
+                                  const uint32_t* tile_order,
                                   float* image, float* alpha, float* depth,
                                   float* pixel_t, uint32_t* pixel_state, void* stream);
 
@@ -214,6 +218,7 @@ GSB_API gsb_status gsb_scale_planes(const float* in, const float* scale, float* 
 GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opts,
                                   int32_t n_gaussians, const float* records,
                                   const uint64_t* sorted_keys, const uint32_t* tile_ranges,
+                                  const uint32_t* tile_order,
                                   const float* pixel_t, const uint32_t* pixel_state,
                                   const float* d_image, const float* d_alpha,
                                   const float* d_depth, const float* view_scale,

@@ -53,12 +53,14 @@ def test_argument_errors_return_codes_without_touching_a_gpu(lib):
     """Invalid arguments are rejected on the host with a status, before any CUDA call."""
     v = _lib.Views()
     assert lib.gsb_depth_order(None, None, None, None, None, 0, None) == 7  # GSB_ERR_ARG
-    assert lib.gsb_raster_fwd(ctypes.byref(v), None, 1, None, None, None, None, None, None, None, None, None) == 7
+    assert lib.gsb_raster_fwd(ctypes.byref(v), None, 1, None, None, None, None, None, None, None, None, None,
+                              None) == 7
     o = _lib.Options()
     o.tile_size = 12
     v.intrinsics = v.camera_to_world = 16
     v.n_views = v.height = v.width = v.views_per_set = 1
-    assert lib.gsb_raster_fwd(ctypes.byref(v), ctypes.byref(o), 1, 16, 16, 16, 16, 16, 16, 16, 16, None) == 7
+    assert lib.gsb_raster_fwd(ctypes.byref(v), ctypes.byref(o), 1, 16, 16, 16, None, 16, 16, 16, 16, 16,
+                              None) == 7
     lo = _lib.LossOptions()
     lo.type = 0
     lo.window_size = 4  # even window

@@ -82,6 +82,17 @@ def test_tiled_compat_lists_match_reference(case, tile):
     np.testing.assert_array_equal(rank, g[f"ref_tiled{tile}_rank"])
 
 
+@pytest.mark.parametrize("case", ["dynamic128_small", "multiview384_small"])
+def test_tile_launch_order_is_a_permutation_by_descending_length(case):
+    wl = load_golden(case).workload()
+    _, _, _, st = stages(wl)
+    order = st.order.cpu().numpy().astype(np.int64)
+    np.testing.assert_array_equal(np.sort(order), np.arange(order.size))
+    r = st.ranges.cpu().numpy().astype(np.int64).reshape(-1, 2)
+    lengths = (r[:, 1] - r[:, 0])[order] >> 4
+    assert np.all(np.diff(lengths) <= 0)
+
+
 @pytest.mark.parametrize("case", GOLDEN_CASES)
 def test_image_loss_and_gradients_match_reference(case):
     g = load_golden(case)
