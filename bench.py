@@ -285,6 +285,24 @@ def reference_arm(args, rank, world):
 # main GPU arm
 
 
+def ncu_traffic(kernel: str, workload: str):
+    """DRAM bytes (read + write) of one launch of `kernel` from the committed ncu summary
+    profiles/<kernel>_<workload>.md, or None when there is none for this workload."""
+    path = ROOT / "profiles" / f"{kernel}_{workload}.md"
+    if not path.exists():
+        return None, None
+    total = 0.0
+    scale = {"byte": 1.0, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
+    found = 0
+    for line in path.read_text().splitlines():
+        for metric in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+            if f"`{metric}`" in line:
+                value, unit = line.split("|")[2].split()
+                total += float(value) * scale.get(unit, 1.0)
+                found += 1
+    return (total if found == 2 else None), str(path.relative_to(ROOT))
+
+
 def hbm_peak():
     try:
         p = json.loads(PEAKS.read_text())
@@ -414,11 +432,13 @@ def main():
     peak, peak_kind = hbm_peak()
     dur_s = means[dominant] / 1e3
     achieved = alg_bytes / dur_s / 1e9
+    traffic, traffic_src = ncu_traffic(dominant, args.workload) if args.tile is None else (None, None)
     roofline = {"bound": "hbm", "kernel": f"{dominant} (gsb_{dominant})", "achieved": achieved, "peak": peak,
-                "unit": "GB/s", "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
-                "bytes_per_launch": int(alg_bytes), "pairs": int(n_pairs), "pixels": int(px),
-                "launch_ms": means[dominant],
-                "note": "raster is FP32/SFU-issue bound (records re-read from L2); see profiles/ for ncu counters"}
+                "unit": "GB/s", "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_src,
+                "peak_source": peak_kind, "bytes_per_launch": int(alg_bytes), "pairs": int(n_pairs),
+                "pixels": int(px), "launch_ms": means[dominant],
+                "note": "raster is issue-bound (records re-read from L2, DRAM traffic below the algorithmic "
+                        "bytes); see profiles/ for the ncu counters"}
     stage_share = {k: round(v / sum(means.values()), 4) for k, v in means.items()} if means else {}
 
     if rank == 0:

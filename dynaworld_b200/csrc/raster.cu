@@ -69,7 +69,23 @@ __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* rec
   // half extents of the ellipse: sqrt(tau (A^-1)_ii), (A^-1)_00 = C/det, (A^-1)_11 = A/det
   const float ex = sqrtf(tau * C / det) * 1.0001f + 0.01f;
   const float ey = sqrtf(tau * A / det) * 1.0001f + 0.01f;
-  return (r0.x + ex >= bx0) && (r0.x - ex <= bx0 + 7.0f) && (r0.y + ey >= by0) && (r0.y - ey <= by0 + 3.0f);
+  if (!((r0.x + ex >= bx0) && (r0.x - ex <= bx0 + 7.0f) && (r0.y + ey >= by0) && (r0.y - ey <= by0 + 3.0f)))
+    return false;
+  // exact: the minimum of q over the block's pixel-centre box (on an edge unless the mean is inside)
+  const float X0 = bx0 - r0.x, X1 = bx0 + 7.0f - r0.x, Y0 = by0 - r0.y, Y1 = by0 + 3.0f - r0.y;
+  if (X0 <= 0.0f && X1 >= 0.0f && Y0 <= 0.0f && Y1 >= 0.0f) return true;
+  const float hC = -0.5f * B / C, hA = -0.5f * B / A;
+  float q = __int_as_float(0x7f800000);
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const float dx = e ? X1 : X0;
+    const float dy = fminf(fmaxf(hC * dx, Y0), Y1);
+    q = fminf(q, (A * dx + B * dy) * dx + C * dy * dy);
+    const float ey2 = e ? Y1 : Y0;
+    const float dx2 = fminf(fmaxf(hA * ey2, X0), X1);
+    q = fminf(q, (A * dx2 + B * ey2) * dx2 + C * ey2 * ey2);
+  }
+  return q <= tau * 1.0001f + 0.01f;
 }
 
 template <int TILE>
