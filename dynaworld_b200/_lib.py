@@ -25,6 +25,9 @@ SCENE_SH_CLAMP = 0x4
 RENDER_TILED_COMPAT = 0x1
 RENDER_DEPTH = 0x2
 RENDER_NO_ELLIPSE = 0x4
+RENDER_NO_CLAMP = 0x8
+SPLATS2D_CONIC = 0
+SPLATS2D_PACKED = 1
 RECORD_FLOATS = 12
 GRAD2D_FLOATS = 10
 
@@ -66,6 +69,17 @@ class LossOptions(C.Structure):
     ]
 
 
+class Splats2D(C.Structure):
+    _fields_ = [
+        ("n_views", C.c_int32), ("n_gaussians", C.c_int32), ("format", C.c_int32), ("reserved", C.c_int32),
+        ("means", vp), ("conics", vp), ("opacities", vp), ("packed", vp), ("colors", vp), ("depths", vp),
+    ]
+
+
+class Splats2DGrads(C.Structure):
+    _fields_ = [("means", vp), ("conics", vp), ("opacities", vp), ("packed", vp), ("colors", vp)]
+
+
 P = C.POINTER
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -89,6 +103,12 @@ SIGNATURES = {
     "gsb_scale_planes": (C.c_int, [vp, vp, vp, C.c_int32, C.c_int64, vp]),
     "gsb_raster_bwd": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "gsb_preprocess_bwd": (C.c_int, [P(Scene), P(Views), P(Options), vp, vp, P(SceneGrads), vp]),
+    "gsb_splats2d_order_workspace": (C.c_size_t, [P(Splats2D)]),
+    "gsb_splats2d_order": (C.c_int, [P(Splats2D), vp, vp, vp, C.c_size_t, vp]),
+    "gsb_splats2d_preprocess_workspace": (C.c_size_t, [P(Splats2D)]),
+    "gsb_splats2d_preprocess": (C.c_int, [P(Splats2D), C.c_int32, C.c_int32, P(Options), vp, vp, vp, vp, vp,
+                                          C.c_size_t, vp]),
+    "gsb_splats2d_preprocess_bwd": (C.c_int, [P(Splats2D), vp, vp, P(Splats2DGrads), vp]),
     "gsb_radix_sort_workspace": (C.c_size_t, [C.c_uint32, C.c_int, C.c_int]),
     "gsb_radix_sort": (C.c_int, [vp, vp, vp, vp, C.c_uint32, C.c_int, C.c_int, C.c_int, vp, C.c_size_t, vp]),
 }

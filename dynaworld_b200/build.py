@@ -19,7 +19,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB = PKG / "libgsb200.so"
-SOURCES = ["abi.cu", "preprocess.cu", "sort.cu", "bin.cu", "raster.cu", "loss.cu"]
+SOURCES = ["abi.cu", "preprocess.cu", "sort.cu", "bin.cu", "raster.cu", "loss.cu", "splat2d.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

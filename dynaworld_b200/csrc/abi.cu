@@ -26,6 +26,7 @@ RenderConsts make_consts(const gsb_views& v, const gsb_options& o) {
   rc.compat = (o.flags & GSB_RENDER_TILED_COMPAT) != 0;
   rc.depth = (o.flags & GSB_RENDER_DEPTH) != 0;
   rc.ellipse = (o.flags & GSB_RENDER_NO_ELLIPSE) == 0;
+  rc.clamp_image = (o.flags & GSB_RENDER_NO_CLAMP) == 0;
   rc.near_plane = o.near_plane;
   rc.alpha_clamp = o.alpha_clamp;
   rc.alpha_cutoff = rc.compat ? 0.0f : o.alpha_cutoff;
@@ -47,6 +48,27 @@ static cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 static gsb_status check_views(const gsb_views* v) {
   if (!v || !v->intrinsics || !v->camera_to_world) return GSB_ERR_ARG;
   if (v->n_views <= 0 || v->height <= 0 || v->width <= 0 || v->views_per_set <= 0) return GSB_ERR_SHAPE;
+  return GSB_OK;
+}
+
+// The bin and raster stages read only the batch and image sizes (no cameras).
+static gsb_status check_frame(const gsb_views* v) {
+  if (!v) return GSB_ERR_ARG;
+  if (v->n_views <= 0 || v->height <= 0 || v->width <= 0) return GSB_ERR_SHAPE;
+  return GSB_OK;
+}
+
+static gsb_status check_splats2d(const gsb_splats2d* s) {
+  if (!s || !s->colors) return GSB_ERR_ARG;
+  if (s->format == GSB_SPLATS2D_CONIC) {
+    if (!s->means || !s->conics || !s->opacities) return GSB_ERR_ARG;
+  } else if (s->format == GSB_SPLATS2D_PACKED) {
+    if (!s->packed) return GSB_ERR_ARG;
+  } else {
+    return GSB_ERR_ARG;
+  }
+  if (s->n_views <= 0 || s->n_gaussians <= 0) return GSB_ERR_SHAPE;
+  if (uint64_t(s->n_views) * uint64_t(s->n_gaussians) >= (uint64_t(1) << 30)) return GSB_ERR_SHAPE;
   return GSB_OK;
 }
 
@@ -231,7 +253,7 @@ GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int3
                            uint64_t* sorted_keys, uint32_t* tile_ranges, uint32_t* tile_order, void* workspace,
                            size_t workspace_bytes, void* stream) {
   gsb_status s;
-  if ((s = check_views(views)) != GSB_OK) return s;
+  if ((s = check_frame(views)) != GSB_OK) return s;
   if ((s = check_opts(opts)) != GSB_OK) return s;
   if (n_gaussians <= 0) return GSB_ERR_SHAPE;
   if (!records || !tile_rects || !pair_offsets || !tile_ranges || !workspace) return GSB_ERR_ARG;
@@ -277,7 +299,7 @@ GSB_API gsb_status gsb_raster_fwd(const gsb_views* views, const gsb_options* opt
                                   const uint32_t* tile_order, float* image, float* alpha, float* depth,
                                   float* pixel_t, uint32_t* pixel_state, void* stream) {
   gsb_status s;
-  if ((s = check_views(views)) != GSB_OK) return s;
+  if ((s = check_frame(views)) != GSB_OK) return s;
   if ((s = check_opts(opts)) != GSB_OK) return s;
   if (n_gaussians <= 0) return GSB_ERR_SHAPE;
   if (!records || !tile_ranges || !image || !pixel_t || !pixel_state) return GSB_ERR_ARG;
@@ -298,7 +320,7 @@ GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opt
                                   const float* d_alpha, const float* d_depth, const float* view_scale, float* grad2d,
                                   void* stream) {
   gsb_status s;
-  if ((s = check_views(views)) != GSB_OK) return s;
+  if ((s = check_frame(views)) != GSB_OK) return s;
   if ((s = check_opts(opts)) != GSB_OK) return s;
   if (n_gaussians <= 0) return GSB_ERR_SHAPE;
   if (!records || !tile_ranges || !pixel_t || !pixel_state || !d_image || !grad2d) return GSB_ERR_ARG;
@@ -341,6 +363,87 @@ GSB_API gsb_status gsb_preprocess_bwd(const gsb_scene* scene, const gsb_views* v
   if (!rank_of || !grad2d || !grads) return GSB_ERR_ARG;
   const RenderConsts rc = make_consts(*views, *opts);
   return launch_preprocess_bwd(*scene, *views, rc, rank_of, grad2d, *grads, as_stream(stream));
+}
+
+// ---- already-projected 2-D Gaussians ---------------------------------------------------------
+
+GSB_API size_t gsb_splats2d_order_workspace(const gsb_splats2d* splats) {
+  if (!splats) return 0;
+  return depth_ws(splats->n_views, splats->n_gaussians);
+}
+
+GSB_API gsb_status gsb_splats2d_order(const gsb_splats2d* splats, int32_t* sorted_ids, int32_t* rank_of,
+                                      void* workspace, size_t workspace_bytes, void* stream) {
+  gsb_status s;
+  if ((s = check_splats2d(splats)) != GSB_OK) return s;
+  if (!sorted_ids || !rank_of || !workspace) return GSB_ERR_ARG;
+  const int32_t B = splats->n_views, G = splats->n_gaussians;
+  if (workspace_bytes < depth_ws(B, G)) return GSB_ERR_WORKSPACE;
+  cudaStream_t st = as_stream(stream);
+  const uint32_t n = uint32_t(size_t(B) * G);
+  const int kb = B > 1 ? 8 : 4;
+  Carver c(workspace, workspace_bytes);
+  c.take<WorkspaceHeader>(1);
+  void* keys = c.take<char>(size_t(n) * kb);
+  uint32_t* vals = c.take<uint32_t>(n);
+  void* skeys = c.take<char>(size_t(n) * kb);
+  uint32_t* svals = c.take<uint32_t>(n);
+  const size_t sws = radix_sort_workspace(n, kb, 1);
+  void* sort_ws = c.take<char>(sws);
+  int32_t* status = begin_status(workspace, st);
+  if ((s = launch_order_keys_2d(*splats, kb == 8 ? static_cast<uint64_t*>(keys) : nullptr,
+                                kb == 4 ? static_cast<uint32_t*>(keys) : nullptr, vals, st)) != GSB_OK)
+    return s;
+  if (splats->depths) {
+    const int bit_hi = 32 + (B > 1 ? bits_for(uint64_t(B)) : 0);
+    if ((s = radix_sort(keys, skeys, vals, svals, n, kb, 0, bit_hi, sort_ws, sws, st, status)) != GSB_OK) return s;
+  } else {
+    svals = vals;  // no depths: index order, the keys are already sorted
+  }
+  return launch_invert_order(svals, B, G, sorted_ids, rank_of, st);
+}
+
+GSB_API size_t gsb_splats2d_preprocess_workspace(const gsb_splats2d* splats) {
+  if (!splats) return 0;
+  return preprocess_ws(splats->n_views, splats->n_gaussians);
+}
+
+GSB_API gsb_status gsb_splats2d_preprocess(const gsb_splats2d* splats, int32_t height, int32_t width,
+                                           const gsb_options* opts, const int32_t* rank_of, float* records,
+                                           int32_t* tile_rects, uint32_t* pair_offsets, void* workspace,
+                                           size_t workspace_bytes, void* stream) {
+  gsb_status s;
+  if ((s = check_splats2d(splats)) != GSB_OK) return s;
+  if ((s = check_opts(opts)) != GSB_OK) return s;
+  if (height <= 0 || width <= 0) return GSB_ERR_SHAPE;
+  if (opts->flags & GSB_RENDER_TILED_COMPAT) return GSB_ERR_ARG;  // tiled.py bounds need a 2-D covariance
+  if (!rank_of || !records || !tile_rects || !pair_offsets || !workspace) return GSB_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(records) % 16 || reinterpret_cast<uintptr_t>(tile_rects) % 16) return GSB_ERR_ARG;
+  const int32_t B = splats->n_views, G = splats->n_gaussians;
+  if (workspace_bytes < preprocess_ws(B, G)) return GSB_ERR_WORKSPACE;
+  cudaStream_t st = as_stream(stream);
+  const uint32_t n = uint32_t(size_t(B) * G);
+  Carver c(workspace, workspace_bytes);
+  c.take<WorkspaceHeader>(1);
+  uint32_t* counts = c.take<uint32_t>(n);
+  const size_t scan_bytes = exclusive_scan_workspace(n);
+  void* scan_ws = c.take<char>(scan_bytes);
+  int32_t* status = begin_status(workspace, st);
+  gsb_views frame{};
+  frame.n_views = B, frame.views_per_set = 1, frame.height = height, frame.width = width;
+  const RenderConsts rc = make_consts(frame, *opts);
+  if ((s = launch_preprocess_2d(*splats, height, width, rc, rank_of, records, reinterpret_cast<int4*>(tile_rects),
+                                counts, st)) != GSB_OK)
+    return s;
+  return exclusive_scan(counts, n, pair_offsets, scan_ws, scan_bytes, st, status);
+}
+
+GSB_API gsb_status gsb_splats2d_preprocess_bwd(const gsb_splats2d* splats, const int32_t* rank_of,
+                                               const float* grad2d, gsb_splats2d_grads* grads, void* stream) {
+  gsb_status s;
+  if ((s = check_splats2d(splats)) != GSB_OK) return s;
+  if (!rank_of || !grad2d || !grads) return GSB_ERR_ARG;
+  return launch_preprocess_2d_bwd(*splats, rank_of, grad2d, *grads, as_stream(stream));
 }
 
 // ---- utility ---------------------------------------------------------------------------------

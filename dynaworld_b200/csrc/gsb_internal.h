@@ -31,6 +31,7 @@ struct RenderConsts {
   bool compat;
   bool depth;
   bool ellipse;
+  bool clamp_image;  // clamp the composited image to [0, 1]
   float near_plane, alpha_clamp, alpha_cutoff, t_threshold, eps, pixel_center;
   float bg[3];
   float bound_scale, tiled_threshold;
@@ -74,6 +75,14 @@ gsb_status launch_preprocess_fwd(const gsb_scene& sc, const gsb_views& vw, const
 gsb_status launch_preprocess_bwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
                                  const int32_t* rank_of, const float* grad2d, const gsb_scene_grads& gr,
                                  cudaStream_t st);
+
+// Already-projected 2-D Gaussians (splat2d.cu).
+gsb_status launch_order_keys_2d(const gsb_splats2d& sp, uint64_t* keys64, uint32_t* keys32, uint32_t* vals,
+                                cudaStream_t st);
+gsb_status launch_preprocess_2d(const gsb_splats2d& sp, int H, int W, const RenderConsts& rc, const int32_t* rank_of,
+                                float* records, int4* rects, uint32_t* counts, cudaStream_t st);
+gsb_status launch_preprocess_2d_bwd(const gsb_splats2d& sp, const int32_t* rank_of, const float* grad2d,
+                                    const gsb_splats2d_grads& gr, cudaStream_t st);
 
 // Binning (bin.cu).
 gsb_status launch_emit(int32_t B, int32_t G, const RenderConsts& rc, int H, int W, const float* records,

@@ -10,7 +10,8 @@
 //   T_i     = prod_{j<i} fl32(fl32(1 - alpha_j) + eps)  over ALL Gaussians of the view in depth
 //             order (dense.py:222-228); a Gaussian that does not touch the pixel contributes
 //             F0 = fl32(1 + eps) (exactly so when its alpha <= 2^-25).
-//   out     = clamp(sum w c + (1 - clamp(sum w, 0, 1)) bg, 0, 1), w = T alpha (dense.py:229-233)
+//   out     = clamp(sum w c + (1 - clamp(sum w, 0, 1)) bg, 0, 1), w = T alpha (dense.py:229-233);
+//             the outer clamp is left out for the 2-D kernels' contract (GSB_RENDER_NO_CLAMP)
 // With pos_i the depth rank of entry i (exact mode) or its index in the tile list (tiled-compat
 // mode, tile-local products as tiled.py:176-185):
 //   T_i = F0^pos_i * S_i,   S_i = prod_{blended j < i} f_j / F0,
@@ -158,8 +159,9 @@ __global__ void __launch_bounds__(TILE* TILE) raster_fwd_kernel(RasterArgs a) {
 #pragma unroll
   for (int ch = 0; ch < 3; ++ch) {
     const float pre = __fadd_rn(cc[ch], __fmul_rn(one_m, rc.bg[ch]));
-    if (pre >= 0.0f && pre <= 1.0f) mask |= 1u << ch;
-    a.image[(size_t(view) * 3 + ch) * HW + poff] = fminf(fmaxf(pre, 0.0f), 1.0f);
+    const bool pass = !rc.clamp_image || (pre >= 0.0f && pre <= 1.0f);
+    if (pass) mask |= 1u << ch;
+    a.image[(size_t(view) * 3 + ch) * HW + poff] = rc.clamp_image ? fminf(fmaxf(pre, 0.0f), 1.0f) : pre;
   }
   if (a.alpha) a.alpha[pix] = Ws;
   if (a.depth) a.depth[pix] = D;

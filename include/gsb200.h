@@ -61,6 +61,9 @@ typedef enum gsb_status {
                                         tile-local (1+eps) products, no cutoff, no early stop */
 #define GSB_RENDER_DEPTH 0x2u        /* write depth = sum_i w_i z_i */
 #define GSB_RENDER_NO_ELLIPSE 0x4u   /* exact mode: keep every tile of the bounding box */
+#define GSB_RENDER_NO_CLAMP 0x8u     /* image = sum w c + (1 - clamp(sum w, 0, 1)) bg, not clamped
+                                        to [0, 1] (the 2-D kernels' output, gsplat_kernels.metal:
+                                        199-201) */
 
 /* Gaussians: n_sets sets of n_gaussians each; view b draws on set b / views_per_set. */
 typedef struct gsb_scene {
@@ -229,6 +232,63 @@ GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opt
 GSB_API gsb_status gsb_preprocess_bwd(const gsb_scene* scene, const gsb_views* views,
                                       const gsb_options* opts, const int32_t* rank_of,
                                       const float* grad2d, gsb_scene_grads* grads, void* stream);
+
+/* ---- already-projected 2-D Gaussians -------------------------------------------------------
+ * The reference's 2-D rasterizer contracts, on the same bin and raster stages as the 3-D path:
+ *   conic  <- third_party/fast-mac-gsplat-scaffold/torch_gsplat_bridge/rasterize.py:93-126
+ *             (rasterize_projected_gaussians, called by src/train/renderers/fast_mac.py:253,301)
+ *             and third_party/raw-metal-mlx-gsplat/mlx_projected_gaussian_rasterizer.py:787;
+ *             kernels gsplat_kernels.metal:40-205
+ *   packed <- the [mean, axis, sigma, opacity] rows of src/train/renderers/taichi.py:107-176 and
+ *             src/benchmarks/splat_renderer_accuracy.py:262-305 (torch_reference_rasterize)
+ * Order: gsb_splats2d_order -> gsb_splats2d_preprocess -> gsb_bin -> gsb_raster_fwd, and
+ * gsb_raster_bwd -> gsb_splats2d_preprocess_bwd; the bin and raster stages take a gsb_views with
+ * n_views = batch, views_per_set = 1 and the image size (intrinsics / camera_to_world unused, may
+ * be NULL there).  Options that give the reference kernels' semantics: eps 0, pixel_center 0.5,
+ * alpha_cutoff = alpha_threshold, transmittance_threshold as given (1 - saturate_threshold for
+ * the packed contract), alpha_clamp 0.99, GSB_RENDER_NO_CLAMP. */
+#define GSB_SPLATS2D_CONIC 0  /* means [B,G,2], conics [B,G,3] (a, b, c): q = a dx^2 + 2 b dx dy
+                                 + c dy^2, opacities [B,G] */
+#define GSB_SPLATS2D_PACKED 1 /* packed [B,G,7]: mean x, y, unit axis x, y, sigma along the axis,
+                                 sigma across it, opacity */
+typedef struct gsb_splats2d {
+  int32_t n_views;        /* B: independent images */
+  int32_t n_gaussians;    /* G per image */
+  int32_t format;         /* GSB_SPLATS2D_* */
+  int32_t reserved;
+  const float* means;     /* conic format */
+  const float* conics;    /* conic format */
+  const float* opacities; /* conic format */
+  const float* packed;    /* packed format */
+  const float* colors;    /* [B,G,3] */
+  const float* depths;    /* [B,G] blend order (ascending, ties by index), or NULL: index order */
+} gsb_splats2d;
+
+typedef struct gsb_splats2d_grads { /* NULL entries are skipped; outputs are overwritten */
+  float* means;
+  float* conics;    /* d/d(a, b, c) with b the half cross coefficient */
+  float* opacities;
+  float* packed;    /* [B,G,7] */
+  float* colors;
+} gsb_splats2d_grads;
+
+GSB_API size_t gsb_splats2d_order_workspace(const gsb_splats2d* splats);
+/* As gsb_depth_order, keyed by the given depths. */
+GSB_API gsb_status gsb_splats2d_order(const gsb_splats2d* splats, int32_t* sorted_ids,
+                                      int32_t* rank_of, void* workspace, size_t workspace_bytes,
+                                      void* stream);
+GSB_API size_t gsb_splats2d_preprocess_workspace(const gsb_splats2d* splats);
+/* As gsb_preprocess_fwd: records (z = the given depth), tile_rects and pair_offsets in blend
+   order.  Conic format also drops Gaussians with a c - b^2 <= 1e-8 (gsplat_kernels.metal:57-59). */
+GSB_API gsb_status gsb_splats2d_preprocess(const gsb_splats2d* splats, int32_t height,
+                                           int32_t width, const gsb_options* opts,
+                                           const int32_t* rank_of, float* records,
+                                           int32_t* tile_rects, uint32_t* pair_offsets,
+                                           void* workspace, size_t workspace_bytes, void* stream);
+/* grad2d (gsb_raster_bwd) -> gradients of the caller's parameters. */
+GSB_API gsb_status gsb_splats2d_preprocess_bwd(const gsb_splats2d* splats, const int32_t* rank_of,
+                                               const float* grad2d, gsb_splats2d_grads* grads,
+                                               void* stream);
 
 /* ---- utility: the library's radix sort on its own (tests, benchmarks) --------------------- */
 GSB_API size_t gsb_radix_sort_workspace(uint32_t n, int key_bytes, int with_values);

@@ -53,6 +53,11 @@ def test_argument_errors_return_codes_without_touching_a_gpu(lib):
     """Invalid arguments are rejected on the host with a status, before any CUDA call."""
     v = _lib.Views()
     assert lib.gsb_depth_order(None, None, None, None, None, 0, None) == 7  # GSB_ERR_ARG
+    # the raster stages need no cameras: an empty frame is a shape error, a missing option block an
+    # argument error
+    assert lib.gsb_raster_fwd(ctypes.byref(v), None, 1, None, None, None, None, None, None, None, None, None,
+                              None) == 1
+    v.n_views = v.height = v.width = 1
     assert lib.gsb_raster_fwd(ctypes.byref(v), None, 1, None, None, None, None, None, None, None, None, None,
                               None) == 7
     o = _lib.Options()
