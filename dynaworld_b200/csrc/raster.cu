@@ -1,9 +1,12 @@
 // Raster: per-tile front-to-back blend and its reverse-order backward.
 //
-// One CTA per (view, tile) of 16x16 pixels, one thread per pixel; each warp owns an 8x4 pixel block
-// and works independently of the other warps (no CTA barrier): it streams the tile's sorted list in
-// chunks of 32 entries (one gather per lane; the 8 warps of a tile read the same records, so all but
-// the first read hit L1), keeps the entries whose ellipse box reaches its block, and walks those.
+// One CTA per (view, tile) of 16x16 pixels, PX (1 or 2) pixels per thread: each warp owns an
+// 8 x 4PX pixel block (lane l: pixels (l % 8, l / 8 + 4k), k < PX) and works independently of the
+// other warps (no CTA barrier): it streams the tile's sorted list in chunks of 32 entries (one
+// gather per lane; the warps of a tile read the same records, so all but the first read hit L1),
+// keeps the entries whose ellipse reaches its block, and walks those.  With PX = 2 the
+// shared-memory reads, the loop control and (backward) the warp reduction and atomics of a kept
+// entry are paid once for both pixels; the launch picks PX from the grid size.
 //
 // Semantics of the reference's dense blend (src/train/renderers/dense.py:208-233):
 //   alpha_i = clamp(o_i exp(min(power_i, 0)), 0, alpha_clamp)     (dense.py:217-220)
@@ -18,6 +21,8 @@
 // so entries a pixel skips leave S unchanged and cost nothing.  A pair is skipped when its alpha
 // is below alpha_cutoff, or when q exceeds the Gaussian's threshold (alpha < max(cutoff, 2^-25));
 // a pixel stops once T falls below the transmittance threshold.
+#include <cstdlib>
+
 #include "gsb_common.cuh"
 #include "gsb_internal.h"
 
@@ -34,12 +39,32 @@ __device__ __forceinline__ float pair_q(float A, float B, float C, float dx, flo
   return __fmaf_rn(__fmul_rn(C, dy), dy, t1);
 }
 
-// Pixel block of warp w inside a TILE x TILE tile: 8 wide, 4 high.
-template <int TILE>
+// PX pixels per lane, 4 rows apart: the warp block is 8 wide and 4 * PX high.
+template <int PX>
+__host__ __device__ constexpr int block_h() { return 4 * PX; }
+
+// Pixel block of warp w inside a TILE x TILE tile.
+template <int TILE, int PX>
 __device__ __forceinline__ void block_of(int warp, int& bx, int& by) {
   constexpr int BX = TILE / 8;
   bx = (warp % BX) * 8;
-  by = (warp / BX) * 4;
+  by = (warp / BX) * block_h<PX>();
+}
+
+template <int PX>
+__device__ __forceinline__ bool all_of(const bool (&v)[PX]) {
+  bool r = true;
+#pragma unroll
+  for (int k = 0; k < PX; ++k) r = r && v[k];
+  return r;
+}
+
+template <int PX>
+__device__ __forceinline__ uint32_t max_of(const uint32_t (&v)[PX]) {
+  uint32_t r = 0;
+#pragma unroll
+  for (int k = 0; k < PX; ++k) r = max(r, v[k]);
+  return r;
 }
 
 struct WarpSlots {
@@ -50,8 +75,9 @@ struct WarpSlots {
 };
 
 // Lane loads list entry idx (list index li) into its warp slot and returns whether the Gaussian's
-// ellipse box {q <= tau} reaches the warp's pixel block [bx0, bx0+7] x [by0, by0+3] (pixel
+// ellipse {q <= tau} reaches the warp's pixel block [bx0, bx0+7] x [by0, by0+BH-1] (pixel
 // centres; conservative).
+template <int BH>
 __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* recs, uint32_t idx, uint32_t li,
                                            float bx0, float by0, const WarpSlots& s, int lane) {
   const uint32_t r = min(uint32_t(a.keys[idx]), uint32_t(a.G - 1));  // ranks are < G for valid keys
@@ -70,10 +96,11 @@ __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* rec
   // half extents of the ellipse: sqrt(tau (A^-1)_ii), (A^-1)_00 = C/det, (A^-1)_11 = A/det
   const float ex = sqrtf(tau * C / det) * 1.0001f + 0.01f;
   const float ey = sqrtf(tau * A / det) * 1.0001f + 0.01f;
-  if (!((r0.x + ex >= bx0) && (r0.x - ex <= bx0 + 7.0f) && (r0.y + ey >= by0) && (r0.y - ey <= by0 + 3.0f)))
+  constexpr float kH = float(BH - 1);
+  if (!((r0.x + ex >= bx0) && (r0.x - ex <= bx0 + 7.0f) && (r0.y + ey >= by0) && (r0.y - ey <= by0 + kH)))
     return false;
   // exact: the minimum of q over the block's pixel-centre box (on an edge unless the mean is inside)
-  const float X0 = bx0 - r0.x, X1 = bx0 + 7.0f - r0.x, Y0 = by0 - r0.y, Y1 = by0 + 3.0f - r0.y;
+  const float X0 = bx0 - r0.x, X1 = bx0 + 7.0f - r0.x, Y0 = by0 - r0.y, Y1 = by0 + kH - r0.y;
   if (X0 <= 0.0f && X1 >= 0.0f && Y0 <= 0.0f && Y1 >= 0.0f) return true;
   const float hC = -0.5f * B / C, hA = -0.5f * B / A;
   float q = __int_as_float(0x7f800000);
@@ -89,9 +116,9 @@ __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* rec
   return q <= tau * 1.0001f + 0.01f;
 }
 
-template <int TILE>
-__global__ void __launch_bounds__(TILE* TILE) raster_fwd_kernel(RasterArgs a) {
-  constexpr int NW = TILE * TILE / 32;
+template <int TILE, int PX>
+__global__ void __launch_bounds__(TILE* TILE / PX) raster_fwd_kernel(RasterArgs a) {
+  constexpr int NW = TILE * TILE / (32 * PX);
   __shared__ float4 s_geo[NW][32], s_cot[NW][32], s_col[NW][32];
   const RenderConsts& rc = a.rc;
   const uint32_t slot = blockIdx.y * uint32_t(rc.n_tiles) + blockIdx.x;
@@ -99,74 +126,90 @@ __global__ void __launch_bounds__(TILE* TILE) raster_fwd_kernel(RasterArgs a) {
   const int view = int(vt / uint32_t(rc.n_tiles)), tile = int(vt % uint32_t(rc.n_tiles));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int bx, by;
-  block_of<TILE>(warp, bx, by);
-  const int px = (tile % rc.tiles_x) * TILE + bx + (lane & 7);
-  const int py = (tile / rc.tiles_x) * TILE + by + (lane >> 3);
-  const float bx0 = float(px - (lane & 7)) + rc.pixel_center, by0 = float(py - (lane >> 3)) + rc.pixel_center;
-  const bool inside = px < a.W && py < a.H;
-  const float fx = float(px) + rc.pixel_center, fy = float(py) + rc.pixel_center;
+  block_of<TILE, PX>(warp, bx, by);
+  const int ox = (tile % rc.tiles_x) * TILE + bx, oy = (tile / rc.tiles_x) * TILE + by;  // block origin
+  const int px = ox + (lane & 7);
+  const float bx0 = float(ox) + rc.pixel_center, by0 = float(oy) + rc.pixel_center;
+  const float fx = float(px) + rc.pixel_center;
   const size_t rb = (size_t(view) * rc.n_tiles + tile) * 2;
   const uint32_t start = a.ranges[rb], end = a.ranges[rb + 1];
   const float* recs = a.records + size_t(view) * a.G * GSB_RECORD_FLOATS;
   const float inv_f0 = 1.0f / rc.f0;
   const WarpSlots ws{s_geo[warp], s_cot[warp], s_col[warp], nullptr};
 
-  float S = 1.0f, C0 = 0.0f, C1 = 0.0f, C2 = 0.0f, Ws = 0.0f, D = 0.0f;
-  uint32_t n_proc = end - start;
-  bool done = !inside;
+  int py[PX];
+  float fy[PX], S[PX], C0[PX], C1[PX], C2[PX], Ws[PX], D[PX];
+  uint32_t n_proc[PX];
+  bool done[PX];
+#pragma unroll
+  for (int k = 0; k < PX; ++k) {
+    py[k] = oy + (lane >> 3) + 4 * k;
+    fy[k] = float(py[k]) + rc.pixel_center;
+    S[k] = 1.0f, C0[k] = C1[k] = C2[k] = Ws[k] = D[k] = 0.0f;
+    n_proc[k] = end - start;
+    done[k] = !(px < a.W && py[k] < a.H);
+  }
   for (uint32_t c = start; c < end; c += 32) {
-    if (__all_sync(kFull, done)) break;
+    if (__all_sync(kFull, all_of(done))) break;
     const uint32_t idx = c + lane;
-    const bool keep = idx < end && load_entry(a, recs, idx, idx - start, bx0, by0, ws, lane);
+    const bool keep = idx < end && load_entry<block_h<PX>()>(a, recs, idx, idx - start, bx0, by0, ws, lane);
     uint32_t m = __ballot_sync(kFull, keep);
     __syncwarp();
-    while (m && !done) {
+    while (m && !all_of(done)) {
       const int j = __ffs(m) - 1;
       m &= m - 1;
       const float4 g = s_geo[warp][j];
       const float4 ct = s_cot[warp][j];
-      const float dx = __fsub_rn(fx, g.x), dy = __fsub_rn(fy, g.y);
-      const float q = pair_q(g.z, g.w, ct.x, dx, dy);
-      if (!(q <= ct.z)) continue;
-      const float e = __expf(fminf(-0.5f * q, 0.0f));
-      const float alpha = fminf(fmaxf(ct.y * e, 0.0f), rc.alpha_clamp);
-      if (!(alpha >= rc.alpha_cutoff)) continue;
-      const float4 col = s_col[warp][j];
-      const float T = S * ct.w;
-      const float w = T * alpha;
-      C0 = fmaf(w, col.x, C0);
-      C1 = fmaf(w, col.y, C1);
-      C2 = fmaf(w, col.z, C2);
-      Ws += w;
-      D = fmaf(w, col.w, D);
-      const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
-      S = S * (f * inv_f0);
-      if (T * f < rc.t_threshold) {  // T after this entry
-        done = true;
-        n_proc = c - start + uint32_t(j) + 1u;
+      const float dx = __fsub_rn(fx, g.x);
+#pragma unroll
+      for (int k = 0; k < PX; ++k) {
+        if (done[k]) continue;
+        const float dy = __fsub_rn(fy[k], g.y);
+        const float q = pair_q(g.z, g.w, ct.x, dx, dy);
+        if (!(q <= ct.z)) continue;
+        const float e = __expf(fminf(-0.5f * q, 0.0f));
+        const float alpha = fminf(fmaxf(ct.y * e, 0.0f), rc.alpha_clamp);
+        if (!(alpha >= rc.alpha_cutoff)) continue;
+        const float4 col = s_col[warp][j];
+        const float T = S[k] * ct.w;
+        const float w = T * alpha;
+        C0[k] = fmaf(w, col.x, C0[k]);
+        C1[k] = fmaf(w, col.y, C1[k]);
+        C2[k] = fmaf(w, col.z, C2[k]);
+        Ws[k] += w;
+        D[k] = fmaf(w, col.w, D[k]);
+        const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
+        S[k] = S[k] * (f * inv_f0);
+        if (T * f < rc.t_threshold) {  // T after this entry
+          done[k] = true;
+          n_proc[k] = c - start + uint32_t(j) + 1u;
+        }
       }
     }
     __syncwarp();  // slots are rewritten by the next chunk
   }
-  if (!inside) return;
   const size_t HW = size_t(a.H) * a.W;
-  const size_t poff = size_t(py) * a.W + px;
-  const size_t pix = size_t(view) * HW + poff;
-  const float wc = fminf(fmaxf(Ws, 0.0f), 1.0f);
-  const float one_m = __fsub_rn(1.0f, wc);
-  const float cc[3] = {C0, C1, C2};
-  uint32_t mask = (Ws >= 0.0f && Ws <= 1.0f) ? 8u : 0u;
 #pragma unroll
-  for (int ch = 0; ch < 3; ++ch) {
-    const float pre = __fadd_rn(cc[ch], __fmul_rn(one_m, rc.bg[ch]));
-    const bool pass = !rc.clamp_image || (pre >= 0.0f && pre <= 1.0f);
-    if (pass) mask |= 1u << ch;
-    a.image[(size_t(view) * 3 + ch) * HW + poff] = rc.clamp_image ? fminf(fmaxf(pre, 0.0f), 1.0f) : pre;
+  for (int k = 0; k < PX; ++k) {
+    if (!(px < a.W && py[k] < a.H)) continue;
+    const size_t poff = size_t(py[k]) * a.W + px;
+    const size_t pix = size_t(view) * HW + poff;
+    const float wc = fminf(fmaxf(Ws[k], 0.0f), 1.0f);
+    const float one_m = __fsub_rn(1.0f, wc);
+    const float cc[3] = {C0[k], C1[k], C2[k]};
+    uint32_t mask = (Ws[k] >= 0.0f && Ws[k] <= 1.0f) ? 8u : 0u;
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+      const float pre = __fadd_rn(cc[ch], __fmul_rn(one_m, rc.bg[ch]));
+      const bool pass = !rc.clamp_image || (pre >= 0.0f && pre <= 1.0f);
+      if (pass) mask |= 1u << ch;
+      a.image[(size_t(view) * 3 + ch) * HW + poff] = rc.clamp_image ? fminf(fmaxf(pre, 0.0f), 1.0f) : pre;
+    }
+    if (a.alpha) a.alpha[pix] = Ws[k];
+    if (a.depth) a.depth[pix] = D[k];
+    a.pixel_t[pix] = S[k];  // normalised transmittance after the last blended entry
+    a.pixel_state[pix] = min(n_proc[k], kCountMask) | (mask << kCountBits);
   }
-  if (a.alpha) a.alpha[pix] = Ws;
-  if (a.depth) a.depth[pix] = D;
-  a.pixel_t[pix] = S;  // normalised transmittance after the last blended entry
-  a.pixel_state[pix] = min(n_proc, kCountMask) | (mask << kCountBits);
 }
 
 // Warp sum of 10 per-lane values (v[10], v[11] are padding).  Afterwards lane l holds the total of
@@ -209,9 +252,9 @@ __device__ __forceinline__ float warp_sum10(float v[12], int lane, int* index) {
 // it the warp reduces first.
 constexpr int kSparseContributors = 4;
 
-template <int TILE, bool DEPTH>  // DEPTH: a depth gradient is given
-__global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
-  constexpr int NW = TILE * TILE / 32;
+template <int TILE, int PX, bool DEPTH>  // DEPTH: a depth gradient is given
+__global__ void __launch_bounds__(TILE* TILE / PX) raster_bwd_kernel(RasterArgs a) {
+  constexpr int NW = TILE * TILE / (32 * PX);
   __shared__ float4 s_geo[NW][32], s_cot[NW][32], s_col[NW][32];
   __shared__ uint32_t s_rank[NW][32];
   const RenderConsts& rc = a.rc;
@@ -220,12 +263,11 @@ __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
   const int view = int(vt / uint32_t(rc.n_tiles)), tile = int(vt % uint32_t(rc.n_tiles));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int bx, by;
-  block_of<TILE>(warp, bx, by);
-  const int px = (tile % rc.tiles_x) * TILE + bx + (lane & 7);
-  const int py = (tile / rc.tiles_x) * TILE + by + (lane >> 3);
-  const float bx0 = float(px - (lane & 7)) + rc.pixel_center, by0 = float(py - (lane >> 3)) + rc.pixel_center;
-  const bool inside = px < a.W && py < a.H;
-  const float fx = float(px) + rc.pixel_center, fy = float(py) + rc.pixel_center;
+  block_of<TILE, PX>(warp, bx, by);
+  const int ox = (tile % rc.tiles_x) * TILE + bx, oy = (tile / rc.tiles_x) * TILE + by;  // block origin
+  const int px = ox + (lane & 7);
+  const float bx0 = float(ox) + rc.pixel_center, by0 = float(oy) + rc.pixel_center;
+  const float fx = float(px) + rc.pixel_center;
   const size_t rb = (size_t(view) * rc.n_tiles + tile) * 2;
   const uint32_t start = a.ranges[rb];
   const float* recs = a.records + size_t(view) * a.G * GSB_RECORD_FLOATS;
@@ -233,30 +275,39 @@ __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
   const WarpSlots ws{s_geo[warp], s_cot[warp], s_col[warp], s_rank[warp]};
 
   const size_t HW = size_t(a.H) * a.W;
-  const size_t poff = size_t(py) * a.W + px;
-  const size_t pix = size_t(view) * HW + poff;
-  float S = 0.0f, g0 = 0.0f, g1 = 0.0f, g2c = 0.0f, gW = 0.0f, gD = 0.0f;
-  uint32_t n_proc = 0;
-  if (inside) {
-    S = a.pixel_t[pix];
-    const uint32_t st = a.pixel_state[pix];
-    n_proc = st & kCountMask;
-    const uint32_t mask = st >> kCountBits;
-    const float sc = a.view_scale ? a.view_scale[view] : 1.0f;
-    const float* di = a.d_image + size_t(view) * 3 * HW + poff;
-    g0 = (mask & 1u) ? di[0] * sc : 0.0f;
-    g1 = (mask & 2u) ? di[HW] * sc : 0.0f;
-    g2c = (mask & 4u) ? di[2 * HW] * sc : 0.0f;
-    gW = (mask & 8u) ? -(g0 * rc.bg[0] + g1 * rc.bg[1] + g2c * rc.bg[2]) : 0.0f;
-    if (a.d_alpha) gW += a.d_alpha[pix];
-    if (a.d_depth) gD = a.d_depth[pix];
+  float fy[PX], S[PX], g0[PX], g1[PX], g2c[PX], gW[PX], gD[PX];
+  float R0[PX], R1[PX], R2[PX], RW[PX], RD[PX];
+  uint32_t n_proc[PX];
+  const float sc = a.view_scale ? a.view_scale[view] : 1.0f;
+#pragma unroll
+  for (int k = 0; k < PX; ++k) {
+    const int py = oy + (lane >> 3) + 4 * k;
+    fy[k] = float(py) + rc.pixel_center;
+    S[k] = g0[k] = g1[k] = g2c[k] = gW[k] = gD[k] = 0.0f;
+    R0[k] = R1[k] = R2[k] = RW[k] = RD[k] = 0.0f;
+    n_proc[k] = 0;
+    if (px < a.W && py < a.H) {
+      const size_t poff = size_t(py) * a.W + px;
+      const size_t pix = size_t(view) * HW + poff;
+      S[k] = a.pixel_t[pix];
+      const uint32_t st = a.pixel_state[pix];
+      n_proc[k] = st & kCountMask;
+      const uint32_t mask = st >> kCountBits;
+      const float* di = a.d_image + size_t(view) * 3 * HW + poff;
+      g0[k] = (mask & 1u) ? di[0] * sc : 0.0f;
+      g1[k] = (mask & 2u) ? di[HW] * sc : 0.0f;
+      g2c[k] = (mask & 4u) ? di[2 * HW] * sc : 0.0f;
+      gW[k] = (mask & 8u) ? -(g0[k] * rc.bg[0] + g1[k] * rc.bg[1] + g2c[k] * rc.bg[2]) : 0.0f;
+      if (a.d_alpha) gW[k] += a.d_alpha[pix];
+      if (a.d_depth) gD[k] = a.d_depth[pix];
+    }
   }
-  const uint32_t wmax = __reduce_max_sync(kFull, n_proc);  // list prefix this warp has to revisit
+  // list prefix this warp has to revisit
+  const uint32_t wmax = __reduce_max_sync(kFull, max_of(n_proc));
 
-  float R0 = 0.0f, R1 = 0.0f, R2 = 0.0f, RW = 0.0f, RD = 0.0f;
   for (int64_t cb = wmax ? int64_t((wmax - 1) / 32) * 32 : -32; cb >= 0; cb -= 32) {
     const uint32_t li = uint32_t(cb) + lane;
-    const bool keep = li < wmax && load_entry(a, recs, start + li, li, bx0, by0, ws, lane);
+    const bool keep = li < wmax && load_entry<block_h<PX>()>(a, recs, start + li, li, bx0, by0, ws, lane);
     uint32_t m = __ballot_sync(kFull, keep);
     __syncwarp();
     while (m) {
@@ -266,51 +317,55 @@ __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
 #pragma unroll
       for (int k = 0; k < 12; ++k) v[k] = 0.0f;
       bool contrib = false;
-      if (uint32_t(cb) + uint32_t(j) < n_proc) {
+      const uint32_t lj = uint32_t(cb) + uint32_t(j);
+      if (lj < max_of(n_proc)) {
         const float4 g = s_geo[warp][j];
         const float4 ct = s_cot[warp][j];
-        const float dx = __fsub_rn(fx, g.x), dy = __fsub_rn(fy, g.y);
-        const float q = pair_q(g.z, g.w, ct.x, dx, dy);
-        if (q <= ct.z) {
+        const float dx = __fsub_rn(fx, g.x);
+#pragma unroll
+        for (int k = 0; k < PX; ++k) {
+          if (!(lj < n_proc[k])) continue;
+          const float dy = __fsub_rn(fy[k], g.y);
+          const float q = pair_q(g.z, g.w, ct.x, dx, dy);
+          if (!(q <= ct.z)) continue;
           const float e = __expf(fminf(-0.5f * q, 0.0f));
           const float araw = ct.y * e;
           const float alpha = fminf(fmaxf(araw, 0.0f), rc.alpha_clamp);
-          if (alpha >= rc.alpha_cutoff) {
-            const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
-            const float rf = __fdividef(1.0f, f);
-            S = S * (rc.f0 * rf);  // S before this entry: S_after / (f / F0)
-            const float T = S * ct.w;
-            const float4 col = s_col[warp][j];
-            const float w = T * alpha;
-            float dldw = g0 * col.x + g1 * col.y + g2c * col.z + gW;
-            float rsum = g0 * R0 + g1 * R1 + g2c * R2 + gW * RW;
-            if (DEPTH) {
-              dldw = fmaf(gD, col.w, dldw);
-              rsum = fmaf(gD, RD, rsum);
-              RD = fmaf(w, col.w, RD);
-            }
-            const float dlda = T * dldw - rsum * rf;
-            R0 = fmaf(w, col.x, R0);
-            R1 = fmaf(w, col.y, R1);
-            R2 = fmaf(w, col.z, R2);
-            RW += w;
-            const float dlr = (araw >= 0.0f && araw <= rc.alpha_clamp) ? dlda : 0.0f;
-            const float power = -0.5f * q;
-            const float pmask = power < 0.0f ? 1.0f : (power == 0.0f ? 0.5f : 0.0f);
-            const float dpow = dlr * araw * pmask;
-            const float u = dpow * dx, t = dpow * dy;
-            v[0] = g.z * u + 0.5f * g.w * t;
-            v[1] = ct.x * t + 0.5f * g.w * u;
-            v[2] = -0.5f * u * dx;
-            v[3] = -0.5f * u * dy;
-            v[4] = -0.5f * t * dy;
-            v[5] = dlr * e;
-            v[6] = g0 * w;
-            v[7] = g1 * w;
-            v[8] = g2c * w;
-            v[9] = DEPTH ? gD * w : 0.0f;
-            contrib = true;
+          if (!(alpha >= rc.alpha_cutoff)) continue;
+          const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
+          const float rf = __fdividef(1.0f, f);
+          S[k] = S[k] * (rc.f0 * rf);  // S before this entry: S_after / (f / F0)
+          const float T = S[k] * ct.w;
+          const float4 col = s_col[warp][j];
+          const float w = T * alpha;
+          float dldw = g0[k] * col.x + g1[k] * col.y + g2c[k] * col.z + gW[k];
+          float rsum = g0[k] * R0[k] + g1[k] * R1[k] + g2c[k] * R2[k] + gW[k] * RW[k];
+          if (DEPTH) {
+            dldw = fmaf(gD[k], col.w, dldw);
+            rsum = fmaf(gD[k], RD[k], rsum);
+            RD[k] = fmaf(w, col.w, RD[k]);
           }
+          const float dlda = T * dldw - rsum * rf;
+          R0[k] = fmaf(w, col.x, R0[k]);
+          R1[k] = fmaf(w, col.y, R1[k]);
+          R2[k] = fmaf(w, col.z, R2[k]);
+          RW[k] += w;
+          const float dlr = (araw >= 0.0f && araw <= rc.alpha_clamp) ? dlda : 0.0f;
+          const float power = -0.5f * q;
+          const float pmask = power < 0.0f ? 1.0f : (power == 0.0f ? 0.5f : 0.0f);
+          const float dpow = dlr * araw * pmask;
+          const float u = dpow * dx, t = dpow * dy;
+          v[0] += g.z * u + 0.5f * g.w * t;
+          v[1] += ct.x * t + 0.5f * g.w * u;
+          v[2] -= 0.5f * u * dx;
+          v[3] -= 0.5f * u * dy;
+          v[4] -= 0.5f * t * dy;
+          v[5] += dlr * e;
+          v[6] += g0[k] * w;
+          v[7] += g1[k] * w;
+          v[8] += g2c[k] * w;
+          if (DEPTH) v[9] += gD[k] * w;
+          contrib = true;
         }
       }
       const uint32_t cm = __ballot_sync(kFull, contrib);
@@ -332,10 +387,49 @@ __global__ void __launch_bounds__(TILE* TILE) raster_bwd_kernel(RasterArgs a) {
   }
 }
 
+// Threads per CTA: one per PX pixels of the tile (the kernels' shared arrays hold one slot set per
+// warp of exactly this many threads).
+template <int TILE, int PX>
+constexpr int raster_threads() { return TILE * TILE / PX; }
+static_assert(raster_threads<16, 2>() == 128 && raster_threads<8, 2>() == 32, "warp blocks must tile the tile");
+static_assert(raster_threads<16, 1>() == 256 && raster_threads<8, 1>() == 64, "warp blocks must tile the tile");
+
+// Two pixels per lane halve the per-pixel cost of list streaming, loop control and (backward)
+// the reductions, but give each tile half the warps and a longer serial walk, which loses while
+// the grid is too small to fill the GPU.  Measured on one B200 (16x16 tiles): the backward gains
+// from 4608 tiles up (8 x 384^2: 1.65 -> 1.53 ms; 32 x 1080p: 208 -> 164 ms) and loses at 1024
+// (16 x 128^2: 1.09 -> 1.14 ms); the forward, whose pixels also stop early, gains only on the
+// largest grids (32 x 1080p: 66 -> 60 ms; 8 x 384^2: 0.60 -> 0.69 ms).
+constexpr uint64_t kFwdPairedTiles = 32768;
+constexpr uint64_t kBwdPairedTiles = 2048;
+
+template <int TILE, int PX>
+static void fwd_launch(const RasterArgs& a, dim3 grid, cudaStream_t st) {
+  note_launch();
+  raster_fwd_kernel<TILE, PX><<<grid, raster_threads<TILE, PX>(), 0, st>>>(a);
+}
+
+template <int TILE, int PX>
+static void bwd_launch(const RasterArgs& a, dim3 grid, cudaStream_t st) {
+  note_launch();
+  if (a.d_depth) raster_bwd_kernel<TILE, PX, true><<<grid, raster_threads<TILE, PX>(), 0, st>>>(a);
+  else raster_bwd_kernel<TILE, PX, false><<<grid, raster_threads<TILE, PX>(), 0, st>>>(a);
+}
+
+// GSB200_RASTER_PX=1 or 2 forces the pixels per lane of both stages (tests and tuning); read at
+// every launch so that a process can switch it between calls.
+static bool paired_launch(uint64_t tiles, uint64_t threshold) {
+  const char* force = std::getenv("GSB200_RASTER_PX");
+  if (force && force[0] == '1' && force[1] == '\0') return false;
+  if (force && force[0] == '2' && force[1] == '\0') return true;
+  return tiles >= threshold;
+}
+
 gsb_status launch_raster_fwd(const RasterArgs& a, cudaStream_t st) {
   const dim3 grid(a.rc.n_tiles, a.B);
-  if (a.rc.tile == 16) { note_launch(); raster_fwd_kernel<16><<<grid, 256, 0, st>>>(a); }
-  else if (a.rc.tile == 8) { note_launch(); raster_fwd_kernel<8><<<grid, 64, 0, st>>>(a); }
+  const bool paired = paired_launch(uint64_t(a.rc.n_tiles) * uint64_t(a.B), kFwdPairedTiles);
+  if (a.rc.tile == 16) paired ? fwd_launch<16, 2>(a, grid, st) : fwd_launch<16, 1>(a, grid, st);
+  else if (a.rc.tile == 8) paired ? fwd_launch<8, 2>(a, grid, st) : fwd_launch<8, 1>(a, grid, st);
   else return GSB_ERR_ARG;
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
@@ -343,11 +437,9 @@ gsb_status launch_raster_fwd(const RasterArgs& a, cudaStream_t st) {
 gsb_status launch_raster_bwd(const RasterArgs& a, cudaStream_t st) {
   if (cudaMemsetAsync(a.grad2d, 0, size_t(a.B) * a.G * GSB_GRAD2D_FLOATS * sizeof(float), st)) return GSB_ERR_CUDA;
   const dim3 grid(a.rc.n_tiles, a.B);
-  const bool depth = a.d_depth != nullptr;
-  if (a.rc.tile == 16 && depth) { note_launch(); raster_bwd_kernel<16, true><<<grid, 256, 0, st>>>(a); }
-  else if (a.rc.tile == 16) { note_launch(); raster_bwd_kernel<16, false><<<grid, 256, 0, st>>>(a); }
-  else if (a.rc.tile == 8 && depth) { note_launch(); raster_bwd_kernel<8, true><<<grid, 64, 0, st>>>(a); }
-  else if (a.rc.tile == 8) { note_launch(); raster_bwd_kernel<8, false><<<grid, 64, 0, st>>>(a); }
+  const bool paired = paired_launch(uint64_t(a.rc.n_tiles) * uint64_t(a.B), kBwdPairedTiles);
+  if (a.rc.tile == 16) paired ? bwd_launch<16, 2>(a, grid, st) : bwd_launch<16, 1>(a, grid, st);
+  else if (a.rc.tile == 8) paired ? bwd_launch<8, 2>(a, grid, st) : bwd_launch<8, 1>(a, grid, st);
   else return GSB_ERR_ARG;
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
