@@ -7,6 +7,7 @@ stream.
 """
 from __future__ import annotations
 
+import threading
 from dataclasses import dataclass
 
 import torch
@@ -83,6 +84,37 @@ def _ws(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
+_PINNED = threading.local()
+
+
+class _Words:
+    """Device int32 words on their way to a pinned host buffer (see read_words)."""
+
+    def __init__(self, buf: torch.Tensor, n: int, event: torch.cuda.Event):
+        self.buf, self.n, self.event = buf, n, event
+
+    def wait(self) -> list[int]:
+        self.event.synchronize()
+        return self.buf[: self.n].tolist()
+
+
+def read_words(words: list[torch.Tensor]) -> _Words:
+    """Queues device->host copies of single int32 words (all on one device) behind that device's
+    current stream and returns at once; .wait() blocks until they have landed.  One pinned buffer
+    per host thread (each wait completes before that thread queues its next read)."""
+    buf = getattr(_PINNED, "buf", None)
+    if buf is None or buf.numel() < len(words):
+        buf = torch.empty(max(8, len(words)), dtype=torch.int32, pin_memory=True)
+        _PINNED.buf = buf
+    dev = words[0].device
+    with torch.cuda.device(dev):
+        for i, w in enumerate(words):
+            buf[i : i + 1].copy_(w, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(dev))
+    return _Words(buf, len(words), ev)
+
+
 def _f32(t: torch.Tensor | None) -> torch.Tensor | None:
     if t is None:
         return None
@@ -143,25 +175,28 @@ def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, n
                                                               records.data_ptr(), rects.data_ptr(),
                                                               offsets.data_ptr(), None, ws2.data_ptr(), ws2.numel(),
                                                               st))
-    # The one host synchronisation of the forward: pair count plus the device status words.
-    head = torch.cat([offsets[-1:], ws1.view(torch.int32)[:1], ws2.view(torch.int32)[:1]]).cpu().tolist()
-    n_pairs = head[0] & 0xFFFFFFFF
-    for name, code in (("gsb_depth_order", head[1]), ("gsb_preprocess_fwd", head[2])):
-        _lib.check(name, code)
+    # The one host synchronisation of the forward: the pair count plus the device status words,
+    # copied into pinned memory behind the kernels; everything that does not depend on the count
+    # is allocated while the GPU still works.
+    head = read_words([offsets[-1:], ws1.view(torch.int32)[:1], ws2.view(torch.int32)[:1]])
     n_tiles = -(-H // cfg.tile_size) * -(-W // cfg.tile_size)
-    keys = torch.empty(max(n_pairs, 1), dtype=torch.int64, device=dev)
     ranges = torch.empty(B * n_tiles * 2, dtype=torch.int32, device=dev)
     order = torch.empty(B * n_tiles, dtype=torch.int32, device=dev)
-    ws3 = _ws(L.gsb_bin_workspace(views, opts, G, n_pairs), dev)
-    with _stage("bin"):
-        _lib.check("gsb_bin", L.gsb_bin(views, opts, G, records.data_ptr(), rects.data_ptr(), offsets.data_ptr(),
-                                        n_pairs, keys.data_ptr(), ranges.data_ptr(), order.data_ptr(), ws3.data_ptr(),
-                                        ws3.numel(), st))
     image = torch.empty(B, 3, H, W, dtype=torch.float32, device=dev)
     alpha = torch.empty(B, H, W, dtype=torch.float32, device=dev)
     depth = torch.empty(B, H, W, dtype=torch.float32, device=dev) if cfg.depth else None
     pixel_t = torch.empty(B, H, W, dtype=torch.float32, device=dev)
     pixel_state = torch.empty(B, H, W, dtype=torch.int32, device=dev)
+    head = head.wait()
+    n_pairs = head[0] & 0xFFFFFFFF
+    for name, code in (("gsb_depth_order", head[1]), ("gsb_preprocess_fwd", head[2])):
+        _lib.check(name, code)
+    keys = torch.empty(max(n_pairs, 1), dtype=torch.int64, device=dev)
+    ws3 = _ws(L.gsb_bin_workspace(views, opts, G, n_pairs), dev)
+    with _stage("bin"):
+        _lib.check("gsb_bin", L.gsb_bin(views, opts, G, records.data_ptr(), rects.data_ptr(), offsets.data_ptr(),
+                                        n_pairs, keys.data_ptr(), ranges.data_ptr(), order.data_ptr(), ws3.data_ptr(),
+                                        ws3.numel(), st))
     with _stage("raster_fwd"):
         _lib.check("gsb_raster_fwd", L.gsb_raster_fwd(views, opts, G, records.data_ptr(), keys.data_ptr(),
                                                       ranges.data_ptr(), order.data_ptr(), image.data_ptr(),

@@ -22,7 +22,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from .render import FrameState, _stage, _stream, _ws
+from .render import FrameState, _stage, _stream, _ws, read_words
 
 CONIC = _lib.SPLATS2D_CONIC
 PACKED = _lib.SPLATS2D_PACKED
@@ -104,23 +104,24 @@ def forward_stages_2d(fmt: int, B: int, G: int, H: int, W: int, opt: Splat2DOpti
         _lib.check("gsb_splats2d_preprocess",
                    L.gsb_splats2d_preprocess(sp, H, W, opts, rank_of.data_ptr(), records.data_ptr(), rects.data_ptr(),
                                              offsets.data_ptr(), ws2.data_ptr(), ws2.numel(), st))
-    head = torch.cat([offsets[-1:], ws1.view(torch.int32)[:1], ws2.view(torch.int32)[:1]]).cpu().tolist()
+    head = read_words([offsets[-1:], ws1.view(torch.int32)[:1], ws2.view(torch.int32)[:1]])
+    n_tiles = -(-H // opt.tile_size) * -(-W // opt.tile_size)
+    ranges = torch.empty(B * n_tiles * 2, dtype=torch.int32, device=dev)
+    order = torch.empty(B * n_tiles, dtype=torch.int32, device=dev)
+    image = torch.empty(B, 3, H, W, dtype=torch.float32, device=dev)
+    alpha = torch.empty(B, H, W, dtype=torch.float32, device=dev)
+    pixel_t = torch.empty(B, H, W, dtype=torch.float32, device=dev)
+    pixel_state = torch.empty(B, H, W, dtype=torch.int32, device=dev)
+    head = head.wait()
     n_pairs = head[0] & 0xFFFFFFFF
     for name, code in (("gsb_splats2d_order", head[1]), ("gsb_splats2d_preprocess", head[2])):
         _lib.check(name, code)
-    n_tiles = -(-H // opt.tile_size) * -(-W // opt.tile_size)
     keys = torch.empty(max(n_pairs, 1), dtype=torch.int64, device=dev)
-    ranges = torch.empty(B * n_tiles * 2, dtype=torch.int32, device=dev)
-    order = torch.empty(B * n_tiles, dtype=torch.int32, device=dev)
     ws3 = _ws(L.gsb_bin_workspace(frame, opts, G, n_pairs), dev)
     with _stage("bin"):
         _lib.check("gsb_bin", L.gsb_bin(frame, opts, G, records.data_ptr(), rects.data_ptr(), offsets.data_ptr(),
                                         n_pairs, keys.data_ptr(), ranges.data_ptr(), order.data_ptr(),
                                         ws3.data_ptr(), ws3.numel(), st))
-    image = torch.empty(B, 3, H, W, dtype=torch.float32, device=dev)
-    alpha = torch.empty(B, H, W, dtype=torch.float32, device=dev)
-    pixel_t = torch.empty(B, H, W, dtype=torch.float32, device=dev)
-    pixel_state = torch.empty(B, H, W, dtype=torch.int32, device=dev)
     with _stage("raster_fwd"):
         _lib.check("gsb_raster_fwd", L.gsb_raster_fwd(frame, opts, G, records.data_ptr(), keys.data_ptr(),
                                                       ranges.data_ptr(), order.data_ptr(), image.data_ptr(),
