@@ -26,6 +26,13 @@ RENDER_TILED_COMPAT = 0x1
 RENDER_DEPTH = 0x2
 RENDER_NO_ELLIPSE = 0x4
 RENDER_NO_CLAMP = 0x8
+LENS_PINHOLE = 0
+LENS_RADIAL_TANGENTIAL = 1
+LENS_OPENCV_FISHEYE = 2
+LENS_CODES = {"pinhole": LENS_PINHOLE, "radial_tangential": LENS_RADIAL_TANGENTIAL,
+              "opencv_fisheye": LENS_OPENCV_FISHEYE}
+LENS_COEFFS = {"pinhole": 0, "radial_tangential": 5, "opencv_fisheye": 4}
+DISTORTION_FLOATS = 5
 SPLATS2D_CONIC = 0
 SPLATS2D_PACKED = 1
 RECORD_FLOATS = 12
@@ -44,7 +51,7 @@ class Scene(C.Structure):
 class Views(C.Structure):
     _fields_ = [
         ("n_views", C.c_int32), ("views_per_set", C.c_int32), ("height", C.c_int32), ("width", C.c_int32),
-        ("intrinsics", vp), ("camera_to_world", vp), ("times", vp),
+        ("intrinsics", vp), ("camera_to_world", vp), ("times", vp), ("lens_models", vp), ("distortion", vp),
     ]
 
 

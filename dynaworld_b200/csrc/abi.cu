@@ -47,6 +47,7 @@ static cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
 static gsb_status check_views(const gsb_views* v) {
   if (!v || !v->intrinsics || !v->camera_to_world) return GSB_ERR_ARG;
+  if (v->lens_models && !v->distortion) return GSB_ERR_ARG;
   if (v->n_views <= 0 || v->height <= 0 || v->width <= 0 || v->views_per_set <= 0) return GSB_ERR_SHAPE;
   return GSB_OK;
 }

@@ -63,21 +63,26 @@ struct Camera {
   float R[9];  // camera_to_world rotation, row-major: R[j*3+k] = c2w[j][k]
   float t[3];  // camera centre (world)
   Intrinsics k;
+  int lens;       // GSB_LENS_*
+  float dist[5];  // distortion coefficients (non-pinhole lenses)
 };
 
-__device__ inline Camera load_camera(const float* intr, const float* c2w, int b) {
+__device__ inline Camera load_camera(const gsb_views& vw, int b) {
   Camera c;
-  const float* m = c2w + b * 16;
+  const float* m = vw.camera_to_world + b * 16;
 #pragma unroll
   for (int j = 0; j < 3; ++j) {
 #pragma unroll
     for (int k = 0; k < 3; ++k) c.R[j * 3 + k] = m[j * 4 + k];
     c.t[j] = m[j * 4 + 3];
   }
-  c.k.fx = intr[b * 4 + 0];
-  c.k.fy = intr[b * 4 + 1];
-  c.k.cx = intr[b * 4 + 2];
-  c.k.cy = intr[b * 4 + 3];
+  c.k.fx = vw.intrinsics[b * 4 + 0];
+  c.k.fy = vw.intrinsics[b * 4 + 1];
+  c.k.cx = vw.intrinsics[b * 4 + 2];
+  c.k.cy = vw.intrinsics[b * 4 + 3];
+  c.lens = vw.lens_models ? vw.lens_models[b] : GSB_LENS_PINHOLE;
+#pragma unroll
+  for (int i = 0; i < 5; ++i) c.dist[i] = (c.lens != GSB_LENS_PINHOLE) ? vw.distortion[b * 5 + i] : 0.0f;
   return c;
 }
 

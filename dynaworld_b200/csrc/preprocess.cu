@@ -5,10 +5,13 @@
 // 149-231): quaternion -> rotation (:169-179), Sigma = (R S)(R S)^T (:181-187), world -> camera
 // (:39-51), near-plane mask keeping the depth slot with opacity 0 (:197-203), EWA Jacobian
 // (:210-214), +0.3 low-pass (:216-218), det clamp 1e-6 and inverse (:220-225), means2D (:227-229).
+// Views with a radial-tangential or fisheye lens take the pixel position and 2 x 3 Jacobian of
+// project_gaussians_2d_camera instead (src/train/renderers/projection.py:227-276; lens.cuh).
 // One thread per (view, Gaussian); outputs go to the Gaussian's depth-rank slot so that the
 // binning and raster stages read them in depth order.
 #include "gsb_common.cuh"
 #include "gsb_internal.h"
+#include "lens.cuh"
 #include "tiles.cuh"
 
 namespace gsb {
@@ -140,7 +143,7 @@ struct Proj {
   float Rq[9];         // Gaussian rotation
   float M[9];          // Rq diag(s)
   float cc[9];         // camera-space covariance
-  float J00, J02, J11, J12;
+  float J00, J01, J02, J10, J11, J12;  // d pixel / d camera point (J01 = J10 = 0 for pinhole)
   float c00, c01, c11; // 2-D covariance incl. the 0.3 low-pass
   float det_raw, det;
   float A, B, C;
@@ -182,24 +185,44 @@ __device__ inline void project(const GaussParams& p, const Camera& cam, float ne
   P.xp = P.front ? P.x : 0.0f;
   P.yp = P.front ? P.y : 0.0f;
   P.o_eff = p.o * (P.front ? 1.0f : 0.0f);
-  const float fx = cam.k.fx, fy = cam.k.fy;
-  const float zs2 = P.zs * P.zs;
-  P.J00 = fx / P.zs;
-  P.J02 = -(fx * P.xp) / zs2;
-  P.J11 = fy / P.zs;
-  P.J12 = -(fy * P.yp) / zs2;
   const float* c = P.cc;
-  P.c00 = P.J00 * P.J00 * c[0] + 2.0f * P.J00 * P.J02 * c[2] + P.J02 * P.J02 * c[8] + 0.3f;
-  P.c11 = P.J11 * P.J11 * c[4] + 2.0f * P.J11 * P.J12 * c[5] + P.J12 * P.J12 * c[8] + 0.3f;
-  P.c01 = P.J00 * P.J11 * c[1] + P.J00 * P.J12 * c[2] + P.J02 * P.J11 * c[5] + P.J02 * P.J12 * c[8];
+  if (cam.lens == GSB_LENS_PINHOLE) {  // common.py:200-215
+    const float fx = cam.k.fx, fy = cam.k.fy;
+    const float zs2 = P.zs * P.zs;
+    P.J00 = fx / P.zs;
+    P.J01 = P.J10 = 0.0f;
+    P.J02 = -(fx * P.xp) / zs2;
+    P.J11 = fy / P.zs;
+    P.J12 = -(fy * P.yp) / zs2;
+    P.c00 = P.J00 * P.J00 * c[0] + 2.0f * P.J00 * P.J02 * c[2] + P.J02 * P.J02 * c[8] + 0.3f;
+    P.c11 = P.J11 * P.J11 * c[4] + 2.0f * P.J11 * P.J12 * c[5] + P.J12 * P.J12 * c[8] + 0.3f;
+    P.c01 = P.J00 * P.J11 * c[1] + P.J00 * P.J12 * c[2] + P.J02 * P.J11 * c[5] + P.J02 * P.J12 * c[8];
+    P.mx = __fadd_rn(__fdiv_rn(__fmul_rn(fx, P.xp), P.zs), cam.k.cx);
+    P.my = __fadd_rn(__fdiv_rn(__fmul_rn(fy, P.yp), P.zs), cam.k.cy);
+  } else {  // projection.py:164-214, 253-263; behind the near plane the Jacobian is zero
+    const LensProjection<float> lp = lens_project<float>(P.xp, P.yp, P.zs, cam);
+    const float m = P.front ? 1.0f : 0.0f;
+    P.J00 = lp.J[0] * m, P.J01 = lp.J[1] * m, P.J02 = lp.J[2] * m;
+    P.J10 = lp.J[3] * m, P.J11 = lp.J[4] * m, P.J12 = lp.J[5] * m;
+    const float u[3] = {P.J00, P.J01, P.J02}, v[3] = {P.J10, P.J11, P.J12};
+    float tu[3], tv[3];  // (J cc) rows
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      tu[k] = u[0] * c[0 * 3 + k] + u[1] * c[1 * 3 + k] + u[2] * c[2 * 3 + k];
+      tv[k] = v[0] * c[0 * 3 + k] + v[1] * c[1 * 3 + k] + v[2] * c[2 * 3 + k];
+    }
+    P.c00 = tu[0] * u[0] + tu[1] * u[1] + tu[2] * u[2] + 0.3f;
+    P.c11 = tv[0] * v[0] + tv[1] * v[1] + tv[2] * v[2] + 0.3f;
+    P.c01 = tu[0] * v[0] + tu[1] * v[1] + tu[2] * v[2];
+    P.mx = lp.mx;
+    P.my = lp.my;
+  }
   P.det_raw = P.c00 * P.c11 - P.c01 * P.c01;
   P.det = fmaxf(P.det_raw, 1e-6f);
   P.A = P.c11 / P.det;
   P.C = P.c00 / P.det;
   const float inv01 = -P.c01 / P.det;
   P.B = inv01 + inv01;
-  P.mx = __fadd_rn(__fdiv_rn(__fmul_rn(fx, P.xp), P.zs), cam.k.cx);
-  P.my = __fadd_rn(__fdiv_rn(__fmul_rn(fy, P.yp), P.zs), cam.k.cy);
 }
 
 template <int K>
@@ -284,7 +307,7 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(gsb_scene sc, gsb_v
     const size_t g = i - size_t(b) * G;
     const size_t pg = size_t(b / vw.views_per_set) * G + g;
     const float t = vw.times ? vw.times[b] : 0.0f;
-    const Camera cam = load_camera(vw.intrinsics, vw.camera_to_world, b);
+    const Camera cam = load_camera(vw, b);
     const GaussParams p = load_params(sc, pg, t);
     Proj P;
     project(p, cam, rc.near_plane, P);
@@ -344,7 +367,9 @@ __device__ inline void quat_rot_vjp(const float q[4], const float G[9], float dq
   dq[3] = 2.0f * (-2.0f * k * G[0] - r * G[1] + i * G[2] + r * G[3] - 2.0f * k * G[4] + j * G[5] + i * G[6] + j * G[7]);
 }
 
-template <int K>  // K = SH coefficients per channel (1, 4, 9, 16) or 0 for plain rgb
+// K = SH coefficients per channel (1, 4, 9, 16) or 0 for plain rgb; LENS: some view has a
+// non-pinhole lens (the dual-number lens backward is compiled into these instances only)
+template <int K, bool LENS>
 __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_views vw, RenderConsts rc,
                                                              const int32_t* __restrict__ rank_of,
                                                              const float* __restrict__ grad2d, gsb_scene_grads gr) {
@@ -370,7 +395,7 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
       const float dcol[3] = {g2[6], g2[7], g2[8]};
       const float dzo = g2[9];
       const float t = vw.times ? vw.times[b] : 0.0f;
-      const Camera cam = load_camera(vw.intrinsics, vw.camera_to_world, b);
+      const Camera cam = load_camera(vw, b);
       const GaussParams p = load_params(sc, pg, t);
       Proj P;
       project(p, cam, rc.near_plane, P);
@@ -423,18 +448,20 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
       const float g00 = dC / det + ddet * P.c11;
       const float g11 = dA / det + ddet * P.c00;
       const float g01 = -2.0f * dB / det - 2.0f * ddet * P.c01;  // total over the two off-diagonals
-      // covariance = J cc J^T, J rows u = (J00, 0, J02), v = (0, J11, J12)
-      const float u[3] = {P.J00, 0.0f, P.J02}, v[3] = {0.0f, P.J11, P.J12};
+      // covariance = J cc J^T, J rows u = (J00, J01, J02), v = (J10, J11, J12)
+      const float u[3] = {P.J00, P.J01, P.J02}, v[3] = {P.J10, P.J11, P.J12};
       float cu[3], cv[3];
 #pragma unroll
       for (int a = 0; a < 3; ++a) {
         cu[a] = P.cc[a * 3 + 0] * u[0] + P.cc[a * 3 + 1] * u[1] + P.cc[a * 3 + 2] * u[2];
         cv[a] = P.cc[a * 3 + 0] * v[0] + P.cc[a * 3 + 1] * v[1] + P.cc[a * 3 + 2] * v[2];
       }
-      const float du0 = 2.0f * g00 * cu[0] + g01 * cv[0];
-      const float du2 = 2.0f * g00 * cu[2] + g01 * cv[2];
-      const float dv1 = 2.0f * g11 * cv[1] + g01 * cu[1];
-      const float dv2 = 2.0f * g11 * cv[2] + g01 * cu[2];
+      float du[3], dv[3];  // d loss / d J rows
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        du[k] = 2.0f * g00 * cu[k] + g01 * cv[k];
+        dv[k] = 2.0f * g11 * cv[k] + g01 * cu[k];
+      }
       float dcc[9];
 #pragma unroll
       for (int a = 0; a < 3; ++a)
@@ -442,13 +469,29 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
         for (int c = 0; c < 3; ++c)
           dcc[a * 3 + c] = g00 * u[a] * u[c] + g11 * v[a] * v[c] + 0.5f * g01 * (u[a] * v[c] + v[a] * u[c]);
       // Jacobian and means2D -> camera coordinates
-      const float fx = cam.k.fx, fy = cam.k.fy, zs = P.zs;
-      const float izs = 1.0f / zs, izs2 = izs * izs, izs3 = izs2 * izs;
-      const float dxp = du2 * (-fx * izs2) + dmx * fx * izs;
-      const float dyp = dv2 * (-fy * izs2) + dmy * fy * izs;
-      const float dzs = du0 * (-fx * izs2) + du2 * (2.0f * fx * P.xp * izs3) + dv1 * (-fy * izs2) +
-                        dv2 * (2.0f * fy * P.yp * izs3) + dmx * (-fx * P.xp * izs2) + dmy * (-fy * P.yp * izs2);
-      const float dmc[3] = {dxp, dyp, dzs + dzo};
+      float dmc[3];
+      if (!LENS || cam.lens == GSB_LENS_PINHOLE) {
+        const float fx = cam.k.fx, fy = cam.k.fy, zs = P.zs;
+        const float izs = 1.0f / zs, izs2 = izs * izs, izs3 = izs2 * izs;
+        dmc[0] = du[2] * (-fx * izs2) + dmx * fx * izs;
+        dmc[1] = dv[2] * (-fy * izs2) + dmy * fy * izs;
+        dmc[2] = du[0] * (-fx * izs2) + du[2] * (2.0f * fx * P.xp * izs3) + dv[1] * (-fy * izs2) +
+                 dv[2] * (2.0f * fy * P.yp * izs3) + dmx * (-fx * P.xp * izs2) + dmy * (-fy * P.yp * izs2);
+      } else {
+        // forward-mode derivatives of the pixel and of every Jacobian entry along x, y, z
+        const LensProjection<Dual3> lp = lens_project<Dual3>(dual(P.xp, 1.0f, 0.0f, 0.0f),
+                                                             dual(P.yp, 0.0f, 1.0f, 0.0f),
+                                                             dual(P.zs, 0.0f, 0.0f, 1.0f), cam);
+        const float dJ[6] = {du[0], du[1], du[2], dv[0], dv[1], dv[2]};
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+          float acc = dmx * lp.mx.d[k] + dmy * lp.my.d[k];
+#pragma unroll
+          for (int e = 0; e < 6; ++e) acc += dJ[e] * lp.J[e].d[k];
+          dmc[k] = acc;
+        }
+      }
+      dmc[2] += dzo;
       // camera -> world: mc = Rcw^T d, cc = Rcw^T S Rcw
 #pragma unroll
       for (int j = 0; j < 3; ++j)
@@ -544,6 +587,19 @@ gsb_status launch_preprocess_fwd(const gsb_scene& sc, const gsb_views& vw, const
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 
+template <bool LENS>
+static void launch_bwd_for_degree(int deg, int grid, const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
+                                  const int32_t* rank_of, const float* grad2d, const gsb_scene_grads& gr,
+                                  cudaStream_t st) {
+  switch (deg) {
+    case -1: preprocess_bwd_kernel<0, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
+    case 0: preprocess_bwd_kernel<1, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
+    case 1: preprocess_bwd_kernel<4, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
+    case 2: preprocess_bwd_kernel<9, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
+    default: preprocess_bwd_kernel<16, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
+  }
+}
+
 gsb_status launch_preprocess_bwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
                                  const int32_t* rank_of, const float* grad2d, const gsb_scene_grads& gr,
                                  cudaStream_t st) {
@@ -551,14 +607,10 @@ gsb_status launch_preprocess_bwd(const gsb_scene& sc, const gsb_views& vw, const
   const int grid = grid_for(n, 128);
   const bool raw = sc.flags & GSB_SCENE_RAW;
   const int deg = raw ? sc.sh_degree : -1;
-  switch (deg) {
-    case -1: { note_launch(); preprocess_bwd_kernel<0><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); } break;
-    case 0: { note_launch(); preprocess_bwd_kernel<1><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); } break;
-    case 1: { note_launch(); preprocess_bwd_kernel<4><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); } break;
-    case 2: { note_launch(); preprocess_bwd_kernel<9><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); } break;
-    case 3: { note_launch(); preprocess_bwd_kernel<16><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); } break;
-    default: return GSB_ERR_ARG;
-  }
+  if (deg < -1 || deg > 3) return GSB_ERR_ARG;
+  note_launch();
+  if (vw.lens_models) launch_bwd_for_degree<true>(deg, grid, sc, vw, rc, rank_of, grad2d, gr, st);
+  else launch_bwd_for_degree<false>(deg, grid, sc, vw, rc, rank_of, grad2d, gr, st);
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 

@@ -140,13 +140,20 @@ def scene_struct(spec: SceneSpec, means, scales, quats, opacities, colors, veloc
     return s
 
 
-def views_struct(spec: ViewSpec, intrinsics, camera_to_world, times) -> _lib.Views:
+def views_struct(spec: ViewSpec, intrinsics, camera_to_world, times, lens_models=None, distortion=None) -> _lib.Views:
     v = _lib.Views()
     v.n_views, v.views_per_set, v.height, v.width = spec.n_views, spec.views_per_set, spec.height, spec.width
     v.intrinsics = intrinsics.data_ptr()
     v.camera_to_world = camera_to_world.data_ptr()
     v.times = times.data_ptr() if times is not None else None
+    v.lens_models = lens_models.data_ptr() if lens_models is not None else None
+    v.distortion = distortion.data_ptr() if lens_models is not None else None
     return v
+
+
+def _views_of(vspec: ViewSpec, tensors: dict) -> _lib.Views:
+    return views_struct(vspec, tensors["intrinsics"], tensors["camera_to_world"], tensors.get("times"),
+                        tensors.get("lens_models"), tensors.get("distortion"))
 
 
 def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, near_plane: float,
@@ -157,7 +164,7 @@ def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, n
     B, G, H, W = vspec.n_views, sspec.n_gaussians, vspec.height, vspec.width
     scene = scene_struct(sspec, tensors["means"], tensors["scales"], tensors["quats"], tensors["opacities"],
                          tensors["colors"], tensors.get("velocity"))
-    views = views_struct(vspec, tensors["intrinsics"], tensors["camera_to_world"], tensors.get("times"))
+    views = _views_of(vspec, tensors)
     opts = cfg.options(near_plane)
 
     sorted_ids = torch.empty(B * G, dtype=torch.int32, device=dev)
@@ -218,7 +225,7 @@ def backward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, 
     B, G = vspec.n_views, sspec.n_gaussians
     scene = scene_struct(sspec, tensors["means"], tensors["scales"], tensors["quats"], tensors["opacities"],
                          tensors["colors"], tensors.get("velocity"))
-    views = views_struct(vspec, tensors["intrinsics"], tensors["camera_to_world"], tensors.get("times"))
+    views = _views_of(vspec, tensors)
     opts = cfg.options(near_plane)
     grad2d = torch.empty(B * G * _lib.GRAD2D_FLOATS, dtype=torch.float32, device=dev)
     with _stage("raster_bwd"):
@@ -249,13 +256,15 @@ class _RenderFunction(torch.autograd.Function):
     scene tensors.  Camera tensors get no gradient (the forward refuses cameras that need one)."""
 
     @staticmethod
-    def forward(ctx, sspec, vspec, cfg, near_plane, means, scales, quats, opacities, colors, velocity, intrinsics,
-                camera_to_world, times):
+    def forward(ctx, sspec, vspec, cfg, near_plane, lens, means, scales, quats, opacities, colors, velocity,
+                intrinsics, camera_to_world, times):
         tensors = {
             "means": _f32(means), "scales": _f32(scales), "quats": _f32(quats), "opacities": _f32(opacities),
             "colors": _f32(colors), "velocity": _f32(velocity), "intrinsics": _f32(intrinsics),
             "camera_to_world": _f32(camera_to_world), "times": _f32(times),
         }
+        if lens is not None:
+            tensors["lens_models"], tensors["distortion"] = lens
         image, alpha, depth, state = forward_stages(sspec, vspec, cfg, near_plane, tensors)
         ctx.sspec, ctx.vspec, ctx.cfg, ctx.near_plane = sspec, vspec, cfg, near_plane
         ctx.tensors = tensors
@@ -285,7 +294,7 @@ class _RenderFunction(torch.autograd.Function):
             else:
                 out.append(grads[name].reshape(shp[0]).to(shp[1]))
         ctx.state = None
-        return (None, None, None, None, *out, None, None, None)
+        return (None, None, None, None, None, *out, None, None, None)
 
 
 def _check_cameras_no_grad(*tensors):
@@ -297,11 +306,51 @@ def _check_cameras_no_grad(*tensors):
             )
 
 
+def lens_tensors(lens_models, distortion, n_views: int, device):
+    """(int32 [B] GSB_LENS_* codes, float32 [B,5] coefficients) on ``device``, or None when every
+    view is pinhole.  ``lens_models`` holds names ("pinhole", "radial_tangential",
+    "opencv_fisheye") or codes; ``distortion`` per-view coefficient lists (None: zeros)."""
+    if lens_models is None:
+        return None
+    if torch.is_tensor(lens_models):
+        codes = [int(c) for c in lens_models.reshape(-1).tolist()]
+    else:
+        for m in lens_models:
+            if isinstance(m, str) and m not in _lib.LENS_CODES:
+                raise ValueError(f"Unknown lens_model: {m}")  # projection.py:203-204
+        codes = [_lib.LENS_CODES[m] if isinstance(m, str) else int(m) for m in lens_models]
+    if len(codes) != n_views:
+        raise ValueError(f"expected {n_views} lens models, got {len(codes)}")
+    if any(c not in _lib.LENS_CODES.values() for c in codes):
+        raise ValueError(f"unknown lens model code in {codes}")
+    if all(c == _lib.LENS_PINHOLE for c in codes):
+        return None
+    coeffs = torch.zeros(n_views, _lib.DISTORTION_FLOATS, dtype=torch.float32)
+    if distortion is not None:
+        if torch.is_tensor(distortion) and distortion.ndim == 2:
+            rows = list(distortion.detach().cpu().to(torch.float32))
+        else:
+            rows = list(distortion)
+        if len(rows) != n_views:
+            raise ValueError(f"expected {n_views} distortion rows, got {len(rows)}")
+        names = {v: k for k, v in _lib.LENS_CODES.items()}
+        for b, (code, row) in enumerate(zip(codes, rows)):
+            if row is None or code == _lib.LENS_PINHOLE:  # pinhole views ignore distortion
+                continue
+            r = torch.as_tensor(row, dtype=torch.float32).flatten().cpu()
+            limit = _lib.LENS_COEFFS[names[code]]
+            if r.numel() > limit:  # projection.py:38-50 (_distortion_tensor)
+                raise ValueError(f"{names[code]} expects at most {limit} distortion coefficients, got {r.numel()}.")
+            coeffs[b, : r.numel()] = r
+    return (torch.tensor(codes, dtype=torch.int32, device=device).contiguous(), coeffs.to(device).contiguous())
+
+
 def render_scene(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, near_plane: float, *, means, scales,
-                 quats, opacities, colors, velocity, intrinsics, camera_to_world, times):
-    """Autograd entry used by every public render function."""
+                 quats, opacities, colors, velocity, intrinsics, camera_to_world, times, lens=None):
+    """Autograd entry used by every public render function.  ``lens``: the pair lens_tensors()
+    returns, or None for pinhole views only."""
     if not means.is_cuda:
         raise RuntimeError("the b200 renderer runs on CUDA devices only (got a tensor on %s)" % means.device)
     _check_cameras_no_grad(intrinsics, camera_to_world, times)
-    return _RenderFunction.apply(sspec, vspec, cfg, float(near_plane), means, scales, quats, opacities, colors,
+    return _RenderFunction.apply(sspec, vspec, cfg, float(near_plane), lens, means, scales, quats, opacities, colors,
                                  velocity, intrinsics, camera_to_world, times)

@@ -11,8 +11,9 @@ from __future__ import annotations
 
 import torch
 
+from . import _lib
 from .config import B200RendererConfig
-from .render import MIN_RENDER_DEPTH, SceneSpec, ViewSpec, render_scene
+from .render import MIN_RENDER_DEPTH, SceneSpec, ViewSpec, lens_tensors, render_scene
 
 
 def _per_view(value, K: int, device) -> torch.Tensor:
@@ -26,20 +27,24 @@ def _intrinsics(fx, fy, cx, cy, K, device) -> torch.Tensor:
     return torch.stack([_per_view(v, K, device) for v in (fx, fy, cx, cy)], dim=-1).contiguous()
 
 
-def _check_projection(projection_mode: str, cameras) -> None:
-    """Pinhole projection only.  ``camera_model`` with all-pinhole cameras is the same projection
-    (src/train/renderers/projection.py delegates it to common.py); other lens models are not
-    implemented by this renderer and are refused."""
+def _lens_of(projection_mode: str, cameras, K: int, device):
+    """Lens models of the views.  ``legacy_pinhole`` projects every view as a pinhole
+    (common.py); ``camera_model`` takes each CameraSpec's lens_model and distortion
+    (projection.py:227-330: pinhole views keep the common.py projection)."""
     if projection_mode == "legacy_pinhole":
-        return
+        return None
     if projection_mode != "camera_model":
         raise ValueError(f"Unknown projection_mode: {projection_mode}")
     cams = list(cameras) if isinstance(cameras, (list, tuple)) else ([cameras] if cameras is not None else [])
     if not cams:
         raise ValueError("camera_model projection requires CameraSpec values.")
-    lens = sorted({getattr(c, "lens_model", "pinhole") for c in cams})
-    if lens != ["pinhole"]:
-        raise NotImplementedError(f"the b200 renderer supports pinhole cameras only (lens models: {lens}).")
+    if len(cams) != K:
+        raise ValueError(f"Expected {K} cameras, got {len(cams)}.")
+    models = [getattr(c, "lens_model", "pinhole") for c in cams]
+    for m in models:
+        if m not in _lib.LENS_CODES:
+            raise ValueError(f"Unknown lens_model: {m}")
+    return lens_tensors(models, [getattr(c, "distortion", None) for c in cams], K, device)
 
 
 def render_b200_3dgs_batch(
@@ -63,10 +68,10 @@ def render_b200_3dgs_batch(
 ) -> torch.Tensor:
     """[K,G,3] means, [K,G,3] scales, [K,G,4] quaternions, [K,G,1] opacities, [K,G,3] rgbs and
     per-frame intrinsics / camera_to_world [K,4,4] -> image [K,3,H,W] in [0,1]."""
-    _check_projection(projection_mode, cameras)
     config = config or B200RendererConfig()
     K, G = int(means3d.shape[0]), int(means3d.shape[1])
     dev = means3d.device
+    lens = _lens_of(projection_mode, cameras, K, dev)
     intr = _intrinsics(fx, fy, cx, cy, K, dev)
     if camera_to_world is None:
         c2w = torch.eye(4, device=dev, dtype=torch.float32).expand(K, 4, 4).contiguous()
@@ -78,7 +83,7 @@ def render_b200_3dgs_batch(
     image, _alpha, _depth = render_scene(
         sspec, vspec, config, near_plane, means=means3d, scales=scales, quats=quats,
         opacities=opacities.reshape(K, G), colors=rgbs, velocity=None, intrinsics=intr, camera_to_world=c2w,
-        times=None,
+        times=None, lens=lens,
     )
     return image
 
@@ -127,6 +132,8 @@ def render_b200(
     views_per_set: int | None = None,
     near_plane: float = MIN_RENDER_DEPTH,
     config: B200RendererConfig | None = None,
+    lens_models=None,
+    distortion=None,
 ):
     """Raw-parameter render.
 
@@ -134,8 +141,11 @@ def render_b200(
     or [S,G], sh [S,G,(d+1)^2,3] (rgb = SH(view dir) + 0.5), velocity [S,G,3] with times [B]
     (means_t = means + t * velocity).  View b uses set b // views_per_set (default: all views
     share set 0 when S == 1, else B // S views per set).  intrinsics [B,4] = fx, fy, cx, cy;
-    camera_to_world [B,4,4].  Returns image [B,3,H,W], alpha [B,H,W] (sum of blend weights) and
-    depth [B,H,W] (sum of weight * camera z; None unless ``config.depth``).
+    camera_to_world [B,4,4].  ``lens_models`` (per view: "pinhole", "radial_tangential",
+    "opencv_fisheye", or their GSB_LENS_* codes) with ``distortion`` (per view [k1, k2, p1, p2, k3]
+    or [k1, k2, k3, k4]) project as project_gaussians_2d_camera does.  Returns image [B,3,H,W],
+    alpha [B,H,W] (sum of blend weights) and depth [B,H,W] (sum of weight * camera z; None unless
+    ``config.depth``).
     """
     config = config or B200RendererConfig()
     if means.ndim == 2:
@@ -161,5 +171,6 @@ def render_b200(
         sspec, vspec, config, near_plane, means=means, scales=log_scales, quats=quats,
         opacities=opacity_logits.reshape(S, G), colors=sh, velocity=velocity,
         intrinsics=intrinsics.reshape(B, 4), camera_to_world=camera_to_world, times=times,
+        lens=lens_tensors(lens_models, distortion, B, means.device),
     )
     return image, alpha, (depth if config.depth else None)

@@ -11,7 +11,9 @@
  *   gsb_depth_order      <- the stable argsort by camera z of
  *                           renderers/common.py:190-195 (project_gaussians_2d_batch)
  *   gsb_preprocess_fwd   <- renderers/common.py:149-231 (projection, EWA covariance,
- *                           near-plane mask) plus raw-parameter activation / SH / time offset
+ *                           near-plane mask) and, per view, the lens models of
+ *                           renderers/projection.py:164-330 (project_gaussians_2d_camera[_batch]),
+ *                           plus raw-parameter activation / SH / time offset
  *                           (the model head of gs_models/blocks.py:172-186), and the per-Gaussian
  *                           tile bounds of renderers/tiled.py:7-28
  *   gsb_bin              <- renderers/tiled.py:31-71 (build_tile_assignments: tile lists in
@@ -79,6 +81,11 @@ typedef struct gsb_scene {
   const float* velocity;  /* [S,G,3] with GSB_SCENE_VELOCITY, else NULL */
 } gsb_scene;
 
+/* Lens models (gsb_views.lens_models), the CameraSpec lens_model values of camera.py:7-31. */
+#define GSB_LENS_PINHOLE 0            /* common.py:149-231 projection */
+#define GSB_LENS_RADIAL_TANGENTIAL 1  /* distortion k1, k2, p1, p2, k3 (projection.py:93-116) */
+#define GSB_LENS_OPENCV_FISHEYE 2     /* distortion k1, k2, k3, k4, 0 (projection.py:119-161) */
+
 /* Views (cameras). */
 typedef struct gsb_views {
   int32_t n_views;
@@ -88,6 +95,8 @@ typedef struct gsb_views {
   const float* intrinsics;      /* [B,4] fx, fy, cx, cy (device) */
   const float* camera_to_world; /* [B,4,4] row-major, camera +z is the optical axis (device) */
   const float* times;           /* [B] or NULL (device) */
+  const int32_t* lens_models;   /* [B] GSB_LENS_* or NULL: every view pinhole (device) */
+  const float* distortion;      /* [B,5] coefficients (zero-padded), read for non-pinhole views */
 } gsb_views;
 
 typedef struct gsb_options {

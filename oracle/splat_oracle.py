@@ -7,6 +7,8 @@ oracle).  Citations are to files of nbardy/dynaworld.
 
 Reference semantics restated:
   * projection  src/train/renderers/common.py:149-231 (project_gaussians_2d_batch)
+  * lenses      src/train/renderers/projection.py:75-214 (camera_model projection:
+                radial-tangential and OpenCV fisheye distortion, closed-form Jacobians)
   * dense blend src/train/renderers/dense.py:170-236  (render_pytorch_3dgs_batch)
   * loss        src/train/losses.py:13-85             (ssim_per_image,
                 reconstruction_loss_per_image)
@@ -181,6 +183,50 @@ def camera_depth_fp32(means: torch.Tensor, camera_to_world: torch.Tensor) -> tor
     return fma_f32(d[..., 2], r2, fma_f32(d[..., 1], r1, p0)).reshape(shape)
 
 
+def lens_distort(x: torch.Tensor, y: torch.Tensor, lens: str, c: torch.Tensor):
+    """Distorted normalised coordinates and the closed-form lens Jacobian [...,2,2] of
+    projection.py:93-116 (radial_tangential, c = k1, k2, p1, p2, k3) and :119-161
+    (opencv_fisheye, c = k1, k2, k3, k4)."""
+    if lens == "radial_tangential":
+        k1, k2, p1, p2, k3 = (c[i] for i in range(5))
+        r2 = x * x + y * y
+        r4 = r2 * r2
+        r6 = r4 * r2
+        radial = 1.0 + k1 * r2 + k2 * r4 + k3 * r6
+        xd = x * radial + 2.0 * p1 * x * y + p2 * (r2 + 2.0 * x * x)
+        yd = y * radial + p1 * (r2 + 2.0 * y * y) + 2.0 * p2 * x * y
+        rd = k1 + 2.0 * k2 * r2 + 3.0 * k3 * r4
+        rdx, rdy = 2.0 * x * rd, 2.0 * y * rd
+        l00 = radial + x * rdx + 2.0 * p1 * y + 6.0 * p2 * x
+        l01 = x * rdy + 2.0 * p1 * x + 2.0 * p2 * y
+        l10 = y * rdx + 2.0 * p1 * x + 2.0 * p2 * y
+        l11 = radial + y * rdy + 6.0 * p1 * y + 2.0 * p2 * x
+    elif lens == "opencv_fisheye":
+        k1, k2, k3, k4 = (c[i] for i in range(4))
+        eps = 1.0e-8
+        r2 = x * x + y * y
+        radius = torch.sqrt(torch.clamp(r2, min=eps * eps))
+        theta = torch.atan(radius)
+        t2 = theta * theta
+        t4 = t2 * t2
+        t6 = t4 * t2
+        t8 = t4 * t4
+        theta_d = theta * (1.0 + k1 * t2 + k2 * t4 + k3 * t6 + k4 * t8)
+        valid = r2 > eps * eps
+        scale = torch.where(valid, theta_d / radius, torch.ones_like(radius))
+        xd, yd = scale * x, scale * y
+        dtd = 1.0 + 3.0 * k1 * t2 + 5.0 * k2 * t4 + 7.0 * k3 * t6 + 9.0 * k4 * t8
+        dtdr = 1.0 / (1.0 + radius * radius)
+        dsdr = torch.where(valid, (dtd * dtdr * radius - theta_d) / (radius * radius), torch.zeros_like(radius))
+        inv_r = torch.where(valid, 1.0 / radius, torch.zeros_like(radius))
+        dsdx, dsdy = dsdr * x * inv_r, dsdr * y * inv_r
+        l00, l01, l10, l11 = scale + x * dsdx, x * dsdy, y * dsdx, scale + y * dsdy
+    else:
+        raise ValueError(f"Unknown lens_model: {lens}")
+    lj = torch.stack([torch.stack([l00, l01], -1), torch.stack([l10, l11], -1)], -2)
+    return xd, yd, lj
+
+
 def project_batch(
     means: torch.Tensor,
     scales: torch.Tensor,
@@ -194,8 +240,12 @@ def project_batch(
     camera_to_world: torch.Tensor,
     near_plane: float = MIN_RENDER_DEPTH,
     sort_key: torch.Tensor | None = None,
+    lens_models: list[str] | None = None,
+    distortion: torch.Tensor | None = None,
 ):
-    """Restates project_gaussians_2d_batch (common.py:149-231).
+    """Restates project_gaussians_2d_batch (common.py:149-231); views whose ``lens_models`` entry
+    is not "pinhole" take the pixel position and Jacobian of project_gaussians_2d_camera
+    (projection.py:75-90, 164-214, 253-263) with ``distortion[b]`` (zero-padded to 5).
 
     Returns, in per-view depth order: means2d [B,G,2], inv_cov [B,G,2,2],
     cov2d [B,G,2,2], opacity [B,G,1] (zeroed behind the near plane), rgb
@@ -239,6 +289,24 @@ def project_batch(
         ],
         dim=-2,
     )
+    means2d = torch.stack([(fx * xp) / z_safe + cx, (fy * yp) / z_safe + cy], -1)
+    if lens_models is not None and any(m != "pinhole" for m in lens_models):
+        jac_rows, m2_rows = [], []
+        for b, lens in enumerate(lens_models):
+            if lens == "pinhole":
+                jac_rows.append(jac[b])
+                m2_rows.append(means2d[b])
+                continue
+            zs = z_safe[b]
+            nj = torch.stack([torch.stack([1.0 / zs, torch.zeros_like(zs), -xp[b] / (zs ** 2)], -1),
+                              torch.stack([torch.zeros_like(zs), 1.0 / zs, -yp[b] / (zs ** 2)], -1)], -2)
+            nj = nj * front[b].to(dtype).view(-1, 1, 1)
+            xd, yd, lj = lens_distort(xp[b] / zs, yp[b] / zs, lens, distortion[b].to(dtype))
+            kj = torch.zeros(2, 2, dtype=dtype)
+            kj[0, 0], kj[1, 1] = fx[b, 0], fy[b, 0]
+            jac_rows.append(kj @ lj @ nj)
+            m2_rows.append(torch.stack([fx[b, 0] * xd + cx[b, 0], fy[b, 0] * yd + cy[b, 0]], -1))
+        jac, means2d = torch.stack(jac_rows), torch.stack(m2_rows)
     cov2 = jac @ cov_cam @ jac.transpose(-1, -2)
     cov2 = cov2 + 0.3 * torch.eye(2, dtype=dtype)  # EWA low-pass, common.py:216-218
     det = torch.clamp(cov2[..., 0, 0] * cov2[..., 1, 1] - cov2[..., 0, 1] * cov2[..., 1, 0], min=1e-6)
@@ -249,7 +317,6 @@ def project_batch(
         ],
         dim=-2,
     )
-    means2d = torch.stack([(fx * xp) / z_safe + cx, (fy * yp) / z_safe + cy], -1)
     return means2d, inv, cov2, opacities, rgbs, z, order
 
 
@@ -319,12 +386,12 @@ def blend_dense(
 def render_dense(
     means, scales, quats, opacities, rgbs, H, W, fx, fy, cx, cy, camera_to_world,
     *, near_plane=MIN_RENDER_DEPTH, pixel_center=0.0, eps=1e-6, alpha_clamp=0.99,
-    background=(1.0, 1.0, 1.0), sort_key=None, x0=0, y0=0,
+    background=(1.0, 1.0, 1.0), sort_key=None, x0=0, y0=0, lens_models=None, distortion=None,
 ):
     """Projection + dense blend: render_pytorch_3dgs_batch restated (dense.py:170-236)."""
     m2, inv, _cov, op, rgb, z, _order = project_batch(
         means, scales, quats, opacities, rgbs, fx, fy, cx, cy, camera_to_world,
-        near_plane=near_plane, sort_key=sort_key,
+        near_plane=near_plane, sort_key=sort_key, lens_models=lens_models, distortion=distortion,
     )
     return blend_dense(
         m2, inv, op, rgb, z, H, W, pixel_center=pixel_center, eps=eps,

@@ -16,7 +16,8 @@ def intrinsics_of(wl, device=DEV):
     return torch.stack([wl.fx, wl.fy, wl.cx, wl.cy], -1).to(device)
 
 
-def render_raw(wl, cfg: B200RendererConfig | None = None, *, grads=True, loss=True, device=DEV):
+def render_raw(wl, cfg: B200RendererConfig | None = None, *, grads=True, loss=True, device=DEV, lens_models=None,
+               distortion=None):
     """render_b200 + reconstruction_loss_per_image on the GPU; returns a dict of CPU tensors."""
     cfg = cfg or B200RendererConfig()
     leaves = {k: getattr(wl, k).to(device).requires_grad_(grads) for k in
@@ -26,7 +27,7 @@ def render_raw(wl, cfg: B200RendererConfig | None = None, *, grads=True, loss=Tr
         leaves["means"], leaves["log_scales"], leaves["quats"], leaves["opacity_logits"], leaves["sh"],
         intrinsics=intrinsics_of(wl, device), camera_to_world=wl.camera_to_world.to(device),
         height=wl.height, width=wl.width, velocity=vel, times=wl.times.to(device),
-        views_per_set=wl.views_per_set, config=cfg,
+        views_per_set=wl.views_per_set, config=cfg, lens_models=lens_models, distortion=distortion,
     )
     out = {"image": image.detach().cpu(), "alpha": alpha.detach().cpu(),
            "depth": None if depth is None else depth.detach().cpu()}
@@ -43,8 +44,9 @@ def render_raw(wl, cfg: B200RendererConfig | None = None, *, grads=True, loss=Tr
     return out
 
 
-def stages(wl, cfg: B200RendererConfig | None = None, device=DEV):
-    """Forward stages only; returns the FrameState and the outputs."""
+def stages(wl, cfg: B200RendererConfig | None = None, device=DEV, lens=None):
+    """Forward stages only; returns the FrameState and the outputs.  ``lens``: the pair
+    render.lens_tensors returns (None: pinhole views)."""
     cfg = cfg or B200RendererConfig()
     S, G = wl.n_sets, wl.n_gaussians
     sspec = SceneSpec(S, G, True, wl.sh_degree, wl.velocity is not None, cfg.sh_clamp)
@@ -57,6 +59,8 @@ def stages(wl, cfg: B200RendererConfig | None = None, device=DEV):
         "intrinsics": intrinsics_of(wl, device).contiguous(),
         "camera_to_world": wl.camera_to_world.to(device).contiguous(), "times": wl.times.to(device).contiguous(),
     }
+    if lens is not None:
+        t["lens_models"], t["distortion"] = lens
     image, alpha, depth, state = forward_stages(sspec, vspec, cfg, 1e-4, t)
     torch.cuda.synchronize()
     return image, alpha, depth, state

@@ -42,9 +42,9 @@ def test_version_and_status_strings(lib):
 
 
 def test_struct_sizes_match_header():
-    # 4 ints + 6 pointers; 4 ints + 3 pointers; 2 ints + 13 floats (incl. background[3])
+    # 4 ints + 6 pointers; 4 ints + 5 pointers; 2 ints + 13 floats (incl. background[3])
     assert ctypes.sizeof(_lib.Scene) == 16 + 6 * 8
-    assert ctypes.sizeof(_lib.Views) == 16 + 3 * 8
+    assert ctypes.sizeof(_lib.Views) == 16 + 5 * 8
     assert ctypes.sizeof(_lib.Options) == 8 + 11 * 4
     assert ctypes.sizeof(_lib.LossOptions) == 16 + 6 * 4
 

@@ -91,10 +91,34 @@ def test_cpu_tensors_fail_loudly():
         reconstruction_loss_per_image(torch.zeros(1, 3, 16, 16), torch.zeros(1, 3, 16, 16))
 
 
-def test_non_pinhole_lenses_are_refused():
-    with pytest.raises(NotImplementedError):
-        render_b200_3dgs_batch(torch.zeros(1, 2, 3), torch.ones(1, 2, 3), torch.ones(1, 2, 4), torch.ones(1, 2, 1),
-                               torch.ones(1, 2, 3), 8, 8, 8.0, 8.0, 4.0, 4.0, cameras=[_Cam("radial_tangential")],
+def test_lens_tables_and_their_argument_errors():
+    """Lens models become per-view codes and zero-padded coefficient rows; the reference's
+    argument errors (projection.py:38-50, :287-288) are raised on the host."""
+    from dynaworld_b200 import _lib
+    from dynaworld_b200.render import lens_tensors
+
+    assert lens_tensors(["pinhole", "pinhole"], None, 2, "cpu") is None
+    codes, coeffs = lens_tensors(["radial_tangential", "pinhole", "opencv_fisheye"],
+                                 [[0.1, -0.02], [9.0, 9.0, 9.0, 9.0, 9.0, 9.0], (0.01, 0.0, 0.002, -0.001)], 3, "cpu")
+    assert codes.tolist() == [_lib.LENS_RADIAL_TANGENTIAL, _lib.LENS_PINHOLE, _lib.LENS_OPENCV_FISHEYE]
+    assert coeffs.shape == (3, 5)
+    assert coeffs[0].tolist() == pytest.approx([0.1, -0.02, 0, 0, 0])
+    assert coeffs[1].tolist() == [0, 0, 0, 0, 0]  # pinhole views ignore distortion
+    assert coeffs[2].tolist() == pytest.approx([0.01, 0.0, 0.002, -0.001, 0])
+    with pytest.raises(ValueError, match="at most 4"):
+        lens_tensors(["opencv_fisheye"], [[0.1] * 5], 1, "cpu")
+    with pytest.raises(ValueError, match="at most 5"):
+        lens_tensors(["radial_tangential"], [[0.1] * 6], 1, "cpu")
+    with pytest.raises(ValueError, match="Unknown lens_model"):
+        lens_tensors(["orthographic"], None, 1, "cpu")
+    args = (torch.zeros(2, 2, 3), torch.ones(2, 2, 3), torch.ones(2, 2, 4), torch.ones(2, 2, 1), torch.ones(2, 2, 3),
+            8, 8, 8.0, 8.0, 4.0, 4.0)
+    with pytest.raises(ValueError, match="Expected 2 cameras, got 1"):
+        render_b200_3dgs_batch(*args, cameras=[_Cam("radial_tangential")], projection_mode="camera_model")
+    with pytest.raises(ValueError, match="requires CameraSpec"):
+        render_b200_3dgs_batch(*args, cameras=None, projection_mode="camera_model")
+    with pytest.raises(RuntimeError, match="CUDA"):  # lens views run on the GPU kernels only
+        render_b200_3dgs_batch(*args, cameras=[_Cam("radial_tangential"), _Cam("opencv_fisheye")],
                                projection_mode="camera_model")
 
 
