@@ -68,6 +68,10 @@ class SceneGrads(C.Structure):
     _fields_ = [("means", vp), ("scales", vp), ("quats", vp), ("opacities", vp), ("colors", vp), ("velocity", vp)]
 
 
+class CameraGrads(C.Structure):
+    _fields_ = [("intrinsics", vp), ("camera_to_world", vp), ("distortion", vp)]
+
+
 class LossOptions(C.Structure):
     _fields_ = [
         ("type", C.c_int32), ("window_size", C.c_int32), ("window", C.c_int32), ("dssim_half", C.c_int32),
@@ -110,6 +114,7 @@ SIGNATURES = {
     "gsb_scale_planes": (C.c_int, [vp, vp, vp, C.c_int32, C.c_int64, vp]),
     "gsb_raster_bwd": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "gsb_preprocess_bwd": (C.c_int, [P(Scene), P(Views), P(Options), vp, vp, P(SceneGrads), vp]),
+    "gsb_camera_bwd": (C.c_int, [P(Scene), P(Views), P(Options), vp, vp, P(CameraGrads), vp]),
     "gsb_splats2d_order_workspace": (C.c_size_t, [P(Splats2D)]),
     "gsb_splats2d_order": (C.c_int, [P(Splats2D), vp, vp, vp, C.c_size_t, vp]),
     "gsb_splats2d_preprocess_workspace": (C.c_size_t, [P(Splats2D)]),

@@ -366,6 +366,18 @@ GSB_API gsb_status gsb_preprocess_bwd(const gsb_scene* scene, const gsb_views* v
   return launch_preprocess_bwd(*scene, *views, rc, rank_of, grad2d, *grads, as_stream(stream));
 }
 
+GSB_API gsb_status gsb_camera_bwd(const gsb_scene* scene, const gsb_views* views, const gsb_options* opts,
+                                  const int32_t* rank_of, const float* grad2d, gsb_camera_grads* grads, void* stream) {
+  gsb_status s;
+  if ((s = check_views(views)) != GSB_OK) return s;
+  if ((s = check_scene(scene, views)) != GSB_OK) return s;
+  if ((s = check_opts(opts)) != GSB_OK) return s;
+  if (!rank_of || !grad2d || !grads) return GSB_ERR_ARG;
+  if (views->n_views > 65535) return GSB_ERR_SHAPE;
+  const RenderConsts rc = make_consts(*views, *opts);
+  return launch_camera_bwd(*scene, *views, rc, rank_of, grad2d, *grads, as_stream(stream));
+}
+
 // ---- already-projected 2-D Gaussians ---------------------------------------------------------
 
 GSB_API size_t gsb_splats2d_order_workspace(const gsb_splats2d* splats) {

@@ -75,6 +75,8 @@ gsb_status launch_preprocess_fwd(const gsb_scene& sc, const gsb_views& vw, const
 gsb_status launch_preprocess_bwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
                                  const int32_t* rank_of, const float* grad2d, const gsb_scene_grads& gr,
                                  cudaStream_t st);
+gsb_status launch_camera_bwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc, const int32_t* rank_of,
+                             const float* grad2d, const gsb_camera_grads& out, cudaStream_t st);
 
 // Already-projected 2-D Gaussians (splat2d.cu).
 gsb_status launch_order_keys_2d(const gsb_splats2d& sp, uint64_t* keys64, uint32_t* keys32, uint32_t* vals,

@@ -4,61 +4,140 @@
 // distortion with the reference's closed-form lens Jacobians, and
 // pixel = (fx xd + cx, fy yd + cy), J = diag(fx, fy) L N (2 x 3, d pixel / d camera point).
 //
-// Written once over a scalar type T: float for the forward, Dual3 (value + derivatives along the
-// three camera coordinates) for the backward, which then differentiates exactly the expressions
-// the reference's autograd differentiates -- the pixel position and every Jacobian entry.
+// Written once over a scalar type T: float for the forward, Dual<N> (value + N derivatives) for
+// the backward -- Dual<3> along the camera-space point (x, y, z), Dual<8> along the point and the
+// five distortion coefficients -- which then differentiates exactly the expressions the
+// reference's autograd differentiates: the pixel position and every Jacobian entry.
 #pragma once
 
 #include "gsb_common.cuh"
 
 namespace gsb {
 
-struct Dual3 {
-  float v, d[3];
+template <int N>
+struct Dual {
+  float v, d[N];
 };
+using Dual3 = Dual<3>;
 
+template <int N>
+__device__ inline Dual<N> seed(float v, int slot) {  // slot < 0: a constant
+  Dual<N> r;
+  r.v = v;
+#pragma unroll
+  for (int k = 0; k < N; ++k) r.d[k] = (k == slot) ? 1.0f : 0.0f;
+  return r;
+}
 __device__ inline Dual3 dual(float v, float d0, float d1, float d2) { return Dual3{v, {d0, d1, d2}}; }
-__device__ inline Dual3 operator+(Dual3 a, Dual3 b) { return dual(a.v + b.v, a.d[0] + b.d[0], a.d[1] + b.d[1], a.d[2] + b.d[2]); }
-__device__ inline Dual3 operator-(Dual3 a, Dual3 b) { return dual(a.v - b.v, a.d[0] - b.d[0], a.d[1] - b.d[1], a.d[2] - b.d[2]); }
-__device__ inline Dual3 operator-(Dual3 a) { return dual(-a.v, -a.d[0], -a.d[1], -a.d[2]); }
-__device__ inline Dual3 operator*(Dual3 a, Dual3 b) {
-  return dual(a.v * b.v, a.d[0] * b.v + a.v * b.d[0], a.d[1] * b.v + a.v * b.d[1], a.d[2] * b.v + a.v * b.d[2]);
+
+template <int N>
+__device__ inline Dual<N> operator+(const Dual<N>& a, const Dual<N>& b) {
+  Dual<N> r;
+  r.v = a.v + b.v;
+#pragma unroll
+  for (int k = 0; k < N; ++k) r.d[k] = a.d[k] + b.d[k];
+  return r;
 }
-__device__ inline Dual3 operator/(Dual3 a, Dual3 b) {
-  const float q = a.v / b.v, ib = 1.0f / b.v;
-  return dual(q, (a.d[0] - q * b.d[0]) * ib, (a.d[1] - q * b.d[1]) * ib, (a.d[2] - q * b.d[2]) * ib);
+template <int N>
+__device__ inline Dual<N> operator-(const Dual<N>& a, const Dual<N>& b) {
+  Dual<N> r;
+  r.v = a.v - b.v;
+#pragma unroll
+  for (int k = 0; k < N; ++k) r.d[k] = a.d[k] - b.d[k];
+  return r;
 }
-__device__ inline Dual3 operator+(Dual3 a, float b) { return dual(a.v + b, a.d[0], a.d[1], a.d[2]); }
-__device__ inline Dual3 operator+(float a, Dual3 b) { return b + a; }
-__device__ inline Dual3 operator-(float a, Dual3 b) { return dual(a - b.v, -b.d[0], -b.d[1], -b.d[2]); }
-__device__ inline Dual3 operator*(float a, Dual3 b) { return dual(a * b.v, a * b.d[0], a * b.d[1], a * b.d[2]); }
-__device__ inline Dual3 operator*(Dual3 a, float b) { return b * a; }
-__device__ inline Dual3 operator/(float a, Dual3 b) {
-  const float q = a / b.v, s = -q / b.v;
-  return dual(q, s * b.d[0], s * b.d[1], s * b.d[2]);
+template <int N>
+__device__ inline Dual<N> operator-(const Dual<N>& a) {
+  Dual<N> r;
+  r.v = -a.v;
+#pragma unroll
+  for (int k = 0; k < N; ++k) r.d[k] = -a.d[k];
+  return r;
+}
+template <int N>
+__device__ inline Dual<N> operator*(const Dual<N>& a, const Dual<N>& b) {
+  Dual<N> r;
+  r.v = a.v * b.v;
+#pragma unroll
+  for (int k = 0; k < N; ++k) r.d[k] = a.d[k] * b.v + a.v * b.d[k];
+  return r;
+}
+template <int N>
+__device__ inline Dual<N> operator/(const Dual<N>& a, const Dual<N>& b) {
+  Dual<N> r;
+  r.v = a.v / b.v;
+  const float ib = 1.0f / b.v;
+#pragma unroll
+  for (int k = 0; k < N; ++k) r.d[k] = (a.d[k] - r.v * b.d[k]) * ib;
+  return r;
+}
+template <int N>
+__device__ inline Dual<N> operator+(const Dual<N>& a, float b) {
+  Dual<N> r = a;
+  r.v = a.v + b;
+  return r;
+}
+template <int N>
+__device__ inline Dual<N> operator+(float a, const Dual<N>& b) { return b + a; }
+template <int N>
+__device__ inline Dual<N> operator-(float a, const Dual<N>& b) { return (-b) + a; }
+template <int N>
+__device__ inline Dual<N> operator*(float a, const Dual<N>& b) {
+  Dual<N> r;
+  r.v = a * b.v;
+#pragma unroll
+  for (int k = 0; k < N; ++k) r.d[k] = a * b.d[k];
+  return r;
+}
+template <int N>
+__device__ inline Dual<N> operator*(const Dual<N>& a, float b) { return b * a; }
+template <int N>
+__device__ inline Dual<N> operator/(float a, const Dual<N>& b) {
+  Dual<N> r;
+  r.v = a / b.v;
+  const float s = -r.v / b.v;
+#pragma unroll
+  for (int k = 0; k < N; ++k) r.d[k] = s * b.d[k];
+  return r;
 }
 
 __device__ inline float value_of(float x) { return x; }
-__device__ inline float value_of(const Dual3& x) { return x.v; }
+template <int N>
+__device__ inline float value_of(const Dual<N>& x) { return x.v; }
+
 __device__ inline float lens_sqrt(float x) { return sqrtf(x); }
-__device__ inline Dual3 lens_sqrt(Dual3 x) {
-  const float r = sqrtf(x.v), s = 0.5f / r;
-  return dual(r, s * x.d[0], s * x.d[1], s * x.d[2]);
+template <int N>
+__device__ inline Dual<N> lens_sqrt(const Dual<N>& x) {
+  Dual<N> r;
+  r.v = sqrtf(x.v);
+  const float s = 0.5f / r.v;
+#pragma unroll
+  for (int k = 0; k < N; ++k) r.d[k] = s * x.d[k];
+  return r;
 }
 __device__ inline float lens_atan(float x) { return atanf(x); }
-__device__ inline Dual3 lens_atan(Dual3 x) {
+template <int N>
+__device__ inline Dual<N> lens_atan(const Dual<N>& x) {
+  Dual<N> r;
+  r.v = atanf(x.v);
   const float s = 1.0f / (1.0f + x.v * x.v);
-  return dual(atanf(x.v), s * x.d[0], s * x.d[1], s * x.d[2]);
+#pragma unroll
+  for (int k = 0; k < N; ++k) r.d[k] = s * x.d[k];
+  return r;
 }
 // torch.clamp(x, min=lo): the gradient passes where x >= lo
 __device__ inline float clamp_min(float x, float lo) { return fmaxf(x, lo); }
-__device__ inline Dual3 clamp_min(Dual3 x, float lo) { return x.v >= lo ? x : dual(lo, 0.0f, 0.0f, 0.0f); }
+template <int N>
+__device__ inline Dual<N> clamp_min(const Dual<N>& x, float lo) { return x.v >= lo ? x : seed<N>(lo, -1); }
+
 template <typename T>
-__device__ inline T constant(float v);
-template <>
-__device__ inline float constant<float>(float v) { return v; }
-template <>
-__device__ inline Dual3 constant<Dual3>(float v) { return dual(v, 0.0f, 0.0f, 0.0f); }
+struct Constant {
+  __device__ static T of(float v) { return v; }
+};
+template <int N>
+struct Constant<Dual<N>> {
+  __device__ static Dual<N> of(float v) { return seed<N>(v, -1); }
+};
 
 template <typename T>
 struct LensJ {
@@ -68,8 +147,8 @@ struct LensJ {
 
 // projection.py:93-116
 template <typename T>
-__device__ inline LensJ<T> radial_tangential(T x, T y, const float c[5]) {
-  const float k1 = c[0], k2 = c[1], p1 = c[2], p2 = c[3], k3 = c[4];
+__device__ inline LensJ<T> radial_tangential(T x, T y, const T c[5]) {
+  const T k1 = c[0], k2 = c[1], p1 = c[2], p2 = c[3], k3 = c[4];
   LensJ<T> o;
   const T r2 = x * x + y * y;
   const T r4 = r2 * r2;
@@ -89,8 +168,8 @@ __device__ inline LensJ<T> radial_tangential(T x, T y, const float c[5]) {
 
 // projection.py:119-161
 template <typename T>
-__device__ inline LensJ<T> opencv_fisheye(T x, T y, const float c[5]) {
-  const float k1 = c[0], k2 = c[1], k3 = c[2], k4 = c[3];
+__device__ inline LensJ<T> opencv_fisheye(T x, T y, const T c[5]) {
+  const T k1 = c[0], k2 = c[1], k3 = c[2], k4 = c[3];
   constexpr float kEps2 = 1.0e-8f * 1.0e-8f;
   LensJ<T> o;
   const T r2 = x * x + y * y;
@@ -102,13 +181,13 @@ __device__ inline LensJ<T> opencv_fisheye(T x, T y, const float c[5]) {
   const T t8 = t4 * t4;
   const T theta_d = theta * (1.0f + k1 * t2 + k2 * t4 + k3 * t6 + k4 * t8);
   const bool valid = value_of(r2) > kEps2;
-  const T scale = valid ? theta_d / radius : constant<T>(1.0f);
+  const T scale = valid ? theta_d / radius : Constant<T>::of(1.0f);
   o.xd = scale * x;
   o.yd = scale * y;
   const T dtd = 1.0f + (3.0f * k1) * t2 + (5.0f * k2) * t4 + (7.0f * k3) * t6 + (9.0f * k4) * t8;
   const T dtdr = 1.0f / (1.0f + radius * radius);
-  const T dsdr = valid ? (dtd * dtdr * radius - theta_d) / (radius * radius) : constant<T>(0.0f);
-  const T inv_r = valid ? 1.0f / radius : constant<T>(0.0f);
+  const T dsdr = valid ? (dtd * dtdr * radius - theta_d) / (radius * radius) : Constant<T>::of(0.0f);
+  const T inv_r = valid ? 1.0f / radius : Constant<T>::of(0.0f);
   const T dsdx = dsdr * x * inv_r;
   const T dsdy = dsdr * y * inv_r;
   o.L00 = scale + x * dsdx;
@@ -122,30 +201,47 @@ template <typename T>
 struct LensProjection {
   T mx, my;        // pixel position
   T J[6];          // d pixel / d camera point, row-major 2 x 3
+  T xd, yd;        // distorted normalised coordinates (d pixel / d (fx, fy))
+  T U[6];          // L N: J with the focal lengths factored out (d J / d (fx, fy))
 };
 
 // Camera-space point (xp, yp, zs) of a Gaussian in front of the near plane (x_project,
-// y_project, z_safe of projection.py:75-90) -> pixel and Jacobian (projection.py:164-214).
+// y_project, z_safe of projection.py:75-90) -> pixel and Jacobian (projection.py:164-214);
+// ``coef`` are the lens's distortion coefficients.
 template <typename T>
-__device__ inline LensProjection<T> lens_project(T xp, T yp, T zs, const Camera& cam) {
+__device__ inline LensProjection<T> lens_project(T xp, T yp, T zs, const Camera& cam, const T coef[5]) {
   const T xn = xp / zs, yn = yp / zs;
   const T n00 = 1.0f / zs;                 // norm_jacobian[0][0] = [1][1]
   const T n02 = -xp / (zs * zs);
   const T n12 = -yp / (zs * zs);
-  const LensJ<T> l = cam.lens == GSB_LENS_OPENCV_FISHEYE ? opencv_fisheye(xn, yn, cam.dist)
-                                                         : radial_tangential(xn, yn, cam.dist);
+  const LensJ<T> l = cam.lens == GSB_LENS_OPENCV_FISHEYE ? opencv_fisheye(xn, yn, coef) : radial_tangential(xn, yn, coef);
   const float fx = cam.k.fx, fy = cam.k.fy;
-  const T a00 = fx * l.L00, a01 = fx * l.L01, a10 = fy * l.L10, a11 = fy * l.L11;  // diag(f) L
   LensProjection<T> p;
+  p.U[0] = l.L00 * n00;
+  p.U[1] = l.L01 * n00;
+  p.U[2] = l.L00 * n02 + l.L01 * n12;
+  p.U[3] = l.L10 * n00;
+  p.U[4] = l.L11 * n00;
+  p.U[5] = l.L10 * n02 + l.L11 * n12;
+  const T a00 = fx * l.L00, a01 = fx * l.L01, a10 = fy * l.L10, a11 = fy * l.L11;  // diag(f) L
   p.J[0] = a00 * n00;
   p.J[1] = a01 * n00;
   p.J[2] = a00 * n02 + a01 * n12;
   p.J[3] = a10 * n00;
   p.J[4] = a11 * n00;
   p.J[5] = a10 * n02 + a11 * n12;
+  p.xd = l.xd;
+  p.yd = l.yd;
   p.mx = fx * l.xd + cam.k.cx;
   p.my = fy * l.yd + cam.k.cy;
   return p;
+}
+
+// The coefficients of a view as constants of type T.
+template <typename T>
+__device__ inline void lens_coefficients(const Camera& cam, T coef[5]) {
+#pragma unroll
+  for (int i = 0; i < 5; ++i) coef[i] = Constant<T>::of(cam.dist[i]);
 }
 
 }  // namespace gsb

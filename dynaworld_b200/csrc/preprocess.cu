@@ -200,7 +200,9 @@ __device__ inline void project(const GaussParams& p, const Camera& cam, float ne
     P.mx = __fadd_rn(__fdiv_rn(__fmul_rn(fx, P.xp), P.zs), cam.k.cx);
     P.my = __fadd_rn(__fdiv_rn(__fmul_rn(fy, P.yp), P.zs), cam.k.cy);
   } else {  // projection.py:164-214, 253-263; behind the near plane the Jacobian is zero
-    const LensProjection<float> lp = lens_project<float>(P.xp, P.yp, P.zs, cam);
+    float coef[5];
+    lens_coefficients(cam, coef);
+    const LensProjection<float> lp = lens_project<float>(P.xp, P.yp, P.zs, cam, coef);
     const float m = P.front ? 1.0f : 0.0f;
     P.J00 = lp.J[0] * m, P.J01 = lp.J[1] * m, P.J02 = lp.J[2] * m;
     P.J10 = lp.J[3] * m, P.J11 = lp.J[4] * m, P.J12 = lp.J[5] * m;
@@ -367,6 +369,115 @@ __device__ inline void quat_rot_vjp(const float q[4], const float G[9], float dq
   dq[3] = 2.0f * (-2.0f * k * G[0] - r * G[1] + i * G[2] + r * G[3] - 2.0f * k * G[4] + j * G[5] + i * G[6] + j * G[7]);
 }
 
+// Colour of one view: d loss / d SH coefficients (accumulated into acol, K = 0: plain rgb) and
+// the part of d loss / d mean that flows through the view direction d / |d| (added to dmt).
+template <int K>
+__device__ inline void sh_backward(const gsb_scene& sc, size_t pg, const float d[3], const float dcol[3],
+                                   bool clamp_sh, float* acol, float dmt[3]) {
+  if (K == 0) {
+    if (acol)
+      for (int c = 0; c < 3; ++c) acol[c] += dcol[c];
+    return;
+  }
+  constexpr int KC = K > 0 ? K : 1;
+  const float n2 = d[0] * d[0] + d[1] * d[1] + d[2] * d[2];
+  const float inv = rsqrtf(n2);
+  const float dir[3] = {d[0] * inv, d[1] * inv, d[2] * inv};
+  float Y[KC];
+  sh_basis<KC>(dir[0], dir[1], dir[2], Y);
+  const float* sh = sc.colors + pg * size_t(KC) * 3;
+  float dc[3];
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    float v = 0.5f;
+#pragma unroll
+    for (int k = 0; k < KC; ++k) v += Y[k] * sh[k * 3 + c];
+    dc[c] = (clamp_sh && !(v >= 0.0f)) ? 0.0f : dcol[c];
+  }
+  if (acol) {
+#pragma unroll
+    for (int k = 0; k < KC; ++k)
+#pragma unroll
+      for (int c = 0; c < 3; ++c) acol[k * 3 + c] += dc[c] * Y[k];
+  }
+  if (KC > 1) {
+    float dY[KC][3];
+    sh_basis_grad<KC>(dir[0], dir[1], dir[2], dY);
+    float ddir[3] = {0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int k = 1; k < KC; ++k) {
+      const float w = dc[0] * sh[k * 3 + 0] + dc[1] * sh[k * 3 + 1] + dc[2] * sh[k * 3 + 2];
+      ddir[0] += w * dY[k][0];
+      ddir[1] += w * dY[k][1];
+      ddir[2] += w * dY[k][2];
+    }
+    const float dd = dir[0] * ddir[0] + dir[1] * ddir[1] + dir[2] * ddir[2];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) dmt[k] += (ddir[k] - dir[k] * dd) * inv;
+  }
+}
+
+// d loss / d (J rows u, v) and d loss / d camera covariance from d loss / d inverse 2-D covariance.
+struct CovGrad {
+  float du[3], dv[3], dcc[9];
+};
+
+__device__ inline void cov_backward(const Proj& P, float dA, float dB, float dC, CovGrad& cg) {
+  // inverse covariance -> covariance (det clamped at 1e-6: no gradient through the clamp)
+  const float det = P.det;
+  const float ddet = (P.det_raw >= 1e-6f) ? -(dA * P.A + dB * P.B + dC * P.C) / det : 0.0f;
+  const float g00 = dC / det + ddet * P.c11;
+  const float g11 = dA / det + ddet * P.c00;
+  const float g01 = -2.0f * dB / det - 2.0f * ddet * P.c01;  // total over the two off-diagonals
+  // covariance = J cc J^T, J rows u = (J00, J01, J02), v = (J10, J11, J12)
+  const float u[3] = {P.J00, P.J01, P.J02}, v[3] = {P.J10, P.J11, P.J12};
+  float cu[3], cv[3];
+#pragma unroll
+  for (int a = 0; a < 3; ++a) {
+    cu[a] = P.cc[a * 3 + 0] * u[0] + P.cc[a * 3 + 1] * u[1] + P.cc[a * 3 + 2] * u[2];
+    cv[a] = P.cc[a * 3 + 0] * v[0] + P.cc[a * 3 + 1] * v[1] + P.cc[a * 3 + 2] * v[2];
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    cg.du[k] = 2.0f * g00 * cu[k] + g01 * cv[k];
+    cg.dv[k] = 2.0f * g11 * cv[k] + g01 * cu[k];
+  }
+#pragma unroll
+  for (int a = 0; a < 3; ++a)
+#pragma unroll
+    for (int c = 0; c < 3; ++c)
+      cg.dcc[a * 3 + c] = g00 * u[a] * u[c] + g11 * v[a] * v[c] + 0.5f * g01 * (u[a] * v[c] + v[a] * u[c]);
+}
+
+// Jacobian and means2D -> camera-space point, pinhole (common.py:205-229).
+__device__ inline void pinhole_point_backward(const Proj& P, const Camera& cam, float dmx, float dmy,
+                                              const CovGrad& cg, float dmc[3]) {
+  const float fx = cam.k.fx, fy = cam.k.fy, zs = P.zs;
+  const float izs = 1.0f / zs, izs2 = izs * izs, izs3 = izs2 * izs;
+  dmc[0] = cg.du[2] * (-fx * izs2) + dmx * fx * izs;
+  dmc[1] = cg.dv[2] * (-fy * izs2) + dmy * fy * izs;
+  dmc[2] = cg.du[0] * (-fx * izs2) + cg.du[2] * (2.0f * fx * P.xp * izs3) + cg.dv[1] * (-fy * izs2) +
+           cg.dv[2] * (2.0f * fy * P.yp * izs3) + dmx * (-fx * P.xp * izs2) + dmy * (-fy * P.yp * izs2);
+}
+
+// The same through a lens: forward-mode derivatives of the pixel and of every Jacobian entry
+// along the camera-space x, y, z.
+__device__ inline void lens_point_backward(const Proj& P, const Camera& cam, float dmx, float dmy, const CovGrad& cg,
+                                           float dmc[3]) {
+  Dual3 coef[5];
+  lens_coefficients(cam, coef);
+  const LensProjection<Dual3> lp = lens_project<Dual3>(dual(P.xp, 1.0f, 0.0f, 0.0f), dual(P.yp, 0.0f, 1.0f, 0.0f),
+                                                       dual(P.zs, 0.0f, 0.0f, 1.0f), cam, coef);
+  const float dJ[6] = {cg.du[0], cg.du[1], cg.du[2], cg.dv[0], cg.dv[1], cg.dv[2]};
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    float acc = dmx * lp.mx.d[k] + dmy * lp.my.d[k];
+#pragma unroll
+    for (int e = 0; e < 6; ++e) acc += dJ[e] * lp.J[e].d[k];
+    dmc[k] = acc;
+  }
+}
+
 // K = SH coefficients per channel (1, 4, 9, 16) or 0 for plain rgb; LENS: some view has a
 // non-pinhole lens (the dual-number lens backward is compiled into these instances only)
 template <int K, bool LENS>
@@ -401,101 +512,18 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
       project(p, cam, rc.near_plane, P);
       if (!P.front) continue;  // opacity * 0: no gradient reaches this Gaussian from this view
       float dmt[3] = {0.0f, 0.0f, 0.0f};
-
-      // colour
-      if (K == 0) {
-#pragma unroll
-        for (int c = 0; c < 3; ++c) acol[c] += dcol[c];
-      } else {
-        const float n2 = P.d[0] * P.d[0] + P.d[1] * P.d[1] + P.d[2] * P.d[2];
-        const float inv = rsqrtf(n2);
-        const float dir[3] = {P.d[0] * inv, P.d[1] * inv, P.d[2] * inv};
-        float Y[KC];
-        sh_basis<KC>(dir[0], dir[1], dir[2], Y);
-        const float* sh = sc.colors + pg * size_t(KC) * 3;
-        float dc[3];
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-          float v = 0.5f;
-#pragma unroll
-          for (int k = 0; k < KC; ++k) v += Y[k] * sh[k * 3 + c];
-          dc[c] = (clamp_sh && !(v >= 0.0f)) ? 0.0f : dcol[c];
-        }
-#pragma unroll
-        for (int k = 0; k < KC; ++k)
-#pragma unroll
-          for (int c = 0; c < 3; ++c) acol[k * 3 + c] += dc[c] * Y[k];
-        if (KC > 1) {
-          float dY[KC][3];
-          sh_basis_grad<KC>(dir[0], dir[1], dir[2], dY);
-          float ddir[3] = {0.0f, 0.0f, 0.0f};
-#pragma unroll
-          for (int k = 1; k < KC; ++k) {
-            const float w = dc[0] * sh[k * 3 + 0] + dc[1] * sh[k * 3 + 1] + dc[2] * sh[k * 3 + 2];
-            ddir[0] += w * dY[k][0];
-            ddir[1] += w * dY[k][1];
-            ddir[2] += w * dY[k][2];
-          }
-          const float dd = dir[0] * ddir[0] + dir[1] * ddir[1] + dir[2] * ddir[2];
-#pragma unroll
-          for (int k = 0; k < 3; ++k) dmt[k] += (ddir[k] - dir[k] * dd) * inv;
-        }
-      }
-
-      // inverse covariance -> covariance
-      const float det = P.det;
-      const float ddet = (P.det_raw >= 1e-6f) ? -(dA * P.A + dB * P.B + dC * P.C) / det : 0.0f;
-      const float g00 = dC / det + ddet * P.c11;
-      const float g11 = dA / det + ddet * P.c00;
-      const float g01 = -2.0f * dB / det - 2.0f * ddet * P.c01;  // total over the two off-diagonals
-      // covariance = J cc J^T, J rows u = (J00, J01, J02), v = (J10, J11, J12)
-      const float u[3] = {P.J00, P.J01, P.J02}, v[3] = {P.J10, P.J11, P.J12};
-      float cu[3], cv[3];
-#pragma unroll
-      for (int a = 0; a < 3; ++a) {
-        cu[a] = P.cc[a * 3 + 0] * u[0] + P.cc[a * 3 + 1] * u[1] + P.cc[a * 3 + 2] * u[2];
-        cv[a] = P.cc[a * 3 + 0] * v[0] + P.cc[a * 3 + 1] * v[1] + P.cc[a * 3 + 2] * v[2];
-      }
-      float du[3], dv[3];  // d loss / d J rows
-#pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        du[k] = 2.0f * g00 * cu[k] + g01 * cv[k];
-        dv[k] = 2.0f * g11 * cv[k] + g01 * cu[k];
-      }
-      float dcc[9];
-#pragma unroll
-      for (int a = 0; a < 3; ++a)
-#pragma unroll
-        for (int c = 0; c < 3; ++c)
-          dcc[a * 3 + c] = g00 * u[a] * u[c] + g11 * v[a] * v[c] + 0.5f * g01 * (u[a] * v[c] + v[a] * u[c]);
-      // Jacobian and means2D -> camera coordinates
+      sh_backward<K>(sc, pg, P.d, dcol, clamp_sh, acol, dmt);
+      CovGrad cg;
+      cov_backward(P, dA, dB, dC, cg);
       float dmc[3];
-      if (!LENS || cam.lens == GSB_LENS_PINHOLE) {
-        const float fx = cam.k.fx, fy = cam.k.fy, zs = P.zs;
-        const float izs = 1.0f / zs, izs2 = izs * izs, izs3 = izs2 * izs;
-        dmc[0] = du[2] * (-fx * izs2) + dmx * fx * izs;
-        dmc[1] = dv[2] * (-fy * izs2) + dmy * fy * izs;
-        dmc[2] = du[0] * (-fx * izs2) + du[2] * (2.0f * fx * P.xp * izs3) + dv[1] * (-fy * izs2) +
-                 dv[2] * (2.0f * fy * P.yp * izs3) + dmx * (-fx * P.xp * izs2) + dmy * (-fy * P.yp * izs2);
-      } else {
-        // forward-mode derivatives of the pixel and of every Jacobian entry along x, y, z
-        const LensProjection<Dual3> lp = lens_project<Dual3>(dual(P.xp, 1.0f, 0.0f, 0.0f),
-                                                             dual(P.yp, 0.0f, 1.0f, 0.0f),
-                                                             dual(P.zs, 0.0f, 0.0f, 1.0f), cam);
-        const float dJ[6] = {du[0], du[1], du[2], dv[0], dv[1], dv[2]};
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-          float acc = dmx * lp.mx.d[k] + dmy * lp.my.d[k];
-#pragma unroll
-          for (int e = 0; e < 6; ++e) acc += dJ[e] * lp.J[e].d[k];
-          dmc[k] = acc;
-        }
-      }
+      if (!LENS || cam.lens == GSB_LENS_PINHOLE) pinhole_point_backward(P, cam, dmx, dmy, cg, dmc);
+      else lens_point_backward(P, cam, dmx, dmy, cg, dmc);
       dmc[2] += dzo;
       // camera -> world: mc = Rcw^T d, cc = Rcw^T S Rcw
 #pragma unroll
       for (int j = 0; j < 3; ++j)
         dmt[j] += cam.R[j * 3 + 0] * dmc[0] + cam.R[j * 3 + 1] * dmc[1] + cam.R[j * 3 + 2] * dmc[2];
+      const float* dcc = cg.dcc;
       float T2[9], dS[9];
 #pragma unroll
       for (int a = 0; a < 3; ++a)
@@ -556,6 +584,127 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
   }
 }
 
+// ---- camera gradients --------------------------------------------------------------------------
+//
+// d loss / d camera of each view, summed over its Gaussians: intrinsics (fx, fy, cx, cy),
+// camera_to_world rotation (mc = R^T d and cc = R^T S R, d = mean_t - centre) and centre
+// (-d loss / d d), and the lens distortion coefficients (forward-mode duals over the point and
+// the five coefficients).  One thread per (view, Gaussian), blockIdx.y = view; a block reduction
+// then one atomic per value per block.
+
+constexpr int kCamValues = 4 + 9 + 3 + 5;
+
+template <int K, bool LENS>
+__global__ void __launch_bounds__(128) camera_bwd_kernel(gsb_scene sc, gsb_views vw, RenderConsts rc,
+                                                         const int32_t* __restrict__ rank_of,
+                                                         const float* __restrict__ grad2d, gsb_camera_grads out) {
+  const int b = blockIdx.y;
+  const size_t G = sc.n_gaussians;
+  const size_t g = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+  float acc[kCamValues];
+#pragma unroll
+  for (int i = 0; i < kCamValues; ++i) acc[i] = 0.0f;
+  if (g < G) {
+    const size_t pg = size_t(b / vw.views_per_set) * G + g;
+    const size_t slot = size_t(b) * G + size_t(rank_of[size_t(b) * G + g]);
+    const float* g2 = grad2d + slot * GSB_GRAD2D_FLOATS;
+    const float dmx = g2[0], dmy = g2[1], dA = g2[2], dB = g2[3], dC = g2[4];
+    const float dcol[3] = {g2[6], g2[7], g2[8]};
+    const float t = vw.times ? vw.times[b] : 0.0f;
+    const Camera cam = load_camera(vw, b);
+    const GaussParams p = load_params(sc, pg, t);
+    Proj P;
+    project(p, cam, rc.near_plane, P);
+    if (P.front) {
+      float dmt[3] = {0.0f, 0.0f, 0.0f};
+      sh_backward<K>(sc, pg, P.d, dcol, sc.flags & GSB_SCENE_SH_CLAMP, nullptr, dmt);
+      CovGrad cg;
+      cov_backward(P, dA, dB, dC, cg);
+      float dmc[3];
+      if (!LENS || cam.lens == GSB_LENS_PINHOLE) {
+        pinhole_point_backward(P, cam, dmx, dmy, cg, dmc);
+        const float izs = 1.0f / P.zs, izs2 = izs * izs;
+        acc[0] = dmx * P.xp * izs + cg.du[0] * izs - cg.du[2] * P.xp * izs2;  // fx (common.py:210-229)
+        acc[1] = dmy * P.yp * izs + cg.dv[1] * izs - cg.dv[2] * P.yp * izs2;  // fy
+      } else {
+        Dual<8> coef[5];
+#pragma unroll
+        for (int i = 0; i < 5; ++i) coef[i] = seed<8>(cam.dist[i], 3 + i);
+        const LensProjection<Dual<8>> lp =
+            lens_project<Dual<8>>(seed<8>(P.xp, 0), seed<8>(P.yp, 1), seed<8>(P.zs, 2), cam, coef);
+        const float dJ[6] = {cg.du[0], cg.du[1], cg.du[2], cg.dv[0], cg.dv[1], cg.dv[2]};
+        float dv8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          float a = dmx * lp.mx.d[k] + dmy * lp.my.d[k];
+#pragma unroll
+          for (int e = 0; e < 6; ++e) a += dJ[e] * lp.J[e].d[k];
+          dv8[k] = a;
+        }
+        dmc[0] = dv8[0], dmc[1] = dv8[1], dmc[2] = dv8[2];
+#pragma unroll
+        for (int i = 0; i < 5; ++i) acc[16 + i] = dv8[3 + i];
+        // pixel = f xd + c, J = diag(f) U
+        acc[0] = dmx * lp.xd.v + cg.du[0] * lp.U[0].v + cg.du[1] * lp.U[1].v + cg.du[2] * lp.U[2].v;
+        acc[1] = dmy * lp.yd.v + cg.dv[0] * lp.U[3].v + cg.dv[1] * lp.U[4].v + cg.dv[2] * lp.U[5].v;
+      }
+      acc[2] = dmx;
+      acc[3] = dmy;
+      dmc[2] += g2[9];  // depth output
+      // rotation: d_j dmc_k from the mean, 2 (S R dcc)_jk from the covariance (S = M M^T)
+      float SR[9];
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+#pragma unroll
+        for (int a = 0; a < 3; ++a) {
+          float s = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 3; ++i) {
+            const float Sji = P.M[j * 3 + 0] * P.M[i * 3 + 0] + P.M[j * 3 + 1] * P.M[i * 3 + 1] + P.M[j * 3 + 2] * P.M[i * 3 + 2];
+            s += Sji * cam.R[i * 3 + a];
+          }
+          SR[j * 3 + a] = s;
+        }
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+          float c = 0.0f;
+#pragma unroll
+          for (int a = 0; a < 3; ++a) c += SR[j * 3 + a] * cg.dcc[a * 3 + k];
+          acc[4 + j * 3 + k] = P.d[j] * dmc[k] + 2.0f * c;
+        }
+      // centre: d = mean_t - centre enters the camera point and the SH direction
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+        acc[13 + j] = -(dmt[j] + cam.R[j * 3 + 0] * dmc[0] + cam.R[j * 3 + 1] * dmc[1] + cam.R[j * 3 + 2] * dmc[2]);
+    }
+  }
+  // block reduction: warps, then the 4 warp partials
+  __shared__ float part[4][kCamValues];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int i = 0; i < kCamValues; ++i) {
+    float v = acc[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) part[warp][i] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < kCamValues) {
+    const int i = threadIdx.x;
+    const float v = part[0][i] + part[1][i] + part[2][i] + part[3][i];
+    if (v != 0.0f) {
+      float* dst = nullptr;
+      if (i < 4) dst = out.intrinsics ? out.intrinsics + b * 4 + i : nullptr;
+      else if (i < 13) dst = out.camera_to_world ? out.camera_to_world + b * 16 + ((i - 4) / 3) * 4 + (i - 4) % 3 : nullptr;
+      else if (i < 16) dst = out.camera_to_world ? out.camera_to_world + b * 16 + (i - 13) * 4 + 3 : nullptr;
+      else dst = out.distortion ? out.distortion + b * 5 + (i - 16) : nullptr;
+      if (dst) atomicAdd(dst, v);
+    }
+  }
+}
+
 // ---- host launchers --------------------------------------------------------------------------
 
 static int grid_for(size_t n, int threads) {
@@ -598,6 +747,36 @@ static void launch_bwd_for_degree(int deg, int grid, const gsb_scene& sc, const 
     case 2: preprocess_bwd_kernel<9, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
     default: preprocess_bwd_kernel<16, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
   }
+}
+
+template <bool LENS>
+static void launch_camera_for_degree(int deg, dim3 grid, const gsb_scene& sc, const gsb_views& vw,
+                                     const RenderConsts& rc, const int32_t* rank_of, const float* grad2d,
+                                     const gsb_camera_grads& out, cudaStream_t st) {
+  switch (deg) {
+    case -1: camera_bwd_kernel<0, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, out); break;
+    case 0: camera_bwd_kernel<1, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, out); break;
+    case 1: camera_bwd_kernel<4, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, out); break;
+    case 2: camera_bwd_kernel<9, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, out); break;
+    default: camera_bwd_kernel<16, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, out); break;
+  }
+}
+
+gsb_status launch_camera_bwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc, const int32_t* rank_of,
+                             const float* grad2d, const gsb_camera_grads& out, cudaStream_t st) {
+  const int B = vw.n_views;
+  if (out.intrinsics && cudaMemsetAsync(out.intrinsics, 0, size_t(B) * 4 * sizeof(float), st)) return GSB_ERR_CUDA;
+  if (out.camera_to_world && cudaMemsetAsync(out.camera_to_world, 0, size_t(B) * 16 * sizeof(float), st))
+    return GSB_ERR_CUDA;
+  if (out.distortion && cudaMemsetAsync(out.distortion, 0, size_t(B) * 5 * sizeof(float), st)) return GSB_ERR_CUDA;
+  const bool raw = sc.flags & GSB_SCENE_RAW;
+  const int deg = raw ? sc.sh_degree : -1;
+  if (deg < -1 || deg > 3) return GSB_ERR_ARG;
+  const dim3 grid(unsigned((size_t(sc.n_gaussians) + 127) / 128), unsigned(B));
+  note_launch();
+  if (vw.lens_models) launch_camera_for_degree<true>(deg, grid, sc, vw, rc, rank_of, grad2d, out, st);
+  else launch_camera_for_degree<false>(deg, grid, sc, vw, rc, rank_of, grad2d, out, st);
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 
 gsb_status launch_preprocess_bwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,

@@ -123,6 +123,13 @@ typedef struct gsb_scene_grads {
   float* velocity;
 } gsb_scene_grads;
 
+/* Gradients of the cameras (device; NULL entries are skipped; outputs are overwritten). */
+typedef struct gsb_camera_grads {
+  float* intrinsics;       /* [B,4] d/d(fx, fy, cx, cy) */
+  float* camera_to_world;  /* [B,4,4] rotation and centre entries (bottom row zero) */
+  float* distortion;       /* [B,5] (zero for pinhole views and unused coefficients) */
+} gsb_camera_grads;
+
 typedef struct gsb_loss_options {
   int32_t type;          /* 0 standard_gs, 1 l1, 2 mse, 3 l1_mse */
   int32_t window_size;   /* odd, 3..31; reference 11 */
@@ -241,6 +248,15 @@ GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opt
 GSB_API gsb_status gsb_preprocess_bwd(const gsb_scene* scene, const gsb_views* views,
                                       const gsb_options* opts, const int32_t* rank_of,
                                       const float* grad2d, gsb_scene_grads* grads, void* stream);
+
+/* ---- stage 7b: camera gradients (torch autograd through common.py / projection.py into the
+   camera tensors, which the implicit-camera models of gs_models/implicit_camera.py:146-262
+   train through the render call) ---------------------------------------------------------- */
+/* Per view, summed over its Gaussians: d/d intrinsics, d/d camera_to_world (rotation entries and
+   the centre column), d/d lens distortion.  Launch only when a camera tensor needs gradients. */
+GSB_API gsb_status gsb_camera_bwd(const gsb_scene* scene, const gsb_views* views,
+                                  const gsb_options* opts, const int32_t* rank_of,
+                                  const float* grad2d, gsb_camera_grads* grads, void* stream);
 
 /* ---- already-projected 2-D Gaussians -------------------------------------------------------
  * The reference's 2-D rasterizer contracts, on the same bin and raster stages as the 3-D path:
