@@ -218,7 +218,10 @@ def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, n
 
 def backward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, near_plane: float, tensors: dict,
                     state: FrameState, d_image: torch.Tensor, d_alpha: torch.Tensor | None,
-                    d_depth: torch.Tensor | None, view_scale: torch.Tensor | None = None) -> dict:
+                    d_depth: torch.Tensor | None, view_scale: torch.Tensor | None = None,
+                    camera: bool = False) -> dict:
+    """Gradients of the scene tensors; with ``camera`` also "cam_intrinsics" [B,4],
+    "cam_camera_to_world" [B,4,4] and, with lenses, "cam_distortion" [B,5]."""
     L = _lib.lib()
     dev = tensors["means"].device
     st = _stream(dev)
@@ -245,32 +248,49 @@ def backward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, 
     with _stage("preprocess_bwd"):
         _lib.check("gsb_preprocess_bwd", L.gsb_preprocess_bwd(scene, views, opts, state.rank_of.data_ptr(),
                                                               grad2d.data_ptr(), g, st))
+    if camera:
+        out["cam_intrinsics"] = torch.empty(B, 4, dtype=torch.float32, device=dev)
+        out["cam_camera_to_world"] = torch.empty(B, 4, 4, dtype=torch.float32, device=dev)
+        cg = _lib.CameraGrads()
+        cg.intrinsics, cg.camera_to_world = out["cam_intrinsics"].data_ptr(), out["cam_camera_to_world"].data_ptr()
+        if tensors.get("lens_models") is not None:
+            out["cam_distortion"] = torch.empty(B, _lib.DISTORTION_FLOATS, dtype=torch.float32, device=dev)
+            cg.distortion = out["cam_distortion"].data_ptr()
+        with _stage("camera_bwd"):
+            _lib.check("gsb_camera_bwd", L.gsb_camera_bwd(scene, views, opts, state.rank_of.data_ptr(),
+                                                          grad2d.data_ptr(), cg, st))
     return out
 
 
 _PARAM_NAMES = ("means", "scales", "quats", "opacities", "colors", "velocity")
 
 
+_CAMERA_NAMES = ("cam_intrinsics", "cam_camera_to_world", None, "cam_distortion")  # times get none
+
+
 class _RenderFunction(torch.autograd.Function):
     """(image [B,3,H,W], alpha [B,H,W], depth [B,H,W]) of the scene; gradients flow to the six
-    scene tensors.  Camera tensors get no gradient (the forward refuses cameras that need one)."""
+    scene tensors and, when they require them, to the intrinsics, camera_to_world and lens
+    distortion (not to the per-view times)."""
 
     @staticmethod
-    def forward(ctx, sspec, vspec, cfg, near_plane, lens, means, scales, quats, opacities, colors, velocity,
-                intrinsics, camera_to_world, times):
+    def forward(ctx, sspec, vspec, cfg, near_plane, lens_models, means, scales, quats, opacities, colors, velocity,
+                intrinsics, camera_to_world, times, distortion):
         tensors = {
             "means": _f32(means), "scales": _f32(scales), "quats": _f32(quats), "opacities": _f32(opacities),
             "colors": _f32(colors), "velocity": _f32(velocity), "intrinsics": _f32(intrinsics),
             "camera_to_world": _f32(camera_to_world), "times": _f32(times),
         }
-        if lens is not None:
-            tensors["lens_models"], tensors["distortion"] = lens
+        if lens_models is not None:
+            tensors["lens_models"], tensors["distortion"] = lens_models, _f32(distortion)
         image, alpha, depth, state = forward_stages(sspec, vspec, cfg, near_plane, tensors)
         ctx.sspec, ctx.vspec, ctx.cfg, ctx.near_plane = sspec, vspec, cfg, near_plane
         ctx.tensors = tensors
         ctx.state = state
         ctx.shapes = [None if t is None else (t.shape, t.dtype) for t in (means, scales, quats, opacities, colors,
                                                                           velocity)]
+        ctx.camera_shapes = [None if t is None else (t.shape, t.dtype) for t in (intrinsics, camera_to_world, times,
+                                                                                 distortion)]
         if depth is None:
             depth = image.new_zeros(0)
             ctx.mark_non_differentiable(depth)
@@ -286,24 +306,27 @@ class _RenderFunction(torch.autograd.Function):
         d_image = d_image.to(torch.float32).contiguous()
         d_alpha = None if d_alpha is None else d_alpha.to(torch.float32).contiguous()
         d_depth = None if (d_depth is None or d_depth.numel() == 0) else d_depth.to(torch.float32).contiguous()
-        grads = backward_stages(ctx.sspec, vspec, ctx.cfg, ctx.near_plane, t, ctx.state, d_image, d_alpha, d_depth)
+        need = ctx.needs_input_grad
+        camera = bool(need[11] or need[12] or need[14])
+        grads = backward_stages(ctx.sspec, vspec, ctx.cfg, ctx.near_plane, t, ctx.state, d_image, d_alpha, d_depth,
+                                camera=camera)
         out = []
-        for name, shp in zip(_PARAM_NAMES, ctx.shapes):
+        for name, shp in zip(_PARAM_NAMES + _CAMERA_NAMES, ctx.shapes + ctx.camera_shapes):
             if shp is None or name not in grads:
                 out.append(None)
             else:
                 out.append(grads[name].reshape(shp[0]).to(shp[1]))
         ctx.state = None
-        return (None, None, None, None, None, *out, None, None, None)
+        # sspec, vspec, cfg, near_plane, lens_models | 6 scene tensors | intrinsics, c2w, times, distortion
+        return (None, None, None, None, None, *out[:6], out[6], out[7], None, out[9])
 
 
-def _check_cameras_no_grad(*tensors):
-    for t in tensors:
-        if isinstance(t, torch.Tensor) and t.requires_grad:
-            raise NotImplementedError(
-                "the b200 renderer does not differentiate camera parameters (intrinsics / camera_to_world / "
-                "times); detach them or use the dense renderer for camera optimisation."
-            )
+def _check_times_no_grad(times):
+    if isinstance(times, torch.Tensor) and times.requires_grad:
+        raise NotImplementedError(
+            "the b200 renderer does not differentiate the per-view times; detach them (the reference's "
+            "renderers take the time-offset means, not times)."
+        )
 
 
 def lens_tensors(lens_models, distortion, n_views: int, device):
@@ -325,32 +348,36 @@ def lens_tensors(lens_models, distortion, n_views: int, device):
         raise ValueError(f"unknown lens model code in {codes}")
     if all(c == _lib.LENS_PINHOLE for c in codes):
         return None
-    coeffs = torch.zeros(n_views, _lib.DISTORTION_FLOATS, dtype=torch.float32)
+    nd = _lib.DISTORTION_FLOATS
+    padded = torch.is_tensor(distortion) and distortion.ndim == 2 and distortion.shape[-1] == nd
+    rows = [None] * n_views
     if distortion is not None:
-        if torch.is_tensor(distortion) and distortion.ndim == 2:
-            rows = list(distortion.detach().cpu().to(torch.float32))
-        else:
-            rows = list(distortion)
+        rows = list(distortion.unbind(0)) if torch.is_tensor(distortion) else list(distortion)
         if len(rows) != n_views:
             raise ValueError(f"expected {n_views} distortion rows, got {len(rows)}")
-        names = {v: k for k, v in _lib.LENS_CODES.items()}
-        for b, (code, row) in enumerate(zip(codes, rows)):
-            if row is None or code == _lib.LENS_PINHOLE:  # pinhole views ignore distortion
-                continue
-            r = torch.as_tensor(row, dtype=torch.float32).flatten().cpu()
-            limit = _lib.LENS_COEFFS[names[code]]
-            if r.numel() > limit:  # projection.py:38-50 (_distortion_tensor)
-                raise ValueError(f"{names[code]} expects at most {limit} distortion coefficients, got {r.numel()}.")
-            coeffs[b, : r.numel()] = r
-    return (torch.tensor(codes, dtype=torch.int32, device=device).contiguous(), coeffs.to(device).contiguous())
+    names = {v: k for k, v in _lib.LENS_CODES.items()}
+    out = []
+    for code, row in zip(codes, rows):
+        if row is None or code == _lib.LENS_PINHOLE:  # pinhole views ignore distortion
+            out.append(torch.zeros(nd, dtype=torch.float32, device=device))
+            continue
+        # tensors keep their autograd graph: the coefficients can be learned through the render
+        r = (row if torch.is_tensor(row) else torch.as_tensor(row)).to(device=device, dtype=torch.float32).reshape(-1)
+        limit = nd if padded else _lib.LENS_COEFFS[names[code]]
+        if r.numel() > limit:  # projection.py:38-50 (_distortion_tensor)
+            raise ValueError(f"{names[code]} expects at most {limit} distortion coefficients, got {r.numel()}.")
+        out.append(torch.nn.functional.pad(r, (0, nd - r.numel())))
+    return (torch.tensor(codes, dtype=torch.int32, device=device).contiguous(), torch.stack(out).contiguous())
 
 
 def render_scene(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, near_plane: float, *, means, scales,
                  quats, opacities, colors, velocity, intrinsics, camera_to_world, times, lens=None):
     """Autograd entry used by every public render function.  ``lens``: the pair lens_tensors()
-    returns, or None for pinhole views only."""
+    returns, or None for pinhole views only.  Intrinsics, camera_to_world and the distortion may
+    require gradients (cameras learned through the render call)."""
     if not means.is_cuda:
         raise RuntimeError("the b200 renderer runs on CUDA devices only (got a tensor on %s)" % means.device)
-    _check_cameras_no_grad(intrinsics, camera_to_world, times)
-    return _RenderFunction.apply(sspec, vspec, cfg, float(near_plane), lens, means, scales, quats, opacities, colors,
-                                 velocity, intrinsics, camera_to_world, times)
+    _check_times_no_grad(times)
+    lens_models, distortion = lens if lens is not None else (None, None)
+    return _RenderFunction.apply(sspec, vspec, cfg, float(near_plane), lens_models, means, scales, quats, opacities,
+                                 colors, velocity, intrinsics, camera_to_world, times, distortion)

@@ -17,8 +17,8 @@ from .render import MIN_RENDER_DEPTH, SceneSpec, ViewSpec, lens_tensors, render_
 
 
 def _per_view(value, K: int, device) -> torch.Tensor:
-    if torch.is_tensor(value):
-        v = value.detach().to(device=device, dtype=torch.float32)
+    if torch.is_tensor(value):  # keeps the autograd graph: learned intrinsics get gradients
+        v = value.to(device=device, dtype=torch.float32)
         return v.expand(K) if v.ndim == 0 else v.reshape(K)
     return torch.full((K,), float(value), device=device, dtype=torch.float32)
 
