@@ -57,6 +57,7 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--stages", action="store_true", help="print per-stage times to stderr")
     ap.add_argument("--tile", type=int, default=None, help="tile size (8 or 16; default: the renderer's)")
+    ap.add_argument("--segments", type=int, default=0, help="backward list segments (1, 2, 4; default: automatic)")
     return ap.parse_args()
 
 
@@ -101,13 +102,13 @@ def workload_config(name, wl, world, scaling):
 class Step:
     """One render + loss forward/backward of a workload resident on the device."""
 
-    def __init__(self, wl, device, world, tile=None):
+    def __init__(self, wl, device, world, tile=None, segments=0):
         from dynaworld_b200.config import B200RendererConfig
 
         self.wl = wl
         self.dev = device
         self.world = world
-        self.cfg = B200RendererConfig() if tile is None else B200RendererConfig(tile_size=tile)
+        self.cfg = B200RendererConfig(tile_size=tile or 16, backward_segments=segments)
         self.params = {k: getattr(wl, k).to(device).contiguous().requires_grad_(True)
                        for k in ("means", "log_scales", "quats", "opacity_logits", "sh")}
         if wl.velocity is not None:
@@ -328,7 +329,7 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     L = _lib.load()
     wl, scaling = make_workload(args.workload, rank, world, args.scale, args.image_scale)
-    step = Step(wl, dev, world, args.tile)
+    step = Step(wl, dev, world, args.tile, args.segments)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
 
     def barrier():
@@ -432,7 +433,7 @@ def main():
     peak, peak_kind = hbm_peak()
     dur_s = means[dominant] / 1e3
     achieved = alg_bytes / dur_s / 1e9
-    traffic, traffic_src = ncu_traffic(dominant, args.workload) if args.tile is None else (None, None)
+    traffic, traffic_src = ncu_traffic(dominant, args.workload) if (args.tile is None and args.segments == 0) else (None, None)
     roofline = {"bound": "hbm", "kernel": f"{dominant} (gsb_{dominant})", "achieved": achieved, "peak": peak,
                 "unit": "GB/s", "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_src,
                 "peak_source": peak_kind, "bytes_per_launch": int(alg_bytes), "pairs": int(n_pairs),

@@ -60,7 +60,7 @@ class Options(C.Structure):
         ("tile_size", C.c_int32), ("flags", C.c_uint32), ("near_plane", C.c_float), ("alpha_clamp", C.c_float),
         ("alpha_cutoff", C.c_float), ("transmittance_threshold", C.c_float), ("eps", C.c_float),
         ("pixel_center", C.c_float), ("background", C.c_float * 3), ("bound_scale", C.c_float),
-        ("tiled_alpha_threshold", C.c_float),
+        ("tiled_alpha_threshold", C.c_float), ("backward_segments", C.c_int32),
     ]
 
 
@@ -105,14 +105,16 @@ SIGNATURES = {
     "gsb_bin_workspace": (C.c_size_t, [P(Views), P(Options), C.c_int32, C.c_uint32]),
     "gsb_bin": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, C.c_uint32, vp, vp, vp, vp, C.c_size_t,
                           vp]),
-    "gsb_raster_fwd": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "gsb_raster_checkpoint_floats": (C.c_size_t, [P(Views), P(Options)]),
+    "gsb_raster_fwd": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "gsb_loss_workspace": (C.c_size_t, [C.c_int32]),
     "gsb_loss_fwd_bwd": (C.c_int, [P(LossOptions), C.c_int32, C.c_int32, C.c_int32, C.c_int32, vp, vp, vp, vp, vp,
                                    C.c_size_t, vp]),
     "gsb_loss_fwd_bwd_noalloc": (C.c_int, [P(LossOptions), C.c_int32, C.c_int32, C.c_int32, C.c_int32, vp, vp, vp,
                                            vp, vp]),
     "gsb_scale_planes": (C.c_int, [vp, vp, vp, C.c_int32, C.c_int64, vp]),
-    "gsb_raster_bwd": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "gsb_raster_bwd": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                                 vp]),
     "gsb_preprocess_bwd": (C.c_int, [P(Scene), P(Views), P(Options), vp, vp, P(SceneGrads), vp]),
     "gsb_camera_bwd": (C.c_int, [P(Scene), P(Views), P(Options), vp, vp, P(CameraGrads), vp]),
     "gsb_splats2d_order_workspace": (C.c_size_t, [P(Splats2D)]),

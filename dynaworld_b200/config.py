@@ -44,12 +44,15 @@ class B200RendererConfig:
     sh_clamp: bool = True
     depth: bool = False
     check_status: bool = False
+    backward_segments: int = 0  # 1, 2, 4: pieces of each tile list in the reverse blend; 0: automatic
 
     def __post_init__(self):
         if self.mode not in MODES:
             raise ValueError(f"b200.mode must be one of {MODES}, got {self.mode!r}.")
         if self.tile_size not in (8, 16):
             raise ValueError(f"b200.tile_size must be 8 or 16, got {self.tile_size}.")
+        if self.backward_segments not in (0, 1, 2, 4):
+            raise ValueError(f"b200.backward_segments must be 0, 1, 2 or 4, got {self.backward_segments}.")
         if len(self.background) != 3:
             raise ValueError(f"b200.background must contain three values, got {self.background!r}.")
 
@@ -86,6 +89,7 @@ class B200RendererConfig:
             sh_clamp=bool(values.get("sh_clamp", cls.sh_clamp)),
             depth=bool(values.get("depth", cls.depth)),
             check_status=bool(values.get("check_status", cls.check_status)),
+            backward_segments=int(values.get("backward_segments", cls.backward_segments)),
         )
 
     def options(self, near_plane: float) -> "_lib.Options":
@@ -109,6 +113,7 @@ class B200RendererConfig:
             o.background[k] = self.background[k]
         o.bound_scale = self.bound_scale
         o.tiled_alpha_threshold = self.tiled_alpha_threshold
+        o.backward_segments = self.backward_segments
         return o
 
 

@@ -88,6 +88,8 @@ static gsb_status check_opts(const gsb_options* o) {
   if (o->tile_size != 8 && o->tile_size != 16) return GSB_ERR_ARG;
   if (!(o->near_plane > 0.0f)) return GSB_ERR_ARG;
   if (!(o->alpha_cutoff >= 0.0f) || !(o->transmittance_threshold >= 0.0f) || !(o->eps >= 0.0f)) return GSB_ERR_ARG;
+  const int seg = o->backward_segments;
+  if (seg != 0 && seg != 1 && seg != 2 && seg != 4) return GSB_ERR_ARG;
   return GSB_OK;
 }
 
@@ -295,10 +297,20 @@ GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int3
 
 // ---- stages 4 and 6 --------------------------------------------------------------------------
 
+static size_t checkpoint_floats(const gsb_views& v, const gsb_options& o) {
+  const int nseg = raster_segments(v, o);
+  return nseg > 1 ? size_t(nseg - 1) * 6 * size_t(v.n_views) * size_t(v.height) * size_t(v.width) : 0;
+}
+
+GSB_API size_t gsb_raster_checkpoint_floats(const gsb_views* views, const gsb_options* opts) {
+  if (check_frame(views) != GSB_OK || check_opts(opts) != GSB_OK) return 0;
+  return checkpoint_floats(*views, *opts);
+}
+
 GSB_API gsb_status gsb_raster_fwd(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians,
                                   const float* records, const uint64_t* sorted_keys, const uint32_t* tile_ranges,
                                   const uint32_t* tile_order, float* image, float* alpha, float* depth,
-                                  float* pixel_t, uint32_t* pixel_state, void* stream) {
+                                  float* pixel_t, uint32_t* pixel_state, float* pixel_ckpt, void* stream) {
   gsb_status s;
   if ((s = check_frame(views)) != GSB_OK) return s;
   if ((s = check_opts(opts)) != GSB_OK) return s;
@@ -310,6 +322,8 @@ GSB_API gsb_status gsb_raster_fwd(const gsb_views* views, const gsb_options* opt
   a.records = records, a.keys = sorted_keys, a.ranges = tile_ranges, a.order = tile_order;
   a.image = image, a.alpha = alpha, a.depth = (opts->flags & GSB_RENDER_DEPTH) ? depth : nullptr;
   a.pixel_t = pixel_t, a.pixel_state = pixel_state;
+  a.nseg = raster_segments(*views, *opts), a.ckpt = pixel_ckpt;
+  if (a.nseg > 1 && !pixel_ckpt) return GSB_ERR_ARG;
   if (views->n_views > 65535) return GSB_ERR_SHAPE;
   return launch_raster_fwd(a, as_stream(stream));
 }
@@ -317,7 +331,7 @@ GSB_API gsb_status gsb_raster_fwd(const gsb_views* views, const gsb_options* opt
 GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians,
                                   const float* records, const uint64_t* sorted_keys, const uint32_t* tile_ranges,
                                   const uint32_t* tile_order, const float* pixel_t, const uint32_t* pixel_state,
-                                  const float* d_image,
+                                  const float* pixel_ckpt, const float* d_image,
                                   const float* d_alpha, const float* d_depth, const float* view_scale, float* grad2d,
                                   void* stream) {
   gsb_status s;
@@ -330,6 +344,8 @@ GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opt
   a.rc = make_consts(*views, *opts);
   a.records = records, a.keys = sorted_keys, a.ranges = tile_ranges, a.order = tile_order;
   a.pixel_t = const_cast<float*>(pixel_t), a.pixel_state = const_cast<uint32_t*>(pixel_state);
+  a.nseg = raster_segments(*views, *opts), a.ckpt = const_cast<float*>(pixel_ckpt);
+  if (a.nseg > 1 && !pixel_ckpt) return GSB_ERR_ARG;
   a.d_image = d_image, a.d_alpha = d_alpha, a.d_depth = d_depth, a.view_scale = view_scale, a.grad2d = grad2d;
   if (views->n_views > 65535) return GSB_ERR_SHAPE;
   return launch_raster_bwd(a, as_stream(stream));

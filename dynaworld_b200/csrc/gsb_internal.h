@@ -55,6 +55,8 @@ struct RasterArgs {
   float* depth;
   float* pixel_t;
   uint32_t* pixel_state;
+  float* ckpt;   // backward segment checkpoints [nseg - 1][6][B*H*W], NULL when nseg == 1
+  int nseg;      // backward list segments per tile (1, 2 or 4)
   const float* d_image;
   const float* d_alpha;
   const float* d_depth;
@@ -63,6 +65,7 @@ struct RasterArgs {
 };
 gsb_status launch_raster_fwd(const RasterArgs& a, cudaStream_t st);
 gsb_status launch_raster_bwd(const RasterArgs& a, cudaStream_t st);
+int raster_segments(const gsb_views& v, const gsb_options& o);  // backward list segments (1, 2, 4)
 
 // Preprocess (preprocess.cu).
 gsb_status launch_depth_keys(const gsb_scene& sc, const gsb_views& vw, uint64_t* keys64, uint32_t* keys32,

@@ -116,9 +116,13 @@ __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* rec
   return q <= tau * 1.0001f + 0.01f;
 }
 
-template <int TILE, int PX>
+// Floats a checkpoint slot holds per pixel: S, then the suffix sums of r, g, b, weight, depth.
+constexpr int kCkptFloats = 6;
+
+template <int TILE, int PX, int NSEG>  // NSEG: list segments of the backward (checkpoints between)
 __global__ void __launch_bounds__(TILE* TILE / PX) raster_fwd_kernel(RasterArgs a) {
   constexpr int NW = TILE * TILE / (32 * PX);
+  constexpr int NB = NSEG > 1 ? NSEG - 1 : 1;  // checkpoint slots (boundaries between segments)
   __shared__ float4 s_geo[NW][32], s_cot[NW][32], s_col[NW][32];
   const RenderConsts& rc = a.rc;
   const uint32_t slot = blockIdx.y * uint32_t(rc.n_tiles) + blockIdx.x;
@@ -149,51 +153,106 @@ __global__ void __launch_bounds__(TILE* TILE / PX) raster_fwd_kernel(RasterArgs 
     n_proc[k] = end - start;
     done[k] = !(px < a.W && py[k] < a.H);
   }
+  // Segment boundaries of the list (the backward runs each segment as its own CTA): the state of
+  // every pixel just before entry bnd[s] is kept, as a prefix, and written out as the suffix the
+  // backward of segment s starts from.
+  uint32_t bnd[NB];
+  float kS[NB][PX], kC0[NB][PX], kC1[NB][PX], kC2[NB][PX], kW[NB][PX], kD[NB][PX];
+  int next = 0;
+#pragma unroll
+  for (int s = 0; s < NB; ++s) bnd[s] = start + uint32_t((uint64_t(s + 1) * (end - start)) / NSEG);
+  auto snapshot = [&](int s) {  // held in registers (global stores inside the walk cost more)
+#pragma unroll
+    for (int k = 0; k < PX; ++k)
+      kS[s][k] = S[k], kC0[s][k] = C0[k], kC1[s][k] = C1[k], kC2[s][k] = C2[k], kW[s][k] = Ws[k], kD[s][k] = D[k];
+  };
+  // blend the entry in slot j of the current chunk (list index c - start + j) into every live pixel
+  auto blend = [&](uint32_t c, int j) {
+    const float4 g = s_geo[warp][j];
+    const float4 ct = s_cot[warp][j];
+    const float dx = __fsub_rn(fx, g.x);
+#pragma unroll
+    for (int k = 0; k < PX; ++k) {
+      if (done[k]) continue;
+      const float dy = __fsub_rn(fy[k], g.y);
+      const float q = pair_q(g.z, g.w, ct.x, dx, dy);
+      if (!(q <= ct.z)) continue;
+      const float e = __expf(fminf(-0.5f * q, 0.0f));
+      const float alpha = fminf(fmaxf(ct.y * e, 0.0f), rc.alpha_clamp);
+      if (!(alpha >= rc.alpha_cutoff)) continue;
+      const float4 col = s_col[warp][j];
+      const float T = S[k] * ct.w;
+      const float w = T * alpha;
+      C0[k] = fmaf(w, col.x, C0[k]);
+      C1[k] = fmaf(w, col.y, C1[k]);
+      C2[k] = fmaf(w, col.z, C2[k]);
+      Ws[k] += w;
+      D[k] = fmaf(w, col.w, D[k]);
+      const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
+      S[k] = S[k] * (f * inv_f0);
+      if (T * f < rc.t_threshold) {  // T after this entry
+        done[k] = true;
+        n_proc[k] = c - start + uint32_t(j) + 1u;
+      }
+    }
+  };
   for (uint32_t c = start; c < end; c += 32) {
     if (__all_sync(kFull, all_of(done))) break;
     const uint32_t idx = c + lane;
     const bool keep = idx < end && load_entry<block_h<PX>()>(a, recs, idx, idx - start, bx0, by0, ws, lane);
     uint32_t m = __ballot_sync(kFull, keep);
     __syncwarp();
-    while (m && !all_of(done)) {
-      const int j = __ffs(m) - 1;
-      m &= m - 1;
-      const float4 g = s_geo[warp][j];
-      const float4 ct = s_cot[warp][j];
-      const float dx = __fsub_rn(fx, g.x);
+    if (NSEG > 1) {
+      // boundaries inside this chunk (warp-uniform): blend the entries before one, then keep the state
 #pragma unroll
-      for (int k = 0; k < PX; ++k) {
-        if (done[k]) continue;
-        const float dy = __fsub_rn(fy[k], g.y);
-        const float q = pair_q(g.z, g.w, ct.x, dx, dy);
-        if (!(q <= ct.z)) continue;
-        const float e = __expf(fminf(-0.5f * q, 0.0f));
-        const float alpha = fminf(fmaxf(ct.y * e, 0.0f), rc.alpha_clamp);
-        if (!(alpha >= rc.alpha_cutoff)) continue;
-        const float4 col = s_col[warp][j];
-        const float T = S[k] * ct.w;
-        const float w = T * alpha;
-        C0[k] = fmaf(w, col.x, C0[k]);
-        C1[k] = fmaf(w, col.y, C1[k]);
-        C2[k] = fmaf(w, col.z, C2[k]);
-        Ws[k] += w;
-        D[k] = fmaf(w, col.w, D[k]);
-        const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
-        S[k] = S[k] * (f * inv_f0);
-        if (T * f < rc.t_threshold) {  // T after this entry
-          done[k] = true;
-          n_proc[k] = c - start + uint32_t(j) + 1u;
+      for (int s = 0; s < NB; ++s) {
+        if (next == s && bnd[s] < c + 32u) {
+          const uint32_t cut = bnd[s] > c ? bnd[s] - c : 0u;  // slots j < cut lie before the boundary
+          const uint32_t before = (1u << cut) - 1u;           // cut <= 31
+          uint32_t mb = m & before;
+          while (mb && !all_of(done)) {
+            const int j = __ffs(mb) - 1;
+            mb &= mb - 1;
+            blend(c, j);
+          }
+          m &= ~before;
+          snapshot(s);
+          next = s + 1;
         }
       }
     }
+    while (m && !all_of(done)) {
+      const int j = __ffs(m) - 1;
+      m &= m - 1;
+      blend(c, j);
+    }
     __syncwarp();  // slots are rewritten by the next chunk
   }
+  if (NSEG > 1) {
+    // boundaries the pixel never reached (stopped early, or no later entry) hold the final state
+#pragma unroll
+    for (int s = 0; s < NB; ++s)
+      if (next <= s) snapshot(s);
+  }
   const size_t HW = size_t(a.H) * a.W;
+  const size_t total_px = size_t(a.B) * HW;
 #pragma unroll
   for (int k = 0; k < PX; ++k) {
     if (!(px < a.W && py[k] < a.H)) continue;
     const size_t poff = size_t(py[k]) * a.W + px;
     const size_t pix = size_t(view) * HW + poff;
+    if (NSEG > 1) {  // slot s: S before bnd[s] and the colour / weight / depth of the entries after it
+#pragma unroll
+      for (int s = 0; s < NB; ++s) {
+        float* ck = a.ckpt + size_t(s) * kCkptFloats * total_px + pix;
+        ck[0] = kS[s][k];
+        ck[total_px] = C0[k] - kC0[s][k];
+        ck[2 * total_px] = C1[k] - kC1[s][k];
+        ck[3 * total_px] = C2[k] - kC2[s][k];
+        ck[4 * total_px] = Ws[k] - kW[s][k];
+        ck[5 * total_px] = D[k] - kD[s][k];
+      }
+    }
     const float wc = fminf(fmaxf(Ws[k], 0.0f), 1.0f);
     const float one_m = __fsub_rn(1.0f, wc);
     const float cc[3] = {C0[k], C1[k], C2[k]};
@@ -252,13 +311,18 @@ __device__ __forceinline__ float warp_sum10(float v[12], int lane, int* index) {
 // it the warp reduces first.
 constexpr int kSparseContributors = 4;
 
-template <int TILE, int PX, bool DEPTH>  // DEPTH: a depth gradient is given
+// DEPTH: a depth gradient is given.  NSEG: the tile's list is cut into NSEG segments
+// [s n / NSEG, (s + 1) n / NSEG), each walked by its own CTA (adjacent in launch order), starting
+// from the forward's checkpoint of its upper boundary (the last segment from the final state).
+template <int TILE, int PX, bool DEPTH, int NSEG>
 __global__ void __launch_bounds__(TILE* TILE / PX) raster_bwd_kernel(RasterArgs a) {
   constexpr int NW = TILE * TILE / (32 * PX);
   __shared__ float4 s_geo[NW][32], s_cot[NW][32], s_col[NW][32];
   __shared__ uint32_t s_rank[NW][32];
   const RenderConsts& rc = a.rc;
-  const uint32_t slot = blockIdx.y * uint32_t(rc.n_tiles) + blockIdx.x;
+  const uint32_t cta = blockIdx.y * uint32_t(rc.n_tiles) * NSEG + blockIdx.x;
+  const uint32_t slot = cta / NSEG;
+  const int seg = int(cta % NSEG);
   const uint32_t vt = a.order ? a.order[slot] : slot;  // heaviest tiles first
   const int view = int(vt / uint32_t(rc.n_tiles)), tile = int(vt % uint32_t(rc.n_tiles));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -270,14 +334,18 @@ __global__ void __launch_bounds__(TILE* TILE / PX) raster_bwd_kernel(RasterArgs 
   const float fx = float(px) + rc.pixel_center;
   const size_t rb = (size_t(view) * rc.n_tiles + tile) * 2;
   const uint32_t start = a.ranges[rb];
+  const uint32_t n_list = a.ranges[rb + 1] - start;
+  const uint32_t lo = uint32_t((uint64_t(seg) * n_list) / NSEG);       // this segment's entries
+  const uint32_t hi = uint32_t((uint64_t(seg + 1) * n_list) / NSEG);
   const float* recs = a.records + size_t(view) * a.G * GSB_RECORD_FLOATS;
   float* g2 = a.grad2d + size_t(view) * a.G * GSB_GRAD2D_FLOATS;
   const WarpSlots ws{s_geo[warp], s_cot[warp], s_col[warp], s_rank[warp]};
 
   const size_t HW = size_t(a.H) * a.W;
+  const size_t total_px = size_t(a.B) * HW;
   float fy[PX], S[PX], g0[PX], g1[PX], g2c[PX], gW[PX], gD[PX];
   float R0[PX], R1[PX], R2[PX], RW[PX], RD[PX];
-  uint32_t n_proc[PX];
+  uint32_t n_proc[PX];  // entries of this segment the pixel blended: list index < n_proc
   const float sc = a.view_scale ? a.view_scale[view] : 1.0f;
 #pragma unroll
   for (int k = 0; k < PX; ++k) {
@@ -291,7 +359,16 @@ __global__ void __launch_bounds__(TILE* TILE / PX) raster_bwd_kernel(RasterArgs 
       const size_t pix = size_t(view) * HW + poff;
       S[k] = a.pixel_t[pix];
       const uint32_t st = a.pixel_state[pix];
-      n_proc[k] = st & kCountMask;
+      n_proc[k] = min(st & kCountMask, hi);
+      if (NSEG > 1 && seg < NSEG - 1) {  // start from the checkpoint at hi
+        const float* ck = a.ckpt + size_t(seg) * kCkptFloats * total_px + pix;
+        S[k] = ck[0];
+        R0[k] = ck[total_px];
+        R1[k] = ck[2 * total_px];
+        R2[k] = ck[3 * total_px];
+        RW[k] = ck[4 * total_px];
+        RD[k] = ck[5 * total_px];
+      }
       const uint32_t mask = st >> kCountBits;
       const float* di = a.d_image + size_t(view) * 3 * HW + poff;
       g0[k] = (mask & 1u) ? di[0] * sc : 0.0f;
@@ -302,12 +379,14 @@ __global__ void __launch_bounds__(TILE* TILE / PX) raster_bwd_kernel(RasterArgs 
       if (a.d_depth) gD[k] = a.d_depth[pix];
     }
   }
-  // list prefix this warp has to revisit
+  // list range [lo, wmax) this warp has to revisit
   const uint32_t wmax = __reduce_max_sync(kFull, max_of(n_proc));
+  const int64_t cb_lo = int64_t(lo / 32) * 32;
 
-  for (int64_t cb = wmax ? int64_t((wmax - 1) / 32) * 32 : -32; cb >= 0; cb -= 32) {
+  for (int64_t cb = wmax > lo ? int64_t((wmax - 1) / 32) * 32 : -32; cb >= cb_lo; cb -= 32) {
     const uint32_t li = uint32_t(cb) + lane;
-    const bool keep = li < wmax && load_entry<block_h<PX>()>(a, recs, start + li, li, bx0, by0, ws, lane);
+    const bool keep = li >= lo && li < wmax &&
+                      load_entry<block_h<PX>()>(a, recs, start + li, li, bx0, by0, ws, lane);
     uint32_t m = __ballot_sync(kFull, keep);
     __syncwarp();
     while (m) {
@@ -402,32 +481,62 @@ static_assert(raster_threads<16, 1>() == 256 && raster_threads<8, 1>() == 64, "w
 // largest grids (32 x 1080p: 66 -> 60 ms; 8 x 384^2: 0.60 -> 0.69 ms).
 constexpr uint64_t kFwdPairedTiles = 32768;
 constexpr uint64_t kBwdPairedTiles = 2048;
+// Below this many tiles the backward cuts every tile's list in four (gsb_options.backward_segments
+// = 0): four times the CTAs and a quarter of the serial walk per tile, which lets it pair pixels
+// per lane at any size, for 72 bytes of checkpoint per pixel.  Measured on one B200, 16 x 128^2
+// (1024 tiles): backward 1.10 ms (1 segment) -> 0.92 (2) -> 0.82 (4) -> 0.81 (8, whose forward
+// checkpoints cost more than that); 8 x 384^2 (4608 tiles): 1.57 -> 1.61 (2), so larger grids keep
+// one segment.
+constexpr uint64_t kSegmentedTiles = 2048;
+constexpr int kAutoSegments = 4;
+
+template <int TILE, int PX, int NSEG>
+static void fwd_launch_seg(const RasterArgs& a, dim3 grid, cudaStream_t st) {
+  raster_fwd_kernel<TILE, PX, NSEG><<<grid, raster_threads<TILE, PX>(), 0, st>>>(a);
+}
 
 template <int TILE, int PX>
 static void fwd_launch(const RasterArgs& a, dim3 grid, cudaStream_t st) {
   note_launch();
-  raster_fwd_kernel<TILE, PX><<<grid, raster_threads<TILE, PX>(), 0, st>>>(a);
+  if (a.nseg == 4) fwd_launch_seg<TILE, PX, 4>(a, grid, st);
+  else if (a.nseg == 2) fwd_launch_seg<TILE, PX, 2>(a, grid, st);
+  else fwd_launch_seg<TILE, PX, 1>(a, grid, st);
+}
+
+template <int TILE, int PX, int NSEG>
+static void bwd_launch_seg(const RasterArgs& a, cudaStream_t st) {
+  const dim3 grid(unsigned(a.rc.n_tiles) * NSEG, a.B);  // the segments of a tile are adjacent
+  if (a.d_depth) raster_bwd_kernel<TILE, PX, true, NSEG><<<grid, raster_threads<TILE, PX>(), 0, st>>>(a);
+  else raster_bwd_kernel<TILE, PX, false, NSEG><<<grid, raster_threads<TILE, PX>(), 0, st>>>(a);
 }
 
 template <int TILE, int PX>
-static void bwd_launch(const RasterArgs& a, dim3 grid, cudaStream_t st) {
+static void bwd_launch(const RasterArgs& a, cudaStream_t st) {
   note_launch();
-  if (a.d_depth) raster_bwd_kernel<TILE, PX, true><<<grid, raster_threads<TILE, PX>(), 0, st>>>(a);
-  else raster_bwd_kernel<TILE, PX, false><<<grid, raster_threads<TILE, PX>(), 0, st>>>(a);
+  if (a.nseg == 4) bwd_launch_seg<TILE, PX, 4>(a, st);
+  else if (a.nseg == 2) bwd_launch_seg<TILE, PX, 2>(a, st);
+  else bwd_launch_seg<TILE, PX, 1>(a, st);
 }
 
-// GSB200_RASTER_PX=1 or 2 forces the pixels per lane of both stages (tests and tuning); read at
-// every launch so that a process can switch it between calls.
-static bool paired_launch(uint64_t tiles, uint64_t threshold) {
-  const char* force = std::getenv("GSB200_RASTER_PX");
-  if (force && force[0] == '1' && force[1] == '\0') return false;
-  if (force && force[0] == '2' && force[1] == '\0') return true;
+// GSB200_RASTER_PX=1 or 2 forces the pixels per lane of both stages, GSB200_RASTER_PX_BWD of the
+// backward alone (tests and tuning; results do not depend on them); read at every launch so that
+// a process can switch them between calls.
+static int forced_px(const char* name) {
+  const char* v = std::getenv(name);
+  if (v && (v[0] == '1' || v[0] == '2') && v[1] == '\0') return v[0] - '0';
+  return 0;
+}
+
+static bool paired_launch(uint64_t tiles, uint64_t threshold, bool backward) {
+  int force = backward ? forced_px("GSB200_RASTER_PX_BWD") : 0;
+  if (!force) force = forced_px("GSB200_RASTER_PX");
+  if (force) return force == 2;
   return tiles >= threshold;
 }
 
 gsb_status launch_raster_fwd(const RasterArgs& a, cudaStream_t st) {
   const dim3 grid(a.rc.n_tiles, a.B);
-  const bool paired = paired_launch(uint64_t(a.rc.n_tiles) * uint64_t(a.B), kFwdPairedTiles);
+  const bool paired = paired_launch(uint64_t(a.rc.n_tiles) * uint64_t(a.B), kFwdPairedTiles, false);
   if (a.rc.tile == 16) paired ? fwd_launch<16, 2>(a, grid, st) : fwd_launch<16, 1>(a, grid, st);
   else if (a.rc.tile == 8) paired ? fwd_launch<8, 2>(a, grid, st) : fwd_launch<8, 1>(a, grid, st);
   else return GSB_ERR_ARG;
@@ -436,12 +545,19 @@ gsb_status launch_raster_fwd(const RasterArgs& a, cudaStream_t st) {
 
 gsb_status launch_raster_bwd(const RasterArgs& a, cudaStream_t st) {
   if (cudaMemsetAsync(a.grad2d, 0, size_t(a.B) * a.G * GSB_GRAD2D_FLOATS * sizeof(float), st)) return GSB_ERR_CUDA;
-  const dim3 grid(a.rc.n_tiles, a.B);
-  const bool paired = paired_launch(uint64_t(a.rc.n_tiles) * uint64_t(a.B), kBwdPairedTiles);
-  if (a.rc.tile == 16) paired ? bwd_launch<16, 2>(a, grid, st) : bwd_launch<16, 1>(a, grid, st);
-  else if (a.rc.tile == 8) paired ? bwd_launch<8, 2>(a, grid, st) : bwd_launch<8, 1>(a, grid, st);
+  // segmented lists restore the parallelism two pixels per lane gives up: pair them always then
+  const bool paired = paired_launch(uint64_t(a.rc.n_tiles) * uint64_t(a.B), a.nseg > 1 ? 0 : kBwdPairedTiles, true);
+  if (a.rc.tile == 16) paired ? bwd_launch<16, 2>(a, st) : bwd_launch<16, 1>(a, st);
+  else if (a.rc.tile == 8) paired ? bwd_launch<8, 2>(a, st) : bwd_launch<8, 1>(a, st);
   else return GSB_ERR_ARG;
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
+int raster_segments(const gsb_views& v, const gsb_options& o) {
+  if (o.backward_segments == 1 || o.backward_segments == 2 || o.backward_segments == 4) return o.backward_segments;
+  const uint64_t tiles = uint64_t(v.n_views) * uint64_t((v.width + o.tile_size - 1) / o.tile_size) *
+                         uint64_t((v.height + o.tile_size - 1) / o.tile_size);
+  return tiles < kSegmentedTiles ? kAutoSegments : 1;
 }
 
 }  // namespace gsb

@@ -74,6 +74,12 @@ class FrameState:
     pixel_t: torch.Tensor
     pixel_state: torch.Tensor
     n_pairs: int
+    ckpt: torch.Tensor | None = None  # backward segment checkpoints (None: one segment)
+
+
+def checkpoint_buffer(views: _lib.Views, opts: _lib.Options, device) -> torch.Tensor | None:
+    n = int(_lib.lib().gsb_raster_checkpoint_floats(views, opts))
+    return torch.empty(n, dtype=torch.float32, device=device) if n else None
 
 
 def _stream(device) -> int:
@@ -194,6 +200,7 @@ def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, n
     depth = torch.empty(B, H, W, dtype=torch.float32, device=dev) if cfg.depth else None
     pixel_t = torch.empty(B, H, W, dtype=torch.float32, device=dev)
     pixel_state = torch.empty(B, H, W, dtype=torch.int32, device=dev)
+    ckpt = checkpoint_buffer(views, opts, dev)
     head = head.wait()
     n_pairs = head[0] & 0xFFFFFFFF
     for name, code in (("gsb_depth_order", head[1]), ("gsb_preprocess_fwd", head[2])):
@@ -209,10 +216,10 @@ def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, n
                                                       ranges.data_ptr(), order.data_ptr(), image.data_ptr(),
                                                       alpha.data_ptr(),
                                                       _lib.ptr(depth), pixel_t.data_ptr(), pixel_state.data_ptr(),
-                                                      st))
+                                                      _lib.ptr(ckpt), st))
     if cfg.check_status:
         _lib.check("gsb_bin", int(ws3.view(torch.int32)[0].item()))
-    state = FrameState(rank_of, records, keys, ranges, order, pixel_t, pixel_state, n_pairs)
+    state = FrameState(rank_of, records, keys, ranges, order, pixel_t, pixel_state, n_pairs, ckpt)
     return image, alpha, depth, state
 
 
@@ -236,6 +243,7 @@ def backward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, 
                                                       state.keys.data_ptr(), state.ranges.data_ptr(),
                                                       state.order.data_ptr(),
                                                       state.pixel_t.data_ptr(), state.pixel_state.data_ptr(),
+                                                      _lib.ptr(state.ckpt),
                                                       d_image.data_ptr(), _lib.ptr(d_alpha), _lib.ptr(d_depth),
                                                       _lib.ptr(view_scale), grad2d.data_ptr(), st))
     out = {k: torch.empty_like(tensors[k]) for k in ("means", "scales", "quats", "opacities", "colors")}

@@ -22,7 +22,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from .render import FrameState, _stage, _stream, _ws, read_words
+from .render import FrameState, _stage, _stream, _ws, checkpoint_buffer, read_words
 
 CONIC = _lib.SPLATS2D_CONIC
 PACKED = _lib.SPLATS2D_PACKED
@@ -112,6 +112,7 @@ def forward_stages_2d(fmt: int, B: int, G: int, H: int, W: int, opt: Splat2DOpti
     alpha = torch.empty(B, H, W, dtype=torch.float32, device=dev)
     pixel_t = torch.empty(B, H, W, dtype=torch.float32, device=dev)
     pixel_state = torch.empty(B, H, W, dtype=torch.int32, device=dev)
+    ckpt = checkpoint_buffer(frame, opts, dev)
     head = head.wait()
     n_pairs = head[0] & 0xFFFFFFFF
     for name, code in (("gsb_splats2d_order", head[1]), ("gsb_splats2d_preprocess", head[2])):
@@ -126,8 +127,8 @@ def forward_stages_2d(fmt: int, B: int, G: int, H: int, W: int, opt: Splat2DOpti
         _lib.check("gsb_raster_fwd", L.gsb_raster_fwd(frame, opts, G, records.data_ptr(), keys.data_ptr(),
                                                       ranges.data_ptr(), order.data_ptr(), image.data_ptr(),
                                                       alpha.data_ptr(), None, pixel_t.data_ptr(),
-                                                      pixel_state.data_ptr(), st))
-    state = FrameState(rank_of, records, keys, ranges, order, pixel_t, pixel_state, n_pairs)
+                                                      pixel_state.data_ptr(), _lib.ptr(ckpt), st))
+    state = FrameState(rank_of, records, keys, ranges, order, pixel_t, pixel_state, n_pairs, ckpt)
     return image, alpha, state
 
 
@@ -144,7 +145,8 @@ def backward_stages_2d(fmt: int, B: int, G: int, H: int, W: int, opt: Splat2DOpt
         _lib.check("gsb_raster_bwd", L.gsb_raster_bwd(frame, opts, G, state.records.data_ptr(),
                                                       state.keys.data_ptr(), state.ranges.data_ptr(),
                                                       state.order.data_ptr(), state.pixel_t.data_ptr(),
-                                                      state.pixel_state.data_ptr(), d_image.data_ptr(),
+                                                      state.pixel_state.data_ptr(), _lib.ptr(state.ckpt),
+                                                      d_image.data_ptr(),
                                                       _lib.ptr(d_alpha), None, None, grad2d.data_ptr(), st))
     names = ("packed", "colors") if fmt == PACKED else ("means", "conics", "opacities", "colors")
     out = {k: torch.empty_like(t[k]) for k in names}

@@ -111,6 +111,10 @@ typedef struct gsb_options {
   float background[3];            /* (1,1,1) (dense.py:231) */
   float bound_scale;              /* tiled compat: 3.0 (tiled.py:7) */
   float tiled_alpha_threshold;    /* tiled compat: 1/255 (tiled.py:7) */
+  int32_t backward_segments;      /* 1, 2 or 4: the reverse blend walks every tile list as that
+                                     many independent pieces (needs gsb_raster_checkpoint_floats
+                                     of checkpoints from the forward); 0: the library's choice for
+                                     the grid size.  Results do not depend on it. */
 } gsb_options;
 
 /* Gradients of the scene parameters (device, shapes as gsb_scene; NULL entries are skipped). */
@@ -193,15 +197,19 @@ GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int3
                            void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- stage 4: front-to-back blend (dense.py:208-236) -------------------------------------- */
+/* Floats of per-pixel checkpoints the reverse blend needs for opts->backward_segments (0: none;
+   then pixel_ckpt may be NULL). */
+GSB_API size_t gsb_raster_checkpoint_floats(const gsb_views* views, const gsb_options* opts);
 /* image [B,3,H,W] (clamped), alpha [B,H,W] = sum of weights, depth [B,H,W] or NULL,
-   pixel_t [B,H,W] and pixel_state [B,H,W]: the per-pixel state gsb_raster_bwd needs.
+   pixel_t [B,H,W], pixel_state [B,H,W] and pixel_ckpt: the per-pixel state gsb_raster_bwd needs.
    tile_order: gsb_bin's launch order, or NULL for (view, tile) order. */
 GSB_API gsb_status gsb_raster_fwd(const gsb_views* views, const gsb_options* opts,
                                   int32_t n_gaussians, const float* records,
                                   const uint64_t* sorted_keys, const uint32_t* tile_ranges,
                                   const uint32_t* tile_order,
                                   float* image, float* alpha, float* depth,
-                                  float* pixel_t, uint32_t* pixel_state, void* stream);
+                                  float* pixel_t, uint32_t* pixel_state, float* pixel_ckpt,
+                                  void* stream);
 
 /* ---- stage 5: fused L1 + SSIM loss and its gradient (losses.py:13-85) --------------------- */
 GSB_API size_t gsb_loss_workspace(int32_t n_images);
@@ -233,12 +241,14 @@ GSB_API gsb_status gsb_scale_planes(const float* in, const float* scale, float* 
 
 /* ---- stage 6: reverse blend, per-(view, Gaussian) 2-D gradients --------------------------- */
 /* grad2d[(b*G + r)*10 ..] = dL/d(mx, my, A, B, C, opacity, r, g, b, z) of the r-th nearest
-   Gaussian of view b; zeroed by the call.  d_alpha, d_depth, view_scale may be NULL. */
+   Gaussian of view b; zeroed by the call.  d_alpha, d_depth, view_scale may be NULL; opts and
+   pixel_ckpt as given to gsb_raster_fwd. */
 GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opts,
                                   int32_t n_gaussians, const float* records,
                                   const uint64_t* sorted_keys, const uint32_t* tile_ranges,
                                   const uint32_t* tile_order,
                                   const float* pixel_t, const uint32_t* pixel_state,
+                                  const float* pixel_ckpt,
                                   const float* d_image, const float* d_alpha,
                                   const float* d_depth, const float* view_scale,
                                   float* grad2d, void* stream);

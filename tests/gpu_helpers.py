@@ -17,8 +17,9 @@ def intrinsics_of(wl, device=DEV):
 
 
 def render_raw(wl, cfg: B200RendererConfig | None = None, *, grads=True, loss=True, device=DEV, lens_models=None,
-               distortion=None):
-    """render_b200 + reconstruction_loss_per_image on the GPU; returns a dict of CPU tensors."""
+               distortion=None, depth_loss=False):
+    """render_b200 + reconstruction_loss_per_image on the GPU; returns a dict of CPU tensors.
+    ``depth_loss``: also back-propagate through the alpha and depth outputs (needs cfg.depth)."""
     cfg = cfg or B200RendererConfig()
     leaves = {k: getattr(wl, k).to(device).requires_grad_(grads) for k in
               ("means", "log_scales", "quats", "opacity_logits", "sh")}
@@ -35,7 +36,10 @@ def render_raw(wl, cfg: B200RendererConfig | None = None, *, grads=True, loss=Tr
         l = reconstruction_loss_per_image(image, wl.target.to(device))
         out["loss"] = l.detach().cpu()
         if grads:
-            l.sum().backward()
+            total = l.sum()
+            if depth_loss:
+                total = total + 1e-3 * (depth * torch.cos(depth)).sum() + 0.05 * (alpha * alpha).sum()
+            total.backward()
             for k, v in leaves.items():
                 out[f"grad_{k}"] = v.grad.detach().cpu()
             if vel is not None:

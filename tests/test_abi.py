@@ -42,10 +42,10 @@ def test_version_and_status_strings(lib):
 
 
 def test_struct_sizes_match_header():
-    # 4 ints + 6 pointers; 4 ints + 5 pointers; 2 ints + 13 floats (incl. background[3])
+    # 4 ints + 6 pointers; 4 ints + 5 pointers; 2 ints + 11 floats (incl. background[3]) + 1 int
     assert ctypes.sizeof(_lib.Scene) == 16 + 6 * 8
     assert ctypes.sizeof(_lib.Views) == 16 + 5 * 8
-    assert ctypes.sizeof(_lib.Options) == 8 + 11 * 4
+    assert ctypes.sizeof(_lib.Options) == 8 + 11 * 4 + 4
     assert ctypes.sizeof(_lib.LossOptions) == 16 + 6 * 4
 
 
@@ -56,16 +56,27 @@ def test_argument_errors_return_codes_without_touching_a_gpu(lib):
     # the raster stages need no cameras: an empty frame is a shape error, a missing option block an
     # argument error
     assert lib.gsb_raster_fwd(ctypes.byref(v), None, 1, None, None, None, None, None, None, None, None, None,
-                              None) == 1
+                              None, None) == 1
     v.n_views = v.height = v.width = 1
     assert lib.gsb_raster_fwd(ctypes.byref(v), None, 1, None, None, None, None, None, None, None, None, None,
-                              None) == 7
+                              None, None) == 7
     o = _lib.Options()
     o.tile_size = 12
     v.intrinsics = v.camera_to_world = 16
     v.n_views = v.height = v.width = v.views_per_set = 1
     assert lib.gsb_raster_fwd(ctypes.byref(v), ctypes.byref(o), 1, 16, 16, 16, None, 16, 16, 16, 16, 16,
-                              None) == 7
+                              None, None) == 7
+    # backward segments: 3 is not a valid count; 2 segments need the checkpoint buffer
+    o.tile_size, o.near_plane, o.backward_segments = 16, 1e-4, 3
+    assert lib.gsb_raster_checkpoint_floats(ctypes.byref(v), ctypes.byref(o)) == 0
+    assert lib.gsb_raster_fwd(ctypes.byref(v), ctypes.byref(o), 1, 16, 16, 16, None, 16, 16, 16, 16, 16,
+                              None, None) == 7
+    o.backward_segments = 2
+    assert lib.gsb_raster_checkpoint_floats(ctypes.byref(v), ctypes.byref(o)) == 6
+    assert lib.gsb_raster_fwd(ctypes.byref(v), ctypes.byref(o), 1, 16, 16, 16, None, 16, 16, 16, 16, 16,
+                              None, None) == 7
+    o.backward_segments = 1
+    assert lib.gsb_raster_checkpoint_floats(ctypes.byref(v), ctypes.byref(o)) == 0
     lo = _lib.LossOptions()
     lo.type = 0
     lo.window_size = 4  # even window

@@ -30,31 +30,37 @@ def px(request, monkeypatch):
 
 @pytest.mark.parametrize("case", GOLDEN_CASES)
 @pytest.mark.parametrize("tile", [8, 16])
-def test_golden_cases_under_each_decomposition(case, tile, px):
+@pytest.mark.parametrize("segments", [1, 2, 4])
+def test_golden_cases_under_each_decomposition(case, tile, segments, px):
+    """Pixels per lane x backward list segments (each segment its own CTA, started from the
+    forward's checkpoint)."""
     g = load_golden(case)
     wl = g.workload()
-    out = render_raw(wl, B200RendererConfig(tile_size=tile))
+    out = render_raw(wl, B200RendererConfig(tile_size=tile, backward_segments=segments, depth=True))
     assert (out["image"] - g.t("ref_image")).abs().max().item() <= IMAGE_TOL
     torch.testing.assert_close(out["loss"], g.t("ref_loss"), rtol=1e-4, atol=2e-6)
     for k in GRAD_KEYS + (("velocity",) if wl.velocity is not None else ()):
         ok, e, s = grad_close(out[f"grad_{k}"], g.t(f"ref_grad_{k}"), GRAD_REL)
-        assert ok, f"{case} px={px} {k}: max err {e:.3e} vs scale {s:.3e}"
+        assert ok, f"{case} px={px} segments={segments} {k}: max err {e:.3e} vs scale {s:.3e}"
 
 
 def test_decompositions_agree_on_a_large_scene(monkeypatch):
-    """multiview384 at a quarter of its Gaussians: 8 x 384^2 (4608 tiles), depth output on."""
+    """multiview384 at a quarter of its Gaussians: 8 x 384^2 (4608 tiles), depth output and a
+    depth gradient on; every (pixels per lane, segments) pair against (1, 1)."""
     wl = synthetic.multiview384(scale=0.25)
-    cfg = B200RendererConfig(depth=True)
     outs = {}
     for px in ("1", "2"):
         monkeypatch.setenv("GSB200_RASTER_PX", px)
-        outs[px] = render_raw(wl, cfg)
-    a, b = outs["1"], outs["2"]
-    for k in ("image", "alpha", "depth"):
-        assert torch.equal(a[k], b[k]), k
-    for k in GRAD_KEYS:
-        ok, e, s = grad_close(b[f"grad_{k}"], a[f"grad_{k}"], 1e-4)
-        assert ok, f"{k}: {e:.3e} vs {s:.3e}"
+        for seg in (1, 2, 4):
+            outs[(px, seg)] = render_raw(wl, B200RendererConfig(depth=True, backward_segments=seg),
+                                         depth_loss=True)
+    a = outs[("1", 1)]
+    for key, b in outs.items():
+        for k in ("image", "alpha", "depth"):
+            assert torch.equal(a[k], b[k]), (key, k)
+        for k in GRAD_KEYS:
+            ok, e, s = grad_close(b[f"grad_{k}"], a[f"grad_{k}"], 1e-4)
+            assert ok, f"{key} {k}: {e:.3e} vs {s:.3e}"
 
 
 def test_packed_2d_under_each_decomposition(px):
