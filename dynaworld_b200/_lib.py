@@ -16,7 +16,7 @@ _load_error: str | None = None
 GSB_OK = 0
 STATUS_NAMES = {
     0: "GSB_OK", 1: "GSB_ERR_SHAPE", 2: "GSB_ERR_WORKSPACE", 3: "GSB_ERR_KEY_OVERFLOW",
-    4: "GSB_ERR_NONFINITE", 5: "GSB_ERR_TIMEOUT", 6: "GSB_ERR_CUDA", 7: "GSB_ERR_ARG",
+    4: "GSB_ERR_NONFINITE", 5: "GSB_ERR_TIMEOUT", 6: "GSB_ERR_CUDA", 7: "GSB_ERR_ARG", 8: "GSB_ERR_CAPACITY",
 }
 
 SCENE_RAW = 0x1

@@ -279,16 +279,21 @@ GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int3
   const size_t ows = radix_sort_workspace(uint32_t(NT), 4, 1);
   void* order_ws = c.take<char>(ows);
   int32_t* status = begin_status(workspace, st);
+  // n_pairs is the capacity of the key buffers; the count itself is read on the device, so the
+  // stage can be queued before the count reaches the host.
+  const uint32_t* n_dev = pair_offsets + size_t(B) * size_t(n_gaussians);
   if (n_pairs > 0) {
     if ((s = launch_emit(B, n_gaussians, rc, views->height, views->width, records,
                          reinterpret_cast<const int4*>(tile_rects), pair_offsets, n_pairs, keys, status, st)) != GSB_OK)
       return s;
     const int bits = bits_for(uint64_t(B) * uint64_t(rc.n_tiles));
-    if ((s = radix_sort(keys, sorted_keys, nullptr, nullptr, n_pairs, 8, 32, 32 + bits, sort_ws, sws, st, status)) !=
-        GSB_OK)
+    if ((s = radix_sort(keys, sorted_keys, nullptr, nullptr, n_pairs, 8, 32, 32 + bits, sort_ws, sws, st, status,
+                        n_dev)) != GSB_OK)
       return s;
   }
-  if ((s = launch_tile_ranges(sorted_keys, n_pairs, tile_ranges, size_t(B) * rc.n_tiles, st)) != GSB_OK) return s;
+  if ((s = launch_tile_ranges(sorted_keys, n_pairs, n_dev, tile_ranges, size_t(B) * rc.n_tiles, status, st)) !=
+      GSB_OK)
+    return s;
   if (!tile_order) return GSB_OK;
   // launch order: tiles by descending list length (16-bit key: length / 16, saturated)
   if ((s = launch_tile_order_keys(tile_ranges, uint32_t(NT), okeys, ovals, st)) != GSB_OK) return s;

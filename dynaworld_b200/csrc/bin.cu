@@ -52,8 +52,15 @@ __global__ void __launch_bounds__(256) emit_keys_kernel(int32_t n_views, int32_t
   }
 }
 
-__global__ void tile_ranges_kernel(const uint64_t* __restrict__ keys, uint32_t n, uint32_t* __restrict__ ranges,
-                                   size_t n_ranges) {
+__global__ void tile_ranges_kernel(const uint64_t* __restrict__ keys, uint32_t cap,
+                                   const uint32_t* __restrict__ n_dev, uint32_t* __restrict__ ranges,
+                                   size_t n_ranges, int32_t* __restrict__ status) {
+  uint32_t n = cap;
+  if (n_dev) {
+    const uint32_t count = *n_dev;
+    if (count > cap && blockIdx.x == 0 && threadIdx.x == 0) record_error(status, GSB_ERR_CAPACITY, int(cap));
+    n = min(cap, count);
+  }
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const uint32_t t = uint32_t(keys[i] >> 32);
     if (t >= n_ranges) continue;
@@ -91,12 +98,13 @@ gsb_status launch_emit(int32_t B, int32_t G, const RenderConsts& rc, int H, int 
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 
-gsb_status launch_tile_ranges(const uint64_t* keys, uint32_t n, uint32_t* ranges, size_t n_ranges, cudaStream_t st) {
+gsb_status launch_tile_ranges(const uint64_t* keys, uint32_t n, const uint32_t* n_dev, uint32_t* ranges,
+                              size_t n_ranges, int32_t* status, cudaStream_t st) {
   if (cudaMemsetAsync(ranges, 0, n_ranges * 2 * sizeof(uint32_t), st)) return GSB_ERR_CUDA;
-  if (n == 0) return GSB_OK;
-  const int grid = int(std::min<uint32_t>((n + 255) / 256, 148u * 32u));
+  if (n == 0 && !n_dev) return GSB_OK;
+  const int grid = int(std::min<uint32_t>(std::max<uint32_t>((n + 255) / 256, 1u), 148u * 32u));
   note_launch();
-  tile_ranges_kernel<<<grid, 256, 0, st>>>(keys, n, ranges, n_ranges);
+  tile_ranges_kernel<<<grid, 256, 0, st>>>(keys, n, n_dev, ranges, n_ranges, status);
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 

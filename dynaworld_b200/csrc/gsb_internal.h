@@ -15,9 +15,11 @@ void note_launch();
 
 // Radix sort (sort.cu).
 size_t radix_sort_workspace(uint32_t n, int key_bytes, int with_values);
+// n_dev (may be NULL): a device word holding the element count; the sort then uses
+// min(n, *n_dev) elements and n is only the capacity its grid and workspace are sized for.
 gsb_status radix_sort(const void* keys_in, void* keys_out, const uint32_t* vals_in, uint32_t* vals_out, uint32_t n,
                       int key_bytes, int bit_lo, int bit_hi, void* ws, size_t ws_bytes, cudaStream_t stream,
-                      int32_t* status);
+                      int32_t* status, const uint32_t* n_dev = nullptr);
 
 // Exclusive scan: offsets[0..n) and offsets[n] = total (sort.cu).
 size_t exclusive_scan_workspace(uint32_t n);
@@ -93,7 +95,10 @@ gsb_status launch_preprocess_2d_bwd(const gsb_splats2d& sp, const int32_t* rank_
 gsb_status launch_emit(int32_t B, int32_t G, const RenderConsts& rc, int H, int W, const float* records,
                        const int4* rects, const uint32_t* offsets, uint32_t n_pairs, uint64_t* keys, int32_t* status,
                        cudaStream_t st);
-gsb_status launch_tile_ranges(const uint64_t* keys, uint32_t n, uint32_t* ranges, size_t n_ranges, cudaStream_t st);
+// n: capacity of keys; the pair count is min(n, *n_dev) (n_dev may be NULL: n pairs).  A count
+// above the capacity records GSB_ERR_CAPACITY.
+gsb_status launch_tile_ranges(const uint64_t* keys, uint32_t n, const uint32_t* n_dev, uint32_t* ranges,
+                              size_t n_ranges, int32_t* status, cudaStream_t st);
 gsb_status launch_tile_order_keys(const uint32_t* ranges, uint32_t n_tiles_total, uint32_t* keys, uint32_t* vals,
                                   cudaStream_t st);
 

@@ -1,10 +1,11 @@
 // Raster: per-tile front-to-back blend and its reverse-order backward.
 //
-// One CTA per (view, tile) of 16x16 pixels, PX (1 or 2) pixels per thread: each warp owns an
-// 8 x 4PX pixel block (lane l: pixels (l % 8, l / 8 + 4k), k < PX) and works independently of the
-// other warps (no CTA barrier): it streams the tile's sorted list in chunks of 32 entries (one
-// gather per lane; the warps of a tile read the same records, so all but the first read hit L1),
-// keeps the entries whose ellipse reaches its block, and walks those.  With PX = 2 the
+// Tiles of 16x16 (or 8x8) pixels, PX (1 or 2) pixels per thread: each warp owns an 8 x 4PX pixel
+// block (lane l: pixels (l % 8, l / 8 + 4k), k < PX) and works independently of the other warps (no
+// CTA barrier), so a tile's warp blocks may sit in one CTA or be spread over adjacent CTAs: a warp
+// streams the tile's sorted list in chunks of 32 entries (one gather per lane; the warps of a tile
+// in one CTA read the same records, so all but the first read hit L1), keeps the entries whose
+// ellipse reaches its block, and walks those.  With PX = 2 the
 // shared-memory reads, the loop control and (backward) the warp reduction and atomics of a kept
 // entry are paid once for both pixels; the launch picks PX from the grid size.
 //
@@ -119,16 +120,22 @@ __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* rec
 // Floats a checkpoint slot holds per pixel: S, then the suffix sums of r, g, b, weight, depth.
 constexpr int kCkptFloats = 6;
 
-template <int TILE, int PX, int NSEG>  // NSEG: list segments of the backward (checkpoints between)
-__global__ void __launch_bounds__(TILE* TILE / PX) raster_fwd_kernel(RasterArgs a) {
+// NSEG: list segments of the backward (checkpoints between).  CW: warps per CTA; the tile's NW warp
+// blocks are spread over NW / CW adjacent CTAs.
+template <int TILE, int PX, int NSEG, int CW>
+__global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
   constexpr int NW = TILE * TILE / (32 * PX);
+  constexpr int SPLIT = NW / CW;
+  static_assert(SPLIT * CW == NW, "CTAs must hold whole warp blocks of one tile");
   constexpr int NB = NSEG > 1 ? NSEG - 1 : 1;  // checkpoint slots (boundaries between segments)
-  __shared__ float4 s_geo[NW][32], s_cot[NW][32], s_col[NW][32];
+  __shared__ float4 s_geo[CW][32], s_cot[CW][32], s_col[CW][32];
   const RenderConsts& rc = a.rc;
-  const uint32_t slot = blockIdx.y * uint32_t(rc.n_tiles) + blockIdx.x;
+  const uint32_t cta = blockIdx.y * uint32_t(rc.n_tiles) * SPLIT + blockIdx.x;
+  const uint32_t slot = cta / SPLIT;
   const uint32_t vt = a.order ? a.order[slot] : slot;  // heaviest tiles first
   const int view = int(vt / uint32_t(rc.n_tiles)), tile = int(vt % uint32_t(rc.n_tiles));
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, lw = tid >> 5;
+  const int warp = int(cta % SPLIT) * CW + lw;  // warp block within the tile
   int bx, by;
   block_of<TILE, PX>(warp, bx, by);
   const int ox = (tile % rc.tiles_x) * TILE + bx, oy = (tile / rc.tiles_x) * TILE + by;  // block origin
@@ -139,7 +146,7 @@ __global__ void __launch_bounds__(TILE* TILE / PX) raster_fwd_kernel(RasterArgs 
   const uint32_t start = a.ranges[rb], end = a.ranges[rb + 1];
   const float* recs = a.records + size_t(view) * a.G * GSB_RECORD_FLOATS;
   const float inv_f0 = 1.0f / rc.f0;
-  const WarpSlots ws{s_geo[warp], s_cot[warp], s_col[warp], nullptr};
+  const WarpSlots ws{s_geo[lw], s_cot[lw], s_col[lw], nullptr};
 
   int py[PX];
   float fy[PX], S[PX], C0[PX], C1[PX], C2[PX], Ws[PX], D[PX];
@@ -168,8 +175,8 @@ __global__ void __launch_bounds__(TILE* TILE / PX) raster_fwd_kernel(RasterArgs 
   };
   // blend the entry in slot j of the current chunk (list index c - start + j) into every live pixel
   auto blend = [&](uint32_t c, int j) {
-    const float4 g = s_geo[warp][j];
-    const float4 ct = s_cot[warp][j];
+    const float4 g = s_geo[lw][j];
+    const float4 ct = s_cot[lw][j];
     const float dx = __fsub_rn(fx, g.x);
 #pragma unroll
     for (int k = 0; k < PX; ++k) {
@@ -180,7 +187,7 @@ __global__ void __launch_bounds__(TILE* TILE / PX) raster_fwd_kernel(RasterArgs 
       const float e = __expf(fminf(-0.5f * q, 0.0f));
       const float alpha = fminf(fmaxf(ct.y * e, 0.0f), rc.alpha_clamp);
       if (!(alpha >= rc.alpha_cutoff)) continue;
-      const float4 col = s_col[warp][j];
+      const float4 col = s_col[lw][j];
       const float T = S[k] * ct.w;
       const float w = T * alpha;
       C0[k] = fmaf(w, col.x, C0[k]);
@@ -314,18 +321,22 @@ constexpr int kSparseContributors = 4;
 // DEPTH: a depth gradient is given.  NSEG: the tile's list is cut into NSEG segments
 // [s n / NSEG, (s + 1) n / NSEG), each walked by its own CTA (adjacent in launch order), starting
 // from the forward's checkpoint of its upper boundary (the last segment from the final state).
-template <int TILE, int PX, bool DEPTH, int NSEG>
-__global__ void __launch_bounds__(TILE* TILE / PX) raster_bwd_kernel(RasterArgs a) {
+// CW: warps per CTA, as in the forward.
+template <int TILE, int PX, bool DEPTH, int NSEG, int CW>
+__global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
   constexpr int NW = TILE * TILE / (32 * PX);
-  __shared__ float4 s_geo[NW][32], s_cot[NW][32], s_col[NW][32];
-  __shared__ uint32_t s_rank[NW][32];
+  constexpr int SPLIT = NW / CW;
+  static_assert(SPLIT * CW == NW, "CTAs must hold whole warp blocks of one tile");
+  __shared__ float4 s_geo[CW][32], s_cot[CW][32], s_col[CW][32];
+  __shared__ uint32_t s_rank[CW][32];
   const RenderConsts& rc = a.rc;
-  const uint32_t cta = blockIdx.y * uint32_t(rc.n_tiles) * NSEG + blockIdx.x;
-  const uint32_t slot = cta / NSEG;
-  const int seg = int(cta % NSEG);
+  const uint32_t cta = blockIdx.y * uint32_t(rc.n_tiles) * (NSEG * SPLIT) + blockIdx.x;
+  const uint32_t slot = cta / (NSEG * SPLIT);
+  const int seg = int((cta / SPLIT) % NSEG);
   const uint32_t vt = a.order ? a.order[slot] : slot;  // heaviest tiles first
   const int view = int(vt / uint32_t(rc.n_tiles)), tile = int(vt % uint32_t(rc.n_tiles));
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, lw = tid >> 5;
+  const int warp = int(cta % SPLIT) * CW + lw;  // warp block within the tile
   int bx, by;
   block_of<TILE, PX>(warp, bx, by);
   const int ox = (tile % rc.tiles_x) * TILE + bx, oy = (tile / rc.tiles_x) * TILE + by;  // block origin
@@ -339,7 +350,7 @@ __global__ void __launch_bounds__(TILE* TILE / PX) raster_bwd_kernel(RasterArgs 
   const uint32_t hi = uint32_t((uint64_t(seg + 1) * n_list) / NSEG);
   const float* recs = a.records + size_t(view) * a.G * GSB_RECORD_FLOATS;
   float* g2 = a.grad2d + size_t(view) * a.G * GSB_GRAD2D_FLOATS;
-  const WarpSlots ws{s_geo[warp], s_cot[warp], s_col[warp], s_rank[warp]};
+  const WarpSlots ws{s_geo[lw], s_cot[lw], s_col[lw], s_rank[lw]};
 
   const size_t HW = size_t(a.H) * a.W;
   const size_t total_px = size_t(a.B) * HW;
@@ -398,8 +409,8 @@ __global__ void __launch_bounds__(TILE* TILE / PX) raster_bwd_kernel(RasterArgs 
       bool contrib = false;
       const uint32_t lj = uint32_t(cb) + uint32_t(j);
       if (lj < max_of(n_proc)) {
-        const float4 g = s_geo[warp][j];
-        const float4 ct = s_cot[warp][j];
+        const float4 g = s_geo[lw][j];
+        const float4 ct = s_cot[lw][j];
         const float dx = __fsub_rn(fx, g.x);
 #pragma unroll
         for (int k = 0; k < PX; ++k) {
@@ -415,7 +426,7 @@ __global__ void __launch_bounds__(TILE* TILE / PX) raster_bwd_kernel(RasterArgs 
           const float rf = __fdividef(1.0f, f);
           S[k] = S[k] * (rc.f0 * rf);  // S before this entry: S_after / (f / F0)
           const float T = S[k] * ct.w;
-          const float4 col = s_col[warp][j];
+          const float4 col = s_col[lw][j];
           const float w = T * alpha;
           float dldw = g0[k] * col.x + g1[k] * col.y + g2c[k] * col.z + gW[k];
           float rsum = g0[k] * R0[k] + g1[k] * R1[k] + g2c[k] * R2[k] + gW[k] * RW[k];
@@ -449,7 +460,7 @@ __global__ void __launch_bounds__(TILE* TILE / PX) raster_bwd_kernel(RasterArgs 
       }
       const uint32_t cm = __ballot_sync(kFull, contrib);
       if (cm == 0u) continue;
-      float* dst = g2 + size_t(s_rank[warp][j]) * GSB_GRAD2D_FLOATS;
+      float* dst = g2 + size_t(s_rank[lw][j]) * GSB_GRAD2D_FLOATS;
       if (__popc(cm) <= kSparseContributors) {
         if (contrib) {
 #pragma unroll
@@ -465,13 +476,6 @@ __global__ void __launch_bounds__(TILE* TILE / PX) raster_bwd_kernel(RasterArgs 
     __syncwarp();  // slots are rewritten by the next chunk
   }
 }
-
-// Threads per CTA: one per PX pixels of the tile (the kernels' shared arrays hold one slot set per
-// warp of exactly this many threads).
-template <int TILE, int PX>
-constexpr int raster_threads() { return TILE * TILE / PX; }
-static_assert(raster_threads<16, 2>() == 128 && raster_threads<8, 2>() == 32, "warp blocks must tile the tile");
-static_assert(raster_threads<16, 1>() == 256 && raster_threads<8, 1>() == 64, "warp blocks must tile the tile");
 
 // Two pixels per lane halve the per-pixel cost of list streaming, loop control and (backward)
 // the reductions, but give each tile half the warps and a longer serial walk, which loses while
@@ -490,24 +494,67 @@ constexpr uint64_t kBwdPairedTiles = 2048;
 constexpr uint64_t kSegmentedTiles = 2048;
 constexpr int kAutoSegments = 4;
 
+// Warps per CTA of the 16x16 kernels: GSB200_RASTER_CW (1, 2, 4 or 8; tuning, results do not
+// depend on it), else 2 for the forward and the whole tile for the backward.  Measured on one B200
+// (16x16 tiles, warps per CTA 8 / 4 / 2 / 1): forward 16 x 128^2 0.417 / 0.407 / 0.400 / 0.437 ms,
+// 8 x 384^2 0.601 / 0.594 / 0.583 / 0.604 ms (small CTAs spread a tile's blocks over SMs that would
+// otherwise idle at the end); backward (two pixels per lane, 4 / 2 / 1 warps) 16 x 128^2
+// 0.823 / 0.864 / 0.874 ms, where the warps of a tile share the records through L1.
+static int cta_warps(int nw, bool backward) {
+  const char* v = std::getenv("GSB200_RASTER_CW");
+  if (v && (v[0] == '1' || v[0] == '2' || v[0] == '4' || v[0] == '8') && v[1] == '\0') return min(nw, v[0] - '0');
+  return backward ? nw : min(nw, 2);
+}
+
+template <int TILE, int PX, int NSEG, int CW>
+static void fwd_launch_cw(const RasterArgs& a, cudaStream_t st) {
+  constexpr int SPLIT = TILE * TILE / (32 * PX) / CW;
+  const dim3 grid(unsigned(a.rc.n_tiles) * SPLIT, a.B);  // the CTAs of a tile are adjacent
+  raster_fwd_kernel<TILE, PX, NSEG, CW><<<grid, 32 * CW, 0, st>>>(a);
+}
+
 template <int TILE, int PX, int NSEG>
-static void fwd_launch_seg(const RasterArgs& a, dim3 grid, cudaStream_t st) {
-  raster_fwd_kernel<TILE, PX, NSEG><<<grid, raster_threads<TILE, PX>(), 0, st>>>(a);
+static void fwd_launch_seg(const RasterArgs& a, cudaStream_t st) {
+  constexpr int NW = TILE * TILE / (32 * PX);
+  if constexpr (TILE == 16) {
+    const int cw = cta_warps(NW, false);
+    if (cw == 1) return fwd_launch_cw<TILE, PX, NSEG, 1>(a, st);
+    if (cw == 2) return fwd_launch_cw<TILE, PX, NSEG, 2>(a, st);
+    if constexpr (NW == 8) {
+      if (cw == 4) return fwd_launch_cw<TILE, PX, NSEG, 4>(a, st);
+    }
+  }
+  fwd_launch_cw<TILE, PX, NSEG, NW>(a, st);
 }
 
 template <int TILE, int PX>
-static void fwd_launch(const RasterArgs& a, dim3 grid, cudaStream_t st) {
+static void fwd_launch(const RasterArgs& a, cudaStream_t st) {
   note_launch();
-  if (a.nseg == 4) fwd_launch_seg<TILE, PX, 4>(a, grid, st);
-  else if (a.nseg == 2) fwd_launch_seg<TILE, PX, 2>(a, grid, st);
-  else fwd_launch_seg<TILE, PX, 1>(a, grid, st);
+  if (a.nseg == 4) fwd_launch_seg<TILE, PX, 4>(a, st);
+  else if (a.nseg == 2) fwd_launch_seg<TILE, PX, 2>(a, st);
+  else fwd_launch_seg<TILE, PX, 1>(a, st);
+}
+
+template <int TILE, int PX, int NSEG, int CW>
+static void bwd_launch_cw(const RasterArgs& a, cudaStream_t st) {
+  constexpr int SPLIT = TILE * TILE / (32 * PX) / CW;
+  const dim3 grid(unsigned(a.rc.n_tiles) * NSEG * SPLIT, a.B);  // the CTAs of a tile are adjacent
+  if (a.d_depth) raster_bwd_kernel<TILE, PX, true, NSEG, CW><<<grid, 32 * CW, 0, st>>>(a);
+  else raster_bwd_kernel<TILE, PX, false, NSEG, CW><<<grid, 32 * CW, 0, st>>>(a);
 }
 
 template <int TILE, int PX, int NSEG>
 static void bwd_launch_seg(const RasterArgs& a, cudaStream_t st) {
-  const dim3 grid(unsigned(a.rc.n_tiles) * NSEG, a.B);  // the segments of a tile are adjacent
-  if (a.d_depth) raster_bwd_kernel<TILE, PX, true, NSEG><<<grid, raster_threads<TILE, PX>(), 0, st>>>(a);
-  else raster_bwd_kernel<TILE, PX, false, NSEG><<<grid, raster_threads<TILE, PX>(), 0, st>>>(a);
+  constexpr int NW = TILE * TILE / (32 * PX);
+  if constexpr (TILE == 16) {
+    const int cw = cta_warps(NW, true);
+    if (cw == 1) return bwd_launch_cw<TILE, PX, NSEG, 1>(a, st);
+    if (cw == 2) return bwd_launch_cw<TILE, PX, NSEG, 2>(a, st);
+    if constexpr (NW == 8) {
+      if (cw == 4) return bwd_launch_cw<TILE, PX, NSEG, 4>(a, st);
+    }
+  }
+  bwd_launch_cw<TILE, PX, NSEG, NW>(a, st);
 }
 
 template <int TILE, int PX>
@@ -535,10 +582,9 @@ static bool paired_launch(uint64_t tiles, uint64_t threshold, bool backward) {
 }
 
 gsb_status launch_raster_fwd(const RasterArgs& a, cudaStream_t st) {
-  const dim3 grid(a.rc.n_tiles, a.B);
   const bool paired = paired_launch(uint64_t(a.rc.n_tiles) * uint64_t(a.B), kFwdPairedTiles, false);
-  if (a.rc.tile == 16) paired ? fwd_launch<16, 2>(a, grid, st) : fwd_launch<16, 1>(a, grid, st);
-  else if (a.rc.tile == 8) paired ? fwd_launch<8, 2>(a, grid, st) : fwd_launch<8, 1>(a, grid, st);
+  if (a.rc.tile == 16) paired ? fwd_launch<16, 2>(a, st) : fwd_launch<16, 1>(a, st);
+  else if (a.rc.tile == 8) paired ? fwd_launch<8, 2>(a, st) : fwd_launch<8, 1>(a, st);
   else return GSB_ERR_ARG;
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }

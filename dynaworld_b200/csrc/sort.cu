@@ -48,8 +48,10 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
 template <typename K>
 __global__ void __launch_bounds__(kSortThreads) radix_hist_kernel(const K* __restrict__ keys, uint32_t n,
                                                                   int bit_lo, int bit_hi, int passes,
-                                                                  uint32_t* __restrict__ hist) {
+                                                                  uint32_t* __restrict__ hist,
+                                                                  const uint32_t* __restrict__ n_dev) {
   __shared__ uint32_t s_hist[8][256];
+  if (n_dev) n = min(n, *n_dev);
   for (int i = threadIdx.x; i < passes * 256; i += blockDim.x) s_hist[i / 256][i % 256] = 0;
   __syncthreads();
   const int lane = threadIdx.x & 31;
@@ -99,8 +101,10 @@ template <typename K, bool kVals>
 __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
     const K* __restrict__ keys_in, K* __restrict__ keys_out, const uint32_t* __restrict__ vals_in,
     uint32_t* __restrict__ vals_out, uint32_t n, int shift, int nbits, const uint32_t* __restrict__ hist,
-    uint32_t* __restrict__ lookback, uint32_t* __restrict__ part_counter, int32_t* __restrict__ status) {
+    uint32_t* __restrict__ lookback, uint32_t* __restrict__ part_counter, int32_t* __restrict__ status,
+    const uint32_t* __restrict__ n_dev) {
   constexpr int kItems = SortTraits<K>::kItems;
+  if (n_dev) n = min(n, *n_dev);  // partitions past the count find no valid key and write nothing
   constexpr uint32_t kPart = kSortThreads * kItems;
   __shared__ uint32_t s_part;
   __shared__ uint32_t s_warp_hist[kSortWarps][256];
@@ -196,7 +200,7 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
     if (kVals) s_vals[lpos] = v[j];
   }
   __syncthreads();
-  const uint32_t n_valid = min(kPart, n - part * kPart);
+  const uint32_t n_valid = part * kPart < n ? min(kPart, n - part * kPart) : 0u;
   for (uint32_t i = tid; i < n_valid; i += kSortThreads) {
     const K key = s_keys[i];
     const uint32_t d = uint32_t((key >> shift) & K(mask));
@@ -233,11 +237,11 @@ size_t radix_sort_workspace(uint32_t n, int key_bytes, int with_values) {
 template <typename K>
 static gsb_status radix_sort_t(const K* keys_in, K* keys_out, const uint32_t* vals_in, uint32_t* vals_out,
                                uint32_t n, int bit_lo, int bit_hi, void* ws, size_t ws_bytes,
-                               cudaStream_t stream, int32_t* status) {
+                               cudaStream_t stream, int32_t* status, const uint32_t* n_dev) {
   const int passes = (bit_hi - bit_lo + 7) / 8;
   const bool with_vals = vals_in != nullptr;
   if (n == 0) return GSB_OK;
-  if (passes <= 0) {
+  if (passes <= 0) {  // one bucket: the input order is the output (copies the capacity)
     if (cudaMemcpyAsync(keys_out, keys_in, size_t(n) * sizeof(K), cudaMemcpyDeviceToDevice, stream)) return GSB_ERR_CUDA;
     if (with_vals && cudaMemcpyAsync(vals_out, vals_in, size_t(n) * 4, cudaMemcpyDeviceToDevice, stream)) return GSB_ERR_CUDA;
     return GSB_OK;
@@ -251,13 +255,14 @@ static gsb_status radix_sort_t(const K* keys_in, K* keys_out, const uint32_t* va
   K* alt_keys = reinterpret_cast<K*>(c.take<char>(size_t(n) * sizeof(K)));
   uint32_t* alt_vals = with_vals ? c.take<uint32_t>(n) : nullptr;
   if (!c.ok()) return GSB_ERR_WORKSPACE;
-  // hist, counters and look-back are contiguous after the header: one memset clears them.
-  const size_t clear_bytes = reinterpret_cast<char*>(lookback + size_t(8) * parts * 256) - reinterpret_cast<char*>(hist);
+  // hist, counters and the look-back of the passes run are contiguous: one memset clears them.
+  const size_t clear_bytes =
+      reinterpret_cast<char*>(lookback + size_t(passes) * parts * 256) - reinterpret_cast<char*>(hist);
   if (cudaMemsetAsync(hist, 0, clear_bytes, stream)) return GSB_ERR_CUDA;
 
   const int hist_blocks = int(std::min<uint32_t>((n + kSortThreads - 1) / kSortThreads, 148u * 8u));
   note_launch();
-  radix_hist_kernel<K><<<hist_blocks, kSortThreads, 0, stream>>>(keys_in, n, bit_lo, bit_hi, passes, hist);
+  radix_hist_kernel<K><<<hist_blocks, kSortThreads, 0, stream>>>(keys_in, n, bit_lo, bit_hi, passes, hist, n_dev);
   const K* src_k = keys_in;
   const uint32_t* src_v = vals_in;
   for (int p = 0; p < passes; ++p) {
@@ -270,12 +275,12 @@ static gsb_status radix_sort_t(const K* keys_in, K* keys_out, const uint32_t* va
       note_launch();
       onesweep_kernel<K, true><<<parts, kSortThreads, 0, stream>>>(src_k, dst_k, src_v, dst_v, n, shift, nbits,
                                                                     hist + 256 * p, lookback + size_t(p) * parts * 256,
-                                                                    counters + p, status);
+                                                                    counters + p, status, n_dev);
     } else {
       note_launch();
       onesweep_kernel<K, false><<<parts, kSortThreads, 0, stream>>>(src_k, dst_k, nullptr, nullptr, n, shift, nbits,
                                                                      hist + 256 * p, lookback + size_t(p) * parts * 256,
-                                                                     counters + p, status);
+                                                                     counters + p, status, n_dev);
     }
     src_k = dst_k;
     src_v = dst_v;
@@ -285,16 +290,16 @@ static gsb_status radix_sort_t(const K* keys_in, K* keys_out, const uint32_t* va
 
 gsb_status radix_sort(const void* keys_in, void* keys_out, const uint32_t* vals_in, uint32_t* vals_out, uint32_t n,
                       int key_bytes, int bit_lo, int bit_hi, void* ws, size_t ws_bytes, cudaStream_t stream,
-                      int32_t* status) {
+                      int32_t* status, const uint32_t* n_dev) {
   if (n >= (1u << 30)) return GSB_ERR_KEY_OVERFLOW;
   if (bit_lo < 0 || bit_hi > key_bytes * 8 || bit_hi < bit_lo) return GSB_ERR_ARG;
   if ((vals_in == nullptr) != (vals_out == nullptr)) return GSB_ERR_ARG;
   if (key_bytes == 4)
     return radix_sort_t<uint32_t>(static_cast<const uint32_t*>(keys_in), static_cast<uint32_t*>(keys_out), vals_in,
-                                  vals_out, n, bit_lo, bit_hi, ws, ws_bytes, stream, status);
+                                  vals_out, n, bit_lo, bit_hi, ws, ws_bytes, stream, status, n_dev);
   if (key_bytes == 8)
     return radix_sort_t<uint64_t>(static_cast<const uint64_t*>(keys_in), static_cast<uint64_t*>(keys_out), vals_in,
-                                  vals_out, n, bit_lo, bit_hi, ws, ws_bytes, stream, status);
+                                  vals_out, n, bit_lo, bit_hi, ws, ws_bytes, stream, status, n_dev);
   return GSB_ERR_ARG;
 }
 

@@ -162,6 +162,19 @@ def _views_of(vspec: ViewSpec, tensors: dict) -> _lib.Views:
                         tensors.get("lens_models"), tensors.get("distortion"))
 
 
+# Pair-key capacity per frame shape (device, views, Gaussians, image, tile size, mode), from the
+# frames rendered before: binning and the blend are queued with it before the exact count reaches
+# the host, so the GPU does not wait on the host there.  A count above it (first frames, growth)
+# re-runs the two stages with the count.
+_PAIR_CAPACITY: dict = {}
+
+
+def _next_capacity(n_pairs: int, cap: int | None) -> int:
+    if cap is not None and n_pairs <= cap and 2 * n_pairs >= cap:
+        return cap
+    return -(-(n_pairs + n_pairs // 4 + 4096) // 65536) * 65536
+
+
 def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, near_plane: float,
                    tensors: dict) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None, FrameState]:
     L = _lib.lib()
@@ -189,8 +202,8 @@ def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, n
                                                               offsets.data_ptr(), None, ws2.data_ptr(), ws2.numel(),
                                                               st))
     # The one host synchronisation of the forward: the pair count plus the device status words,
-    # copied into pinned memory behind the kernels; everything that does not depend on the count
-    # is allocated while the GPU still works.
+    # copied into pinned memory behind the kernels.  Binning reads the count on the device, so with
+    # a capacity known from earlier frames of this shape it and the blend are queued first.
     head = read_words([offsets[-1:], ws1.view(torch.int32)[:1], ws2.view(torch.int32)[:1]])
     n_tiles = -(-H // cfg.tile_size) * -(-W // cfg.tile_size)
     ranges = torch.empty(B * n_tiles * 2, dtype=torch.int32, device=dev)
@@ -201,22 +214,32 @@ def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, n
     pixel_t = torch.empty(B, H, W, dtype=torch.float32, device=dev)
     pixel_state = torch.empty(B, H, W, dtype=torch.int32, device=dev)
     ckpt = checkpoint_buffer(views, opts, dev)
+
+    def bin_and_blend(capacity: int):
+        keys = torch.empty(max(capacity, 1), dtype=torch.int64, device=dev)
+        ws3 = _ws(L.gsb_bin_workspace(views, opts, G, capacity), dev)
+        with _stage("bin"):
+            _lib.check("gsb_bin", L.gsb_bin(views, opts, G, records.data_ptr(), rects.data_ptr(),
+                                            offsets.data_ptr(), capacity, keys.data_ptr(), ranges.data_ptr(),
+                                            order.data_ptr(), ws3.data_ptr(), ws3.numel(), st))
+        with _stage("raster_fwd"):
+            _lib.check("gsb_raster_fwd", L.gsb_raster_fwd(views, opts, G, records.data_ptr(), keys.data_ptr(),
+                                                          ranges.data_ptr(), order.data_ptr(), image.data_ptr(),
+                                                          alpha.data_ptr(), _lib.ptr(depth), pixel_t.data_ptr(),
+                                                          pixel_state.data_ptr(), _lib.ptr(ckpt), st))
+        return keys, ws3
+
+    shape = (dev.index, B, G, H, W, cfg.tile_size, cfg.mode)
+    cap = _PAIR_CAPACITY.get(shape)
+    if cap is not None:
+        keys, ws3 = bin_and_blend(cap)
     head = head.wait()
     n_pairs = head[0] & 0xFFFFFFFF
     for name, code in (("gsb_depth_order", head[1]), ("gsb_preprocess_fwd", head[2])):
         _lib.check(name, code)
-    keys = torch.empty(max(n_pairs, 1), dtype=torch.int64, device=dev)
-    ws3 = _ws(L.gsb_bin_workspace(views, opts, G, n_pairs), dev)
-    with _stage("bin"):
-        _lib.check("gsb_bin", L.gsb_bin(views, opts, G, records.data_ptr(), rects.data_ptr(), offsets.data_ptr(),
-                                        n_pairs, keys.data_ptr(), ranges.data_ptr(), order.data_ptr(), ws3.data_ptr(),
-                                        ws3.numel(), st))
-    with _stage("raster_fwd"):
-        _lib.check("gsb_raster_fwd", L.gsb_raster_fwd(views, opts, G, records.data_ptr(), keys.data_ptr(),
-                                                      ranges.data_ptr(), order.data_ptr(), image.data_ptr(),
-                                                      alpha.data_ptr(),
-                                                      _lib.ptr(depth), pixel_t.data_ptr(), pixel_state.data_ptr(),
-                                                      _lib.ptr(ckpt), st))
+    if cap is None or n_pairs > cap:  # no guess yet, or too small: again with the count
+        keys, ws3 = bin_and_blend(n_pairs)
+    _PAIR_CAPACITY[shape] = _next_capacity(n_pairs, cap)
     if cfg.check_status:
         _lib.check("gsb_bin", int(ws3.view(torch.int32)[0].item()))
     state = FrameState(rank_of, records, keys, ranges, order, pixel_t, pixel_state, n_pairs, ckpt)

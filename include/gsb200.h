@@ -48,7 +48,8 @@ typedef enum gsb_status {
   GSB_ERR_NONFINITE = 4,    /* non-finite projected values were counted (see gsb_read_status) */
   GSB_ERR_TIMEOUT = 5,      /* a bounded device-side wait gave up */
   GSB_ERR_CUDA = 6,         /* a CUDA runtime call failed (launch error etc.) */
-  GSB_ERR_ARG = 7           /* NULL pointer or bad option value */
+  GSB_ERR_ARG = 7,          /* NULL pointer or bad option value */
+  GSB_ERR_CAPACITY = 8      /* gsb_bin: more pairs than the capacity given (outputs invalid) */
 } gsb_status;
 
 /* Scene flags (gsb_scene.flags). */
@@ -186,7 +187,12 @@ GSB_API gsb_status gsb_preprocess_fwd(const gsb_scene* scene, const gsb_views* v
 /* ---- stage 3: pair keys, radix sort by (view, tile), tile ranges (tiled.py:31-71) ---------- */
 GSB_API size_t gsb_bin_workspace(const gsb_views* views, const gsb_options* opts,
                                  int32_t n_gaussians, uint32_t n_pairs);
-/* sorted_keys[n_pairs]: ((view*n_tiles + tile) << 32) | depth_rank, ascending.
+/* n_pairs: capacity of sorted_keys, at least the pair count pair_offsets[B*G] (passing the count
+   itself is the usual call).  The count is read on the device, so the stage (and the raster after
+   it) can be queued before the count reaches the host, with a capacity guessed from earlier
+   frames; a count above the capacity records GSB_ERR_CAPACITY (gsb_read_status), writes nothing
+   past the capacity and leaves the outputs invalid: call again with the count.
+   sorted_keys[count]: ((view*n_tiles + tile) << 32) | depth_rank, ascending.
    tile_ranges[B*n_tiles*2]: [start, end) of each tile's run in sorted_keys.
    tile_order[B*n_tiles] (may be NULL): view*n_tiles + tile, longest lists first -- the launch
    order the raster stages use so that the heaviest tiles do not finish last. */

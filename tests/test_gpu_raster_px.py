@@ -44,6 +44,21 @@ def test_golden_cases_under_each_decomposition(case, tile, segments, px):
         assert ok, f"{case} px={px} segments={segments} {k}: max err {e:.3e} vs scale {s:.3e}"
 
 
+@pytest.mark.parametrize("case", GOLDEN_CASES)
+@pytest.mark.parametrize("cw", ["1", "4", "8"])
+def test_golden_cases_under_each_cta_split(case, cw, px, monkeypatch):
+    """A tile's warp blocks in one CTA or spread over 2, 4, 8 adjacent CTAs (GSB200_RASTER_CW
+    warps per CTA; the default is 2 for the forward and the whole tile for the backward)."""
+    monkeypatch.setenv("GSB200_RASTER_CW", cw)
+    g = load_golden(case)
+    wl = g.workload()
+    out = render_raw(wl, B200RendererConfig(depth=True))
+    assert (out["image"] - g.t("ref_image")).abs().max().item() <= IMAGE_TOL
+    for k in GRAD_KEYS + (("velocity",) if wl.velocity is not None else ()):
+        ok, e, s = grad_close(out[f"grad_{k}"], g.t(f"ref_grad_{k}"), GRAD_REL)
+        assert ok, f"{case} px={px} cw={cw} {k}: max err {e:.3e} vs scale {s:.3e}"
+
+
 def test_decompositions_agree_on_a_large_scene(monkeypatch):
     """multiview384 at a quarter of its Gaussians: 8 x 384^2 (4608 tiles), depth output and a
     depth gradient on; every (pixels per lane, segments) pair against (1, 1)."""
