@@ -22,6 +22,8 @@ STATUS_NAMES = {
 SCENE_RAW = 0x1
 SCENE_VELOCITY = 0x2
 SCENE_SH_CLAMP = 0x4
+SCENE_BANK = 0x8
+BANK_MAX_BASIS = 16
 RENDER_TILED_COMPAT = 0x1
 RENDER_DEPTH = 0x2
 RENDER_NO_ELLIPSE = 0x4
@@ -45,6 +47,7 @@ class Scene(C.Structure):
     _fields_ = [
         ("n_sets", C.c_int32), ("n_gaussians", C.c_int32), ("sh_degree", C.c_int32), ("flags", C.c_uint32),
         ("means", vp), ("scales", vp), ("quats", vp), ("opacities", vp), ("colors", vp), ("velocity", vp),
+        ("bank_mu", vp), ("bank_rot", vp), ("bank_alpha", vp), ("bank_first", C.c_int32), ("bank_basis", C.c_int32),
     ]
 
 
@@ -52,6 +55,7 @@ class Views(C.Structure):
     _fields_ = [
         ("n_views", C.c_int32), ("views_per_set", C.c_int32), ("height", C.c_int32), ("width", C.c_int32),
         ("intrinsics", vp), ("camera_to_world", vp), ("times", vp), ("lens_models", vp), ("distortion", vp),
+        ("basis", vp),
     ]
 
 
@@ -65,7 +69,8 @@ class Options(C.Structure):
 
 
 class SceneGrads(C.Structure):
-    _fields_ = [("means", vp), ("scales", vp), ("quats", vp), ("opacities", vp), ("colors", vp), ("velocity", vp)]
+    _fields_ = [("means", vp), ("scales", vp), ("quats", vp), ("opacities", vp), ("colors", vp), ("velocity", vp),
+                ("bank_mu", vp), ("bank_rot", vp), ("bank_alpha", vp)]
 
 
 class CameraGrads(C.Structure):

@@ -80,6 +80,12 @@ static gsb_status check_scene(const gsb_scene* s, const gsb_views* v) {
   if ((v->n_views - 1) / v->views_per_set >= s->n_sets) return GSB_ERR_SHAPE;
   if ((s->flags & GSB_SCENE_RAW) && (s->sh_degree < 0 || s->sh_degree > 3)) return GSB_ERR_ARG;
   if (uint64_t(v->n_views) * uint64_t(s->n_gaussians) >= (uint64_t(1) << 30)) return GSB_ERR_SHAPE;
+  if (s->flags & GSB_SCENE_BANK) {  // activated values only, one motion model per scene
+    if (s->flags & (GSB_SCENE_RAW | GSB_SCENE_VELOCITY)) return GSB_ERR_ARG;
+    if (!s->bank_mu || !s->bank_rot || !s->bank_alpha || !v->basis) return GSB_ERR_ARG;
+    if (s->bank_basis < 1 || s->bank_basis > GSB_BANK_MAX_BASIS) return GSB_ERR_ARG;
+    if (s->bank_first < 0 || s->bank_first > s->n_gaussians) return GSB_ERR_SHAPE;
+  }
   return GSB_OK;
 }
 
@@ -119,6 +125,7 @@ GSB_API const char* gsb_status_string(int s) {
     case GSB_ERR_TIMEOUT: return "a bounded device-side wait gave up";
     case GSB_ERR_CUDA: return "CUDA runtime error";
     case GSB_ERR_ARG: return "invalid argument";
+    case GSB_ERR_CAPACITY: return "more (tile, Gaussian) pairs than the capacity given to gsb_bin";
     default: return "unknown status";
   }
 }

@@ -95,14 +95,108 @@ struct GaussParams {
   float o;       // opacity
 };
 
-__device__ inline GaussParams load_params(const gsb_scene& sc, size_t pg, float t) {
-  GaussParams p;
-  const bool raw = sc.flags & GSB_SCENE_RAW;
+// ---- dynamic bank: gs_models/dynamic_video_token_gs_implicit_camera.py:1206-1224 ----------------
+
+// Row of Gaussian pg in the bank arrays; false for a static Gaussian or a scene without a bank.
+__device__ inline bool bank_row(const gsb_scene& sc, size_t pg, size_t& row) {
+  if (!(sc.flags & GSB_SCENE_BANK)) return false;
+  const size_t G = size_t(sc.n_gaussians), first = size_t(sc.bank_first);
+  const size_t s = pg / G, g = pg - s * G;
+  if (g < first) return false;
+  row = s * (G - first) + (g - first);
+  return true;
+}
+
+// The temporal basis of view b (NULL without a bank).
+__device__ inline const float* view_basis(const gsb_scene& sc, const gsb_views& vw, int b) {
+  return (sc.flags & GSB_SCENE_BANK) ? vw.basis + size_t(b) * size_t(sc.bank_basis) : nullptr;
+}
+
+// out[c] = sum_m phi_m A[row, m, c] (the einsum "bm,bgmc->bgc" of :1213-1215).
+template <int C>
+__device__ inline void bank_combine(const float* __restrict__ A, size_t row, int M, const float* phi, float out[C]) {
+  const float* a = A + row * size_t(M) * C;
+#pragma unroll
+  for (int c = 0; c < C; ++c) out[c] = 0.0f;
+  for (int m = 0; m < M; ++m)
+#pragma unroll
+    for (int c = 0; c < C; ++c) out[c] = fmaf(phi[m], a[m * C + c], out[c]);
+}
+
+// Hamilton product (r, i, j, k) of :841-852.
+__device__ inline void quat_mul(const float l[4], const float r[4], float u[4]) {
+  u[0] = l[0] * r[0] - l[1] * r[1] - l[2] * r[2] - l[3] * r[3];
+  u[1] = l[0] * r[1] + l[1] * r[0] + l[2] * r[3] - l[3] * r[2];
+  u[2] = l[0] * r[2] - l[1] * r[3] + l[2] * r[0] + l[3] * r[1];
+  u[3] = l[0] * r[3] + l[1] * r[2] - l[2] * r[1] + l[3] * r[0];
+}
+
+// y = x / max(|x|, 1e-12) (F.normalize); returns |x|.
+__device__ inline float normalize4(const float x[4], float y[4]) {
+  const float n = sqrtf(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
+  const float d = fmaxf(n, 1e-12f);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) y[k] = x[k] / d;
+  return n;
+}
+
+// quat_t = normalize(q0 (x) normalize(cos(a/2), r sin(a/2) / a)), a = |r| (:828-838), with the
+// intermediates the backward needs.
+struct BankRotation {
+  float r[3];
+  float angle, half, s;  // |r|, |r| / 2, sin(half) / angle (series 0.5 - a^2 / 48 below 1e-6)
+  float v[4], vn;        // (cos(half), r s) and its norm
+  float qa[4];           // v normalised
+  float u[4], un;        // q0 (x) qa and its norm
+  float q[4];            // u normalised
+};
+
+__device__ inline void bank_rotation(const float q0[4], const float r[3], BankRotation& R) {
+#pragma unroll
+  for (int k = 0; k < 3; ++k) R.r[k] = r[k];
+  R.angle = sqrtf(r[0] * r[0] + r[1] * r[1] + r[2] * r[2]);
+  R.half = 0.5f * R.angle;
+  R.s = R.angle < 1e-6f ? 0.5f - R.angle * R.angle / 48.0f : sinf(R.half) / fmaxf(R.angle, 1e-12f);
+  R.v[0] = cosf(R.half);
+#pragma unroll
+  for (int k = 0; k < 3; ++k) R.v[k + 1] = r[k] * R.s;
+  R.vn = normalize4(R.v, R.qa);
+  quat_mul(q0, R.qa, R.u);
+  R.un = normalize4(R.u, R.q);
+}
+
+// opacity_t = sigmoid(logit(clamp(o0, 1e-6, 1 - 1e-6)) + da) (:1216, 1222)
+__device__ inline float bank_clamped(float o0) { return fminf(fmaxf(o0, 1e-6f), 1.0f - 1e-6f); }
+__device__ inline float bank_opacity(float o0, float da) {
+  const float c = bank_clamped(o0);
+  return 1.0f / (1.0f + expf(-(logf(c / (1.0f - c)) + da)));
+}
+
+// Mean at view time t (velocity) or with the bank offset of basis phi (NULL: none).
+__device__ inline void mean_at(const gsb_scene& sc, size_t pg, float t, const float* phi, float m[3]) {
 #pragma unroll
   for (int k = 0; k < 3; ++k) {
-    float m = sc.means[pg * 3 + k];
-    if (sc.flags & GSB_SCENE_VELOCITY) m = __fadd_rn(m, __fmul_rn(t, sc.velocity[pg * 3 + k]));
-    p.m[k] = m;
+    m[k] = sc.means[pg * 3 + k];
+    if (sc.flags & GSB_SCENE_VELOCITY) m[k] = __fadd_rn(m[k], __fmul_rn(t, sc.velocity[pg * 3 + k]));
+  }
+  size_t row;
+  if (phi && bank_row(sc, pg, row)) {
+    float dm[3];
+    bank_combine<3>(sc.bank_mu, row, sc.bank_basis, phi, dm);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) m[k] = __fadd_rn(m[k], dm[k]);
+  }
+}
+
+// Parameters of Gaussian pg at one view (time t, bank basis phi or NULL); rot (may be NULL)
+// receives the bank rotation's intermediates of a bank Gaussian.
+__device__ inline GaussParams load_params(const gsb_scene& sc, size_t pg, float t, const float* phi,
+                                          BankRotation* rot = nullptr) {
+  GaussParams p;
+  const bool raw = sc.flags & GSB_SCENE_RAW;
+  mean_at(sc, pg, t, phi, p.m);
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
     const float s = sc.scales[pg * 3 + k];
     p.s[k] = raw ? expf(s) : s;
   }
@@ -117,6 +211,18 @@ __device__ inline GaussParams load_params(const gsb_scene& sc, size_t pg, float 
   }
   const float o = sc.opacities[pg];
   p.o = raw ? 1.0f / (1.0f + expf(-o)) : o;
+  size_t row;
+  if (phi && bank_row(sc, pg, row)) {
+    float r[3], da;
+    bank_combine<3>(sc.bank_rot, row, sc.bank_basis, phi, r);
+    BankRotation R;
+    bank_rotation(p.q, r, R);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) p.q[k] = R.q[k];
+    if (rot) *rot = R;
+    bank_combine<1>(sc.bank_alpha, row, sc.bank_basis, phi, &da);
+    p.o = bank_opacity(o, da);
+  }
   return p;
 }
 
@@ -258,6 +364,8 @@ __device__ inline void load_color(const gsb_scene& sc, size_t pg, const float d[
 
 // ---- stage 1 kernels: depth keys and inverse permutation -------------------------------------
 
+// BANK: the scene has a dynamic bank (compiled out of the other instances).
+template <bool BANK>
 __global__ void depth_key_kernel(gsb_scene sc, gsb_views vw, uint64_t* __restrict__ keys64,
                                  uint32_t* __restrict__ keys32, uint32_t* __restrict__ vals) {
   const size_t G = sc.n_gaussians;
@@ -268,12 +376,11 @@ __global__ void depth_key_kernel(gsb_scene sc, gsb_views vw, uint64_t* __restric
     const size_t pg = size_t(b / vw.views_per_set) * G + g;
     const float t = vw.times ? vw.times[b] : 0.0f;
     const float* c2w = vw.camera_to_world + b * 16;
-    float d[3], R[9];
+    float m[3], d[3], R[9];
+    mean_at(sc, pg, t, BANK ? view_basis(sc, vw, b) : nullptr, m);
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
-      float m = sc.means[pg * 3 + k];
-      if (sc.flags & GSB_SCENE_VELOCITY) m = __fadd_rn(m, __fmul_rn(t, sc.velocity[pg * 3 + k]));
-      d[k] = __fsub_rn(m, c2w[k * 4 + 3]);
+      d[k] = __fsub_rn(m[k], c2w[k * 4 + 3]);
 #pragma unroll
       for (int j = 0; j < 3; ++j) R[k * 3 + j] = c2w[k * 4 + j];
     }
@@ -298,6 +405,7 @@ __global__ void invert_order_kernel(const uint32_t* __restrict__ sorted_vals, in
 
 // ---- stage 2: projection + bounds ------------------------------------------------------------
 
+template <bool BANK>
 __global__ void __launch_bounds__(256) preprocess_fwd_kernel(gsb_scene sc, gsb_views vw, RenderConsts rc,
                                                              const int32_t* __restrict__ rank_of,
                                                              float* __restrict__ records, int4* __restrict__ rects,
@@ -310,7 +418,7 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(gsb_scene sc, gsb_v
     const size_t pg = size_t(b / vw.views_per_set) * G + g;
     const float t = vw.times ? vw.times[b] : 0.0f;
     const Camera cam = load_camera(vw, b);
-    const GaussParams p = load_params(sc, pg, t);
+    const GaussParams p = load_params(sc, pg, t, BANK ? view_basis(sc, vw, b) : nullptr);
     Proj P;
     project(p, cam, rc.near_plane, P);
     float rgb[3];
@@ -478,9 +586,47 @@ __device__ inline void lens_point_backward(const Proj& P, const Camera& cam, flo
   }
 }
 
+// Backward of normalize4: d loss / d x from d loss / d y, y = x / max(n, 1e-12), n = |x|.
+__device__ inline void normalize4_vjp(const float y[4], float n, const float dy[4], float dx[4]) {
+  if (n >= 1e-12f) {
+    const float dot = y[0] * dy[0] + y[1] * dy[1] + y[2] * dy[2] + y[3] * dy[3];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) dx[k] = (dy[k] - y[k] * dot) / n;
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) dx[k] = dy[k] / 1e-12f;
+  }
+}
+
+// Backward of quat_mul: d loss / d l and d loss / d r from d loss / d (l (x) r).
+__device__ inline void quat_mul_vjp(const float l[4], const float r[4], const float du[4], float dl[4], float dr[4]) {
+  dl[0] = du[0] * r[0] + du[1] * r[1] + du[2] * r[2] + du[3] * r[3];
+  dl[1] = -du[0] * r[1] + du[1] * r[0] - du[2] * r[3] + du[3] * r[2];
+  dl[2] = -du[0] * r[2] + du[1] * r[3] + du[2] * r[0] - du[3] * r[1];
+  dl[3] = -du[0] * r[3] - du[1] * r[2] + du[2] * r[1] + du[3] * r[0];
+  dr[0] = du[0] * l[0] + du[1] * l[1] + du[2] * l[2] + du[3] * l[3];
+  dr[1] = -du[0] * l[1] + du[1] * l[0] + du[2] * l[3] - du[3] * l[2];
+  dr[2] = -du[0] * l[2] - du[1] * l[3] + du[2] * l[0] + du[3] * l[1];
+  dr[3] = -du[0] * l[3] + du[1] * l[2] - du[2] * l[1] + du[3] * l[0];
+}
+
+// Backward of v = (cos(a/2), r s(a)), a = |r|, through the branch bank_rotation took (torch.where
+// routes the gradient to the chosen branch; the norm's gradient is 0 at r = 0).
+__device__ inline void axis_angle_vjp(const BankRotation& R, const float dv[4], float dr[3]) {
+  const float a = R.angle;
+  const float dvr = dv[1] * R.r[0] + dv[2] * R.r[1] + dv[3] * R.r[2];
+  const float ds = a < 1e-6f ? -a / 24.0f : (0.5f * cosf(R.half) * a - sinf(R.half)) / (a * a);
+  const float da = dv[0] * (-0.5f * sinf(R.half)) + dvr * ds;
+  const float ia = a > 0.0f ? 1.0f / a : 0.0f;
+#pragma unroll
+  for (int k = 0; k < 3; ++k) dr[k] = dv[k + 1] * R.s + da * R.r[k] * ia;
+}
+
 // K = SH coefficients per channel (1, 4, 9, 16) or 0 for plain rgb; LENS: some view has a
-// non-pinhole lens (the dual-number lens backward is compiled into these instances only)
-template <int K, bool LENS>
+// non-pinhole lens (the dual-number lens backward is compiled into these instances only); BANK:
+// the scene has a dynamic bank (activated values, K = 0): the gradients of its coefficients are
+// summed over the set's views in registers, GSB_BANK_MAX_BASIS x 7 per Gaussian.
+template <int K, bool LENS, bool BANK>
 __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_views vw, RenderConsts rc,
                                                              const int32_t* __restrict__ rank_of,
                                                              const float* __restrict__ grad2d, gsb_scene_grads gr) {
@@ -490,6 +636,8 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
   const bool vel = sc.flags & GSB_SCENE_VELOCITY;
   const bool clamp_sh = sc.flags & GSB_SCENE_SH_CLAMP;
   constexpr int KC = K > 0 ? K : 1;
+  constexpr int NB = BANK ? GSB_BANK_MAX_BASIS : 1;
+  const int M = sc.bank_basis;
   for (size_t pg = blockIdx.x * size_t(blockDim.x) + threadIdx.x; pg < total; pg += size_t(gridDim.x) * blockDim.x) {
     const int s = int(pg / G);
     const size_t g = pg - size_t(s) * G;
@@ -497,6 +645,11 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
     float acol[KC * 3];
 #pragma unroll
     for (int k = 0; k < KC * 3; ++k) acol[k] = 0.0f;
+    size_t row = 0;
+    const bool banked = BANK && bank_row(sc, pg, row);
+    float amu[NB][3], arot[NB][3], aal[NB];
+#pragma unroll
+    for (int m = 0; m < NB; ++m) amu[m][0] = amu[m][1] = amu[m][2] = arot[m][0] = arot[m][1] = arot[m][2] = aal[m] = 0.0f;
     const int b0 = s * vw.views_per_set;
     const int b1 = min(b0 + vw.views_per_set, vw.n_views);
     for (int b = b0; b < b1; ++b) {
@@ -507,7 +660,9 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
       const float dzo = g2[9];
       const float t = vw.times ? vw.times[b] : 0.0f;
       const Camera cam = load_camera(vw, b);
-      const GaussParams p = load_params(sc, pg, t);
+      const float* phi = BANK ? view_basis(sc, vw, b) : nullptr;
+      BankRotation R;
+      const GaussParams p = load_params(sc, pg, t, phi, &R);
       Proj P;
       project(p, cam, rc.near_plane, P);
       if (!P.front) continue;  // opacity * 0: no gradient reaches this Gaussian from this view
@@ -557,6 +712,36 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
 #pragma unroll
         for (int k = 0; k < 3; ++k) as[k] += dsv[k] * p.s[k];
         ao += dO * p.o * (1.0f - p.o);
+      } else if (banked) {
+        // quat_t = normalize(q0 (x) normalize(v(r))), r = sum_m phi_m bank_rot[m]
+        const float4 q4 = reinterpret_cast<const float4*>(sc.quats)[pg];
+        const float q0[4] = {q4.x, q4.y, q4.z, q4.w};
+        float du[4], dq0[4], dqa[4], dv[4], dr[3];
+        normalize4_vjp(R.q, R.un, dq, du);
+        quat_mul_vjp(q0, R.qa, du, dq0, dqa);
+        normalize4_vjp(R.qa, R.vn, dqa, dv);
+        axis_angle_vjp(R, dv, dr);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) aq[k] += dq0[k];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) as[k] += dsv[k];
+        // opacity_t = sigmoid(logit(clamp(o0)) + sum_m phi_m bank_alpha[m]); clamp passes the
+        // gradient inside its range
+        const float o0 = sc.opacities[pg];
+        const float c = bank_clamped(o0);
+        const float dz = dO * p.o * (1.0f - p.o);
+        if (o0 >= 1e-6f && o0 <= 1.0f - 1e-6f) ao += dz / (c * (1.0f - c));
+#pragma unroll
+        for (int m = 0; m < NB; ++m) {
+          if (m >= M) break;
+          const float f = phi[m];
+#pragma unroll
+          for (int k = 0; k < 3; ++k) {
+            amu[m][k] = fmaf(f, dmt[k], amu[m][k]);
+            arot[m][k] = fmaf(f, dr[k], arot[m][k]);
+          }
+          aal[m] = fmaf(f, dz, aal[m]);
+        }
       } else {
 #pragma unroll
         for (int k = 0; k < 4; ++k) aq[k] += dq[k];
@@ -581,6 +766,18 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
       for (int k = 0; k < KC * 3; ++k) gr.colors[pg * KC * 3 + k] = acol[k];
     if (gr.velocity && vel)
       for (int k = 0; k < 3; ++k) gr.velocity[pg * 3 + k] = av[k];
+    if (banked) {
+#pragma unroll
+      for (int m = 0; m < NB; ++m) {
+        if (m >= M) break;
+        const size_t o = row * size_t(M) + size_t(m);
+        if (gr.bank_mu)
+          for (int k = 0; k < 3; ++k) gr.bank_mu[o * 3 + k] = amu[m][k];
+        if (gr.bank_rot)
+          for (int k = 0; k < 3; ++k) gr.bank_rot[o * 3 + k] = arot[m][k];
+        if (gr.bank_alpha) gr.bank_alpha[o] = aal[m];
+      }
+    }
   }
 }
 
@@ -612,7 +809,7 @@ __global__ void __launch_bounds__(128) camera_bwd_kernel(gsb_scene sc, gsb_views
     const float dcol[3] = {g2[6], g2[7], g2[8]};
     const float t = vw.times ? vw.times[b] : 0.0f;
     const Camera cam = load_camera(vw, b);
-    const GaussParams p = load_params(sc, pg, t);
+    const GaussParams p = load_params(sc, pg, t, view_basis(sc, vw, b));
     Proj P;
     project(p, cam, rc.near_plane, P);
     if (P.front) {
@@ -716,7 +913,8 @@ gsb_status launch_depth_keys(const gsb_scene& sc, const gsb_views& vw, uint64_t*
                              uint32_t* vals, cudaStream_t st) {
   const size_t n = size_t(vw.n_views) * sc.n_gaussians;
   note_launch();
-  depth_key_kernel<<<grid_for(n, 256), 256, 0, st>>>(sc, vw, keys64, keys32, vals);
+  if (sc.flags & GSB_SCENE_BANK) depth_key_kernel<true><<<grid_for(n, 256), 256, 0, st>>>(sc, vw, keys64, keys32, vals);
+  else depth_key_kernel<false><<<grid_for(n, 256), 256, 0, st>>>(sc, vw, keys64, keys32, vals);
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 
@@ -732,7 +930,10 @@ gsb_status launch_preprocess_fwd(const gsb_scene& sc, const gsb_views& vw, const
                                  cudaStream_t st) {
   const size_t n = size_t(vw.n_views) * sc.n_gaussians;
   note_launch();
-  preprocess_fwd_kernel<<<grid_for(n, 256), 256, 0, st>>>(sc, vw, rc, rank_of, records, rects, counts, cov);
+  if (sc.flags & GSB_SCENE_BANK)
+    preprocess_fwd_kernel<true><<<grid_for(n, 256), 256, 0, st>>>(sc, vw, rc, rank_of, records, rects, counts, cov);
+  else
+    preprocess_fwd_kernel<false><<<grid_for(n, 256), 256, 0, st>>>(sc, vw, rc, rank_of, records, rects, counts, cov);
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 
@@ -740,12 +941,16 @@ template <bool LENS>
 static void launch_bwd_for_degree(int deg, int grid, const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
                                   const int32_t* rank_of, const float* grad2d, const gsb_scene_grads& gr,
                                   cudaStream_t st) {
+  if (sc.flags & GSB_SCENE_BANK) {  // activated values only (checked at the entry points)
+    preprocess_bwd_kernel<0, LENS, true><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr);
+    return;
+  }
   switch (deg) {
-    case -1: preprocess_bwd_kernel<0, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
-    case 0: preprocess_bwd_kernel<1, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
-    case 1: preprocess_bwd_kernel<4, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
-    case 2: preprocess_bwd_kernel<9, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
-    default: preprocess_bwd_kernel<16, LENS><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
+    case -1: preprocess_bwd_kernel<0, LENS, false><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
+    case 0: preprocess_bwd_kernel<1, LENS, false><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
+    case 1: preprocess_bwd_kernel<4, LENS, false><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
+    case 2: preprocess_bwd_kernel<9, LENS, false><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
+    default: preprocess_bwd_kernel<16, LENS, false><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr); break;
   }
 }
 

@@ -52,6 +52,8 @@ class SceneSpec:
     sh_degree: int
     velocity: bool
     sh_clamp: bool
+    bank_basis: int = 0  # dynamic bank: temporal basis functions M (0: no bank)
+    bank_first: int = 0  # dynamic bank: Gaussians before this index are static
 
 
 @dataclass
@@ -127,7 +129,8 @@ def _f32(t: torch.Tensor | None) -> torch.Tensor | None:
     return t.detach().to(dtype=torch.float32).contiguous()
 
 
-def scene_struct(spec: SceneSpec, means, scales, quats, opacities, colors, velocity) -> _lib.Scene:
+def scene_struct(spec: SceneSpec, means, scales, quats, opacities, colors, velocity, bank=None) -> _lib.Scene:
+    """``bank``: (bank_mu, bank_rot, bank_alpha) device tensors when spec.bank_basis > 0."""
     s = _lib.Scene()
     s.n_sets = spec.n_sets
     s.n_gaussians = spec.n_gaussians
@@ -139,6 +142,10 @@ def scene_struct(spec: SceneSpec, means, scales, quats, opacities, colors, veloc
             flags |= _lib.SCENE_SH_CLAMP
     if spec.velocity:
         flags |= _lib.SCENE_VELOCITY
+    if spec.bank_basis:
+        flags |= _lib.SCENE_BANK
+        s.bank_mu, s.bank_rot, s.bank_alpha = (t.data_ptr() for t in bank)
+        s.bank_first, s.bank_basis = spec.bank_first, spec.bank_basis
     s.flags = flags
     s.means, s.scales, s.quats = means.data_ptr(), scales.data_ptr(), quats.data_ptr()
     s.opacities, s.colors = opacities.data_ptr(), colors.data_ptr()
@@ -146,7 +153,14 @@ def scene_struct(spec: SceneSpec, means, scales, quats, opacities, colors, veloc
     return s
 
 
-def views_struct(spec: ViewSpec, intrinsics, camera_to_world, times, lens_models=None, distortion=None) -> _lib.Views:
+def _scene_of(sspec: SceneSpec, t: dict) -> _lib.Scene:
+    bank = (t["bank_mu"], t["bank_rot"], t["bank_alpha"]) if sspec.bank_basis else None
+    return scene_struct(sspec, t["means"], t["scales"], t["quats"], t["opacities"], t["colors"], t.get("velocity"),
+                        bank)
+
+
+def views_struct(spec: ViewSpec, intrinsics, camera_to_world, times, lens_models=None, distortion=None,
+                 basis=None) -> _lib.Views:
     v = _lib.Views()
     v.n_views, v.views_per_set, v.height, v.width = spec.n_views, spec.views_per_set, spec.height, spec.width
     v.intrinsics = intrinsics.data_ptr()
@@ -154,12 +168,13 @@ def views_struct(spec: ViewSpec, intrinsics, camera_to_world, times, lens_models
     v.times = times.data_ptr() if times is not None else None
     v.lens_models = lens_models.data_ptr() if lens_models is not None else None
     v.distortion = distortion.data_ptr() if lens_models is not None else None
+    v.basis = basis.data_ptr() if basis is not None else None
     return v
 
 
 def _views_of(vspec: ViewSpec, tensors: dict) -> _lib.Views:
     return views_struct(vspec, tensors["intrinsics"], tensors["camera_to_world"], tensors.get("times"),
-                        tensors.get("lens_models"), tensors.get("distortion"))
+                        tensors.get("lens_models"), tensors.get("distortion"), tensors.get("basis"))
 
 
 # Pair-key capacity per frame shape (device, views, Gaussians, image, tile size, mode), from the
@@ -181,8 +196,7 @@ def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, n
     dev = tensors["means"].device
     st = _stream(dev)
     B, G, H, W = vspec.n_views, sspec.n_gaussians, vspec.height, vspec.width
-    scene = scene_struct(sspec, tensors["means"], tensors["scales"], tensors["quats"], tensors["opacities"],
-                         tensors["colors"], tensors.get("velocity"))
+    scene = _scene_of(sspec, tensors)
     views = _views_of(vspec, tensors)
     opts = cfg.options(near_plane)
 
@@ -256,8 +270,7 @@ def backward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, 
     dev = tensors["means"].device
     st = _stream(dev)
     B, G = vspec.n_views, sspec.n_gaussians
-    scene = scene_struct(sspec, tensors["means"], tensors["scales"], tensors["quats"], tensors["opacities"],
-                         tensors["colors"], tensors.get("velocity"))
+    scene = _scene_of(sspec, tensors)
     views = _views_of(vspec, tensors)
     opts = cfg.options(near_plane)
     grad2d = torch.empty(B * G * _lib.GRAD2D_FLOATS, dtype=torch.float32, device=dev)
@@ -276,6 +289,10 @@ def backward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, 
     g.means, g.scales, g.quats = out["means"].data_ptr(), out["scales"].data_ptr(), out["quats"].data_ptr()
     g.opacities, g.colors = out["opacities"].data_ptr(), out["colors"].data_ptr()
     g.velocity = out["velocity"].data_ptr() if "velocity" in out else None
+    if sspec.bank_basis:
+        for k in ("bank_mu", "bank_rot", "bank_alpha"):
+            out[k] = torch.empty_like(tensors[k])
+        g.bank_mu, g.bank_rot, g.bank_alpha = (out[k].data_ptr() for k in ("bank_mu", "bank_rot", "bank_alpha"))
     with _stage("preprocess_bwd"):
         _lib.check("gsb_preprocess_bwd", L.gsb_preprocess_bwd(scene, views, opts, state.rank_of.data_ptr(),
                                                               grad2d.data_ptr(), g, st))
@@ -294,6 +311,7 @@ def backward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, 
 
 
 _PARAM_NAMES = ("means", "scales", "quats", "opacities", "colors", "velocity")
+_BANK_NAMES = ("bank_mu", "bank_rot", "bank_alpha")
 
 
 _CAMERA_NAMES = ("cam_intrinsics", "cam_camera_to_world", None, "cam_distortion")  # times get none
@@ -301,16 +319,17 @@ _CAMERA_NAMES = ("cam_intrinsics", "cam_camera_to_world", None, "cam_distortion"
 
 class _RenderFunction(torch.autograd.Function):
     """(image [B,3,H,W], alpha [B,H,W], depth [B,H,W]) of the scene; gradients flow to the six
-    scene tensors and, when they require them, to the intrinsics, camera_to_world and lens
-    distortion (not to the per-view times)."""
+    scene tensors, the dynamic bank's coefficients and, when they require them, to the
+    intrinsics, camera_to_world and lens distortion (not to the per-view times or the basis)."""
 
     @staticmethod
     def forward(ctx, sspec, vspec, cfg, near_plane, lens_models, means, scales, quats, opacities, colors, velocity,
-                intrinsics, camera_to_world, times, distortion):
+                intrinsics, camera_to_world, times, distortion, bank_mu, bank_rot, bank_alpha, basis):
         tensors = {
             "means": _f32(means), "scales": _f32(scales), "quats": _f32(quats), "opacities": _f32(opacities),
             "colors": _f32(colors), "velocity": _f32(velocity), "intrinsics": _f32(intrinsics),
-            "camera_to_world": _f32(camera_to_world), "times": _f32(times),
+            "camera_to_world": _f32(camera_to_world), "times": _f32(times), "bank_mu": _f32(bank_mu),
+            "bank_rot": _f32(bank_rot), "bank_alpha": _f32(bank_alpha), "basis": _f32(basis),
         }
         if lens_models is not None:
             tensors["lens_models"], tensors["distortion"] = lens_models, _f32(distortion)
@@ -322,6 +341,7 @@ class _RenderFunction(torch.autograd.Function):
                                                                           velocity)]
         ctx.camera_shapes = [None if t is None else (t.shape, t.dtype) for t in (intrinsics, camera_to_world, times,
                                                                                  distortion)]
+        ctx.bank_shapes = [None if t is None else (t.shape, t.dtype) for t in (bank_mu, bank_rot, bank_alpha)]
         if depth is None:
             depth = image.new_zeros(0)
             ctx.mark_non_differentiable(depth)
@@ -342,14 +362,16 @@ class _RenderFunction(torch.autograd.Function):
         grads = backward_stages(ctx.sspec, vspec, ctx.cfg, ctx.near_plane, t, ctx.state, d_image, d_alpha, d_depth,
                                 camera=camera)
         out = []
-        for name, shp in zip(_PARAM_NAMES + _CAMERA_NAMES, ctx.shapes + ctx.camera_shapes):
+        for name, shp in zip(_PARAM_NAMES + _CAMERA_NAMES + _BANK_NAMES,
+                             ctx.shapes + ctx.camera_shapes + ctx.bank_shapes):
             if shp is None or name not in grads:
                 out.append(None)
             else:
                 out.append(grads[name].reshape(shp[0]).to(shp[1]))
         ctx.state = None
         # sspec, vspec, cfg, near_plane, lens_models | 6 scene tensors | intrinsics, c2w, times, distortion
-        return (None, None, None, None, None, *out[:6], out[6], out[7], None, out[9])
+        # | bank_mu, bank_rot, bank_alpha, basis
+        return (None, None, None, None, None, *out[:6], out[6], out[7], None, out[9], *out[10:13], None)
 
 
 def _check_times_no_grad(times):
@@ -402,13 +424,19 @@ def lens_tensors(lens_models, distortion, n_views: int, device):
 
 
 def render_scene(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, near_plane: float, *, means, scales,
-                 quats, opacities, colors, velocity, intrinsics, camera_to_world, times, lens=None):
+                 quats, opacities, colors, velocity, intrinsics, camera_to_world, times, lens=None, bank=None,
+                 basis=None):
     """Autograd entry used by every public render function.  ``lens``: the pair lens_tensors()
     returns, or None for pinhole views only.  Intrinsics, camera_to_world and the distortion may
-    require gradients (cameras learned through the render call)."""
+    require gradients (cameras learned through the render call).  ``bank``: (bank_mu, bank_rot,
+    bank_alpha) with ``basis`` [B, M] when sspec.bank_basis > 0."""
     if not means.is_cuda:
         raise RuntimeError("the b200 renderer runs on CUDA devices only (got a tensor on %s)" % means.device)
     _check_times_no_grad(times)
     lens_models, distortion = lens if lens is not None else (None, None)
+    bank_mu, bank_rot, bank_alpha = bank if bank is not None else (None, None, None)
+    if sspec.bank_basis and (bank is None or basis is None):
+        raise ValueError("a scene with a dynamic bank needs the bank tensors and the per-view basis")
     return _RenderFunction.apply(sspec, vspec, cfg, float(near_plane), lens_models, means, scales, quats, opacities,
-                                 colors, velocity, intrinsics, camera_to_world, times, distortion)
+                                 colors, velocity, intrinsics, camera_to_world, times, distortion, bank_mu, bank_rot,
+                                 bank_alpha, basis)

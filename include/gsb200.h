@@ -58,6 +58,9 @@ typedef enum gsb_status {
                                    the reference's render call takes them) */
 #define GSB_SCENE_VELOCITY 0x2u /* means_t = means + t_view * velocity */
 #define GSB_SCENE_SH_CLAMP 0x4u /* rgb = max(SH(dir) + 0.5, 0) (raw mode only) */
+#define GSB_SCENE_BANK 0x8u     /* dynamic Gaussian bank (activated mode only, no velocity): see
+                                   gsb_scene.bank_mu */
+#define GSB_BANK_MAX_BASIS 16   /* temporal basis functions a bank may have */
 
 /* Render flags (gsb_options.flags). */
 #define GSB_RENDER_TILED_COMPAT 0x1u /* tiled.py bounds (bound_scale, 1/255 threshold) and
@@ -80,6 +83,19 @@ typedef struct gsb_scene {
   const float* opacities; /* [S,G]   opacity in [0,1] (activated) or logits (raw) */
   const float* colors;    /* [S,G,3] rgb (activated) or SH [S,G,(d+1)^2,3] (raw) */
   const float* velocity;  /* [S,G,3] with GSB_SCENE_VELOCITY, else NULL */
+  /* Dynamic bank (GSB_SCENE_BANK), the evaluation of
+     gs_models/dynamic_video_token_gs_implicit_camera.py:1206-1224 (_eval_dynamic_bank) fused into
+     the projection.  Gaussians g < bank_first are static; for g >= bank_first, d = g - bank_first
+     and phi = gsb_views.basis[view] (M values):
+       mean_t    = means + sum_m phi_m bank_mu[d,m]
+       quat_t    = normalize(quats (x) axis_angle_quat(sum_m phi_m bank_rot[d,m]))   (:828-852)
+       opacity_t = sigmoid(logit(clamp(opacities, 1e-6, 1 - 1e-6)) + sum_m phi_m bank_alpha[d,m])
+     scales and colors as given (per set: arrays of S * (G - bank_first) rows). */
+  const float* bank_mu;    /* [S, G - bank_first, M, 3] */
+  const float* bank_rot;   /* [S, G - bank_first, M, 3] axis-angle, radians */
+  const float* bank_alpha; /* [S, G - bank_first, M]    opacity-logit offsets */
+  int32_t bank_first;      /* 0 <= bank_first <= G */
+  int32_t bank_basis;      /* M, 1 .. GSB_BANK_MAX_BASIS */
 } gsb_scene;
 
 /* Lens models (gsb_views.lens_models), the CameraSpec lens_model values of camera.py:7-31. */
@@ -98,6 +114,8 @@ typedef struct gsb_views {
   const float* times;           /* [B] or NULL (device) */
   const int32_t* lens_models;   /* [B] GSB_LENS_* or NULL: every view pinhole (device) */
   const float* distortion;      /* [B,5] coefficients (zero-padded), read for non-pinhole views */
+  const float* basis;           /* [B,M] temporal basis of each view's time (GSB_SCENE_BANK; the
+                                   reference's _temporal_basis, :806-825), else NULL */
 } gsb_views;
 
 typedef struct gsb_options {
@@ -126,6 +144,9 @@ typedef struct gsb_scene_grads {
   float* opacities;
   float* colors;
   float* velocity;
+  float* bank_mu;    /* GSB_SCENE_BANK: shapes as gsb_scene */
+  float* bank_rot;
+  float* bank_alpha;
 } gsb_scene_grads;
 
 /* Gradients of the cameras (device; NULL entries are skipped; outputs are overwritten). */

@@ -37,14 +37,17 @@ def test_bindings_cover_the_header():
 
 def test_version_and_status_strings(lib):
     assert b"sm_100a" in lib.gsb_version()
-    for code in range(8):
-        assert lib.gsb_status_string(code)
+    for code in range(9):
+        assert lib.gsb_status_string(code) != b"unknown status"
+    assert lib.gsb_status_string(99) == b"unknown status"
 
 
 def test_struct_sizes_match_header():
-    # 4 ints + 6 pointers; 4 ints + 5 pointers; 2 ints + 11 floats (incl. background[3]) + 1 int
-    assert ctypes.sizeof(_lib.Scene) == 16 + 6 * 8
-    assert ctypes.sizeof(_lib.Views) == 16 + 5 * 8
+    # 4 ints + 9 pointers + 2 ints; 4 ints + 6 pointers; 2 ints + 11 floats (incl. background[3])
+    # + 1 int; 9 pointers
+    assert ctypes.sizeof(_lib.Scene) == 16 + 9 * 8 + 8
+    assert ctypes.sizeof(_lib.Views) == 16 + 6 * 8
+    assert ctypes.sizeof(_lib.SceneGrads) == 9 * 8
     assert ctypes.sizeof(_lib.Options) == 8 + 11 * 4 + 4
     assert ctypes.sizeof(_lib.LossOptions) == 16 + 6 * 4
 
@@ -81,6 +84,38 @@ def test_argument_errors_return_codes_without_touching_a_gpu(lib):
     lo.type = 0
     lo.window_size = 4  # even window
     assert lib.gsb_loss_fwd_bwd(ctypes.byref(lo), 1, 3, 16, 16, 16, 16, 16, None, 16, 4096, None) == 7
+
+
+def test_bank_scene_checks_are_host_only(lib):
+    """A dynamic bank needs the activated scene without velocity, its three coefficient arrays, a
+    per-view basis, 1..16 basis functions and 0 <= bank_first <= G; anything else is rejected
+    before a kernel runs."""
+    s, v = _lib.Scene(), _lib.Views()
+    s.n_sets, s.n_gaussians = 1, 10
+    s.means = s.scales = s.quats = s.opacities = s.colors = 16
+    v.n_views = v.views_per_set = v.height = v.width = 1
+    v.intrinsics = v.camera_to_world = 16
+
+    def depth_order():
+        return lib.gsb_depth_order(ctypes.byref(s), ctypes.byref(v), 16, 16, 16, 1 << 30, None)
+
+    s.flags = _lib.SCENE_BANK
+    assert depth_order() == 7  # no coefficient arrays
+    s.bank_mu = s.bank_rot = s.bank_alpha = 16
+    s.bank_basis = 8
+    assert depth_order() == 7  # no basis
+    v.basis = 16
+    s.flags = _lib.SCENE_BANK | _lib.SCENE_RAW
+    assert depth_order() == 7
+    s.flags = _lib.SCENE_BANK | _lib.SCENE_VELOCITY
+    s.velocity = 16
+    assert depth_order() == 7
+    s.flags = _lib.SCENE_BANK
+    for m in (0, 17):
+        s.bank_basis = m
+        assert depth_order() == 7
+    s.bank_basis, s.bank_first = 8, 11
+    assert depth_order() == 1  # GSB_ERR_SHAPE
 
 
 def test_workspace_queries_are_host_only(lib):
