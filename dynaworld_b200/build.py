@@ -48,18 +48,22 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
               f"-I{INCLUDE}", f"-I{CSRC}", "--expt-relaxed-constexpr"]
     if ptxas_info:
         common.append("-Xptxas=-v")
-    objs = []
-    for src in SOURCES:
-        obj = objdir / (Path(src).stem + ".o")
-        cmd = common + ["-c", str(CSRC / src), "-o", str(obj)]
-        if verbose:
+    objs = [str(objdir / (Path(src).stem + ".o")) for src in SOURCES]
+    cmds = [common + ["-c", str(CSRC / src), "-o", obj] for src, obj in zip(SOURCES, objs)]
+    if verbose:
+        for cmd in cmds:
             print(" ".join(cmd), flush=True)
-        res = subprocess.run(cmd, capture_output=True, text=True)
-        if res.returncode != 0 or (verbose and res.stderr):
-            sys.stderr.write(res.stderr)
-        if res.returncode != 0:
-            raise RuntimeError(f"nvcc failed on {src}")
-        objs.append(str(obj))
+    # one nvcc per source file, all at once (the raster file dominates the build time)
+    procs = [subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True) for cmd in cmds]
+    failed = []
+    for src, proc in zip(SOURCES, procs):
+        _out, err = proc.communicate()
+        if proc.returncode != 0 or (verbose and err):
+            sys.stderr.write(err)
+        if proc.returncode != 0:
+            failed.append(src)
+    if failed:
+        raise RuntimeError(f"nvcc failed on {', '.join(failed)}")
     tmp = LIB.with_suffix(".so.tmp")
     link = [nvcc, *ARCH, "-shared", "-o", str(tmp), *objs, "-cudart", "static"]
     if verbose:

@@ -358,7 +358,9 @@ GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opt
   a.pixel_t = const_cast<float*>(pixel_t), a.pixel_state = const_cast<uint32_t*>(pixel_state);
   a.nseg = raster_segments(*views, *opts), a.ckpt = const_cast<float*>(pixel_ckpt);
   if (a.nseg > 1 && !pixel_ckpt) return GSB_ERR_ARG;
-  a.d_image = d_image, a.d_alpha = d_alpha, a.d_depth = d_depth, a.view_scale = view_scale, a.grad2d = grad2d;
+  // the depth gradient needs the forward's depth sums (GSB_RENDER_DEPTH, the option the forward ran with)
+  a.d_image = d_image, a.d_alpha = d_alpha, a.view_scale = view_scale, a.grad2d = grad2d;
+  a.d_depth = (opts->flags & GSB_RENDER_DEPTH) ? d_depth : nullptr;
   if (views->n_views > 65535) return GSB_ERR_SHAPE;
   return launch_raster_bwd(a, as_stream(stream));
 }

@@ -33,6 +33,16 @@ constexpr uint32_t kCountBits = 28;
 constexpr uint32_t kCountMask = (1u << kCountBits) - 1u;
 constexpr uint32_t kFull = 0xffffffffu;
 
+// exp(-q / 2) as 2^(q * (-log2(e) / 2)) on the SFU's base-2 exponential (PTX ex2.approx; relative
+// error about 2^-22), one multiply and one SFU op per pair.  Forward and backward evaluate the same
+// expression, so the backward's alpha is the forward's to the bit.
+constexpr float kNegHalfLog2E = -0.72134752044448170368f;
+__device__ __forceinline__ float gauss_falloff(float q) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(fminf(q * kNegHalfLog2E, 0.0f)));
+  return y;
+}
+
 // q = A dx^2 + B dx dy + C dy^2 with a fixed rounding sequence (forward and backward agree).
 __device__ __forceinline__ float pair_q(float A, float B, float C, float dx, float dy) {
   const float t0 = __fmul_rn(__fmul_rn(A, dx), dx);
@@ -121,8 +131,9 @@ __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* rec
 constexpr int kCkptFloats = 6;
 
 // NSEG: list segments of the backward (checkpoints between).  CW: warps per CTA; the tile's NW warp
-// blocks are spread over NW / CW adjacent CTAs.
-template <int TILE, int PX, int NSEG, int CW>
+// blocks are spread over NW / CW adjacent CTAs.  DEPTH: the depth output is written (and its sums
+// kept for the backward).
+template <int TILE, int PX, int NSEG, int CW, bool DEPTH>
 __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
   constexpr int NW = TILE * TILE / (32 * PX);
   constexpr int SPLIT = NW / CW;
@@ -184,7 +195,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
       const float dy = __fsub_rn(fy[k], g.y);
       const float q = pair_q(g.z, g.w, ct.x, dx, dy);
       if (!(q <= ct.z)) continue;
-      const float e = __expf(fminf(-0.5f * q, 0.0f));
+      const float e = gauss_falloff(q);
       const float alpha = fminf(fmaxf(ct.y * e, 0.0f), rc.alpha_clamp);
       if (!(alpha >= rc.alpha_cutoff)) continue;
       const float4 col = s_col[lw][j];
@@ -194,7 +205,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
       C1[k] = fmaf(w, col.y, C1[k]);
       C2[k] = fmaf(w, col.z, C2[k]);
       Ws[k] += w;
-      D[k] = fmaf(w, col.w, D[k]);
+      if (DEPTH) D[k] = fmaf(w, col.w, D[k]);
       const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
       S[k] = S[k] * (f * inv_f0);
       if (T * f < rc.t_threshold) {  // T after this entry
@@ -257,7 +268,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
         ck[2 * total_px] = C1[k] - kC1[s][k];
         ck[3 * total_px] = C2[k] - kC2[s][k];
         ck[4 * total_px] = Ws[k] - kW[s][k];
-        ck[5 * total_px] = D[k] - kD[s][k];
+        if (DEPTH) ck[5 * total_px] = D[k] - kD[s][k];
       }
     }
     const float wc = fminf(fmaxf(Ws[k], 0.0f), 1.0f);
@@ -272,7 +283,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
       a.image[(size_t(view) * 3 + ch) * HW + poff] = rc.clamp_image ? fminf(fmaxf(pre, 0.0f), 1.0f) : pre;
     }
     if (a.alpha) a.alpha[pix] = Ws[k];
-    if (a.depth) a.depth[pix] = D[k];
+    if (DEPTH) a.depth[pix] = D[k];
     a.pixel_t[pix] = S[k];  // normalised transmittance after the last blended entry
     a.pixel_state[pix] = min(n_proc[k], kCountMask) | (mask << kCountBits);
   }
@@ -378,7 +389,7 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
         R1[k] = ck[2 * total_px];
         R2[k] = ck[3 * total_px];
         RW[k] = ck[4 * total_px];
-        RD[k] = ck[5 * total_px];
+        if (DEPTH) RD[k] = ck[5 * total_px];  // written by the forward only with the depth output
       }
       const uint32_t mask = st >> kCountBits;
       const float* di = a.d_image + size_t(view) * 3 * HW + poff;
@@ -418,7 +429,7 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           const float dy = __fsub_rn(fy[k], g.y);
           const float q = pair_q(g.z, g.w, ct.x, dx, dy);
           if (!(q <= ct.z)) continue;
-          const float e = __expf(fminf(-0.5f * q, 0.0f));
+          const float e = gauss_falloff(q);
           const float araw = ct.y * e;
           const float alpha = fminf(fmaxf(araw, 0.0f), rc.alpha_clamp);
           if (!(alpha >= rc.alpha_cutoff)) continue;
@@ -441,8 +452,8 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           R2[k] = fmaf(w, col.z, R2[k]);
           RW[k] += w;
           const float dlr = (araw >= 0.0f && araw <= rc.alpha_clamp) ? dlda : 0.0f;
-          const float power = -0.5f * q;
-          const float pmask = power < 0.0f ? 1.0f : (power == 0.0f ? 0.5f : 0.0f);
+          // d min(power, 0) / d power, power = -q / 2 (torch splits a tie at 0 evenly)
+          const float pmask = q > 0.0f ? 1.0f : (q == 0.0f ? 0.5f : 0.0f);
           const float dpow = dlr * araw * pmask;
           const float u = dpow * dx, t = dpow * dy;
           v[0] += g.z * u + 0.5f * g.w * t;
@@ -510,7 +521,8 @@ template <int TILE, int PX, int NSEG, int CW>
 static void fwd_launch_cw(const RasterArgs& a, cudaStream_t st) {
   constexpr int SPLIT = TILE * TILE / (32 * PX) / CW;
   const dim3 grid(unsigned(a.rc.n_tiles) * SPLIT, a.B);  // the CTAs of a tile are adjacent
-  raster_fwd_kernel<TILE, PX, NSEG, CW><<<grid, 32 * CW, 0, st>>>(a);
+  if (a.depth) raster_fwd_kernel<TILE, PX, NSEG, CW, true><<<grid, 32 * CW, 0, st>>>(a);
+  else raster_fwd_kernel<TILE, PX, NSEG, CW, false><<<grid, 32 * CW, 0, st>>>(a);
 }
 
 template <int TILE, int PX, int NSEG>

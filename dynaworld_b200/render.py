@@ -18,8 +18,10 @@ from .config import B200RendererConfig
 MIN_RENDER_DEPTH = 1e-4  # src/train/renderers/common.py:3
 
 # Optional stage timing: when set to a list, every C-ABI stage call appends
-# (stage name, start event, end event), both recorded on the launching stream.
+# (stage name, start event, end event), both recorded on the launching stream; STAGE_FILTER (a set
+# of stage names, or None for all) limits which stages are bracketed.
 STAGE_EVENTS: list | None = None
+STAGE_FILTER: set | None = None
 
 
 class _stage:
@@ -30,7 +32,7 @@ class _stage:
         self.ev = None
 
     def __enter__(self):
-        if STAGE_EVENTS is not None:
+        if STAGE_EVENTS is not None and (STAGE_FILTER is None or self.name in STAGE_FILTER):
             self.ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             self.ev[0].record()
         return self
