@@ -302,9 +302,9 @@ GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int3
       GSB_OK)
     return s;
   if (!tile_order) return GSB_OK;
-  // launch order: tiles by descending list length (16-bit key: length / 16, saturated)
+  // launch order: tiles by descending list length (8-bit log-scale key, one radix pass)
   if ((s = launch_tile_order_keys(tile_ranges, uint32_t(NT), okeys, ovals, st)) != GSB_OK) return s;
-  return radix_sort(okeys, okeys_sorted, ovals, tile_order, uint32_t(NT), 4, 0, 16, order_ws, ows, st, status);
+  return radix_sort(okeys, okeys_sorted, ovals, tile_order, uint32_t(NT), 4, 0, 8, order_ws, ows, st, status);
 }
 
 // ---- stages 4 and 6 --------------------------------------------------------------------------

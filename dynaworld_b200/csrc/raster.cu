@@ -423,6 +423,7 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
         const float4 g = s_geo[lw][j];
         const float4 ct = s_cot[lw][j];
         const float dx = __fsub_rn(fx, g.x);
+        const float hB = 0.5f * g.w;  // half the cross coefficient
 #pragma unroll
         for (int k = 0; k < PX; ++k) {
           if (!(lj < n_proc[k])) continue;
@@ -456,16 +457,16 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           const float pmask = q > 0.0f ? 1.0f : (q == 0.0f ? 0.5f : 0.0f);
           const float dpow = dlr * araw * pmask;
           const float u = dpow * dx, t = dpow * dy;
-          v[0] += g.z * u + 0.5f * g.w * t;
-          v[1] += ct.x * t + 0.5f * g.w * u;
-          v[2] -= 0.5f * u * dx;
-          v[3] -= 0.5f * u * dy;
-          v[4] -= 0.5f * t * dy;
-          v[5] += dlr * e;
-          v[6] += g0[k] * w;
-          v[7] += g1[k] * w;
-          v[8] += g2c[k] * w;
-          if (DEPTH) v[9] += gD[k] * w;
+          v[0] = fmaf(g.z, u, fmaf(hB, t, v[0]));
+          v[1] = fmaf(ct.x, t, fmaf(hB, u, v[1]));
+          v[2] = fmaf(u, dx, v[2]);  // conic gradients: times -1/2 once the pixels are summed
+          v[3] = fmaf(u, dy, v[3]);
+          v[4] = fmaf(t, dy, v[4]);
+          v[5] = fmaf(dlr, e, v[5]);
+          v[6] = fmaf(g0[k], w, v[6]);
+          v[7] = fmaf(g1[k], w, v[7]);
+          v[8] = fmaf(g2c[k], w, v[8]);
+          if (DEPTH) v[9] = fmaf(gD[k], w, v[9]);
           contrib = true;
         }
       }
@@ -476,11 +477,12 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
         if (contrib) {
 #pragma unroll
           for (int k = 0; k < GSB_GRAD2D_FLOATS; ++k)
-            if (v[k] != 0.0f) atomicAdd(dst + k, v[k]);
+            if (v[k] != 0.0f) atomicAdd(dst + k, (k >= 2 && k <= 4) ? -0.5f * v[k] : v[k]);
         }
       } else {
         int k;
-        const float s = warp_sum10(v, lane, &k);
+        float s = warp_sum10(v, lane, &k);
+        if (k >= 2 && k <= 4) s *= -0.5f;
         if ((lane & 1) == 0 && k < GSB_GRAD2D_FLOATS && s != 0.0f) atomicAdd(dst + k, s);
       }
     }

@@ -89,8 +89,12 @@ def test_tile_launch_order_is_a_permutation_by_descending_length(case):
     order = st.order.cpu().numpy().astype(np.int64)
     np.testing.assert_array_equal(np.sort(order), np.arange(order.size))
     r = st.ranges.cpu().numpy().astype(np.int64).reshape(-1, 2)
-    lengths = (r[:, 1] - r[:, 0])[order] >> 4
-    assert np.all(np.diff(lengths) <= 0)
+    lengths = r[:, 1] - r[:, 0]
+    # 8-bit log-scale length class (exact below 16, 8 steps per power of two), longest first, ties
+    # in (view, tile) order
+    e = np.array([max(int(n).bit_length() - 1, 0) for n in lengths], dtype=np.int64)
+    cls = np.where(lengths < 8, lengths, (e - 2) * 8 + ((lengths >> np.maximum(e - 3, 0)) & 7))
+    np.testing.assert_array_equal(order, np.argsort(255 - cls, kind="stable"))
 
 
 @pytest.mark.parametrize("case", GOLDEN_CASES)
