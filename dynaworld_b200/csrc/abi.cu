@@ -141,16 +141,16 @@ GSB_API gsb_status gsb_read_status(const void* workspace, int* status_out, void*
 
 // ---- stage 1 ---------------------------------------------------------------------------------
 
+// Per-view segmented sort of 32-bit depth keys: the views are independent runs of G keys.
 static size_t depth_ws(int32_t B, int32_t G) {
   const uint32_t n = uint32_t(size_t(B) * G);
-  const int kb = B > 1 ? 8 : 4;
   Carver c(nullptr, 0);
   c.take<WorkspaceHeader>(1);
-  c.take<char>(size_t(n) * kb);  // keys
-  c.take<uint32_t>(n);           // values
-  c.take<char>(size_t(n) * kb);  // sorted keys
-  c.take<uint32_t>(n);           // sorted values
-  c.take<char>(radix_sort_workspace(n, kb, 1));
+  c.take<uint32_t>(n);  // keys
+  c.take<uint32_t>(n);  // values
+  c.take<uint32_t>(n);  // sorted keys
+  c.take<uint32_t>(n);  // sorted values
+  c.take<char>(segmented_sort_workspace(uint32_t(B), uint32_t(G)));
   return c.used;
 }
 
@@ -169,21 +169,21 @@ GSB_API gsb_status gsb_depth_order(const gsb_scene* scene, const gsb_views* view
   if (workspace_bytes < depth_ws(B, G)) return GSB_ERR_WORKSPACE;
   cudaStream_t st = as_stream(stream);
   const uint32_t n = uint32_t(size_t(B) * G);
-  const int kb = B > 1 ? 8 : 4;
   Carver c(workspace, workspace_bytes);
   c.take<WorkspaceHeader>(1);
-  void* keys = c.take<char>(size_t(n) * kb);
+  uint32_t* keys = c.take<uint32_t>(n);
   uint32_t* vals = c.take<uint32_t>(n);
-  void* skeys = c.take<char>(size_t(n) * kb);
+  uint32_t* skeys = c.take<uint32_t>(n);
   uint32_t* svals = c.take<uint32_t>(n);
-  const size_t sws = radix_sort_workspace(n, kb, 1);
+  const size_t sws = segmented_sort_workspace(uint32_t(B), uint32_t(G));
   void* sort_ws = c.take<char>(sws);
   int32_t* status = begin_status(workspace, st);
-  if ((s = launch_depth_keys(*scene, *views, kb == 8 ? static_cast<uint64_t*>(keys) : nullptr,
-                             kb == 4 ? static_cast<uint32_t*>(keys) : nullptr, vals, st)) != GSB_OK)
+  uint32_t* hist = nullptr;
+  if ((s = segmented_sort_prepare(sort_ws, sws, uint32_t(B), uint32_t(G), st, &hist)) != GSB_OK) return s;
+  if ((s = launch_depth_keys(*scene, *views, keys, vals, hist, st)) != GSB_OK) return s;
+  if ((s = segmented_sort_run(keys, skeys, vals, svals, uint32_t(B), uint32_t(G), sort_ws, sws, st, status)) !=
+      GSB_OK)
     return s;
-  const int bit_hi = 32 + (B > 1 ? bits_for(uint64_t(B)) : 0);
-  if ((s = radix_sort(keys, skeys, vals, svals, n, kb, 0, bit_hi, sort_ws, sws, st, status)) != GSB_OK) return s;
   return launch_invert_order(svals, B, G, sorted_ids, rank_of, st);
 }
 
@@ -424,22 +424,22 @@ GSB_API gsb_status gsb_splats2d_order(const gsb_splats2d* splats, int32_t* sorte
   if (workspace_bytes < depth_ws(B, G)) return GSB_ERR_WORKSPACE;
   cudaStream_t st = as_stream(stream);
   const uint32_t n = uint32_t(size_t(B) * G);
-  const int kb = B > 1 ? 8 : 4;
-  Carver c(workspace, workspace_bytes);
+  Carver c(workspace, workspace_bytes);  // the layout of depth_ws
   c.take<WorkspaceHeader>(1);
-  void* keys = c.take<char>(size_t(n) * kb);
+  uint32_t* keys = c.take<uint32_t>(n);
   uint32_t* vals = c.take<uint32_t>(n);
-  void* skeys = c.take<char>(size_t(n) * kb);
+  uint32_t* skeys = c.take<uint32_t>(n);
   uint32_t* svals = c.take<uint32_t>(n);
-  const size_t sws = radix_sort_workspace(n, kb, 1);
+  const size_t sws = segmented_sort_workspace(uint32_t(B), uint32_t(G));
   void* sort_ws = c.take<char>(sws);
   int32_t* status = begin_status(workspace, st);
-  if ((s = launch_order_keys_2d(*splats, kb == 8 ? static_cast<uint64_t*>(keys) : nullptr,
-                                kb == 4 ? static_cast<uint32_t*>(keys) : nullptr, vals, st)) != GSB_OK)
-    return s;
+  uint32_t* hist = nullptr;
+  if ((s = segmented_sort_prepare(sort_ws, sws, uint32_t(B), uint32_t(G), st, &hist)) != GSB_OK) return s;
+  if ((s = launch_order_keys_2d(*splats, keys, vals, hist, st)) != GSB_OK) return s;
   if (splats->depths) {
-    const int bit_hi = 32 + (B > 1 ? bits_for(uint64_t(B)) : 0);
-    if ((s = radix_sort(keys, skeys, vals, svals, n, kb, 0, bit_hi, sort_ws, sws, st, status)) != GSB_OK) return s;
+    if ((s = segmented_sort_run(keys, skeys, vals, svals, uint32_t(B), uint32_t(G), sort_ws, sws, st, status)) !=
+        GSB_OK)
+      return s;
   } else {
     svals = vals;  // no depths: index order, the keys are already sorted
   }

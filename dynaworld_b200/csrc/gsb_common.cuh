@@ -51,6 +51,27 @@ __device__ __host__ inline uint32_t float_sort_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Warp-aggregated counts of the four 8-bit digits of each lane's key into a block's histograms
+// (the segmented sort's counts, taken by the kernel that writes the keys).  Every lane of the warp
+// calls it; lanes with valid = false count nothing.
+__device__ inline void count_digits4(uint32_t (*s_hist)[256], uint32_t key, bool valid) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t digit = valid ? (key >> (8 * p)) & 0xffu : 0xffffffffu;
+    const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+    if (valid && lane == __ffs(peers) - 1) atomicAdd(&s_hist[p][digit], uint32_t(__popc(peers)));
+  }
+}
+
+// Adds a block's four digit histograms to the segment's [4][256] counts in global memory.
+__device__ inline void flush_digits4(const uint32_t (*s_hist)[256], uint32_t* __restrict__ hist) {
+  for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) {
+    const uint32_t c = s_hist[i / 256][i % 256];
+    if (c) atomicAdd(hist + i, c);
+  }
+}
+
 // log2(fl32(1 + 1e-6)) = log2(1 + 2^-20): the per-Gaussian transmittance growth of dense.py:225.
 constexpr double kLog2F0 = 1.3757959012e-06;
 

@@ -21,6 +21,16 @@ gsb_status radix_sort(const void* keys_in, void* keys_out, const uint32_t* vals_
                       int key_bytes, int bit_lo, int bit_hi, void* ws, size_t ws_bytes, cudaStream_t stream,
                       int32_t* status, const uint32_t* n_dev = nullptr);
 
+// Segmented sort of 32-bit keys with values (sort.cu): n_seg independent runs of seg_len keys.
+// segmented_sort_prepare clears the workspace's counters and returns the digit histograms
+// [n_seg][4][256] that the kernel writing the keys must fill before segmented_sort_run.
+size_t segmented_sort_workspace(uint32_t n_seg, uint32_t seg_len);
+gsb_status segmented_sort_prepare(void* ws, size_t ws_bytes, uint32_t n_seg, uint32_t seg_len, cudaStream_t stream,
+                                  uint32_t** hist);
+gsb_status segmented_sort_run(const uint32_t* keys_in, uint32_t* keys_out, const uint32_t* vals_in, uint32_t* vals_out,
+                              uint32_t n_seg, uint32_t seg_len, void* ws, size_t ws_bytes, cudaStream_t stream,
+                              int32_t* status);
+
 // Exclusive scan: offsets[0..n) and offsets[n] = total (sort.cu).
 size_t exclusive_scan_workspace(uint32_t n);
 gsb_status exclusive_scan(const uint32_t* counts, uint32_t n, uint32_t* offsets, void* scratch, size_t scratch_bytes,
@@ -70,8 +80,9 @@ gsb_status launch_raster_bwd(const RasterArgs& a, cudaStream_t st);
 int raster_segments(const gsb_views& v, const gsb_options& o);  // backward list segments (1, 2, 4)
 
 // Preprocess (preprocess.cu).
-gsb_status launch_depth_keys(const gsb_scene& sc, const gsb_views& vw, uint64_t* keys64, uint32_t* keys32,
-                             uint32_t* vals, cudaStream_t st);
+// Depth keys [B*G] and Gaussian indices per view, digit histograms [B][4][256] accumulated.
+gsb_status launch_depth_keys(const gsb_scene& sc, const gsb_views& vw, uint32_t* keys, uint32_t* vals, uint32_t* hist,
+                             cudaStream_t st);
 gsb_status launch_invert_order(const uint32_t* sorted_vals, int32_t B, int32_t G, int32_t* sorted_ids,
                                int32_t* rank_of, cudaStream_t st);
 gsb_status launch_preprocess_fwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
@@ -84,7 +95,7 @@ gsb_status launch_camera_bwd(const gsb_scene& sc, const gsb_views& vw, const Ren
                              const float* grad2d, const gsb_camera_grads& out, cudaStream_t st);
 
 // Already-projected 2-D Gaussians (splat2d.cu).
-gsb_status launch_order_keys_2d(const gsb_splats2d& sp, uint64_t* keys64, uint32_t* keys32, uint32_t* vals,
+gsb_status launch_order_keys_2d(const gsb_splats2d& sp, uint32_t* keys, uint32_t* vals, uint32_t* hist,
                                 cudaStream_t st);
 gsb_status launch_preprocess_2d(const gsb_splats2d& sp, int H, int W, const RenderConsts& rc, const int32_t* rank_of,
                                 float* records, int4* rects, uint32_t* counts, cudaStream_t st);

@@ -364,31 +364,53 @@ __device__ inline void load_color(const gsb_scene& sc, size_t pg, const float d[
 
 // ---- stage 1 kernels: depth keys and inverse permutation -------------------------------------
 
+constexpr int kKeyThreads = 256;
+constexpr int kKeyItems = 8;  // Gaussians per thread
+
+// Depth sort keys of view blockIdx.y (the order-preserving bits of the camera z, common.py:190-195)
+// with the Gaussian index as value, plus the view's four 8-bit digit histograms for the
+// segmented radix sort (warp-aggregated shared-memory counts, one global add per non-zero bin).
 // BANK: the scene has a dynamic bank (compiled out of the other instances).
 template <bool BANK>
-__global__ void depth_key_kernel(gsb_scene sc, gsb_views vw, uint64_t* __restrict__ keys64,
-                                 uint32_t* __restrict__ keys32, uint32_t* __restrict__ vals) {
+__global__ void __launch_bounds__(kKeyThreads) depth_key_kernel(gsb_scene sc, gsb_views vw,
+                                                                uint32_t* __restrict__ keys,
+                                                                uint32_t* __restrict__ vals,
+                                                                uint32_t* __restrict__ hist) {
+  __shared__ uint32_t s_hist[4][256];
+  for (int i = threadIdx.x; i < 4 * 256; i += kKeyThreads) s_hist[i / 256][i % 256] = 0u;
+  __syncthreads();
+  const int b = blockIdx.y;
   const size_t G = sc.n_gaussians;
-  const size_t total = size_t(vw.n_views) * G;
-  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
-    const int b = int(i / G);
-    const size_t g = i - size_t(b) * G;
-    const size_t pg = size_t(b / vw.views_per_set) * G + g;
-    const float t = vw.times ? vw.times[b] : 0.0f;
-    const float* c2w = vw.camera_to_world + b * 16;
-    float m[3], d[3], R[9];
-    mean_at(sc, pg, t, BANK ? view_basis(sc, vw, b) : nullptr, m);
+  const size_t set0 = size_t(b / vw.views_per_set) * G;
+  const float t = vw.times ? vw.times[b] : 0.0f;
+  const float* phi = BANK ? view_basis(sc, vw, b) : nullptr;
+  const float* c2w = vw.camera_to_world + b * 16;
+  float R[9], centre[3];
 #pragma unroll
-    for (int k = 0; k < 3; ++k) {
-      d[k] = __fsub_rn(m[k], c2w[k * 4 + 3]);
+  for (int k = 0; k < 3; ++k) {
+    centre[k] = c2w[k * 4 + 3];
 #pragma unroll
-      for (int j = 0; j < 3; ++j) R[k * 3 + j] = c2w[k * 4 + j];
-    }
-    const uint32_t key = float_sort_key(cam_coord(d, R, 2));
-    if (keys64) keys64[i] = (uint64_t(b) << 32) | key;
-    else keys32[i] = key;
-    vals[i] = uint32_t(g);
+    for (int j = 0; j < 3; ++j) R[k * 3 + j] = c2w[k * 4 + j];
   }
+  const size_t g0 = size_t(blockIdx.x) * kKeyThreads * kKeyItems + threadIdx.x;
+#pragma unroll 2
+  for (int it = 0; it < kKeyItems; ++it) {
+    const size_t g = g0 + size_t(it) * kKeyThreads;
+    const bool valid = g < G;
+    uint32_t key = 0u;
+    if (valid) {
+      float m[3], d[3];
+      mean_at(sc, set0 + g, t, phi, m);
+#pragma unroll
+      for (int k = 0; k < 3; ++k) d[k] = __fsub_rn(m[k], centre[k]);
+      key = float_sort_key(cam_coord(d, R, 2));
+      keys[size_t(b) * G + g] = key;
+      vals[size_t(b) * G + g] = uint32_t(g);
+    }
+    count_digits4(s_hist, key, valid);
+  }
+  __syncthreads();
+  flush_digits4(s_hist, hist + size_t(b) * 4 * 256);
 }
 
 __global__ void invert_order_kernel(const uint32_t* __restrict__ sorted_vals, int32_t n_views, int32_t G,
@@ -909,12 +931,13 @@ static int grid_for(size_t n, int threads) {
   return int(std::min<size_t>(blocks, size_t(148) * 64));
 }
 
-gsb_status launch_depth_keys(const gsb_scene& sc, const gsb_views& vw, uint64_t* keys64, uint32_t* keys32,
-                             uint32_t* vals, cudaStream_t st) {
-  const size_t n = size_t(vw.n_views) * sc.n_gaussians;
+gsb_status launch_depth_keys(const gsb_scene& sc, const gsb_views& vw, uint32_t* keys, uint32_t* vals, uint32_t* hist,
+                             cudaStream_t st) {
+  const dim3 grid(unsigned((size_t(sc.n_gaussians) + kKeyThreads * kKeyItems - 1) / (kKeyThreads * kKeyItems)),
+                  unsigned(vw.n_views));
   note_launch();
-  if (sc.flags & GSB_SCENE_BANK) depth_key_kernel<true><<<grid_for(n, 256), 256, 0, st>>>(sc, vw, keys64, keys32, vals);
-  else depth_key_kernel<false><<<grid_for(n, 256), 256, 0, st>>>(sc, vw, keys64, keys32, vals);
+  if (sc.flags & GSB_SCENE_BANK) depth_key_kernel<true><<<grid, kKeyThreads, 0, st>>>(sc, vw, keys, vals, hist);
+  else depth_key_kernel<false><<<grid, kKeyThreads, 0, st>>>(sc, vw, keys, vals, hist);
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 

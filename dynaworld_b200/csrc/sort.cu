@@ -97,14 +97,17 @@ __device__ __forceinline__ uint32_t block_excl_scan_256(uint32_t v, uint32_t* s_
   return warp_base + x - v;
 }
 
-template <typename K, bool kVals>
+// kSeg: the keys form segments of seg_len that are sorted independently (partitions never straddle
+// a segment: parts_per_seg per segment; digit histograms per segment, hist_stride apart); else one
+// sequence of n keys (or of *n_dev, when given).
+template <typename K, bool kVals, bool kSeg>
 __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
     const K* __restrict__ keys_in, K* __restrict__ keys_out, const uint32_t* __restrict__ vals_in,
     uint32_t* __restrict__ vals_out, uint32_t n, int shift, int nbits, const uint32_t* __restrict__ hist,
     uint32_t* __restrict__ lookback, uint32_t* __restrict__ part_counter, int32_t* __restrict__ status,
-    const uint32_t* __restrict__ n_dev) {
+    const uint32_t* __restrict__ n_dev, uint32_t seg_len, uint32_t parts_per_seg, uint32_t hist_stride) {
   constexpr int kItems = SortTraits<K>::kItems;
-  if (n_dev) n = min(n, *n_dev);  // partitions past the count find no valid key and write nothing
+  if (!kSeg && n_dev) n = min(n, *n_dev);  // partitions past the count find no valid key and write nothing
   constexpr uint32_t kPart = kSortThreads * kItems;
   __shared__ uint32_t s_part;
   __shared__ uint32_t s_warp_hist[kSortWarps][256];
@@ -120,10 +123,25 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
   __syncthreads();
   const uint32_t part = s_part;
   const uint32_t mask = (1u << nbits) - 1u;
+  // this partition's keys [lo, hi) in the segment [seg_lo, seg_hi); first_part opens the segment
+  uint32_t lo, hi, seg_lo, seg_hi, first_part;
+  if (kSeg) {
+    const uint32_t seg = part / parts_per_seg, lp = part - seg * parts_per_seg;
+    seg_lo = seg * seg_len;
+    seg_hi = seg_lo + seg_len;
+    lo = seg_lo + lp * kPart;
+    hi = min(lo + kPart, seg_hi);
+    first_part = part - lp;
+    hist += size_t(seg) * hist_stride;
+  } else {
+    seg_lo = 0u, seg_hi = n, first_part = 0u;
+    lo = part * kPart;
+    hi = lo < n ? min(lo + kPart, n) : lo;
+  }
 
-  // Warp-striped load: warp w owns keys [part*kPart + w*32*kItems, +32*kItems), item j of lane l
-  // is key base + 32*j + l, so (j, lane) order is input order: the ranking below is stable.
-  const uint32_t base = part * kPart + warp * 32 * kItems + lane;
+  // Warp-striped load: warp w owns keys [lo + w*32*kItems, +32*kItems), item j of lane l is key
+  // base + 32*j + l, so (j, lane) order is input order: the ranking below is stable.
+  const uint32_t base = lo + warp * 32 * kItems + lane;
   K k[kItems];
   uint32_t v[kItems];
   uint32_t rank[kItems];
@@ -131,7 +149,7 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
 #pragma unroll
   for (int j = 0; j < kItems; ++j) {
     const uint32_t idx = base + 32 * j;
-    const bool valid = idx < n;
+    const bool valid = idx < hi;
     k[j] = valid ? keys_in[idx] : K(0);
     if (kVals) v[j] = valid ? vals_in[idx] : 0u;
     dig[j] = valid ? uint32_t((k[j] >> shift) & K(mask)) : 0xffffffffu;
@@ -160,13 +178,13 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
   }
   // Publish this partition's digit count, then look back for the exclusive prefix.
   uint32_t* my = lookback + size_t(part) * 256 + tid;
-  if (part == 0) {
+  if (part == first_part) {
     st_release_u32(my, kFlagIncl | total);
   } else {
     st_release_u32(my, kFlagAgg | total);
   }
   uint32_t excl = 0;
-  if (part > 0) {
+  if (part > first_part) {  // partitions of this segment only: first_part's word is inclusive
     int64_t p = int64_t(part) - 1;
     int spins = 0;
     while (p >= 0) {
@@ -188,7 +206,7 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
   // Digit runs of this partition: local start of each digit, global start of its run.
   s_local[tid] = block_excl_scan_256(total, s_tmp, nullptr);
   const uint32_t digit_start = block_excl_scan_256(hist[tid], s_tmp, nullptr);
-  s_base[tid] = digit_start + excl;
+  s_base[tid] = seg_lo + digit_start + excl;
   __syncthreads();
   // Stage the partition in (digit, input) order, then write each digit's run contiguously.
 #pragma unroll
@@ -200,12 +218,12 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
     if (kVals) s_vals[lpos] = v[j];
   }
   __syncthreads();
-  const uint32_t n_valid = part * kPart < n ? min(kPart, n - part * kPart) : 0u;
+  const uint32_t n_valid = hi - lo;
   for (uint32_t i = tid; i < n_valid; i += kSortThreads) {
     const K key = s_keys[i];
     const uint32_t d = uint32_t((key >> shift) & K(mask));
     const uint32_t pos = s_base[d] + (i - s_local[d]);
-    if (pos >= n) {  // only after a timed-out look-back: never write outside the output
+    if (pos >= seg_hi) {  // only after a timed-out look-back: never write outside the segment
       record_error(status, GSB_ERR_TIMEOUT, int(part));
       continue;
     }
@@ -273,14 +291,14 @@ static gsb_status radix_sort_t(const K* keys_in, K* keys_out, const uint32_t* va
     const int nbits = std::min(8, bit_hi - shift);
     if (with_vals) {
       note_launch();
-      onesweep_kernel<K, true><<<parts, kSortThreads, 0, stream>>>(src_k, dst_k, src_v, dst_v, n, shift, nbits,
-                                                                    hist + 256 * p, lookback + size_t(p) * parts * 256,
-                                                                    counters + p, status, n_dev);
+      onesweep_kernel<K, true, false><<<parts, kSortThreads, 0, stream>>>(
+          src_k, dst_k, src_v, dst_v, n, shift, nbits, hist + 256 * p, lookback + size_t(p) * parts * 256, counters + p,
+          status, n_dev, 0u, 0u, 0u);
     } else {
       note_launch();
-      onesweep_kernel<K, false><<<parts, kSortThreads, 0, stream>>>(src_k, dst_k, nullptr, nullptr, n, shift, nbits,
-                                                                     hist + 256 * p, lookback + size_t(p) * parts * 256,
-                                                                     counters + p, status, n_dev);
+      onesweep_kernel<K, false, false><<<parts, kSortThreads, 0, stream>>>(
+          src_k, dst_k, nullptr, nullptr, n, shift, nbits, hist + 256 * p, lookback + size_t(p) * parts * 256,
+          counters + p, status, n_dev, 0u, 0u, 0u);
     }
     src_k = dst_k;
     src_v = dst_v;
@@ -301,6 +319,85 @@ gsb_status radix_sort(const void* keys_in, void* keys_out, const uint32_t* vals_
     return radix_sort_t<uint64_t>(static_cast<const uint64_t*>(keys_in), static_cast<uint64_t*>(keys_out), vals_in,
                                   vals_out, n, bit_lo, bit_hi, ws, ws_bytes, stream, status, n_dev);
   return GSB_ERR_ARG;
+}
+
+// ---- segmented sort: independent runs of 32-bit keys (the per-view depth order) --------------
+//
+// n_seg segments of seg_len keys, each sorted on its own (stable, ascending, all 32 bits: four
+// passes).  Partitions never straddle a segment and look back only within theirs; the digit
+// histograms are per segment and are accumulated by the kernel that writes the keys (it gets
+// their address from segmented_sort_prepare), so no pass re-reads the keys to count them.
+
+constexpr int kSegPasses = 4;
+
+static uint32_t seg_parts(uint32_t seg_len) {
+  const uint32_t part = kSortThreads * SortTraits<uint32_t>::kItems;
+  return (seg_len + part - 1) / part;
+}
+
+size_t segmented_sort_workspace(uint32_t n_seg, uint32_t seg_len) {
+  const size_t parts = size_t(n_seg) * seg_parts(seg_len);
+  Carver c(nullptr, 0);
+  c.take<WorkspaceHeader>(1);
+  c.take<uint32_t>(size_t(n_seg) * kSegPasses * 256);   // histograms [seg][pass][digit]
+  c.take<uint32_t>(kSegPasses);                          // partition counters
+  c.take<uint32_t>(size_t(kSegPasses) * parts * 256);   // look-back
+  c.take<uint32_t>(size_t(n_seg) * seg_len);            // ping-pong keys
+  c.take<uint32_t>(size_t(n_seg) * seg_len);            // ping-pong values
+  return c.used;
+}
+
+struct SegWorkspace {
+  uint32_t *hist, *counters, *lookback, *alt_keys, *alt_vals;
+  size_t clear_bytes;
+};
+
+static bool seg_carve(void* ws, size_t ws_bytes, uint32_t n_seg, uint32_t seg_len, SegWorkspace& w) {
+  const size_t parts = size_t(n_seg) * seg_parts(seg_len);
+  Carver c(ws, ws_bytes);
+  c.take<WorkspaceHeader>(1);
+  w.hist = c.take<uint32_t>(size_t(n_seg) * kSegPasses * 256);
+  w.counters = c.take<uint32_t>(kSegPasses);
+  w.lookback = c.take<uint32_t>(size_t(kSegPasses) * parts * 256);
+  w.alt_keys = c.take<uint32_t>(size_t(n_seg) * seg_len);
+  w.alt_vals = c.take<uint32_t>(size_t(n_seg) * seg_len);
+  w.clear_bytes = reinterpret_cast<char*>(w.lookback + size_t(kSegPasses) * parts * 256) -
+                  reinterpret_cast<char*>(w.hist);  // hist, counters, look-back are contiguous
+  return c.ok() && ws != nullptr;
+}
+
+gsb_status segmented_sort_prepare(void* ws, size_t ws_bytes, uint32_t n_seg, uint32_t seg_len, cudaStream_t stream,
+                                  uint32_t** hist) {
+  SegWorkspace w;
+  if (!seg_carve(ws, ws_bytes, n_seg, seg_len, w)) return GSB_ERR_WORKSPACE;
+  if (cudaMemsetAsync(w.hist, 0, w.clear_bytes, stream)) return GSB_ERR_CUDA;
+  *hist = w.hist;
+  return GSB_OK;
+}
+
+gsb_status segmented_sort_run(const uint32_t* keys_in, uint32_t* keys_out, const uint32_t* vals_in, uint32_t* vals_out,
+                              uint32_t n_seg, uint32_t seg_len, void* ws, size_t ws_bytes, cudaStream_t stream,
+                              int32_t* status) {
+  if (size_t(n_seg) * seg_len >= (size_t(1) << 30)) return GSB_ERR_KEY_OVERFLOW;
+  if (n_seg == 0 || seg_len == 0) return GSB_OK;
+  SegWorkspace w;
+  if (!seg_carve(ws, ws_bytes, n_seg, seg_len, w)) return GSB_ERR_WORKSPACE;
+  const uint32_t pps = seg_parts(seg_len);
+  const uint32_t parts = n_seg * pps;
+  const uint32_t* src_k = keys_in;
+  const uint32_t* src_v = vals_in;
+  for (int p = 0; p < kSegPasses; ++p) {
+    const bool to_out = ((kSegPasses - 1 - p) % 2) == 0;
+    uint32_t* dst_k = to_out ? keys_out : w.alt_keys;
+    uint32_t* dst_v = to_out ? vals_out : w.alt_vals;
+    note_launch();
+    onesweep_kernel<uint32_t, true, true><<<parts, kSortThreads, 0, stream>>>(
+        src_k, dst_k, src_v, dst_v, n_seg * seg_len, 8 * p, 8, w.hist + 256 * p, w.lookback + size_t(p) * parts * 256,
+        w.counters + p, status, nullptr, seg_len, pps, uint32_t(kSegPasses * 256));
+    src_k = dst_k;
+    src_v = dst_v;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 
 // ---- exclusive prefix scan of uint32 counts (three phases, no inter-block waits) -------------

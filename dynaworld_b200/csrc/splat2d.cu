@@ -46,15 +46,34 @@ __device__ inline Conic2D load_conic(const gsb_splats2d& sp, size_t i) {
   return g;
 }
 
-__global__ void order_keys_2d_kernel(const float* __restrict__ depths, size_t n, int32_t G, uint64_t* keys64,
-                                     uint32_t* keys32, uint32_t* __restrict__ vals) {
-  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
-    const uint32_t b = uint32_t(i / G);
-    const uint32_t key = depths ? float_sort_key(depths[i]) : 0u;  // NULL depths: stable sort keeps index order
-    if (keys64) keys64[i] = (uint64_t(b) << 32) | key;
-    else keys32[i] = key;
-    vals[i] = uint32_t(i - size_t(b) * G);
+constexpr int kOrderThreads = 256;
+constexpr int kOrderItems = 8;  // Gaussians per thread
+
+// Depth keys of view blockIdx.y (NULL depths: index order, keys 0) with the index as value, and the
+// view's digit histograms for the segmented sort.
+__global__ void __launch_bounds__(kOrderThreads) order_keys_2d_kernel(const float* __restrict__ depths, int32_t G,
+                                                                      uint32_t* __restrict__ keys,
+                                                                      uint32_t* __restrict__ vals,
+                                                                      uint32_t* __restrict__ hist) {
+  __shared__ uint32_t s_hist[4][256];
+  for (int i = threadIdx.x; i < 4 * 256; i += kOrderThreads) s_hist[i / 256][i % 256] = 0u;
+  __syncthreads();
+  const size_t b = blockIdx.y;
+  const size_t g0 = size_t(blockIdx.x) * kOrderThreads * kOrderItems + threadIdx.x;
+  for (int it = 0; it < kOrderItems; ++it) {
+    const size_t g = g0 + size_t(it) * kOrderThreads;
+    const bool valid = g < size_t(G);
+    uint32_t key = 0u;
+    if (valid) {
+      const size_t i = b * size_t(G) + g;
+      key = depths ? float_sort_key(depths[i]) : 0u;
+      keys[i] = key;
+      vals[i] = uint32_t(g);
+    }
+    count_digits4(s_hist, key, valid);
   }
+  __syncthreads();
+  flush_digits4(s_hist, hist + b * 4 * 256);
 }
 
 __global__ void __launch_bounds__(256) preprocess_2d_kernel(gsb_splats2d sp, int H, int W, RenderConsts rc,
@@ -143,11 +162,12 @@ int grid_for(size_t n) { return int(std::min<size_t>((n + 255) / 256, size_t(148
 
 }  // namespace
 
-gsb_status launch_order_keys_2d(const gsb_splats2d& sp, uint64_t* keys64, uint32_t* keys32, uint32_t* vals,
+gsb_status launch_order_keys_2d(const gsb_splats2d& sp, uint32_t* keys, uint32_t* vals, uint32_t* hist,
                                 cudaStream_t st) {
-  const size_t n = size_t(sp.n_views) * sp.n_gaussians;
+  const dim3 grid(unsigned((size_t(sp.n_gaussians) + kOrderThreads * kOrderItems - 1) / (kOrderThreads * kOrderItems)),
+                  unsigned(sp.n_views));
   note_launch();
-  order_keys_2d_kernel<<<grid_for(n), 256, 0, st>>>(sp.depths, n, sp.n_gaussians, keys64, keys32, vals);
+  order_keys_2d_kernel<<<grid, kOrderThreads, 0, st>>>(sp.depths, sp.n_gaussians, keys, vals, hist);
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 
