@@ -326,8 +326,10 @@ __device__ __forceinline__ float warp_sum10(float v[12], int lane, int* index) {
 }
 
 // Lanes contributing to one entry at or below this count add their own values atomically; above
-// it the warp reduces first.
-constexpr int kSparseContributors = 4;
+// it the warp reduces first.  Measured on one B200 (backward ms, 16 x 128^2 / 8 x 384^2): 2: 0.796 /
+// 1.570, 4: 0.792 / 1.554, 8: 0.786 / 1.543, 12: 0.783 / 1.537, 16: 0.789 / 1.553, 24: 1.10 / 2.12
+// (the atomics then contend).
+constexpr int kSparseContributors = 12;
 
 // DEPTH: a depth gradient is given.  NSEG: the tile's list is cut into NSEG segments
 // [s n / NSEG, (s + 1) n / NSEG), each walked by its own CTA (adjacent in launch order), starting
