@@ -232,12 +232,12 @@ GSB_API gsb_status gsb_preprocess_fwd(const gsb_scene* scene, const gsb_views* v
 
 // ---- stage 3 ---------------------------------------------------------------------------------
 
-static size_t bin_ws(uint32_t n_pairs, size_t n_tiles_total) {
+static size_t bin_ws(uint32_t n_pairs, uint32_t n_views, size_t n_tiles_total) {
   const uint32_t nt = uint32_t(n_tiles_total);
   Carver c(nullptr, 0);
   c.take<WorkspaceHeader>(1);
   c.take<uint64_t>(n_pairs);
-  c.take<char>(radix_sort_workspace(n_pairs, 8, 0));
+  c.take<char>(pair_sort_workspace(n_pairs, n_views, n_views ? nt / n_views : 0u));
   c.take<uint32_t>(nt);  // order keys
   c.take<uint32_t>(nt);  // order values
   c.take<uint32_t>(nt);  // sorted order keys
@@ -255,7 +255,7 @@ static size_t n_tiles_total(const gsb_views* views, const gsb_options* opts) {
 GSB_API size_t gsb_bin_workspace(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians,
                                  uint32_t n_pairs) {
   (void)n_gaussians;
-  return bin_ws(n_pairs, n_tiles_total(views, opts));
+  return bin_ws(n_pairs, views ? uint32_t(views->n_views) : 0u, n_tiles_total(views, opts));
 }
 
 GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int32_t n_gaussians, const float* records,
@@ -271,14 +271,14 @@ GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int3
   if (n_pairs >= (1u << 30)) return GSB_ERR_KEY_OVERFLOW;
   const size_t NT = n_tiles_total(views, opts);
   if (NT >= (size_t(1) << 30)) return GSB_ERR_SHAPE;
-  if (workspace_bytes < bin_ws(n_pairs, NT)) return GSB_ERR_WORKSPACE;
+  if (workspace_bytes < bin_ws(n_pairs, uint32_t(views->n_views), NT)) return GSB_ERR_WORKSPACE;
   cudaStream_t st = as_stream(stream);
   const RenderConsts rc = make_consts(*views, *opts);
   const int32_t B = views->n_views;
   Carver c(workspace, workspace_bytes);
   c.take<WorkspaceHeader>(1);
   uint64_t* keys = c.take<uint64_t>(n_pairs);
-  const size_t sws = radix_sort_workspace(n_pairs, 8, 0);
+  const size_t sws = pair_sort_workspace(n_pairs, uint32_t(B), uint32_t(rc.n_tiles));
   void* sort_ws = c.take<char>(sws);
   uint32_t* okeys = c.take<uint32_t>(NT);
   uint32_t* ovals = c.take<uint32_t>(NT);
@@ -289,13 +289,16 @@ GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int3
   // n_pairs is the capacity of the key buffers; the count itself is read on the device, so the
   // stage can be queued before the count reaches the host.
   const uint32_t* n_dev = pair_offsets + size_t(B) * size_t(n_gaussians);
-  if (n_pairs > 0) {
-    if ((s = launch_emit(B, n_gaussians, rc, views->height, views->width, records,
-                         reinterpret_cast<const int4*>(tile_rects), pair_offsets, n_pairs, keys, status, st)) != GSB_OK)
+  if (n_pairs > 0) {  // keys in (view, rank) order, then each view's run sorted by tile
+    uint32_t* hist = nullptr;
+    if ((s = pair_sort_prepare(sort_ws, sws, n_pairs, uint32_t(B), uint32_t(rc.n_tiles), st, &hist)) != GSB_OK)
       return s;
-    const int bits = bits_for(uint64_t(B) * uint64_t(rc.n_tiles));
-    if ((s = radix_sort(keys, sorted_keys, nullptr, nullptr, n_pairs, 8, 32, 32 + bits, sort_ws, sws, st, status,
-                        n_dev)) != GSB_OK)
+    if ((s = launch_emit(B, n_gaussians, rc, views->height, views->width, records,
+                         reinterpret_cast<const int4*>(tile_rects), pair_offsets, n_pairs, keys, hist,
+                         pair_sort_passes(uint32_t(rc.n_tiles)), status, st)) != GSB_OK)
+      return s;
+    if ((s = pair_sort_run(keys, sorted_keys, n_pairs, uint32_t(B), uint32_t(rc.n_tiles), n_gaussians, pair_offsets,
+                           sort_ws, sws, st, status)) != GSB_OK)
       return s;
   }
   if ((s = launch_tile_ranges(sorted_keys, n_pairs, n_dev, tile_ranges, size_t(B) * rc.n_tiles, status, st)) !=

@@ -12,21 +12,37 @@
 
 namespace gsb {
 
-__global__ void __launch_bounds__(256) emit_keys_kernel(int32_t n_views, int32_t G, RenderConsts rc, int H, int W,
+constexpr int kMaxTilePasses = 4;
+
+// One thread per (view blockIdx.y, depth rank): the Gaussian's keys in its slot of the pair array,
+// and the block's counts of the tile digits its written keys carry (the per-view histograms of
+// the pair sort's passes).
+__global__ void __launch_bounds__(256) emit_keys_kernel(int32_t G, RenderConsts rc, int H, int W,
                                                         const float* __restrict__ records,
                                                         const int4* __restrict__ rects,
                                                         const uint32_t* __restrict__ offsets, uint32_t n_pairs,
-                                                        uint64_t* __restrict__ keys, int32_t* __restrict__ status) {
-  const size_t total = size_t(n_views) * G;
-  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
-    const uint32_t start = offsets[i];
-    const uint32_t end = offsets[i + 1];
-    if (start == end) continue;
-    const uint32_t b = uint32_t(i / G);
-    const uint32_t r = uint32_t(i - size_t(b) * G);
+                                                        uint64_t* __restrict__ keys, uint32_t* __restrict__ hist,
+                                                        int passes, int32_t* __restrict__ status) {
+  __shared__ uint32_t s_hist[kMaxTilePasses][256];
+  for (int i = threadIdx.x; i < kMaxTilePasses * 256; i += blockDim.x) s_hist[i / 256][i % 256] = 0u;
+  __syncthreads();
+  const uint32_t b = blockIdx.y;
+  const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t i = size_t(b) * G + r;
+  const uint32_t start = r < uint32_t(G) ? offsets[i] : 0u;
+  const uint32_t end = r < uint32_t(G) ? offsets[i + 1] : 0u;
+  const uint64_t view_base = uint64_t(b) * rc.n_tiles;
+  uint32_t k = start;
+  auto put = [&](int tx, int ty) {
+    if (k < end && k < n_pairs) {
+      const uint32_t t = uint32_t(ty * rc.tiles_x + tx);
+      keys[k] = ((view_base + t) << 32) | r;
+      for (int p = 0; p < passes; ++p) atomicAdd(&s_hist[p][(t >> (8 * p)) & 0xffu], 1u);
+    }
+    ++k;
+  };
+  if (start != end) {
     const int4 rc4 = rects[i];
-    const uint64_t view_base = uint64_t(b) * rc.n_tiles;
-    uint32_t k = start;
     if (!rc.compat && rc.ellipse) {
       const float4 r0 = reinterpret_cast<const float4*>(records)[i * 3 + 0];
       const float4 r1 = reinterpret_cast<const float4*>(records)[i * 3 + 1];
@@ -35,20 +51,20 @@ __global__ void __launch_bounds__(256) emit_keys_kernel(int32_t n_views, int32_t
         for (int ty = rc4.y; ty <= rc4.w; ++ty) {
           int tx0, tx1;
           if (!exact_row(es, ty, rc.tile, rc.pixel_center, &tx0, &tx1)) continue;
-          for (int tx = tx0; tx <= tx1; ++tx) {
-            if (k < end && k < n_pairs) keys[k] = ((view_base + uint64_t(ty) * rc.tiles_x + tx) << 32) | r;
-            ++k;
-          }
+          for (int tx = tx0; tx <= tx1; ++tx) put(tx, ty);
         }
       }
     } else {
       for (int ty = rc4.y; ty <= rc4.w; ++ty)
-        for (int tx = rc4.x; tx <= rc4.z; ++tx) {
-          if (k < end && k < n_pairs) keys[k] = ((view_base + uint64_t(ty) * rc.tiles_x + tx) << 32) | r;
-          ++k;
-        }
+        for (int tx = rc4.x; tx <= rc4.z; ++tx) put(tx, ty);
     }
     if (k != end) record_error(status, GSB_ERR_KEY_OVERFLOW, int(i));
+  }
+  __syncthreads();
+  uint32_t* h = hist + size_t(b) * passes * 256;
+  for (int j = threadIdx.x; j < passes * 256; j += blockDim.x) {
+    const uint32_t c = s_hist[j / 256][j % 256];
+    if (c) atomicAdd(h + j, c);
   }
 }
 
@@ -97,12 +113,12 @@ gsb_status launch_tile_order_keys(const uint32_t* ranges, uint32_t n, uint32_t* 
 }
 
 gsb_status launch_emit(int32_t B, int32_t G, const RenderConsts& rc, int H, int W, const float* records,
-                       const int4* rects, const uint32_t* offsets, uint32_t n_pairs, uint64_t* keys, int32_t* status,
-                       cudaStream_t st) {
-  const size_t n = size_t(B) * G;
-  const int grid = int(std::min<size_t>((n + 255) / 256, size_t(148) * 32));
+                       const int4* rects, const uint32_t* offsets, uint32_t n_pairs, uint64_t* keys, uint32_t* hist,
+                       int passes, int32_t* status, cudaStream_t st) {
+  if (passes < 0 || passes > kMaxTilePasses) return GSB_ERR_SHAPE;
+  const dim3 grid(unsigned((size_t(G) + 255) / 256), unsigned(B));
   note_launch();
-  emit_keys_kernel<<<grid, 256, 0, st>>>(B, G, rc, H, W, records, rects, offsets, n_pairs, keys, status);
+  emit_keys_kernel<<<grid, 256, 0, st>>>(G, rc, H, W, records, rects, offsets, n_pairs, keys, hist, passes, status);
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 

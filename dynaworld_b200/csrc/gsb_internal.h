@@ -31,6 +31,18 @@ gsb_status segmented_sort_run(const uint32_t* keys_in, uint32_t* keys_out, const
                               uint32_t n_seg, uint32_t seg_len, void* ws, size_t ws_bytes, cudaStream_t stream,
                               int32_t* status);
 
+// Pair keys sorted by tile within each view's run (sort.cu): pair_sort_prepare clears the
+// workspace and returns the digit histograms [n_views][passes][256] of the tile index (passes =
+// ceil(log2(n_tiles) / 8)) that the kernel writing the keys fills; pair_sort_run reads the run
+// bounds from pair_offsets (view v starts at pair_offsets[v * G], clipped to cap).
+size_t pair_sort_workspace(uint32_t cap, uint32_t n_views, uint32_t n_tiles);
+int pair_sort_passes(uint32_t n_tiles);
+gsb_status pair_sort_prepare(void* ws, size_t ws_bytes, uint32_t cap, uint32_t n_views, uint32_t n_tiles,
+                             cudaStream_t stream, uint32_t** hist);
+gsb_status pair_sort_run(const uint64_t* keys_in, uint64_t* keys_out, uint32_t cap, uint32_t n_views, uint32_t n_tiles,
+                         int32_t G, const uint32_t* pair_offsets, void* ws, size_t ws_bytes, cudaStream_t stream,
+                         int32_t* status);
+
 // Exclusive scan: offsets[0..n) and offsets[n] = total (sort.cu).
 size_t exclusive_scan_workspace(uint32_t n);
 gsb_status exclusive_scan(const uint32_t* counts, uint32_t n, uint32_t* offsets, void* scratch, size_t scratch_bytes,
@@ -103,9 +115,10 @@ gsb_status launch_preprocess_2d_bwd(const gsb_splats2d& sp, const int32_t* rank_
                                     const gsb_splats2d_grads& gr, cudaStream_t st);
 
 // Binning (bin.cu).
+// Pair keys in (view, rank) order; hist [B][passes][256] gets the counts of their tile digits.
 gsb_status launch_emit(int32_t B, int32_t G, const RenderConsts& rc, int H, int W, const float* records,
-                       const int4* rects, const uint32_t* offsets, uint32_t n_pairs, uint64_t* keys, int32_t* status,
-                       cudaStream_t st);
+                       const int4* rects, const uint32_t* offsets, uint32_t n_pairs, uint64_t* keys, uint32_t* hist,
+                       int passes, int32_t* status, cudaStream_t st);
 // n: capacity of keys; the pair count is min(n, *n_dev) (n_dev may be NULL: n pairs).  A count
 // above the capacity records GSB_ERR_CAPACITY.
 gsb_status launch_tile_ranges(const uint64_t* keys, uint32_t n, const uint32_t* n_dev, uint32_t* ranges,

@@ -97,19 +97,30 @@ __device__ __forceinline__ uint32_t block_excl_scan_256(uint32_t v, uint32_t* s_
   return warp_base + x - v;
 }
 
-// kSeg: the keys form segments of seg_len that are sorted independently (partitions never straddle
-// a segment: parts_per_seg per segment; digit histograms per segment, hist_stride apart); else one
-// sequence of n keys (or of *n_dev, when given).
-template <typename K, bool kVals, bool kSeg>
+// How the keys split into independently sorted segments (kSegNone: one sequence).
+enum SegMode { kSegNone = 0, kSegFixed = 1, kSegRuns = 2 };
+struct Segments {
+  uint32_t hist_stride;        // histogram words per segment (digit histograms per segment)
+  uint32_t fixed_len;          // kSegFixed: segment length
+  uint32_t parts_per_seg;      // kSegFixed: partitions per segment
+  uint32_t n_seg;              // kSegRuns: segments
+  const uint32_t* start;       // kSegRuns: [n_seg + 1] first key of each segment (device)
+  const uint32_t* part_start;  // kSegRuns: [n_seg + 1] first partition of each segment (device)
+  uint32_t key_stride;         // kSegRuns: the digits are those of (key >> 32) - segment * key_stride
+};
+
+// One LSD pass.  Partitions never straddle a segment and look back only within theirs; with
+// segments the digit histograms are per segment.  kSegNone sorts n keys (or *n_dev, when given).
+template <typename K, bool kVals, int kSeg>
 __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
     const K* __restrict__ keys_in, K* __restrict__ keys_out, const uint32_t* __restrict__ vals_in,
     uint32_t* __restrict__ vals_out, uint32_t n, int shift, int nbits, const uint32_t* __restrict__ hist,
     uint32_t* __restrict__ lookback, uint32_t* __restrict__ part_counter, int32_t* __restrict__ status,
-    const uint32_t* __restrict__ n_dev, uint32_t seg_len, uint32_t parts_per_seg, uint32_t hist_stride) {
+    const uint32_t* __restrict__ n_dev, Segments sg) {
   constexpr int kItems = SortTraits<K>::kItems;
-  if (!kSeg && n_dev) n = min(n, *n_dev);  // partitions past the count find no valid key and write nothing
+  if (kSeg == kSegNone && n_dev) n = min(n, *n_dev);  // partitions past the count find no key, write nothing
   constexpr uint32_t kPart = kSortThreads * kItems;
-  __shared__ uint32_t s_part;
+  __shared__ uint32_t s_part, s_seg;
   __shared__ uint32_t s_warp_hist[kSortWarps][256];
   __shared__ uint32_t s_base[256];
   __shared__ uint32_t s_local[256];
@@ -118,21 +129,48 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
   __shared__ uint32_t s_vals[kVals ? kPart : 1];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) s_part = atomicAdd(part_counter, 1u);
+  if (tid == 0) {
+    const uint32_t p = atomicAdd(part_counter, 1u);
+    s_part = p;
+    if (kSeg == kSegRuns) {  // the segment whose partitions hold p (empty segments have none)
+      uint32_t a = 0, b = sg.n_seg;  // invariant: part_start[a] <= p < part_start[b] (or p is past all)
+      if (p >= sg.part_start[sg.n_seg]) a = sg.n_seg;
+      while (b - a > 1 && a < sg.n_seg) {
+        const uint32_t m = (a + b) / 2;
+        if (sg.part_start[m] <= p) a = m;
+        else b = m;
+      }
+      s_seg = a;
+    }
+  }
   for (int w = 0; w < kSortWarps; ++w) s_warp_hist[w][tid] = 0;
   __syncthreads();
   const uint32_t part = s_part;
+  if (kSeg == kSegRuns && s_seg >= sg.n_seg) return;  // a spare partition: the grid covers the worst case
   const uint32_t mask = (1u << nbits) - 1u;
+  const uint32_t seg = kSeg == kSegRuns ? s_seg : 0u;
+  const uint32_t key_base = kSeg == kSegRuns ? seg * sg.key_stride : 0u;
+  auto digit_of = [&](K key) -> uint32_t {
+    if (kSeg == kSegRuns) return ((uint32_t(uint64_t(key) >> 32) - key_base) >> shift) & mask;
+    return uint32_t((key >> shift) & K(mask));
+  };
   // this partition's keys [lo, hi) in the segment [seg_lo, seg_hi); first_part opens the segment
   uint32_t lo, hi, seg_lo, seg_hi, first_part;
-  if (kSeg) {
-    const uint32_t seg = part / parts_per_seg, lp = part - seg * parts_per_seg;
-    seg_lo = seg * seg_len;
-    seg_hi = seg_lo + seg_len;
+  if (kSeg == kSegFixed) {
+    const uint32_t sf = part / sg.parts_per_seg, lp = part - sf * sg.parts_per_seg;
+    seg_lo = sf * sg.fixed_len;
+    seg_hi = seg_lo + sg.fixed_len;
     lo = seg_lo + lp * kPart;
     hi = min(lo + kPart, seg_hi);
     first_part = part - lp;
-    hist += size_t(seg) * hist_stride;
+    hist += size_t(sf) * sg.hist_stride;
+  } else if (kSeg == kSegRuns) {
+    seg_lo = sg.start[seg];
+    seg_hi = max(sg.start[seg + 1], seg_lo);
+    first_part = sg.part_start[seg];
+    lo = seg_lo + (part - first_part) * kPart;
+    hi = lo < seg_hi ? min(lo + kPart, seg_hi) : lo;
+    hist += size_t(seg) * sg.hist_stride;
   } else {
     seg_lo = 0u, seg_hi = n, first_part = 0u;
     lo = part * kPart;
@@ -152,7 +190,7 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
     const bool valid = idx < hi;
     k[j] = valid ? keys_in[idx] : K(0);
     if (kVals) v[j] = valid ? vals_in[idx] : 0u;
-    dig[j] = valid ? uint32_t((k[j] >> shift) & K(mask)) : 0xffffffffu;
+    dig[j] = valid ? digit_of(k[j]) : 0xffffffffu;
   }
 #pragma unroll
   for (int j = 0; j < kItems; ++j) {
@@ -221,7 +259,7 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
   const uint32_t n_valid = hi - lo;
   for (uint32_t i = tid; i < n_valid; i += kSortThreads) {
     const K key = s_keys[i];
-    const uint32_t d = uint32_t((key >> shift) & K(mask));
+    const uint32_t d = digit_of(key);
     const uint32_t pos = s_base[d] + (i - s_local[d]);
     if (pos >= seg_hi) {  // only after a timed-out look-back: never write outside the segment
       record_error(status, GSB_ERR_TIMEOUT, int(part));
@@ -291,14 +329,14 @@ static gsb_status radix_sort_t(const K* keys_in, K* keys_out, const uint32_t* va
     const int nbits = std::min(8, bit_hi - shift);
     if (with_vals) {
       note_launch();
-      onesweep_kernel<K, true, false><<<parts, kSortThreads, 0, stream>>>(
+      onesweep_kernel<K, true, kSegNone><<<parts, kSortThreads, 0, stream>>>(
           src_k, dst_k, src_v, dst_v, n, shift, nbits, hist + 256 * p, lookback + size_t(p) * parts * 256, counters + p,
-          status, n_dev, 0u, 0u, 0u);
+          status, n_dev, Segments{});
     } else {
       note_launch();
-      onesweep_kernel<K, false, false><<<parts, kSortThreads, 0, stream>>>(
+      onesweep_kernel<K, false, kSegNone><<<parts, kSortThreads, 0, stream>>>(
           src_k, dst_k, nullptr, nullptr, n, shift, nbits, hist + 256 * p, lookback + size_t(p) * parts * 256,
-          counters + p, status, n_dev, 0u, 0u, 0u);
+          counters + p, status, n_dev, Segments{});
     }
     src_k = dst_k;
     src_v = dst_v;
@@ -391,11 +429,129 @@ gsb_status segmented_sort_run(const uint32_t* keys_in, uint32_t* keys_out, const
     uint32_t* dst_k = to_out ? keys_out : w.alt_keys;
     uint32_t* dst_v = to_out ? vals_out : w.alt_vals;
     note_launch();
-    onesweep_kernel<uint32_t, true, true><<<parts, kSortThreads, 0, stream>>>(
+    Segments sg{};
+    sg.hist_stride = uint32_t(kSegPasses * 256), sg.fixed_len = seg_len, sg.parts_per_seg = pps;
+    onesweep_kernel<uint32_t, true, kSegFixed><<<parts, kSortThreads, 0, stream>>>(
         src_k, dst_k, src_v, dst_v, n_seg * seg_len, 8 * p, 8, w.hist + 256 * p, w.lookback + size_t(p) * parts * 256,
-        w.counters + p, status, nullptr, seg_len, pps, uint32_t(kSegPasses * 256));
+        w.counters + p, status, nullptr, sg);
     src_k = dst_k;
     src_v = dst_v;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}
+
+// ---- pair keys: runs of one view each, sorted by tile ------------------------------------------
+//
+// The pair keys ((view * n_tiles + tile) << 32 | depth rank) arrive in (view, rank) order, so each
+// view's pairs are a contiguous run, starting at pair_offsets[view * G].  Sorting every run by its
+// tile index alone (stable) gives the (view, tile, rank) order with ceil(log2(n_tiles) / 8) passes
+// instead of the passes of log2(B * n_tiles) bits.  The run bounds come from the device offsets
+// (clipped to the keys' capacity), so the grid is sized for the worst case and spare partitions
+// return at once.
+
+constexpr uint32_t kPairPart = kSortThreads * SortTraits<uint64_t>::kItems;
+
+static int pair_passes(uint32_t n_tiles) { return (bits_for(n_tiles) + 7) / 8; }
+int pair_sort_passes(uint32_t n_tiles) { return pair_passes(n_tiles); }
+
+static uint32_t pair_parts_max(uint32_t cap, uint32_t n_views) {
+  return (cap + kPairPart - 1) / kPairPart + n_views;  // each run adds at most one partial partition
+}
+
+size_t pair_sort_workspace(uint32_t cap, uint32_t n_views, uint32_t n_tiles) {
+  const int passes = std::max(pair_passes(n_tiles), 1);
+  Carver c(nullptr, 0);
+  c.take<WorkspaceHeader>(1);
+  c.take<uint32_t>(size_t(n_views) * passes * 256);                             // histograms [view][pass][digit]
+  c.take<uint32_t>(passes);                                                      // partition counters
+  c.take<uint32_t>(size_t(passes) * pair_parts_max(cap, n_views) * 256);         // look-back
+  c.take<uint32_t>(size_t(n_views) + 1);                                         // run starts
+  c.take<uint32_t>(size_t(n_views) + 1);                                         // first partition of each run
+  c.take<uint64_t>(std::max<uint32_t>(cap, 1));                                  // ping-pong keys
+  return c.used;
+}
+
+struct PairWorkspace {
+  uint32_t *hist, *counters, *lookback, *start, *part_start;
+  uint64_t* alt;
+  size_t clear_bytes;
+};
+
+static bool pair_carve(void* ws, size_t ws_bytes, uint32_t cap, uint32_t n_views, uint32_t n_tiles, PairWorkspace& w) {
+  const int passes = std::max(pair_passes(n_tiles), 1);
+  Carver c(ws, ws_bytes);
+  c.take<WorkspaceHeader>(1);
+  w.hist = c.take<uint32_t>(size_t(n_views) * passes * 256);
+  w.counters = c.take<uint32_t>(passes);
+  w.lookback = c.take<uint32_t>(size_t(passes) * pair_parts_max(cap, n_views) * 256);
+  w.start = c.take<uint32_t>(size_t(n_views) + 1);
+  w.part_start = c.take<uint32_t>(size_t(n_views) + 1);
+  w.alt = c.take<uint64_t>(std::max<uint32_t>(cap, 1));
+  w.clear_bytes = reinterpret_cast<char*>(w.lookback + size_t(passes) * pair_parts_max(cap, n_views) * 256) -
+                  reinterpret_cast<char*>(w.hist);
+  return c.ok() && ws != nullptr;
+}
+
+// Run bounds start[v] = min(pair_offsets[v * G], cap) (v <= n_views) and the exclusive prefix of
+// the runs' partition counts; one block, runs in chunks of one per thread.
+__global__ void __launch_bounds__(kSortThreads) pair_runs_kernel(const uint32_t* __restrict__ offsets, uint32_t n_views,
+                                                                uint32_t G, uint32_t cap, uint32_t* __restrict__ start,
+                                                                uint32_t* __restrict__ part_start) {
+  __shared__ uint32_t s_tmp[kSortWarps];
+  uint32_t carry = 0;
+  for (uint32_t v0 = 0; v0 <= n_views; v0 += kSortThreads) {
+    const uint32_t v = v0 + threadIdx.x;
+    uint32_t parts = 0;
+    if (v <= n_views) {
+      const uint32_t a = min(offsets[size_t(v) * G], cap);
+      start[v] = a;
+      if (v < n_views) {
+        const uint32_t b = min(offsets[size_t(v + 1) * G], cap);
+        parts = b > a ? (b - a + kPairPart - 1) / kPairPart : 0u;
+      }
+    }
+    uint32_t total = 0;
+    const uint32_t ex = block_excl_scan_256(parts, s_tmp, &total);
+    if (v <= n_views) part_start[v] = carry + ex;
+    carry += total;
+  }
+}
+
+gsb_status pair_sort_prepare(void* ws, size_t ws_bytes, uint32_t cap, uint32_t n_views, uint32_t n_tiles,
+                             cudaStream_t stream, uint32_t** hist) {
+  PairWorkspace w;
+  if (!pair_carve(ws, ws_bytes, cap, n_views, n_tiles, w)) return GSB_ERR_WORKSPACE;
+  if (cudaMemsetAsync(w.hist, 0, w.clear_bytes, stream)) return GSB_ERR_CUDA;
+  *hist = w.hist;
+  return GSB_OK;
+}
+
+gsb_status pair_sort_run(const uint64_t* keys_in, uint64_t* keys_out, uint32_t cap, uint32_t n_views, uint32_t n_tiles,
+                         int32_t G, const uint32_t* pair_offsets, void* ws, size_t ws_bytes, cudaStream_t stream,
+                         int32_t* status) {
+  if (cap == 0) return GSB_OK;
+  PairWorkspace w;
+  if (!pair_carve(ws, ws_bytes, cap, n_views, n_tiles, w)) return GSB_ERR_WORKSPACE;
+  const int passes = pair_passes(n_tiles);
+  if (passes == 0) {  // one tile per view: the runs are in order already
+    return cudaMemcpyAsync(keys_out, keys_in, size_t(cap) * 8, cudaMemcpyDeviceToDevice, stream) ? GSB_ERR_CUDA
+                                                                                                    : GSB_OK;
+  }
+  note_launch();
+  pair_runs_kernel<<<1, kSortThreads, 0, stream>>>(pair_offsets, n_views, uint32_t(G), cap, w.start, w.part_start);
+  const uint32_t parts = pair_parts_max(cap, n_views);
+  Segments sg{};
+  sg.hist_stride = uint32_t(passes * 256), sg.n_seg = n_views, sg.start = w.start, sg.part_start = w.part_start;
+  sg.key_stride = n_tiles;
+  const uint64_t* src = keys_in;
+  for (int p = 0; p < passes; ++p) {
+    uint64_t* dst = ((passes - 1 - p) % 2) == 0 ? keys_out : w.alt;
+    const int nbits = std::min(8, bits_for(n_tiles) - 8 * p);
+    note_launch();
+    onesweep_kernel<uint64_t, false, kSegRuns><<<parts, kSortThreads, 0, stream>>>(
+        src, dst, nullptr, nullptr, cap, 8 * p, nbits, w.hist + 256 * p, w.lookback + size_t(p) * parts * 256,
+        w.counters + p, status, nullptr, sg);
+    src = dst;
   }
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
