@@ -1,11 +1,12 @@
-// Binning: one 64-bit key per (view, tile, Gaussian) pair, stable radix sort by (view, tile), and
-// the [start, end) run of every tile.
+// Binning: one 64-bit key per (view, tile, Gaussian) pair, a stable radix sort by tile within each
+// view, and the [start, end) run of every tile.
 //
 // Restates build_tile_assignments (src/train/renderers/tiled.py:31-71): the reference lists
 // (tile, Gaussian) pairs and stable-argsorts them by tile (:59), with Gaussians already in depth
 // order (renderers/common.py:191), so each tile's list is in depth order.  Here the pairs are
-// emitted in (view, depth rank) order with the rank in the key's low 32 bits, and only the
-// (view, tile) bits are sorted -- the stability of the LSD sort keeps depth order within a tile.
+// emitted in (view, depth rank) order with the rank in the key's low 32 bits, so every view's
+// pairs are one contiguous run, and each run is sorted by its tile index alone -- the stability
+// of the LSD sort keeps depth order within a tile.
 #include "gsb_common.cuh"
 #include "gsb_internal.h"
 #include "tiles.cuh"
