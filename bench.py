@@ -304,6 +304,25 @@ def ncu_traffic(kernel: str, workload: str):
     return (total if found == 2 else None), str(path.relative_to(ROOT))
 
 
+def ncu_issue(kernel: str, workload: str):
+    """Issue-slot and SM-busy fractions of `kernel` from the same committed ncu summary (the bound
+    the raster kernels actually meet), or None."""
+    path = ROOT / "profiles" / f"{kernel}_{workload}.md"
+    if not path.exists():
+        return None
+    out = {}
+    for line in path.read_text().splitlines():
+        for metric, key in (("smsp__issue_active.avg.pct_of_peak_sustained_active", "issue_active_pct"),
+                            ("sm__throughput.avg.pct_of_peak_sustained_elapsed", "sm_throughput_pct"),
+                            ("smsp__inst_executed.sum", "warp_instructions")):
+            if f"`{metric}`" in line:
+                out[key] = float(line.split("|")[2].split()[0])
+    if len(out) != 3:
+        return None
+    out["source"] = str(path.relative_to(ROOT))
+    return out
+
+
 def hbm_peak():
     try:
         p = json.loads(PEAKS.read_text())
@@ -479,8 +498,9 @@ def main():
                 "unit": "GB/s", "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_src,
                 "peak_source": peak_kind, "bytes_per_launch": int(alg_bytes), "pairs": int(n_pairs),
                 "pixels": int(px), "launch_ms": means[dominant],
+                "issue": ncu_issue(dominant, args.workload) if (args.tile is None and args.segments == 0) else None,
                 "note": "raster is issue-bound (records re-read from L2, DRAM traffic below the algorithmic "
-                        "bytes); see profiles/ for the ncu counters"}
+                        "bytes): 'issue' gives the ncu issue-slot use of the same kernel; see profiles/"}
     stage_share = {k: round(v / sum(means.values()), 4) for k, v in means.items()} if means else {}
 
     if rank == 0:
