@@ -25,7 +25,9 @@ __global__ void __launch_bounds__(256) emit_keys_kernel(int32_t G, RenderConsts 
                                                         uint64_t* __restrict__ keys, uint32_t* __restrict__ hist,
                                                         int passes, int32_t* __restrict__ status) {
   __shared__ uint32_t s_hist[kMaxTilePasses][256];
+  __shared__ uint32_t s_done;
   for (int i = threadIdx.x; i < kMaxTilePasses * 256; i += blockDim.x) s_hist[i / 256][i % 256] = 0u;
+  if (threadIdx.x == 0) s_done = 0u;
   __syncthreads();
   const uint32_t b = blockIdx.y;
   const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
@@ -61,10 +63,19 @@ __global__ void __launch_bounds__(256) emit_keys_kernel(int32_t G, RenderConsts 
     }
     if (k != end) record_error(status, GSB_ERR_KEY_OVERFLOW, int(i));
   }
-  __syncthreads();
+  // The last warp to finish adds the block's counts to the view's histograms: no block barrier, so
+  // warps done with short Gaussians do not wait for the block's longest one.
+  __syncwarp();
+  __threadfence_block();
+  const int lane = threadIdx.x & 31;
+  uint32_t done = 0u;
+  if (lane == 0) done = atomicAdd(&s_done, 1u);
+  done = __shfl_sync(0xffffffffu, done, 0);
+  if (done != blockDim.x / 32 - 1) return;
+  __threadfence_block();
   uint32_t* h = hist + size_t(b) * passes * 256;
-  for (int j = threadIdx.x; j < passes * 256; j += blockDim.x) {
-    const uint32_t c = s_hist[j / 256][j % 256];
+  for (int j = lane; j < passes * 256; j += 32) {
+    const uint32_t c = atomicAdd(&s_hist[j / 256][j % 256], 0u);  // read after the other warps' counts
     if (c) atomicAdd(h + j, c);
   }
 }
