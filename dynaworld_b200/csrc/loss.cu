@@ -21,7 +21,10 @@
 namespace gsb {
 
 constexpr int kLossTile = 32;
-constexpr int kLossThreads = 256;
+// 512 threads: the ~100 KB of shared memory per tile allows two CTAs per SM, so the CTA size sets
+// the warps in flight.  Measured on one B200 (ms, 16 x 128^2 / 8 x 384^2): 256 threads 0.068 /
+// 0.216, 512 0.062 / 0.192, 1024 0.064 / 0.201.
+constexpr int kLossThreads = 512;
 
 struct LossArgs {
   int B, C, H, W;
@@ -253,11 +256,25 @@ __global__ void loss_fixup_kernel(int B, int C, int H, int W, float c_l1, const 
   }
 }
 
+// out[b] = scale[b] * in[b]: image blockIdx.y, 16-byte accesses when the planes allow them.
 __global__ void scale_planes_kernel(const float* __restrict__ in, const float* __restrict__ scale,
-                                    float* __restrict__ out, int32_t B, int64_t per) {
-  const int64_t total = per * B;
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x)
-    out[i] = in[i] * scale[i / per];
+                                    float* __restrict__ out, int64_t per) {
+  const int64_t b = blockIdx.y;
+  const float s = scale[b];
+  const float* src = in + b * per;
+  float* dst = out + b * per;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  const int64_t first = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if ((per & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    for (int64_t i = first; i < per / 4; i += stride) {
+      const float4 v = s4[i];
+      d4[i] = make_float4(v.x * s, v.y * s, v.z * s, v.w * s);
+    }
+  } else {
+    for (int64_t i = first; i < per; i += stride) dst[i] = src[i] * s;
+  }
 }
 
 // ---- host ------------------------------------------------------------------------------------
@@ -344,9 +361,10 @@ gsb_status scale_planes(const float* in, const float* scale, float* out, int32_t
   if (!in || !scale || !out || B < 0 || per < 0) return GSB_ERR_ARG;
   const int64_t total = per * B;
   if (total == 0) return GSB_OK;
-  const int grid = int(std::min<int64_t>((total + 255) / 256, 148 * 16));
+  if (B > 65535) return GSB_ERR_SHAPE;
+  const dim3 grid(unsigned(std::min<int64_t>((per / 4 + 255) / 256 + 1, 64)), unsigned(B));
   note_launch();
-  scale_planes_kernel<<<grid, 256, 0, st>>>(in, scale, out, B, per);
+  scale_planes_kernel<<<grid, 256, 0, st>>>(in, scale, out, per);
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
 

@@ -262,7 +262,8 @@ GSB_API gsb_status gsb_loss_fwd_bwd_noalloc(const gsb_loss_options* lopts, int32
                                             int32_t channels, int32_t height, int32_t width,
                                             const float* pred, const float* target, float* loss,
                                             float* dpred, void* stream);
-/* out[b, ...] = scale[b] * in[b, ...] for n_images planes of plane_elems floats (in == out ok). */
+/* out[b, ...] = scale[b] * in[b, ...] for n_images (<= 65535, else GSB_ERR_SHAPE) planes of
+   plane_elems floats (in == out ok). */
 GSB_API gsb_status gsb_scale_planes(const float* in, const float* scale, float* out,
                                     int32_t n_images, int64_t plane_elems, void* stream);
 
