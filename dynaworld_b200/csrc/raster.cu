@@ -368,15 +368,17 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
   const size_t HW = size_t(a.H) * a.W;
   const size_t total_px = size_t(a.B) * HW;
   float fy[PX], S[PX], g0[PX], g1[PX], g2c[PX], gW[PX], gD[PX];
-  float R0[PX], R1[PX], R2[PX], RW[PX], RD[PX];
+  // d loss / d (weights of the entries after the current one), folded with the pixel's upstream
+  // gradients: rs = sum_c g_c R_c + gW RW + gD RD over the suffix sums R of colour, weight and depth.
+  // One entry adds w * dldw to it, so the suffix sums themselves are never kept.
+  float rs[PX];
   uint32_t n_proc[PX];  // entries of this segment the pixel blended: list index < n_proc
   const float sc = a.view_scale ? a.view_scale[view] : 1.0f;
 #pragma unroll
   for (int k = 0; k < PX; ++k) {
     const int py = oy + (lane >> 3) + 4 * k;
     fy[k] = float(py) + rc.pixel_center;
-    S[k] = g0[k] = g1[k] = g2c[k] = gW[k] = gD[k] = 0.0f;
-    R0[k] = R1[k] = R2[k] = RW[k] = RD[k] = 0.0f;
+    S[k] = g0[k] = g1[k] = g2c[k] = gW[k] = gD[k] = rs[k] = 0.0f;
     n_proc[k] = 0;
     if (px < a.W && py < a.H) {
       const size_t poff = size_t(py) * a.W + px;
@@ -384,15 +386,6 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
       S[k] = a.pixel_t[pix];
       const uint32_t st = a.pixel_state[pix];
       n_proc[k] = min(st & kCountMask, hi);
-      if (NSEG > 1 && seg < NSEG - 1) {  // start from the checkpoint at hi
-        const float* ck = a.ckpt + size_t(seg) * kCkptFloats * total_px + pix;
-        S[k] = ck[0];
-        R0[k] = ck[total_px];
-        R1[k] = ck[2 * total_px];
-        R2[k] = ck[3 * total_px];
-        RW[k] = ck[4 * total_px];
-        if (DEPTH) RD[k] = ck[5 * total_px];  // written by the forward only with the depth output
-      }
       const uint32_t mask = st >> kCountBits;
       const float* di = a.d_image + size_t(view) * 3 * HW + poff;
       g0[k] = (mask & 1u) ? di[0] * sc : 0.0f;
@@ -401,6 +394,12 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
       gW[k] = (mask & 8u) ? -(g0[k] * rc.bg[0] + g1[k] * rc.bg[1] + g2c[k] * rc.bg[2]) : 0.0f;
       if (a.d_alpha) gW[k] += a.d_alpha[pix];
       if (a.d_depth) gD[k] = a.d_depth[pix];
+      if (NSEG > 1 && seg < NSEG - 1) {  // start from the checkpoint at hi
+        const float* ck = a.ckpt + size_t(seg) * kCkptFloats * total_px + pix;
+        S[k] = ck[0];
+        rs[k] = g0[k] * ck[total_px] + g1[k] * ck[2 * total_px] + g2c[k] * ck[3 * total_px] + gW[k] * ck[4 * total_px];
+        if (DEPTH) rs[k] = fmaf(gD[k], ck[5 * total_px], rs[k]);  // written by the forward only with depth on
+      }
     }
   }
   // list range [lo, wmax) this warp has to revisit
@@ -443,17 +442,9 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           const float4 col = s_col[lw][j];
           const float w = T * alpha;
           float dldw = g0[k] * col.x + g1[k] * col.y + g2c[k] * col.z + gW[k];
-          float rsum = g0[k] * R0[k] + g1[k] * R1[k] + g2c[k] * R2[k] + gW[k] * RW[k];
-          if (DEPTH) {
-            dldw = fmaf(gD[k], col.w, dldw);
-            rsum = fmaf(gD[k], RD[k], rsum);
-            RD[k] = fmaf(w, col.w, RD[k]);
-          }
-          const float dlda = T * dldw - rsum * rf;
-          R0[k] = fmaf(w, col.x, R0[k]);
-          R1[k] = fmaf(w, col.y, R1[k]);
-          R2[k] = fmaf(w, col.z, R2[k]);
-          RW[k] += w;
+          if (DEPTH) dldw = fmaf(gD[k], col.w, dldw);
+          const float dlda = T * dldw - rs[k] * rf;
+          rs[k] = fmaf(w, dldw, rs[k]);
           const float dlr = (araw >= 0.0f && araw <= rc.alpha_clamp) ? dlda : 0.0f;
           // d min(power, 0) / d power, power = -q / 2 (torch splits a tie at 0 evenly)
           const float pmask = q > 0.0f ? 1.0f : (q == 0.0f ? 0.5f : 0.0f);
