@@ -181,10 +181,9 @@ GSB_API gsb_status gsb_depth_order(const gsb_scene* scene, const gsb_views* view
   uint32_t* hist = nullptr;
   if ((s = segmented_sort_prepare(sort_ws, sws, uint32_t(B), uint32_t(G), st, &hist)) != GSB_OK) return s;
   if ((s = launch_depth_keys(*scene, *views, keys, vals, hist, st)) != GSB_OK) return s;
-  if ((s = segmented_sort_run(keys, skeys, vals, svals, uint32_t(B), uint32_t(G), sort_ws, sws, st, status)) !=
-      GSB_OK)
-    return s;
-  return launch_invert_order(svals, B, G, sorted_ids, rank_of, st);
+  // the last pass writes sorted_ids and rank_of directly
+  return segmented_sort_run(keys, skeys, vals, svals, uint32_t(B), uint32_t(G), sort_ws, sws, st, status, sorted_ids,
+                            rank_of);
 }
 
 // ---- stage 2 ---------------------------------------------------------------------------------
@@ -289,6 +288,7 @@ GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int3
   // n_pairs is the capacity of the key buffers; the count itself is read on the device, so the
   // stage can be queued before the count reaches the host.
   const uint32_t* n_dev = pair_offsets + size_t(B) * size_t(n_gaussians);
+  bool ranges_done = false;
   if (n_pairs > 0) {  // keys in (view, rank) order, then each view's run sorted by tile
     uint32_t* hist = nullptr;
     if ((s = pair_sort_prepare(sort_ws, sws, n_pairs, uint32_t(B), uint32_t(rc.n_tiles), st, &hist)) != GSB_OK)
@@ -298,15 +298,16 @@ GSB_API gsb_status gsb_bin(const gsb_views* views, const gsb_options* opts, int3
                          pair_sort_passes(uint32_t(rc.n_tiles)), status, st)) != GSB_OK)
       return s;
     if ((s = pair_sort_run(keys, sorted_keys, n_pairs, uint32_t(B), uint32_t(rc.n_tiles), n_gaussians, pair_offsets,
-                           sort_ws, sws, st, status)) != GSB_OK)
+                           sort_ws, sws, st, status, tile_ranges, tile_order ? okeys : nullptr, ovals,
+                           &ranges_done)) != GSB_OK)
       return s;
   }
-  if ((s = launch_tile_ranges(sorted_keys, n_pairs, n_dev, tile_ranges, size_t(B) * rc.n_tiles, status, st)) !=
-      GSB_OK)
+  if (!ranges_done &&
+      (s = launch_tile_ranges(sorted_keys, n_pairs, n_dev, tile_ranges, size_t(B) * rc.n_tiles, status, st)) != GSB_OK)
     return s;
   if (!tile_order) return GSB_OK;
   // launch order: tiles by descending list length (8-bit log-scale key, one radix pass)
-  if ((s = launch_tile_order_keys(tile_ranges, uint32_t(NT), okeys, ovals, st)) != GSB_OK) return s;
+  if (!ranges_done && (s = launch_tile_order_keys(tile_ranges, uint32_t(NT), okeys, ovals, st)) != GSB_OK) return s;
   return radix_sort(okeys, okeys_sorted, ovals, tile_order, uint32_t(NT), 4, 0, 8, order_ws, ows, st, status);
 }
 

@@ -97,14 +97,6 @@ __global__ void tile_ranges_kernel(const uint64_t* __restrict__ keys, uint32_t c
   }
 }
 
-// List length on a log scale in 8 bits (exact below 16, then 8 steps per power of two), so that
-// one 8-bit radix pass orders the tiles.
-__device__ inline uint32_t length_class(uint32_t len) {
-  if (len < 8u) return len;
-  const int e = 31 - __clz(len);  // 3 .. 31
-  return uint32_t(e - 2) * 8u + ((len >> (e - 3)) & 7u);  // 8 .. 239, non-decreasing in len
-}
-
 // Sort key of a tile's launch slot: longer lists first.
 __global__ void tile_order_keys_kernel(const uint32_t* __restrict__ ranges, uint32_t n, uint32_t* __restrict__ keys,
                                        uint32_t* __restrict__ vals) {

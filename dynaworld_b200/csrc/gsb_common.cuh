@@ -72,6 +72,14 @@ __device__ inline void flush_digits4(const uint32_t (*s_hist)[256], uint32_t* __
   }
 }
 
+// List length on a log scale in 8 bits (exact below 16, then 8 steps per power of two), so that
+// one 8-bit radix pass orders the tiles (the raster launch order, longest lists first).
+__device__ inline uint32_t length_class(uint32_t len) {
+  if (len < 8u) return len;
+  const int e = 31 - __clz(len);  // 3 .. 31
+  return uint32_t(e - 2) * 8u + ((len >> (e - 3)) & 7u);  // 8 .. 239, non-decreasing in len
+}
+
 // log2(fl32(1 + 1e-6)) = log2(1 + 2^-20): the per-Gaussian transmittance growth of dense.py:225.
 constexpr double kLog2F0 = 1.3757959012e-06;
 

@@ -27,9 +27,12 @@ gsb_status radix_sort(const void* keys_in, void* keys_out, const uint32_t* vals_
 size_t segmented_sort_workspace(uint32_t n_seg, uint32_t seg_len);
 gsb_status segmented_sort_prepare(void* ws, size_t ws_bytes, uint32_t n_seg, uint32_t seg_len, cudaStream_t stream,
                                   uint32_t** hist);
+// ids_out / rank_out (both or neither): the last pass writes the sorted values as ids_out and
+// their inverse permutation per segment (rank_out[seg * seg_len + value] = position in the segment)
+// instead of keys_out / vals_out.
 gsb_status segmented_sort_run(const uint32_t* keys_in, uint32_t* keys_out, const uint32_t* vals_in, uint32_t* vals_out,
                               uint32_t n_seg, uint32_t seg_len, void* ws, size_t ws_bytes, cudaStream_t stream,
-                              int32_t* status);
+                              int32_t* status, int32_t* ids_out = nullptr, int32_t* rank_out = nullptr);
 
 // Pair keys sorted by tile within each view's run (sort.cu): pair_sort_prepare clears the
 // workspace and returns the digit histograms [n_views][passes][256] of the tile index (passes =
@@ -39,9 +42,12 @@ size_t pair_sort_workspace(uint32_t cap, uint32_t n_views, uint32_t n_tiles);
 int pair_sort_passes(uint32_t n_tiles);
 gsb_status pair_sort_prepare(void* ws, size_t ws_bytes, uint32_t cap, uint32_t n_views, uint32_t n_tiles,
                              cudaStream_t stream, uint32_t** hist);
+// tile_ranges (may be NULL) [n_views * n_tiles * 2] and, when order_keys is given, the launch-order
+// keys and values: written from the pass's counts when one pass sorts the runs (*ranges_done).
 gsb_status pair_sort_run(const uint64_t* keys_in, uint64_t* keys_out, uint32_t cap, uint32_t n_views, uint32_t n_tiles,
                          int32_t G, const uint32_t* pair_offsets, void* ws, size_t ws_bytes, cudaStream_t stream,
-                         int32_t* status);
+                         int32_t* status, uint32_t* tile_ranges, uint32_t* order_keys, uint32_t* order_vals,
+                         bool* ranges_done);
 
 // Exclusive scan: offsets[0..n) and offsets[n] = total (sort.cu).
 size_t exclusive_scan_workspace(uint32_t n);

@@ -445,7 +445,7 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           if (DEPTH) dldw = fmaf(gD[k], col.w, dldw);
           const float dlda = T * dldw - rs[k] * rf;
           rs[k] = fmaf(w, dldw, rs[k]);
-          const float dlr = (araw >= 0.0f && araw <= rc.alpha_clamp) ? dlda : 0.0f;
+          const float dlr = alpha == araw ? dlda : 0.0f;  // the clamp to [0, alpha_clamp] is inactive
           // d min(power, 0) / d power, power = -q / 2 (torch splits a tie at 0 evenly)
           const float pmask = q > 0.0f ? 1.0f : (q == 0.0f ? 0.5f : 0.0f);
           const float dpow = dlr * araw * pmask;

@@ -107,6 +107,8 @@ struct Segments {
   const uint32_t* start;       // kSegRuns: [n_seg + 1] first key of each segment (device)
   const uint32_t* part_start;  // kSegRuns: [n_seg + 1] first partition of each segment (device)
   uint32_t key_stride;         // kSegRuns: the digits are those of (key >> 32) - segment * key_stride
+  int32_t* ids_out;            // kSegFixed, last pass (may be NULL): write the values as ids_out[pos]
+  int32_t* rank_out;           //   and the inverse rank_out[segment start + value] = pos - segment start
 };
 
 // One LSD pass.  Partitions never straddle a segment and look back only within theirs; with
@@ -265,6 +267,12 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
       record_error(status, GSB_ERR_TIMEOUT, int(part));
       continue;
     }
+    if (kSeg == kSegFixed && kVals && sg.ids_out) {  // the permutation and its inverse, not the keys
+      const uint32_t val = s_vals[i];
+      sg.ids_out[pos] = int32_t(val);
+      if (val < seg_hi - seg_lo) sg.rank_out[seg_lo + val] = int32_t(pos - seg_lo);
+      continue;
+    }
     keys_out[pos] = key;
     if (kVals) vals_out[pos] = s_vals[i];
   }
@@ -415,7 +423,8 @@ gsb_status segmented_sort_prepare(void* ws, size_t ws_bytes, uint32_t n_seg, uin
 
 gsb_status segmented_sort_run(const uint32_t* keys_in, uint32_t* keys_out, const uint32_t* vals_in, uint32_t* vals_out,
                               uint32_t n_seg, uint32_t seg_len, void* ws, size_t ws_bytes, cudaStream_t stream,
-                              int32_t* status) {
+                              int32_t* status, int32_t* ids_out, int32_t* rank_out) {
+  if ((ids_out == nullptr) != (rank_out == nullptr)) return GSB_ERR_ARG;
   if (size_t(n_seg) * seg_len >= (size_t(1) << 30)) return GSB_ERR_KEY_OVERFLOW;
   if (n_seg == 0 || seg_len == 0) return GSB_OK;
   SegWorkspace w;
@@ -431,6 +440,7 @@ gsb_status segmented_sort_run(const uint32_t* keys_in, uint32_t* keys_out, const
     note_launch();
     Segments sg{};
     sg.hist_stride = uint32_t(kSegPasses * 256), sg.fixed_len = seg_len, sg.parts_per_seg = pps;
+    if (p == kSegPasses - 1) sg.ids_out = ids_out, sg.rank_out = rank_out;
     onesweep_kernel<uint32_t, true, kSegFixed><<<parts, kSortThreads, 0, stream>>>(
         src_k, dst_k, src_v, dst_v, n_seg * seg_len, 8 * p, 8, w.hist + 256 * p, w.lookback + size_t(p) * parts * 256,
         w.counters + p, status, nullptr, sg);
@@ -526,9 +536,34 @@ gsb_status pair_sort_prepare(void* ws, size_t ws_bytes, uint32_t cap, uint32_t n
   return GSB_OK;
 }
 
+// With one pass (at most 256 tiles per view) the pass's digit counts are the tile list lengths:
+// view blockIdx.x's tile ranges are its run start plus their exclusive prefix, and the launch-order
+// keys (longest first) follow from the same counts, so no kernel re-reads the sorted keys.
+__global__ void __launch_bounds__(kSortThreads) run_tile_ranges_kernel(
+    const uint32_t* __restrict__ hist, const uint32_t* __restrict__ start, uint32_t n_tiles,
+    uint32_t* __restrict__ ranges, uint32_t* __restrict__ order_keys, uint32_t* __restrict__ order_vals,
+    const uint32_t* __restrict__ n_dev, uint32_t cap, int32_t* __restrict__ status) {
+  __shared__ uint32_t s_tmp[kSortWarps];
+  const uint32_t v = blockIdx.x, t = threadIdx.x;
+  if (v == 0 && t == 0 && *n_dev > cap) record_error(status, GSB_ERR_CAPACITY, int(cap));
+  const uint32_t c = t < n_tiles ? hist[size_t(v) * 256 + t] : 0u;
+  const uint32_t before = block_excl_scan_256(c, s_tmp, nullptr);
+  if (t < n_tiles) {
+    const size_t slot = size_t(v) * n_tiles + t;
+    ranges[slot * 2] = start[v] + before;
+    ranges[slot * 2 + 1] = start[v] + before + c;
+    if (order_keys) {
+      order_keys[slot] = 255u - length_class(c);
+      order_vals[slot] = uint32_t(slot);
+    }
+  }
+}
+
 gsb_status pair_sort_run(const uint64_t* keys_in, uint64_t* keys_out, uint32_t cap, uint32_t n_views, uint32_t n_tiles,
                          int32_t G, const uint32_t* pair_offsets, void* ws, size_t ws_bytes, cudaStream_t stream,
-                         int32_t* status) {
+                         int32_t* status, uint32_t* tile_ranges, uint32_t* order_keys, uint32_t* order_vals,
+                         bool* ranges_done) {
+  *ranges_done = false;
   if (cap == 0) return GSB_OK;
   PairWorkspace w;
   if (!pair_carve(ws, ws_bytes, cap, n_views, n_tiles, w)) return GSB_ERR_WORKSPACE;
@@ -552,6 +587,13 @@ gsb_status pair_sort_run(const uint64_t* keys_in, uint64_t* keys_out, uint32_t c
         src, dst, nullptr, nullptr, cap, 8 * p, nbits, w.hist + 256 * p, w.lookback + size_t(p) * parts * 256,
         w.counters + p, status, nullptr, sg);
     src = dst;
+  }
+  if (passes == 1 && tile_ranges) {
+    note_launch();
+    run_tile_ranges_kernel<<<n_views, kSortThreads, 0, stream>>>(w.hist, w.start, n_tiles, tile_ranges, order_keys,
+                                                                 order_vals, pair_offsets + size_t(n_views) * G, cap,
+                                                                 status);
+    *ranges_done = true;
   }
   return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
