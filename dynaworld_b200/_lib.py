@@ -37,7 +37,7 @@ LENS_COEFFS = {"pinhole": 0, "radial_tangential": 5, "opencv_fisheye": 4}
 DISTORTION_FLOATS = 5
 SPLATS2D_CONIC = 0
 SPLATS2D_PACKED = 1
-RECORD_FLOATS = 12
+RECORD_FLOATS = 16
 GRAD2D_FLOATS = 10
 
 vp = C.c_void_p

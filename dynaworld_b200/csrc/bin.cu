@@ -47,8 +47,8 @@ __global__ void __launch_bounds__(256) emit_keys_kernel(int32_t G, RenderConsts 
   if (start != end) {
     const int4 rc4 = rects[i];
     if (!rc.compat && rc.ellipse) {
-      const float4 r0 = reinterpret_cast<const float4*>(records)[i * 3 + 0];
-      const float4 r1 = reinterpret_cast<const float4*>(records)[i * 3 + 1];
+      const float4* rec = reinterpret_cast<const float4*>(records + i * GSB_RECORD_FLOATS);
+      const float4 r0 = rec[0], r1 = rec[1];
       ExactShape es;
       if (exact_shape(r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, rc.alpha_cutoff, H, W, rc.pixel_center, &es)) {
         for (int ty = rc4.y; ty <= rc4.w; ++ty) {

@@ -72,6 +72,19 @@ __device__ inline void flush_digits4(const uint32_t (*s_hist)[256], uint32_t* __
   }
 }
 
+// Culling extents of the ellipse {q <= tau}, q = A dx^2 + B dx dy + C dy^2, that the raster's
+// warp-block test reads from the record's fourth float4: half widths sqrt(tau (A^-1)_ii) (with a
+// relative and an absolute margin) and the slopes of the lines through its extreme points;
+// +inf half widths mark a conic that is never culled.
+__device__ inline float4 cull_extents(float A, float B, float C, float tau) {
+  const float det = A * C - 0.25f * B * B;
+  if (!(det > 0.0f) || !(tau >= 0.0f) || !isfinite(tau))
+    return make_float4(__int_as_float(0x7f800000), __int_as_float(0x7f800000), 0.0f, 0.0f);
+  const float ex = sqrtf(tau * C / det) * 1.0001f + 0.01f;
+  const float ey = sqrtf(tau * A / det) * 1.0001f + 0.01f;
+  return make_float4(ex, ey, -0.5f * B / C, -0.5f * B / A);
+}
+
 // List length on a log scale in 8 bits (exact below 16, then 8 steps per power of two), so that
 // one 8-bit radix pass orders the tiles (the raster launch order, longest lists first).
 __device__ inline uint32_t length_class(uint32_t len) {

@@ -482,6 +482,7 @@ __global__ void __launch_bounds__(256, 4) preprocess_fwd_kernel(gsb_scene sc, gs
     rec[0] = make_float4(P.mx, P.my, P.A, P.B);
     rec[1] = make_float4(P.C, P.o_eff, P.z, tau_f);
     rec[2] = make_float4(rgb[0], rgb[1], rgb[2], 0.0f);
+    rec[3] = cull_extents(P.A, P.B, P.C, tau_f);
     rects[slot] = make_int4(rect.tx0, rect.ty0, rect.tx1, rect.ty1);
     counts[slot] = count;
     if (cov_out) {

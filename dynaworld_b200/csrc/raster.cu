@@ -93,7 +93,7 @@ __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* rec
                                            float bx0, float by0, const WarpSlots& s, int lane) {
   const uint32_t r = min(uint32_t(a.keys[idx]), uint32_t(a.G - 1));  // ranks are < G for valid keys
   const float4* rec = reinterpret_cast<const float4*>(recs + size_t(r) * GSB_RECORD_FLOATS);
-  const float4 r0 = __ldg(rec + 0), r1 = __ldg(rec + 1), r2 = __ldg(rec + 2);
+  const float4 r0 = __ldg(rec + 0), r1 = __ldg(rec + 1), r2 = __ldg(rec + 2), r3 = __ldg(rec + 3);
   const float pos = a.rc.compat ? float(li) : float(r);
   const float pw = exp2f(pos * a.rc.log2_f0);
   s.geo[lane] = r0;
@@ -102,18 +102,16 @@ __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* rec
   if (s.rank) s.rank[lane] = r;
   const float A = r0.z, B = r0.w, C = r1.x, tau = r1.w;
   if (!(tau >= 0.0f)) return false;
-  const float det = A * C - 0.25f * B * B;
-  if (!(det > 0.0f) || !isfinite(tau)) return true;
-  // half extents of the ellipse: sqrt(tau (A^-1)_ii), (A^-1)_00 = C/det, (A^-1)_11 = A/det
-  const float ex = sqrtf(tau * C / det) * 1.0001f + 0.01f;
-  const float ey = sqrtf(tau * A / det) * 1.0001f + 0.01f;
+  // half extents of the ellipse (cull_extents: sqrt(tau (A^-1)_ii), +inf for a degenerate conic)
+  const float ex = r3.x, ey = r3.y;
+  if (!(ex < __int_as_float(0x7f800000))) return true;
   constexpr float kH = float(BH - 1);
   if (!((r0.x + ex >= bx0) && (r0.x - ex <= bx0 + 7.0f) && (r0.y + ey >= by0) && (r0.y - ey <= by0 + kH)))
     return false;
   // exact: the minimum of q over the block's pixel-centre box (on an edge unless the mean is inside)
   const float X0 = bx0 - r0.x, X1 = bx0 + 7.0f - r0.x, Y0 = by0 - r0.y, Y1 = by0 + kH - r0.y;
   if (X0 <= 0.0f && X1 >= 0.0f && Y0 <= 0.0f && Y1 >= 0.0f) return true;
-  const float hC = -0.5f * B / C, hA = -0.5f * B / A;
+  const float hC = r3.z, hA = r3.w;
   float q = __int_as_float(0x7f800000);
 #pragma unroll
   for (int e = 0; e < 2; ++e) {

@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(256) preprocess_2d_kernel(gsb_splats2d sp, int
     rec[0] = make_float4(g.mx, g.my, g.A, g.B);
     rec[1] = make_float4(g.C, g.o, sp.depths ? sp.depths[i] : 0.0f, tau_f);
     rec[2] = make_float4(sp.colors[i * 3 + 0], sp.colors[i * 3 + 1], sp.colors[i * 3 + 2], 0.0f);
+    rec[3] = cull_extents(g.A, g.B, g.C, tau_f);
     rects[slot] = make_int4(rect.tx0, rect.ty0, rect.tx1, rect.ty1);
     counts[slot] = count;
   }

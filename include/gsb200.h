@@ -170,8 +170,10 @@ typedef struct gsb_loss_options {
 } gsb_loss_options;
 
 /* Size of one projected record (floats), of one 2-D gradient record (floats), and of the
-   per-pixel state the backward reads. */
-#define GSB_RECORD_FLOATS 12
+   per-pixel state the backward reads.  A record is mx, my, A, B, C, opacity, z, tau, r, g, b, 0,
+   then the ellipse's culling extents: half widths ex, ey of {q <= tau} (with margins; +inf for a
+   degenerate conic) and the slopes -B/(2C), -B/(2A) of its extreme points. */
+#define GSB_RECORD_FLOATS 16
 #define GSB_GRAD2D_FLOATS 10
 
 /* ---- library ------------------------------------------------------------------------------ */

@@ -4,6 +4,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
+from dynaworld_b200 import _lib
 from dynaworld_b200.config import B200RendererConfig
 from dynaworld_b200.losses import reconstruction_loss_per_image
 from dynaworld_b200.render import SceneSpec, ViewSpec, forward_stages
@@ -78,7 +79,7 @@ def sorted_ids_from_rank(rank_of: torch.Tensor, B: int, G: int) -> np.ndarray:
 
 
 def records_np(state, B: int, G: int) -> np.ndarray:
-    return state.records.view(B, G, 12).cpu().numpy()
+    return state.records.view(B, G, _lib.RECORD_FLOATS).cpu().numpy()
 
 
 def keys_np(state) -> np.ndarray:
