@@ -195,9 +195,9 @@ GSB_API gsb_status gsb_depth_order(const gsb_scene* scene, const gsb_views* view
 
 /* ---- stage 2: projection in depth order, tile bounds, pair count prefix ------------------- */
 GSB_API size_t gsb_preprocess_workspace(const gsb_views* views, int32_t n_gaussians);
-/* records[(b*G + r)*12 ..] = mx, my, A, B, C, opacity, z, tau, r, g, b, 0 for the r-th nearest
-   Gaussian of view b (A, B, C: inv_cov00, inv_cov01+inv_cov10, inv_cov11; tau: the q above
-   which alpha < alpha_cutoff).  tile_rects[(b*G + r)*4 ..] = tx0, ty0, tx1, ty1 (inclusive;
+/* records[(b*G + r)*GSB_RECORD_FLOATS ..] = mx, my, A, B, C, opacity, z, tau, r, g, b, 0, then
+   the culling extents, for the r-th nearest Gaussian of view b (A, B, C: inv_cov00,
+   inv_cov01+inv_cov10, inv_cov11; tau: the q above which alpha < alpha_cutoff).  tile_rects[(b*G + r)*4 ..] = tx0, ty0, tx1, ty1 (inclusive;
    empty when tx0 > tx1).  pair_offsets[B*G + 1]: exclusive prefix of the per-Gaussian pair
    counts; pair_offsets[B*G] is the total (<= 2^30, else GSB_ERR_KEY_OVERFLOW at gsb_bin).
    cov2d_out ([B*G*3] c00, c01, c11 in depth order) may be NULL. */
