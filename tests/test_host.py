@@ -139,3 +139,45 @@ def test_synthetic_shapes_full_size_metadata():
     torch.testing.assert_close(cont.camera_to_world, wl.camera_to_world[14:16])
     torch.testing.assert_close(cont.target, wl.target[14:16])
     torch.testing.assert_close(cont.times, wl.times[14:16])
+
+
+def test_pair_capacity_guess():
+    """The binning capacity guessed from earlier frames: 1.25x the count plus slack, in 64 Ki steps,
+    kept while the count stays between half the capacity and the capacity."""
+    from dynaworld_b200.render import _next_capacity
+
+    first = _next_capacity(1_000_000, None)
+    assert first % 65536 == 0 and first >= 1_250_000
+    assert _next_capacity(1_100_000, first) == first          # still fits: keep
+    assert _next_capacity(first + 1, first) > first + 1        # overflow: grow past the count
+    assert _next_capacity(first // 3, first) < first           # far below: shrink
+    assert _next_capacity(0, None) == 65536
+
+
+def test_training_host_helpers():
+    from types import SimpleNamespace
+
+    from dynaworld_b200.training import resize_images, temporal_recon_chunk_size, viewport_cameras
+
+    assert [temporal_recon_chunk_size(s, 8, 3) for s in ("batched", "framewise", "microbatch")] == [8, 1, 3]
+    x = torch.rand(2, 4, 3, 16, 16)
+    assert resize_images(x, 16) is x
+    y = resize_images(x, 8)
+    assert y.shape == (2, 4, 3, 8, 8)
+    torch.testing.assert_close(y[0, 0], torch.nn.functional.interpolate(x[0, :1], size=(8, 8), mode="bilinear",
+                                                                        align_corners=False)[0])
+    cam = SimpleNamespace(fx=100.0, fy=80.0, cx=32.0, cy=30.0, camera_to_world=torch.eye(4))
+    (c,) = viewport_cameras((cam,), 64, 32)
+    assert (c.fx, c.fy, c.cx, c.cy) == (50.0, 40.0, 16.0, 15.0) and c.camera_to_world is cam.camera_to_world
+
+
+def test_bank_basis_and_argument_checks_on_cpu():
+    from dynaworld_b200.bank import DynamicGaussianBank, render_dynamic_bank, temporal_basis
+
+    phi = temporal_basis(torch.tensor([0.0, 0.25]), 5, 8.0)
+    assert phi.shape == (2, 5)
+    torch.testing.assert_close(phi[:, 4], torch.tensor([-1.0, -0.5]))  # odd count: 2t - 1
+    bank = DynamicGaussianBank(*(torch.zeros(3, c) for c in (3, 3, 4, 1, 3)), torch.zeros(3, 2, 3),
+                               torch.zeros(3, 2, 3), torch.zeros(3, 2, 1))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        render_dynamic_bank(bank, torch.zeros(2), 8, 8, 10.0, 10.0, 4.0, 4.0)
