@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(256) emit_keys_kernel(int32_t G, RenderConsts 
       if (exact_shape(r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, rc.alpha_cutoff, H, W, rc.pixel_center, &es)) {
         for (int ty = rc4.y; ty <= rc4.w; ++ty) {
           int tx0, tx1;
-          if (!exact_row(es, ty, rc.tile, rc.pixel_center, &tx0, &tx1)) continue;
+          if (!exact_row_pairs(es, ty, rc.tile, rc.pixel_center, &tx0, &tx1)) continue;
           for (int tx = tx0; tx <= tx1; ++tx) put(tx, ty);
         }
       }

@@ -30,6 +30,8 @@ struct ExactShape {
   double L;                // ellipse level: tau (1 + rel) + abs
   double ex, ey;           // half extents sqrt(L c / det), sqrt(L a / det)
   int px0, px1, py0, py1;  // pixel rectangle (inclusive), clipped to the image
+  double ul;               // row offset b ex / (2c) of the leftmost point (exact_row's one division
+                           // that does not depend on the row, formed once)
 };
 
 __device__ inline double dmul(double x, double y) { return __dmul_rn(x, y); }
@@ -57,6 +59,7 @@ __device__ inline bool exact_shape(float mxf, float myf, float af, float bf, flo
   if (!(px0 <= px1) || !(py0 <= py1) || !isfinite(mx) || !isfinite(my)) return false;
   s->mx = mx, s->my = my, s->a = a, s->b = b, s->c = c, s->det = det, s->L = L, s->ex = ex, s->ey = ey;
   s->px0 = int(px0), s->px1 = int(px1), s->py0 = int(py0), s->py1 = int(py1);
+  s->ul = ddiv(dmul(b, ex), dmul(2.0, c));
   return true;
 }
 
@@ -77,10 +80,45 @@ __device__ inline bool exact_row(const ExactShape& s, int ty, int tile, float pc
   const double u1 = fmin(dsub(Y1, s.my), s.ey);
   if (!(u0 <= u1)) return false;
   // leftmost point of the ellipse at u = b ex / (2c), rightmost at -b ex / (2c)
-  const double ul = ddiv(dmul(s.b, s.ex), dmul(2.0, s.c));
+  const double ul = s.ul;
   const double ur = -ul;
   const double xl = (u0 <= ul && ul <= u1) ? -s.ex : fmin(ellipse_x(s, u0, false), ellipse_x(s, u1, false));
   const double xr = (u0 <= ur && ur <= u1) ? s.ex : fmax(ellipse_x(s, u0, true), ellipse_x(s, u1, true));
+  const double qx0 = fmax(ceil(dsub(dadd(s.mx, xl), dpc)), double(s.px0));
+  const double qx1 = fmin(floor(dsub(dadd(s.mx, xr), dpc)), double(s.px1));
+  if (!(qx0 <= qx1)) return false;
+  *tx0 = int(qx0) / tile;
+  *tx1 = int(qx1) / tile;
+  return true;
+}
+
+// exact_row with the left and right boundaries at u0 and u1 taken from one square root each (the
+// same values; more registers live at once, so the register-capped preprocess count keeps
+// exact_row and the key emission uses this one).
+__device__ inline bool exact_row_pairs(const ExactShape& s, int ty, int tile, float pc, int* tx0, int* tx1) {
+  const double dpc = pc;
+  const double Y0 = dadd(double(max(ty * tile, s.py0)), dpc);
+  const double Y1 = dadd(double(min(ty * tile + tile - 1, s.py1)), dpc);
+  const double u0 = fmax(dsub(Y0, s.my), -s.ey);
+  const double u1 = fmin(dsub(Y1, s.my), s.ey);
+  if (!(u0 <= u1)) return false;
+  const double ul = s.ul, ur = -s.ul;
+  const bool at_l = u0 <= ul && ul <= u1, at_r = u0 <= ur && ur <= u1;
+  double xl = -s.ex, xr = s.ex;
+  if (!at_l || !at_r) {
+    const double four_aL = dmul(dmul(4.0, s.a), s.L), four_det = dmul(4.0, s.det), two_a = dmul(2.0, s.a);
+    double l[2], r[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const double u = e ? u1 : u0;
+      const double root = __dsqrt_rn(fmax(dsub(four_aL, dmul(four_det, dmul(u, u))), 0.0));
+      const double nb = -dmul(s.b, u);
+      l[e] = ddiv(dsub(nb, root), two_a);
+      r[e] = ddiv(dadd(nb, root), two_a);
+    }
+    if (!at_l) xl = fmin(l[0], l[1]);
+    if (!at_r) xr = fmax(r[0], r[1]);
+  }
   const double qx0 = fmax(ceil(dsub(dadd(s.mx, xl), dpc)), double(s.px0));
   const double qx1 = fmin(floor(dsub(dadd(s.mx, xr), dpc)), double(s.px1));
   if (!(qx0 <= qx1)) return false;
