@@ -333,12 +333,31 @@ __device__ inline void project(const GaussParams& p, const Camera& cam, float ne
   P.B = inv01 + inv01;
 }
 
+// The K x 3 SH coefficients of Gaussian pg: 16-byte loads when the rows allow them (K = 4, 16 and
+// an aligned array), so the load queue holds a quarter of the requests.
+template <int K>
+__device__ inline void load_sh(const gsb_scene& sc, size_t pg, float sh[K * 3]) {
+  const float* src = sc.colors + pg * size_t(K) * 3;
+  if ((K * 3) % 4 == 0 && (reinterpret_cast<uintptr_t>(sc.colors) & 15) == 0) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+    for (int i = 0; i < (K * 3) / 4; ++i) {
+      const float4 v = __ldg(s4 + i);
+      sh[4 * i] = v.x, sh[4 * i + 1] = v.y, sh[4 * i + 2] = v.z, sh[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < K * 3; ++i) sh[i] = __ldg(src + i);
+  }
+}
+
 template <int K>
 __device__ inline void eval_color(const gsb_scene& sc, size_t pg, const float d[3], bool clamp, float rgb[3]) {
   const float inv = rsqrtf(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
   float Y[K];
   sh_basis<K>(d[0] * inv, d[1] * inv, d[2] * inv, Y);
-  const float* sh = sc.colors + pg * size_t(K) * 3;
+  float sh[K * 3];
+  load_sh<K>(sc, pg, sh);
 #pragma unroll
   for (int c = 0; c < 3; ++c) {
     float v = 0.5f;
