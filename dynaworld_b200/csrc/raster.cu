@@ -493,9 +493,10 @@ constexpr uint64_t kBwdPairedTiles = 2048;
 // = 0): four times the CTAs and a quarter of the serial walk per tile, which lets it pair pixels
 // per lane at any size, for 72 bytes of checkpoint per pixel.  Measured on one B200, 16 x 128^2
 // (1024 tiles): backward 1.10 ms (1 segment) -> 0.92 (2) -> 0.82 (4) -> 0.81 (8, whose forward
-// checkpoints cost more than that); 8 x 384^2 (4608 tiles): 1.57 -> 1.61 (2), so larger grids keep
-// one segment.
-constexpr uint64_t kSegmentedTiles = 2048;
+// checkpoints cost more than that); with the later kernels 8 x 384^2 (4608 tiles): step 352.8 ->
+// 356.4 Mpix/s with 4 segments (backward 1.49 -> 1.43 ms, forward 0.54 -> 0.57); 32 x 1080p
+// (261k tiles): 281.6 -> 279.5 with 2, so grids that large keep one segment.
+constexpr uint64_t kSegmentedTiles = 8192;
 constexpr int kAutoSegments = 4;
 
 // Warps per CTA of the 16x16 kernels: GSB200_RASTER_CW (1, 2, 4 or 8; tuning, results do not
