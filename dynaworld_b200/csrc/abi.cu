@@ -355,6 +355,7 @@ GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opt
   if ((s = check_opts(opts)) != GSB_OK) return s;
   if (n_gaussians <= 0) return GSB_ERR_SHAPE;
   if (!records || !tile_ranges || !pixel_t || !pixel_state || !d_image || !grad2d) return GSB_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(grad2d) % 8u) return GSB_ERR_ARG;  // added to as pairs of floats
   RasterArgs a{};
   a.B = views->n_views, a.G = n_gaussians, a.H = views->height, a.W = views->width;
   a.rc = make_consts(*views, *opts);

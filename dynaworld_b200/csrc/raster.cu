@@ -323,11 +323,14 @@ __device__ __forceinline__ float warp_sum10(float v[12], int lane, int* index) {
   return v[0] + __shfl_xor_sync(kFull, v[0], 1);
 }
 
-// Lanes contributing to one entry at or below this count add their own values atomically; above
-// it the warp reduces first.  Measured on one B200 (backward ms, 16 x 128^2 / 8 x 384^2): 2: 0.796 /
-// 1.570, 4: 0.792 / 1.554, 8: 0.786 / 1.543, 12: 0.783 / 1.537, 16: 0.789 / 1.553, 24: 1.10 / 2.12
-// (the atomics then contend).
-constexpr int kSparseContributors = 12;
+// Lanes contributing to one entry at or below this count add their own values atomically, as five
+// 8-byte vector reductions (red.global.add.v2.f32; a gradient slot is 40 bytes, so every pair of
+// floats is 8-byte aligned); above it the warp reduces first.  Measured on one B200 (backward ms,
+// 16 x 128^2 / 8 x 384^2): scalar atomics, one per nonzero value, 12: 0.730 / 1.433; vector pairs
+// 12: 0.667 / 1.312, 16: 0.660 / 1.291, 20: 0.661 / 1.289, 24: 0.692 / 1.349; 16-byte vectors
+// (three per slot, placed by the slot's alignment) 16: 0.664 / 1.336, 24: 0.649 / 1.296, 32 (never
+// reduce in the warp): 0.893 / 1.714.
+constexpr int kSparseContributors = 16;
 
 // DEPTH: a depth gradient is given.  NSEG: the tile's list is cut into NSEG segments
 // [s n / NSEG, (s + 1) n / NSEG), each walked by its own CTA (adjacent in launch order), starting
@@ -466,9 +469,13 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
       float* dst = g2 + size_t(s_rank[lw][j]) * GSB_GRAD2D_FLOATS;
       if (__popc(cm) <= kSparseContributors) {
         if (contrib) {
-#pragma unroll
-          for (int k = 0; k < GSB_GRAD2D_FLOATS; ++k)
-            if (v[k] != 0.0f) atomicAdd(dst + k, (k >= 2 && k <= 4) ? -0.5f * v[k] : v[k]);
+          float2* d2 = reinterpret_cast<float2*>(dst);
+          atomicAdd(d2 + 0, make_float2(v[0], v[1]));
+          atomicAdd(d2 + 1, make_float2(-0.5f * v[2], -0.5f * v[3]));
+          atomicAdd(d2 + 2, make_float2(-0.5f * v[4], v[5]));
+          atomicAdd(d2 + 3, make_float2(v[6], v[7]));
+          if (DEPTH) atomicAdd(d2 + 4, make_float2(v[8], v[9]));
+          else atomicAdd(dst + 8, v[8]);
         }
       } else {
         int k;

@@ -271,8 +271,9 @@ GSB_API gsb_status gsb_scale_planes(const float* in, const float* scale, float* 
 
 /* ---- stage 6: reverse blend, per-(view, Gaussian) 2-D gradients --------------------------- */
 /* grad2d[(b*G + r)*10 ..] = dL/d(mx, my, A, B, C, opacity, r, g, b, z) of the r-th nearest
-   Gaussian of view b; zeroed by the call.  d_alpha, d_depth, view_scale may be NULL (d_depth is
-   read only with GSB_RENDER_DEPTH); opts and pixel_ckpt as given to gsb_raster_fwd. */
+   Gaussian of view b; zeroed by the call; grad2d 8-byte aligned (GSB_ERR_ARG otherwise).
+   d_alpha, d_depth, view_scale may be NULL (d_depth is read only with GSB_RENDER_DEPTH); opts
+   and pixel_ckpt as given to gsb_raster_fwd. */
 GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opts,
                                   int32_t n_gaussians, const float* records,
                                   const uint64_t* sorted_keys, const uint32_t* tile_ranges,

@@ -80,6 +80,9 @@ def test_argument_errors_return_codes_without_touching_a_gpu(lib):
                               None, None) == 7
     o.backward_segments = 1
     assert lib.gsb_raster_checkpoint_floats(ctypes.byref(v), ctypes.byref(o)) == 0
+    # the backward adds to grad2d in pairs of floats: a buffer off an 8-byte boundary is refused
+    assert lib.gsb_raster_bwd(ctypes.byref(v), ctypes.byref(o), 1, 16, 16, 16, None, 16, 16, None, 16, None, None,
+                              None, 20, None) == 7
     lo = _lib.LossOptions()
     lo.type = 0
     lo.window_size = 4  # even window
