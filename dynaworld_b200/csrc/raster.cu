@@ -33,15 +33,22 @@ constexpr uint32_t kCountBits = 28;
 constexpr uint32_t kCountMask = (1u << kCountBits) - 1u;
 constexpr uint32_t kFull = 0xffffffffu;
 
-// exp(-q / 2) as 2^(q * (-log2(e) / 2)) on the SFU's base-2 exponential (PTX ex2.approx; relative
-// error about 2^-22), one multiply and one SFU op per pair.  Forward and backward evaluate the same
-// expression, so the backward's alpha is the forward's to the bit.
-constexpr float kNegHalfLog2E = -0.72134752044448170368f;
-__device__ __forceinline__ float gauss_falloff(float q) {
+// exp(-q / 2) = 2^(q k), k = -log2(e) / 2, on the SFU's base-2 exponential (PTX ex2.approx; relative
+// error about 2^-22).  The warp slots hold the conic and the threshold tau already multiplied by k
+// (one multiply per entry and lane when the chunk is loaded), so a pixel evaluates qk = q k directly
+// and pays one SFU op; tau k < 0 flips the threshold test to qk >= tau k.  Forward and backward
+// evaluate the same expression, so the backward's alpha is the forward's to the bit.
+constexpr float kFalloffScale = -0.72134752044448170368f;  // k
+__device__ __forceinline__ float gauss_falloff(float qk) {
   float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(fminf(q * kNegHalfLog2E, 0.0f)));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(fminf(qk, 0.0f)));
   return y;
 }
+// The backward's per-pixel power gradient is kept divided by k (the 1/k rides on the mask of
+// d min(power, 0) / d power), so the mean gradients come out of the k-scaled conic unchanged and the
+// conic gradients -1/2 sum dpow dx^2 (and so on) take the factor -k / 2 when they are flushed.
+constexpr float kInvFalloffScale = -1.38629436111989061883f;  // 1 / k = -2 ln 2
+constexpr float kConicGradScale = 0.36067376022224085184f;    // -k / 2
 
 // q = A dx^2 + B dx dy + C dy^2 with a fixed rounding sequence (forward and backward agree).
 __device__ __forceinline__ float pair_q(float A, float B, float C, float dx, float dy) {
@@ -79,16 +86,18 @@ __device__ __forceinline__ uint32_t max_of(const uint32_t (&v)[PX]) {
 }
 
 struct WarpSlots {
-  float4* geo;     // mx, my, A, B
-  float4* cot;     // C, opacity, tau, F0^pos
-  float4* col;     // r, g, b, z
+  float4* geo;     // mx, my, A k, B k
+  float4* cot;     // C k, opacity (forward: max(opacity, 0)), tau k, F0^pos
+  float4* col;     // r, g, b, z (forward without depth: the stop bound t_threshold / (F0 F0^pos))
   uint32_t* rank;  // depth rank (gradient slot)
 };
 
 // Lane loads list entry idx (list index li) into its warp slot and returns whether the Gaussian's
 // ellipse {q <= tau} reaches the warp's pixel block [bx0, bx0+7] x [by0, by0+BH-1] (pixel
-// centres; conservative).
-template <int BH>
+// centres; conservative).  FWD_BOUND: the forward without depth, whose slot carries the bound on S
+// below which the pixel stops, in place of z.  With alpha = clamp(o e, 0, alpha_clamp) and e > 0,
+// max(o, 0) e equals max(o e, 0) exactly, so the forward keeps max(o, 0) and skips the lower clamp.
+template <int BH, bool FWD, bool FWD_BOUND>
 __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* recs, uint32_t idx, uint32_t li,
                                            float bx0, float by0, const WarpSlots& s, int lane) {
   const uint32_t r = min(uint32_t(a.keys[idx]), uint32_t(a.G - 1));  // ranks are < G for valid keys
@@ -96,11 +105,12 @@ __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* rec
   const float4 r0 = __ldg(rec + 0), r1 = __ldg(rec + 1), r2 = __ldg(rec + 2), r3 = __ldg(rec + 3);
   const float pos = a.rc.compat ? float(li) : float(r);
   const float pw = exp2f(pos * a.rc.log2_f0);
-  s.geo[lane] = r0;
-  s.cot[lane] = make_float4(r1.x, r1.y, r1.w, pw);
-  s.col[lane] = make_float4(r2.x, r2.y, r2.z, r1.z);
-  if (s.rank) s.rank[lane] = r;
   const float A = r0.z, B = r0.w, C = r1.x, tau = r1.w;
+  s.geo[lane] = make_float4(r0.x, r0.y, A * kFalloffScale, B * kFalloffScale);
+  s.cot[lane] = make_float4(C * kFalloffScale, FWD ? fmaxf(r1.y, 0.0f) : r1.y, tau * kFalloffScale, pw);
+  // T after an entry = S after it * F0 * F0^pos: the forward compares S with this bound
+  s.col[lane] = make_float4(r2.x, r2.y, r2.z, FWD_BOUND ? __fdividef(a.rc.t_threshold, a.rc.f0 * pw) : r1.z);
+  if (s.rank) s.rank[lane] = r;
   if (!(tau >= 0.0f)) return false;
   // half extents of the ellipse (cull_extents: sqrt(tau (A^-1)_ii), +inf for a degenerate conic)
   const float ex = r3.x, ey = r3.y;
@@ -191,10 +201,10 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
     for (int k = 0; k < PX; ++k) {
       if (done[k]) continue;
       const float dy = __fsub_rn(fy[k], g.y);
-      const float q = pair_q(g.z, g.w, ct.x, dx, dy);
-      if (!(q <= ct.z)) continue;
-      const float e = gauss_falloff(q);
-      const float alpha = fminf(fmaxf(ct.y * e, 0.0f), rc.alpha_clamp);
+      const float qk = pair_q(g.z, g.w, ct.x, dx, dy);
+      if (!(qk >= ct.z)) continue;
+      const float e = gauss_falloff(qk);
+      const float alpha = fminf(ct.y * e, rc.alpha_clamp);  // ct.y >= 0
       if (!(alpha >= rc.alpha_cutoff)) continue;
       const float4 col = s_col[lw][j];
       const float T = S[k] * ct.w;
@@ -206,7 +216,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
       if (DEPTH) D[k] = fmaf(w, col.w, D[k]);
       const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
       S[k] = S[k] * (f * inv_f0);
-      if (T * f < rc.t_threshold) {  // T after this entry
+      if (DEPTH ? T * f < rc.t_threshold : S[k] < col.w) {  // T after this entry below the threshold
         done[k] = true;
         n_proc[k] = c - start + uint32_t(j) + 1u;
       }
@@ -215,7 +225,8 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
   for (uint32_t c = start; c < end; c += 32) {
     if (__all_sync(kFull, all_of(done))) break;
     const uint32_t idx = c + lane;
-    const bool keep = idx < end && load_entry<block_h<PX>()>(a, recs, idx, idx - start, bx0, by0, ws, lane);
+    const bool keep =
+        idx < end && load_entry<block_h<PX>(), true, !DEPTH>(a, recs, idx, idx - start, bx0, by0, ws, lane);
     uint32_t m = __ballot_sync(kFull, keep);
     __syncwarp();
     if (NSEG > 1) {
@@ -410,7 +421,7 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
   for (int64_t cb = wmax > lo ? int64_t((wmax - 1) / 32) * 32 : -32; cb >= cb_lo; cb -= 32) {
     const uint32_t li = uint32_t(cb) + lane;
     const bool keep = li >= lo && li < wmax &&
-                      load_entry<block_h<PX>()>(a, recs, start + li, li, bx0, by0, ws, lane);
+                      load_entry<block_h<PX>(), false, false>(a, recs, start + li, li, bx0, by0, ws, lane);
     uint32_t m = __ballot_sync(kFull, keep);
     __syncwarp();
     while (m) {
@@ -430,9 +441,9 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
         for (int k = 0; k < PX; ++k) {
           if (!(lj < n_proc[k])) continue;
           const float dy = __fsub_rn(fy[k], g.y);
-          const float q = pair_q(g.z, g.w, ct.x, dx, dy);
-          if (!(q <= ct.z)) continue;
-          const float e = gauss_falloff(q);
+          const float qk = pair_q(g.z, g.w, ct.x, dx, dy);
+          if (!(qk >= ct.z)) continue;
+          const float e = gauss_falloff(qk);
           const float araw = ct.y * e;
           const float alpha = fminf(fmaxf(araw, 0.0f), rc.alpha_clamp);
           if (!(alpha >= rc.alpha_cutoff)) continue;
@@ -447,13 +458,14 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           const float dlda = T * dldw - rs[k] * rf;
           rs[k] = fmaf(w, dldw, rs[k]);
           const float dlr = alpha == araw ? dlda : 0.0f;  // the clamp to [0, alpha_clamp] is inactive
-          // d min(power, 0) / d power, power = -q / 2 (torch splits a tie at 0 evenly)
-          const float pmask = q > 0.0f ? 1.0f : (q == 0.0f ? 0.5f : 0.0f);
+          // d min(power, 0) / d power, power = -q / 2 (torch splits a tie at 0 evenly), divided by k;
+          // q > 0 where qk < 0
+          const float pmask = qk < 0.0f ? kInvFalloffScale : (qk == 0.0f ? 0.5f * kInvFalloffScale : 0.0f);
           const float dpow = dlr * araw * pmask;
           const float u = dpow * dx, t = dpow * dy;
           v[0] = fmaf(g.z, u, fmaf(hB, t, v[0]));
           v[1] = fmaf(ct.x, t, fmaf(hB, u, v[1]));
-          v[2] = fmaf(u, dx, v[2]);  // conic gradients: times -1/2 once the pixels are summed
+          v[2] = fmaf(u, dx, v[2]);  // conic gradients: times -k/2 once the pixels are summed
           v[3] = fmaf(u, dy, v[3]);
           v[4] = fmaf(t, dy, v[4]);
           v[5] = fmaf(dlr, e, v[5]);
@@ -471,8 +483,8 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
         if (contrib) {
           float2* d2 = reinterpret_cast<float2*>(dst);
           atomicAdd(d2 + 0, make_float2(v[0], v[1]));
-          atomicAdd(d2 + 1, make_float2(-0.5f * v[2], -0.5f * v[3]));
-          atomicAdd(d2 + 2, make_float2(-0.5f * v[4], v[5]));
+          atomicAdd(d2 + 1, make_float2(kConicGradScale * v[2], kConicGradScale * v[3]));
+          atomicAdd(d2 + 2, make_float2(kConicGradScale * v[4], v[5]));
           atomicAdd(d2 + 3, make_float2(v[6], v[7]));
           if (DEPTH) atomicAdd(d2 + 4, make_float2(v[8], v[9]));
           else atomicAdd(dst + 8, v[8]);
@@ -480,7 +492,7 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
       } else {
         int k;
         float s = warp_sum10(v, lane, &k);
-        if (k >= 2 && k <= 4) s *= -0.5f;
+        if (k >= 2 && k <= 4) s *= kConicGradScale;
         if ((lane & 1) == 0 && k < GSB_GRAD2D_FLOATS && s != 0.0f) atomicAdd(dst + k, s);
       }
     }
