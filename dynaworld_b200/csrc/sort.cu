@@ -21,9 +21,12 @@ constexpr int kSpinLimit = 1 << 22;
 
 template <typename K>
 struct SortTraits;
+// Keys per thread of a partition.  32-bit keys (the depth order, the tile launch order): 8, measured
+// on one B200 against 16 / 12 (depth order, 8 x 200k keys: 0.188 / 0.179 ms -> 0.180 ms; 16 x 32768
+// keys: 0.084 / 0.090 -> 0.084): twice the partitions fill the GPU at these sizes.
 template <>
 struct SortTraits<uint32_t> {
-  static constexpr int kItems = 16;
+  static constexpr int kItems = 8;
 };
 template <>
 struct SortTraits<uint64_t> {
