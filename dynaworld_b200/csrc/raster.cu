@@ -26,6 +26,7 @@
 // well costs more than the falloff it would save (measured on one B200, 16 x 128^2: forward 0.345
 // -> 0.337 ms, backward 0.657 -> 0.633 ms without it).
 #include <cstdlib>
+#include <type_traits>
 
 #include "gsb_common.cuh"
 #include "gsb_internal.h"
@@ -45,6 +46,13 @@ constexpr float kFalloffScale = -0.72134752044448170368f;  // k
 __device__ __forceinline__ float gauss_falloff(float qk) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(fminf(qk, 0.0f)));
+  return y;
+}
+// The same for an entry whose computed qk cannot be positive (a well-conditioned conic: see
+// load_entry), where the clamp to 0 is the identity.
+__device__ __forceinline__ float gauss_falloff_nonpos(float qk) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(qk));
   return y;
 }
 // The backward's per-pixel power gradient is kept divided by k (the 1/k rides on the mask of
@@ -100,9 +108,17 @@ struct WarpSlots {
 // centres; conservative).  FWD: the forward's slot carries the bound on S below which the pixel
 // stops, and max(o, 0) for the opacity: with alpha = clamp(o e, 0, alpha_clamp) and e > 0,
 // max(o, 0) e equals max(o e, 0) exactly, so the forward skips the lower clamp.
+//
+// conditioned: the entry is kept with finite extents and a finite conic with A, C > 0 and
+// B^2 <= 4 A C (1 - 2^-8).  Then |B dx dy| <= 0.999 (A dx^2 + C dy^2), so q >= 0.001 (A dx^2 +
+// C dy^2) while the rounding of pair_q stays below 8 ulp of that sum: the computed q is never
+// negative (qk never positive), the falloff needs no clamp and d min(power, 0) / d power is 1
+// wherever dx or dy is nonzero.  A chunk whose kept entries are all conditioned takes that path;
+// both paths give the same bits for such an entry, so forward and backward agree whichever each takes.
 template <int BH, bool FWD>
 __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* recs, uint32_t idx, uint32_t li,
-                                           float bx0, float by0, const WarpSlots& s, int lane) {
+                                           float bx0, float by0, const WarpSlots& s, int lane, bool& conditioned) {
+  conditioned = false;
   const uint32_t r = min(uint32_t(a.keys[idx]), uint32_t(a.G - 1));  // ranks are < G for valid keys
   const float4* rec = reinterpret_cast<const float4*>(recs + size_t(r) * GSB_RECORD_FLOATS);
   const float4 r0 = __ldg(rec + 0), r1 = __ldg(rec + 1), r2 = __ldg(rec + 2), r3 = __ldg(rec + 3);
@@ -122,6 +138,8 @@ __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* rec
   constexpr float kH = float(BH - 1);
   if (!((r0.x + ex >= bx0) && (r0.x - ex <= bx0 + 7.0f) && (r0.y + ey >= by0) && (r0.y - ey <= by0 + kH)))
     return false;
+  conditioned = A > 0.0f && C > 0.0f && A < 1e30f && C < 1e30f && fabsf(B) < 1e30f &&
+                B * B <= 4.0f * A * C * (1.0f - 1.0f / 256.0f);
   // exact: the minimum of q over the block's pixel-centre box (on an edge unless the mean is inside)
   const float X0 = bx0 - r0.x, X1 = bx0 + 7.0f - r0.x, Y0 = by0 - r0.y, Y1 = by0 + kH - r0.y;
   if (X0 <= 0.0f && X1 >= 0.0f && Y0 <= 0.0f && Y1 >= 0.0f) return true;
@@ -196,8 +214,9 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
     for (int k = 0; k < PX; ++k)
       kS[s][k] = S[k], kC0[s][k] = C0[k], kC1[s][k] = C1[k], kC2[s][k] = C2[k], kW[s][k] = Ws[k], kD[s][k] = D[k];
   };
-  // blend the entry in slot j of the current chunk (list index c - start + j) into every live pixel
-  auto blend = [&](uint32_t c, int j) {
+  // blend the entry in slot j of the current chunk (list index c - start + j) into every live pixel;
+  // fast: std::true_type when every kept entry of the chunk is conditioned
+  auto blend = [&](uint32_t c, int j, auto fast) {
     const float4 g = s_geo[lw][j];
     const float4 ct = s_cot[lw][j];
     const float dx = __fsub_rn(fx, g.x);
@@ -206,7 +225,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
       if (done[k]) continue;
       const float dy = __fsub_rn(fy[k], g.y);
       const float qk = pair_q(g.z, g.w, ct.x, dx, dy);
-      const float e = gauss_falloff(qk);
+      const float e = decltype(fast)::value ? gauss_falloff_nonpos(qk) : gauss_falloff(qk);
       const float alpha = fminf(ct.y * e, rc.alpha_clamp);  // ct.y >= 0
       if (!(alpha >= rc.alpha_cutoff)) continue;
       const float4 col = s_col[lw][j];
@@ -225,13 +244,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
       }
     }
   };
-  for (uint32_t c = start; c < end; c += 32) {
-    if (__all_sync(kFull, all_of(done))) break;
-    const uint32_t idx = c + lane;
-    const bool keep =
-        idx < end && load_entry<block_h<PX>(), true>(a, recs, idx, idx - start, bx0, by0, ws, lane);
-    uint32_t m = __ballot_sync(kFull, keep);
-    __syncwarp();
+  auto walk = [&](uint32_t c, uint32_t m, auto fast) {
     if (NSEG > 1) {
       // boundaries inside this chunk (warp-uniform): blend the entries before one, then keep the state
 #pragma unroll
@@ -243,7 +256,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
           while (mb && !all_of(done)) {
             const int j = __ffs(mb) - 1;
             mb &= mb - 1;
-            blend(c, j);
+            blend(c, j, fast);
           }
           m &= ~before;
           snapshot(s);
@@ -254,8 +267,20 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
     while (m && !all_of(done)) {
       const int j = __ffs(m) - 1;
       m &= m - 1;
-      blend(c, j);
+      blend(c, j, fast);
     }
+  };
+  for (uint32_t c = start; c < end; c += 32) {
+    if (__all_sync(kFull, all_of(done))) break;
+    const uint32_t idx = c + lane;
+    bool cond = false;
+    const bool keep =
+        idx < end && load_entry<block_h<PX>(), true>(a, recs, idx, idx - start, bx0, by0, ws, lane, cond);
+    const uint32_t m = __ballot_sync(kFull, keep);
+    const bool fast = __all_sync(kFull, cond || !keep);
+    __syncwarp();
+    if (fast) walk(c, m, std::true_type{});
+    else walk(c, m, std::false_type{});
     __syncwarp();  // slots are rewritten by the next chunk
   }
   if (NSEG > 1) {
@@ -421,12 +446,8 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
   const uint32_t wmax = __reduce_max_sync(kFull, max_of(n_proc));
   const int64_t cb_lo = int64_t(lo / 32) * 32;
 
-  for (int64_t cb = wmax > lo ? int64_t((wmax - 1) / 32) * 32 : -32; cb >= cb_lo; cb -= 32) {
-    const uint32_t li = uint32_t(cb) + lane;
-    const bool keep = li >= lo && li < wmax &&
-                      load_entry<block_h<PX>(), false>(a, recs, start + li, li, bx0, by0, ws, lane);
-    uint32_t m = __ballot_sync(kFull, keep);
-    __syncwarp();
+  // the kept entries m of the chunk at list index cb, last first; fast as in the forward
+  auto walk = [&](int64_t cb, uint32_t m, auto fast) {
     while (m) {
       const int j = 31 - __clz(m);
       m &= ~(1u << j);
@@ -445,7 +466,7 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           if (!(lj < n_proc[k])) continue;
           const float dy = __fsub_rn(fy[k], g.y);
           const float qk = pair_q(g.z, g.w, ct.x, dx, dy);
-          const float e = gauss_falloff(qk);
+          const float e = decltype(fast)::value ? gauss_falloff_nonpos(qk) : gauss_falloff(qk);
           const float araw = ct.y * e;
           const float alpha = fminf(fmaxf(araw, 0.0f), rc.alpha_clamp);
           if (!(alpha >= rc.alpha_cutoff)) continue;
@@ -461,8 +482,11 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           rs[k] = fmaf(w, dldw, rs[k]);
           const float dlr = alpha == araw ? dlda : 0.0f;  // the clamp to [0, alpha_clamp] is inactive
           // d min(power, 0) / d power, power = -q / 2 (torch splits a tie at 0 evenly), divided by k;
-          // q > 0 where qk < 0
-          const float pmask = qk < 0.0f ? kInvFalloffScale : (qk == 0.0f ? 0.5f * kInvFalloffScale : 0.0f);
+          // q > 0 where qk < 0.  A conditioned entry has q = 0 only at dx = dy = 0, where the mask
+          // multiplies zeros.
+          const float pmask = decltype(fast)::value
+                                  ? kInvFalloffScale
+                                  : (qk < 0.0f ? kInvFalloffScale : (qk == 0.0f ? 0.5f * kInvFalloffScale : 0.0f));
           const float dpow = dlr * araw * pmask;
           const float u = dpow * dx, t = dpow * dy;
           v[0] = fmaf(g.z, u, fmaf(hB, t, v[0]));
@@ -498,6 +522,17 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
         if ((lane & 1) == 0 && k < GSB_GRAD2D_FLOATS && s != 0.0f) atomicAdd(dst + k, s);
       }
     }
+  };
+  for (int64_t cb = wmax > lo ? int64_t((wmax - 1) / 32) * 32 : -32; cb >= cb_lo; cb -= 32) {
+    const uint32_t li = uint32_t(cb) + lane;
+    bool cond = false;
+    const bool keep = li >= lo && li < wmax &&
+                      load_entry<block_h<PX>(), false>(a, recs, start + li, li, bx0, by0, ws, lane, cond);
+    const uint32_t m = __ballot_sync(kFull, keep);
+    const bool fast = __all_sync(kFull, cond || !keep);
+    __syncwarp();
+    if (fast) walk(cb, m, std::true_type{});
+    else walk(cb, m, std::false_type{});
     __syncwarp();  // slots are rewritten by the next chunk
   }
 }
