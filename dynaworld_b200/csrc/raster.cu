@@ -364,12 +364,16 @@ __device__ __forceinline__ float warp_sum10(float v[12], int lane, int* index) {
 
 // Lanes contributing to one entry at or below this count add their own values atomically, as five
 // 8-byte vector reductions (red.global.add.v2.f32; a gradient slot is 40 bytes, so every pair of
-// floats is 8-byte aligned); above it the warp reduces first.  Measured on one B200 (backward ms,
-// 16 x 128^2 / 8 x 384^2): scalar atomics, one per nonzero value, 12: 0.730 / 1.433; vector pairs
-// 12: 0.667 / 1.312, 16: 0.660 / 1.291, 20: 0.661 / 1.289, 24: 0.692 / 1.349; 16-byte vectors
-// (three per slot, placed by the slot's alignment) 16: 0.664 / 1.336, 24: 0.649 / 1.296, 32 (never
-// reduce in the warp): 0.893 / 1.714.
+// floats is 8-byte aligned); up to kPartialContributors the warp first sums each pixel column's four
+// rows (two transpose steps, three values per lane, two reductions per lane); above that it sums
+// over the whole warp (warp_sum10).  Measured on one B200 (backward ms, 16 x 128^2 / 8 x 384^2):
+// scalar atomics, one per nonzero value, up to 12: 0.730 / 1.433; vector pairs up to 12: 0.667 /
+// 1.312, 16: 0.660 / 1.291, 20: 0.661 / 1.289, 24: 0.692 / 1.349; 16-byte vectors (three per slot,
+// placed by the slot's alignment) up to 16: 0.664 / 1.336, 24: 0.649 / 1.296, 32 (never reduce in
+// the warp): 0.893 / 1.714.  Then, with pairs up to 16, column sums up to 20: 0.627 / 1.140, 24:
+// 0.631 / 1.147, 28: 0.635 / 1.152, 32: 0.646 / 1.262, none: 0.630 / 1.233.
 constexpr int kSparseContributors = 16;
+constexpr int kPartialContributors = 20;
 
 // DEPTH: a depth gradient is given.  NSEG: the tile's list is cut into NSEG segments
 // [s n / NSEG, (s + 1) n / NSEG), each walked by its own CTA (adjacent in launch order), starting
@@ -515,6 +519,33 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           if (DEPTH) atomicAdd(d2 + 4, make_float2(v[8], v[9]));
           else atomicAdd(dst + 8, v[8]);
         }
+      } else if (__popc(cm) <= kPartialContributors) {
+        // column sums: lane l keeps values 3 grp + (0, 1, 2), grp = 2 b4 + b3, summed over l ^ {8, 16, 24}
+#pragma unroll
+        for (int k = 0; k < 6; ++k) {
+          const bool up = lane & 16;
+          const float send = up ? v[k] : v[k + 6];
+          const float keep = up ? v[k + 6] : v[k];
+          v[k] = keep + __shfl_xor_sync(kFull, send, 16);
+        }
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+          const bool up = lane & 8;
+          const float send = up ? v[k] : v[k + 3];
+          const float keep = up ? v[k + 3] : v[k];
+          v[k] = keep + __shfl_xor_sync(kFull, send, 8);
+        }
+        const int grp = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
+        // a float pair at dst + p2 (8-byte aligned: p2 is 0, 4 or 6) and one float at dst + p1
+        float2 pv;
+        float sv;
+        int p2, p1;
+        if (grp == 0) pv = make_float2(v[0], v[1]), p2 = 0, sv = kConicGradScale * v[2], p1 = 2;
+        else if (grp == 1) pv = make_float2(kConicGradScale * v[1], v[2]), p2 = 4, sv = kConicGradScale * v[0], p1 = 3;
+        else if (grp == 2) pv = make_float2(v[0], v[1]), p2 = 6, sv = v[2], p1 = 8;
+        else pv = make_float2(0.0f, 0.0f), p2 = 0, sv = DEPTH ? v[0] : 0.0f, p1 = 9;
+        if (pv.x != 0.0f || pv.y != 0.0f) atomicAdd(reinterpret_cast<float2*>(dst + p2), pv);
+        if (sv != 0.0f) atomicAdd(dst + p1, sv);
       } else {
         int k;
         float s = warp_sum10(v, lane, &k);
