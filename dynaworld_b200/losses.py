@@ -13,11 +13,7 @@ import torch
 
 from . import _lib
 from .config import LossConfig
-from .render import _stage
-
-
-def _stream(device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+from .render import _stage, _stream
 
 
 def loss_forward(pred: torch.Tensor, target: torch.Tensor, cfg: LossConfig, need_grad: bool = True):

@@ -87,7 +87,10 @@ def checkpoint_buffer(views: _lib.Views, opts: _lib.Options, device) -> torch.Te
 
 
 def _stream(device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """Raw handle of the device's current stream (the handle torch.cuda.current_stream(device)
+    wraps, without building the Stream object: this runs several times per step on the host)."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    return torch._C._cuda_getCurrentRawStream(index)
 
 
 def _ws(nbytes: int, device) -> torch.Tensor:
