@@ -384,7 +384,10 @@ __device__ inline void load_color(const gsb_scene& sc, size_t pg, const float d[
 // ---- stage 1 kernels: depth keys and inverse permutation -------------------------------------
 
 constexpr int kKeyThreads = 256;
-constexpr int kKeyItems = 8;  // Gaussians per thread
+// Gaussians per thread.  Measured on one B200 (depth order ms, 16 x 32768 / 8 x 200k): 8: 0.0838 /
+// 0.1799, 4: 0.0821 / 0.1794, 2: 0.0800 / 0.1753 -- more blocks hide the latency of the shared
+// digit counts.
+constexpr int kKeyItems = 2;
 
 // Depth sort keys of view blockIdx.y (the order-preserving bits of the camera z, common.py:190-195)
 // with the Gaussian index as value, plus the view's four 8-bit digit histograms for the
@@ -1016,8 +1019,8 @@ static void bwd_launch_lpg(const gsb_scene& sc, const gsb_views& vw, const Rende
 
 // Lanes per Gaussian: 4 when a set has 4 views or more, else 1.  Measured on one B200 (ms, 16
 // views per set x 32768 Gaussians SH1 / 8 views x 200k SH3): one lane 0.049 / 0.283, four 0.044 /
-// 0.213; sixteen lanes (one view each) 0.059 on the first, where the shuffles of the group sums
-// cost more than the extra parallelism gains.
+// 0.213; eight lanes 0.045 / 0.255 and sixteen (one view each) 0.059 on the first, where the
+// shuffles of the group sums cost more than the extra parallelism gains.
 template <int K, bool LENS>
 static void bwd_launch_k(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc, const int32_t* rank_of,
                          const float* grad2d, const gsb_scene_grads& gr, cudaStream_t st) {
