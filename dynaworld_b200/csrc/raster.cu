@@ -370,10 +370,11 @@ __device__ __forceinline__ float warp_sum10(float v[12], int lane, int* index) {
 // scalar atomics, one per nonzero value, up to 12: 0.730 / 1.433; vector pairs up to 12: 0.667 /
 // 1.312, 16: 0.660 / 1.291, 20: 0.661 / 1.289, 24: 0.692 / 1.349; 16-byte vectors (three per slot,
 // placed by the slot's alignment) up to 16: 0.664 / 1.336, 24: 0.649 / 1.296, 32 (never reduce in
-// the warp): 0.893 / 1.714.  Then, with pairs up to 16, column sums up to 20: 0.627 / 1.140, 24:
-// 0.631 / 1.147, 28: 0.635 / 1.152, 32: 0.646 / 1.262, none: 0.630 / 1.233.
+// the warp): 0.893 / 1.714.  Then, with pairs up to 16, column sums up to 18: 0.625 / 1.135, 20:
+// 0.627 / 1.139, 22: 0.629 / 1.143, 24: 0.631 / 1.147, 28: 0.635 / 1.152, 32: 0.646 / 1.262, none:
+// 0.630 / 1.233; pairs up to 12 or 14 with column sums up to 20: 0.637 / 1.164, 0.632 / 1.152.
 constexpr int kSparseContributors = 16;
-constexpr int kPartialContributors = 20;
+constexpr int kPartialContributors = 18;
 
 // DEPTH: a depth gradient is given.  NSEG: the tile's list is cut into NSEG segments
 // [s n / NSEG, (s + 1) n / NSEG), each walked by its own CTA (adjacent in launch order), starting
