@@ -4,9 +4,11 @@
 
 One step = depth order -> projection/binning -> blend -> fused L1+SSIM loss and gradient ->
 reverse blend -> chain rule to the Gaussian parameters (+ one NCCL all-reduce of the gradients
-when N > 1).  Default workload: "dynamic128" (16 frames of 128x128, 32768 Gaussians with
-velocities, SH degree 1, one camera per frame on an arc, gradients summed over frames).  With N
-GPUs every rank renders 16 more frames of the same arc (weak scaling) against the same Gaussian set.
+when N > 1).  Default workload: "large1080" (32 views of 1920x1080, 1,000,000 Gaussians, SH degree
+3, cameras on a 4x8 grid of translations, gradients summed over views), the largest of the five
+seeded workloads that fits one GPU.  With N GPUs the views are sharded over the ranks (4 per GPU at
+8) against one replicated Gaussian set: the total work is fixed (strong scaling).  Per-clip
+workloads (clips256) shard whole clips and need no all-reduce.
 
 Prints one JSON line (rank 0).  Metric: Mpix/s (rendered pixels per second, all ranks).
 """
@@ -47,12 +49,14 @@ FWD_BYTES_PER_PAIR, FWD_BYTES_PER_PIXEL = 56, 24
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", default="dynamic128")
+    ap.add_argument("--workload", default="large1080")
     ap.add_argument("--scale", type=float, default=1.0, help="Gaussian-count scale (1 = full workload)")
     ap.add_argument("--image-scale", type=float, default=1.0)
+    ap.add_argument("--views", type=int, default=0,
+                    help="render only the first N views of the workload (a slice for profiling; 0 = all)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--stages", action="store_true", help="print per-stage times to stderr")
@@ -65,33 +69,37 @@ def parse_args():
 # workloads
 
 
-def make_workload(name: str, rank: int, world: int, scale: float, image_scale: float):
+def make_workload(name: str, rank: int, world: int, scale: float, image_scale: float, views: int = 0):
+    """(the whole workload, this rank's shard of its views).  Views are sharded over the ranks;
+    per-clip Gaussian sets keep a clip's frames on one rank."""
     from dynaworld_b200 import synthetic as syn
     from dynaworld_b200.distributed import shard_views
 
-    if name == "dynamic128":
-        return syn.dynamic128(scale=scale, image_scale=image_scale, frames=16, frame_offset=16 * rank,
-                              total_frames=16 * world), "weak"
     full = syn.WORKLOADS[name](scale=scale, image_scale=image_scale)
+    if views:
+        full = full.views(0, min(views, full.n_views))
     shared = full.views_per_set >= full.n_views
     sh = shard_views(full.n_views, world, rank, full.views_per_set, shared_set=shared)
-    return full.views(sh.start, sh.stop), ("strong" if world > 1 else "weak")
+    return full, full.views(sh.start, sh.stop)
 
 
-def workload_config(name, wl, world, scaling):
+def workload_config(name, full, shard, world):
     return {
-        "workload": f"{name}: {wl.n_views * world if scaling == 'weak' else wl.n_views} views/frames at "
-                    f"{wl.height}x{wl.width}, {wl.n_gaussians} Gaussians per set, SH degree {wl.sh_degree}"
-                    + (", velocities" if wl.velocity is not None else ""),
-        "views_per_gpu": wl.n_views,
-        "gaussians": wl.n_gaussians,
-        "height": wl.height,
-        "width": wl.width,
-        "sh_degree": wl.sh_degree,
+        "workload": f"{name}: {full.n_views} views/frames at {full.height}x{full.width}, {full.n_gaussians} "
+                    f"Gaussians per set ({full.n_sets} set{'s' if full.n_sets > 1 else ''}), SH degree {full.sh_degree}"
+                    + (", velocities" if full.velocity is not None else ""),
+        "views": full.n_views,
+        "views_per_gpu": shard.n_views,
+        "gaussians": full.n_gaussians,
+        "height": full.height,
+        "width": full.width,
+        "sh_degree": full.sh_degree,
         "loss": "standard_gs: 0.8*L1 + 0.2*(1-SSIM)/2, 11x11 box window (reference losses.py)",
         "renderer": "exact (dense.py semantics), tile 16, alpha cutoff 2^-25",
-        "parallelism": f"dp{world} over views, NCCL all-reduce of Gaussian gradients" if world > 1 else "single GPU",
-        "l2": "flushed between timed steps (256 MiB write outside the timed events)",
+        "parallelism": (f"dp{world} over views, Gaussians replicated, NCCL all-reduce of the Gaussian gradients"
+                        if full.views_per_set >= full.n_views else f"dp{world} over clips, per-clip gradients")
+        if world > 1 else "single GPU",
+        "l2": "flushed between timed steps (256 MiB write outside the timed events); inputs larger than L2",
     }
 
 
@@ -203,78 +211,156 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------------------
-# CPU port (the oracle's restatement of the reference's dense renderer + loss)
+# CPU ports of the reference's renderers (the oracle's restatements of dense.py + losses.py and of
+# tiled.py), timed on this host's cores on bounded samples of the workload
 
 
-def cpu_sample_time(wl, window: int, frame: int = 0, reps: int = 1):
+# Window side of the dense samples: pixels x Gaussians of about 30-70 M pair evaluations, so one
+# fwd+bwd sample takes seconds.  The dense renderer blends every Gaussian at every pixel, so its
+# cost is the same at every pixel and Mpix/s on a window is Mpix/s on the frame.
+CPU_WINDOW = {"static64": 64, "dynamic128": 32, "multiview384": 16, "large1080": 8, "clips256": 32}
+TILED_SAMPLE_TILES = 24
+TILED_TILE = 8  # tiled.py's default tile size
+
+
+def _view_leaves(wl, frame):
+    s = 0 if wl.views_per_set >= wl.n_views else frame // wl.views_per_set
+    leaves = {k: getattr(wl, k)[s][None].clone().requires_grad_(True)
+              for k in ("means", "log_scales", "quats", "opacity_logits", "sh")}
+    vel = wl.velocity[s][None].clone().requires_grad_(True) if wl.velocity is not None else None
+    return leaves, vel
+
+
+def cpu_sample_time(wl, window: int, frame: int = 0):
     """Seconds for one fwd+bwd of the reference algorithm (dense render of every Gaussian at every
-    pixel + standard_gs loss) on a window x window crop of one frame, on this host's cores."""
+    pixel + standard_gs loss) on the centre window x window of one frame, on this host's cores."""
     from oracle import splat_oracle as so
 
-    W0 = (wl.width - window) // 2
-    H0 = (wl.height - window) // 2
+    x0 = (wl.width - window) // 2
+    y0 = (wl.height - window) // 2
     sl = slice(frame, frame + 1)
-    times = []
-    for _ in range(reps):
-        leaves = {k: getattr(wl, k)[0 if wl.views_per_set >= wl.n_views else frame // wl.views_per_set][None]
-                  .clone().requires_grad_(True) for k in ("means", "log_scales", "quats", "opacity_logits", "sh")}
-        vel = None
-        if wl.velocity is not None:
-            vel = wl.velocity[0][None].clone().requires_grad_(True)
-        t0 = time.perf_counter()
-        raw = so.RawGaussians(leaves["means"], leaves["log_scales"], leaves["quats"], leaves["opacity_logits"],
-                              leaves["sh"], vel)
-        m, s, q, o, rgb = so.activate(raw, wl.times[sl], wl.camera_to_world[sl], 1)
-        key = so.camera_depth_fp32(m.detach(), wl.camera_to_world[sl])
-        img, _, _ = so.render_dense(m, s, q, o, rgb, window, window, wl.fx[sl], wl.fy[sl], wl.cx[sl], wl.cy[sl],
-                                    wl.camera_to_world[sl], sort_key=key, x0=W0, y0=H0)
-        tgt = wl.target[sl][:, :, H0:H0 + window, W0:W0 + window]
-        so.reconstruction_loss_per_image(img, tgt).sum().backward()
-        times.append(time.perf_counter() - t0)
-    return statistics.median(times)
+    leaves, vel = _view_leaves(wl, frame)
+    t0 = time.perf_counter()
+    raw = so.RawGaussians(leaves["means"], leaves["log_scales"], leaves["quats"], leaves["opacity_logits"],
+                          leaves["sh"], vel)
+    m, s, q, o, rgb = so.activate(raw, wl.times[sl], wl.camera_to_world[sl], 1)
+    key = so.camera_depth_fp32(m.detach(), wl.camera_to_world[sl])
+    img, _, _ = so.render_dense(m, s, q, o, rgb, window, window, wl.fx[sl], wl.fy[sl], wl.cx[sl], wl.cy[sl],
+                                wl.camera_to_world[sl], sort_key=key, x0=x0, y0=y0)
+    tgt = wl.target[sl][:, :, y0:y0 + window, x0:x0 + window]
+    so.reconstruction_loss_per_image(img, tgt).sum().backward()
+    return time.perf_counter() - t0
 
 
-def cpu_baseline(wl, budget_s: float = 15.0):
+def cpu_window(name: str, wl) -> int:
+    return min(CPU_WINDOW.get(name, 16), wl.height, wl.width)
+
+
+def cpu_baseline(name, wl, reps: int = 2):
+    """Dense line: the centre window of frame 0, one warm-up on a 4x4 window, median of ``reps``."""
     torch.set_num_threads(os.cpu_count() or 1)
     cores = torch.get_num_threads()
-    t8 = cpu_sample_time(wl, 8)
-    per_px = t8 / 64.0
-    window = int(max(8, min(64, math.sqrt(budget_s / 2.0 / max(per_px, 1e-9)))))
-    t = cpu_sample_time(wl, window, reps=2)
+    window = cpu_window(name, wl)
+    cpu_sample_time(wl, 4)
+    t = statistics.median(cpu_sample_time(wl, window) for _ in range(reps))
     return {
         "value": (window * window) / t / 1e6,
         "unit": UNIT,
         "cores": cores,
         "kind": "port",
-        "sample": f"{window}x{window} centre window of frame 0 ({wl.n_gaussians} Gaussians, all blended at every "
-                  f"pixel as dense.py does), fwd+bwd with the standard_gs loss, median of 2",
+        "sample": f"dense.py + losses.py restated (oracle/splat_oracle.py): {window}x{window} centre window of frame 0 "
+                  f"({wl.n_gaussians} Gaussians, all blended at every pixel as dense.py does), fwd+bwd with the "
+                  f"standard_gs loss, median of {reps}; the same window as the --impl reference arm. Mpix/s "
+                  f"extrapolated from the window (dense cost is the same at every pixel)",
+    }
+
+
+def cpu_tiled_baseline(wl, tiles: int = TILED_SAMPLE_TILES, tile: int = TILED_TILE, seed: int = 0):
+    """Tiled line (tiled.py's faster CPU renderer, restated per tile in oracle/tiled_oracle.py):
+    frame 0's activation, projection and tile bounds over every Gaussian (forward and backward),
+    plus the blend and loss of ``tiles`` random tiles (forward and backward), extrapolated to the
+    frame's tiles."""
+    from oracle import splat_oracle as so
+    from oracle import tiled_oracle as to
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    sl = slice(0, 1)
+    leaves, vel = _view_leaves(wl, 0)
+    t0 = time.perf_counter()
+    raw = so.RawGaussians(leaves["means"], leaves["log_scales"], leaves["quats"], leaves["opacity_logits"],
+                          leaves["sh"], vel)
+    m, s, q, o, rgb = so.activate(raw, wl.times[sl], wl.camera_to_world[sl], 1)
+    proj = to.project_view(m[0], s[0], q[0], o[0], rgb[0], wl.fx[0], wl.fy[0], wl.cx[0], wl.cy[0],
+                           wl.camera_to_world[0])
+    m2, inv, cov, op, rgbp = proj
+    bounds = to.gaussian_bounds(m2.detach(), cov.detach(), op.detach(), wl.height, wl.width)
+    g = torch.Generator().manual_seed(seed)
+    torch.autograd.backward([m2, inv, op, rgbp], [torch.randn(v.shape, generator=g) for v in (m2, inv, op, rgbp)])
+    t_frame_fixed = time.perf_counter() - t0
+
+    tiles_x, tiles_y = -(-wl.width // tile), -(-wl.height // tile)
+    n_tiles = tiles_x * tiles_y
+    pick = torch.randperm(n_tiles, generator=g)[:tiles].tolist()
+    lf = [v.detach().clone().requires_grad_(True) for v in (m2, inv, op, rgbp)]
+    t0 = time.perf_counter()
+    lists = to.tile_lists(*bounds, tile, tiles_x, only=pick)
+    outs, tgts = [], []
+    for tid in pick:
+        ox, oy = (tid % tiles_x) * tile, (tid // tiles_x) * tile
+        if tid in lists:
+            outs.append(to.blend_tile(*lf, lists[tid], ox, oy, tile).clamp(0.0, 1.0).permute(2, 0, 1))
+        else:
+            outs.append(torch.ones(3, tile, tile))
+        tgt = torch.ones(3, tile, tile)
+        h, w = min(tile, wl.height - oy), min(tile, wl.width - ox)
+        tgt[:, :h, :w] = wl.target[0, :, oy:oy + h, ox:ox + w]
+        tgts.append(tgt)
+    loss = so.reconstruction_loss_per_image(torch.stack(outs), torch.stack(tgts)).sum()
+    if loss.requires_grad:
+        loss.backward()
+    t_tiles = time.perf_counter() - t0
+    t_frame = t_frame_fixed + t_tiles * n_tiles / len(pick)
+    return {
+        "value": wl.height * wl.width / t_frame / 1e6,
+        "unit": UNIT,
+        "cores": cores,
+        "kind": "port",
+        "sample": f"tiled.py restated per tile (oracle/tiled_oracle.py, tile {tile}): frame 0's activation, projection "
+                  f"and bounds over all {wl.n_gaussians} Gaussians fwd+bwd ({t_frame_fixed:.2f} s) plus the blend and "
+                  f"standard_gs loss of {len(pick)} random tiles of {n_tiles} fwd+bwd ({t_tiles:.2f} s), extrapolated "
+                  f"to the frame's tiles. The reference's tiled.py pads every tile to the longest list "
+                  f"([tiles, longest, {tile}, {tile}] tensors) and is slower than this restatement; it does not fit "
+                  f"in memory at 1920x1080 with 1M Gaussians",
     }
 
 
 def reference_arm(args, rank, world):
-    """--impl reference: the reference's CPU algorithm (oracle port of dense.py + losses.py)."""
+    """--impl reference: the reference's CPU algorithm (the oracle's port of dense.py + losses.py),
+    one centre window of one frame per step (frames cycled), the window cpu_baseline also uses."""
     if rank != 0:
         return 0
-    wl, scaling = make_workload(args.workload, 0, 1, args.scale, args.image_scale)
+    full, _ = make_workload(args.workload, 0, 1, args.scale, args.image_scale, args.views)
+    wl = full
     torch.set_num_threads(os.cpu_count() or 1)
     cores = torch.get_num_threads()
-    per_px = cpu_sample_time(wl, 8) / 64.0
+    window = cpu_window(args.workload, wl)
     steps = max(1, args.steps)
-    budget = 120.0
-    window = int(max(4, min(64, math.sqrt(budget / (steps + args.warmup) / max(per_px, 1e-9)))))
-    for _ in range(args.warmup):
-        cpu_sample_time(wl, window, frame=0)
+    for k in range(args.warmup):
+        cpu_sample_time(wl, window, frame=k % wl.n_views)
     total = 0.0
     for k in range(steps):
         total += cpu_sample_time(wl, window, frame=k % wl.n_views)
     value = steps * window * window / total / 1e6
-    sample = (f"{window}x{window} centre window of one frame per step ({wl.n_gaussians} Gaussians, dense "
-              f"all-pairs blend + standard_gs loss, fwd+bwd), frames cycled")
+    sample = (f"dense.py + losses.py restated (oracle/splat_oracle.py): {window}x{window} centre window of one frame "
+              f"per step ({wl.n_gaussians} Gaussians, dense all-pairs blend + standard_gs loss, fwd+bwd), frames "
+              f"cycled; Mpix/s extrapolated from the window (dense cost is the same at every pixel)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / steps, "higher_is_better": True,
-        "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(args.workload, wl, 1, scaling),
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args.workload, full, make_workload(args.workload, 0, world, args.scale,
+                                                                     args.image_scale, args.views)[1], world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -347,7 +433,7 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     L = _lib.load()
-    wl, scaling = make_workload(args.workload, rank, world, args.scale, args.image_scale)
+    full, wl = make_workload(args.workload, rank, world, args.scale, args.image_scale, args.views)
     step = Step(wl, dev, world, args.tile, args.segments)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
 
@@ -399,7 +485,7 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms = float(t.item())
-    pixels_per_step = wl.n_views * wl.height * wl.width * world
+    pixels_per_step = full.n_views * full.height * full.width  # every rank's views
     value = pixels_per_step * args.steps / (total_ms / 1e3) / 1e6
 
     # pair count of the workload (for the roofline), from one more forward
@@ -504,15 +590,17 @@ def main():
     stage_share = {k: round(v / sum(means.values()), 4) for k, v in means.items()} if means else {}
 
     if rank == 0:
-        cpu = None
+        cpu = cpu_tiled = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline(wl)
+            cpu = cpu_baseline(args.workload, wl)
+            cpu_tiled = cpu_tiled_baseline(wl)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-            "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": workload_config(args.workload, wl, world, scaling),
-            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args.workload, full, wl, world),
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "cpu_baseline_tiled": cpu_tiled,
+            "clocks": clocks,
             "gpu_launches": int(launches), "stage_ms": {k: round(v, 4) for k, v in means.items()},
             "stage_share": stage_share,
         }

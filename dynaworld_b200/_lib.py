@@ -14,6 +14,8 @@ _lib = None
 _load_error: str | None = None
 
 GSB_OK = 0
+GSB_ERR_NONFINITE = 4
+GSB_ERR_TIMEOUT = 5
 STATUS_NAMES = {
     0: "GSB_OK", 1: "GSB_ERR_SHAPE", 2: "GSB_ERR_WORKSPACE", 3: "GSB_ERR_KEY_OVERFLOW",
     4: "GSB_ERR_NONFINITE", 5: "GSB_ERR_TIMEOUT", 6: "GSB_ERR_CUDA", 7: "GSB_ERR_ARG", 8: "GSB_ERR_CAPACITY",
@@ -23,6 +25,7 @@ SCENE_RAW = 0x1
 SCENE_VELOCITY = 0x2
 SCENE_SH_CLAMP = 0x4
 SCENE_BANK = 0x8
+SCENE_HEAD = 0x10
 BANK_MAX_BASIS = 16
 RENDER_TILED_COMPAT = 0x1
 RENDER_DEPTH = 0x2
@@ -48,6 +51,8 @@ class Scene(C.Structure):
         ("n_sets", C.c_int32), ("n_gaussians", C.c_int32), ("sh_degree", C.c_int32), ("flags", C.c_uint32),
         ("means", vp), ("scales", vp), ("quats", vp), ("opacities", vp), ("colors", vp), ("velocity", vp),
         ("bank_mu", vp), ("bank_rot", vp), ("bank_alpha", vp), ("bank_first", C.c_int32), ("bank_basis", C.c_int32),
+        ("head_xy_extent", C.c_float), ("head_z_min", C.c_float), ("head_z_extent", C.c_float),
+        ("head_scale_init", C.c_float),
     ]
 
 
@@ -130,6 +135,7 @@ SIGNATURES = {
     "gsb_splats2d_preprocess_bwd": (C.c_int, [P(Splats2D), vp, vp, P(Splats2DGrads), vp]),
     "gsb_radix_sort_workspace": (C.c_size_t, [C.c_uint32, C.c_int, C.c_int]),
     "gsb_radix_sort": (C.c_int, [vp, vp, vp, vp, C.c_uint32, C.c_int, C.c_int, C.c_int, vp, C.c_size_t, vp]),
+    "gsb_debug_sort_lookback_timeout": (C.c_int, [vp, vp, C.c_uint32, C.c_uint32, vp, C.c_size_t, vp]),
 }
 
 

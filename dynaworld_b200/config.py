@@ -43,7 +43,8 @@ class B200RendererConfig:
     ellipse_culling: bool = True
     sh_clamp: bool = True
     depth: bool = False
-    check_status: bool = False
+    check_status: bool = False  # wait for binning's status word at once (else: at the next sync point)
+    check_finite: bool = True  # raise FloatingPointError on non-finite projected Gaussians
     backward_segments: int = 0  # 1, 2, 4: pieces of each tile list in the reverse blend; 0: automatic
 
     def __post_init__(self):
@@ -89,6 +90,7 @@ class B200RendererConfig:
             sh_clamp=bool(values.get("sh_clamp", cls.sh_clamp)),
             depth=bool(values.get("depth", cls.depth)),
             check_status=bool(values.get("check_status", cls.check_status)),
+            check_finite=bool(values.get("check_finite", cls.check_finite)),
             backward_segments=int(values.get("backward_segments", cls.backward_segments)),
         )
 

@@ -80,6 +80,11 @@ static gsb_status check_scene(const gsb_scene* s, const gsb_views* v) {
   if ((v->n_views - 1) / v->views_per_set >= s->n_sets) return GSB_ERR_SHAPE;
   if ((s->flags & GSB_SCENE_RAW) && (s->sh_degree < 0 || s->sh_degree > 3)) return GSB_ERR_ARG;
   if (uint64_t(v->n_views) * uint64_t(s->n_gaussians) >= (uint64_t(1) << 30)) return GSB_ERR_SHAPE;
+  if (s->flags & GSB_SCENE_HEAD) {  // the head's raw outputs: its own activation, rgb colours
+    if (s->flags & (GSB_SCENE_RAW | GSB_SCENE_BANK)) return GSB_ERR_ARG;
+    if (!(s->head_scale_init > 0.0f) || !(s->head_xy_extent >= 0.0f) || !(s->head_z_extent >= 0.0f))
+      return GSB_ERR_ARG;
+  }
   if (s->flags & GSB_SCENE_BANK) {  // activated values only, one motion model per scene
     if (s->flags & (GSB_SCENE_RAW | GSB_SCENE_VELOCITY)) return GSB_ERR_ARG;
     if (!s->bank_mu || !s->bank_rot || !s->bank_alpha || !v->basis) return GSB_ERR_ARG;
@@ -99,9 +104,11 @@ static gsb_status check_opts(const gsb_options* o) {
   return GSB_OK;
 }
 
+// Clears the status words of a workspace header: code, detail and a count (used by the projection's
+// non-finite check).
 static int32_t* begin_status(void* ws, cudaStream_t st) {
   auto* h = static_cast<WorkspaceHeader*>(ws);
-  cudaMemsetAsync(h, 0, 8, st);
+  cudaMemsetAsync(h, 0, 12, st);
   return &h->status;
 }
 
@@ -224,7 +231,7 @@ GSB_API gsb_status gsb_preprocess_fwd(const gsb_scene* scene, const gsb_views* v
   int32_t* status = begin_status(workspace, st);
   const RenderConsts rc = make_consts(*views, *opts);
   if ((s = launch_preprocess_fwd(*scene, *views, rc, rank_of, records, reinterpret_cast<int4*>(tile_rects), counts,
-                                 cov2d_out, st)) != GSB_OK)
+                                 cov2d_out, st, status)) != GSB_OK)
     return s;
   return exclusive_scan(counts, n, pair_offsets, scan_ws, scan_bytes, st, status);
 }
@@ -512,6 +519,19 @@ GSB_API gsb_status gsb_radix_sort(const void* keys_in, void* keys_out, const uin
   char* inner = static_cast<char*>(workspace) + align_up(sizeof(WorkspaceHeader));
   return radix_sort(keys_in, keys_out, values_in, values_out, n, key_bytes, bit_lo, bit_hi, inner,
                     workspace_bytes - align_up(sizeof(WorkspaceHeader)), st, status);
+}
+
+GSB_API gsb_status gsb_debug_sort_lookback_timeout(const uint32_t* keys_in, uint32_t* keys_out, uint32_t n,
+                                                   uint32_t spin_limit, void* workspace, size_t workspace_bytes,
+                                                   void* stream) {
+  if (!keys_in || !keys_out || !workspace) return GSB_ERR_ARG;
+  const size_t need = gsb_radix_sort_workspace(n, 4, 0);
+  if (workspace_bytes < need) return GSB_ERR_WORKSPACE;
+  cudaStream_t st = as_stream(stream);
+  int32_t* status = begin_status(workspace, st);
+  char* inner = static_cast<char*>(workspace) + align_up(sizeof(WorkspaceHeader));
+  return sort_lookback_timeout_probe(keys_in, keys_out, n, spin_limit, inner,
+                                     workspace_bytes - align_up(sizeof(WorkspaceHeader)), st, status);
 }
 
 }  // extern "C"

@@ -113,7 +113,7 @@ gsb_status launch_tile_order_keys(const uint32_t* ranges, uint32_t n, uint32_t* 
   const int grid = int(std::min<uint32_t>((n + 255) / 256, 148u * 16u));
   note_launch();
   tile_order_keys_kernel<<<grid, 256, 0, st>>>(ranges, n, keys, vals);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 gsb_status launch_emit(int32_t B, int32_t G, const RenderConsts& rc, int H, int W, const float* records,
@@ -123,7 +123,7 @@ gsb_status launch_emit(int32_t B, int32_t G, const RenderConsts& rc, int H, int 
   const dim3 grid(unsigned((size_t(G) + 255) / 256), unsigned(B));
   note_launch();
   emit_keys_kernel<<<grid, 256, 0, st>>>(G, rc, H, W, records, rects, offsets, n_pairs, keys, hist, passes, status);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 gsb_status launch_tile_ranges(const uint64_t* keys, uint32_t n, const uint32_t* n_dev, uint32_t* ranges,
@@ -133,7 +133,7 @@ gsb_status launch_tile_ranges(const uint64_t* keys, uint32_t n, const uint32_t* 
   const int grid = int(std::min<uint32_t>(std::max<uint32_t>((n + 255) / 256, 1u), 148u * 32u));
   note_launch();
   tile_ranges_kernel<<<grid, 256, 0, st>>>(keys, n, n_dev, ranges, n_ranges, status);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 }  // namespace gsb

@@ -13,6 +13,15 @@ namespace gsb {
 // Counts kernel launches made by this library (diagnostic; read by gsb_kernel_launches()).
 void note_launch();
 
+// Status of the launches just queued: GSB_ERR_CUDA when one failed.  A failed launch's error is
+// cleared from the thread's last-error slot (cudaGetLastError), so it is reported once, by this
+// library, and does not make later calls of this library or of the caller fail as well.
+inline gsb_status launch_status() {
+  if (cudaPeekAtLastError() == cudaSuccess) return GSB_OK;
+  (void)cudaGetLastError();
+  return GSB_ERR_CUDA;
+}
+
 // Radix sort (sort.cu).
 size_t radix_sort_workspace(uint32_t n, int key_bytes, int with_values);
 // n_dev (may be NULL): a device word holding the element count; the sort then uses
@@ -20,6 +29,11 @@ size_t radix_sort_workspace(uint32_t n, int key_bytes, int with_values);
 gsb_status radix_sort(const void* keys_in, void* keys_out, const uint32_t* vals_in, uint32_t* vals_out, uint32_t n,
                       int key_bytes, int bit_lo, int bit_hi, void* ws, size_t ws_bytes, cudaStream_t stream,
                       int32_t* status, const uint32_t* n_dev = nullptr);
+
+// Test hook: one look-back pass whose first partition never runs, so the bounded wait after it
+// runs out (GSB_ERR_TIMEOUT); see sort.cu.
+gsb_status sort_lookback_timeout_probe(const uint32_t* keys_in, uint32_t* keys_out, uint32_t n, uint32_t spin_limit,
+                                       void* ws, size_t ws_bytes, cudaStream_t stream, int32_t* status);
 
 // Segmented sort of 32-bit keys with values (sort.cu): n_seg independent runs of seg_len keys.
 // segmented_sort_prepare clears the workspace's counters and returns the digit histograms
@@ -105,7 +119,7 @@ gsb_status launch_invert_order(const uint32_t* sorted_vals, int32_t B, int32_t G
                                int32_t* rank_of, cudaStream_t st);
 gsb_status launch_preprocess_fwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
                                  const int32_t* rank_of, float* records, int4* rects, uint32_t* counts, float* cov,
-                                 cudaStream_t st);
+                                 cudaStream_t st, int32_t* status);
 gsb_status launch_preprocess_bwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
                                  const int32_t* rank_of, const float* grad2d, const gsb_scene_grads& gr,
                                  cudaStream_t st);

@@ -33,6 +33,7 @@ struct LossArgs {
   float c_l1, c_mse, c_ssim;  // gradient coefficients (already divided by C*H*W)
   float w[16];                // window taps, w[k + half]
   int box;                    // every tap equal (the box window): running sums
+  int plane_base;             // first image plane (image * C + channel) of this launch
   const float* pred;
   const float* target;
   float* dpred;
@@ -57,7 +58,7 @@ __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
   float* ha = gm + 3 * M * M;       // [3][M][kLossTile]
   __shared__ double s_red[3][kLossThreads / 32];
 
-  const int plane = blockIdx.z, b = plane / a.C;
+  const int plane = a.plane_base + int(blockIdx.z), b = plane / a.C;
   const int x0 = blockIdx.x * kLossTile, y0 = blockIdx.y * kLossTile;
   const int H = a.H, W = a.W;
   const size_t poff = size_t(plane) * H * W;
@@ -327,22 +328,48 @@ size_t loss_workspace(int32_t n_images) {
   return c.used;
 }
 
+// Largest grid.z of a launch: image planes beyond it go to further launches of the same kernel.
+constexpr int64_t kMaxGridZ = 65535;
+
 template <int HW>
 static gsb_status launch_loss_t(const LossArgs& a, cudaStream_t st) {
   constexpr int R = kLossTile + 4 * HW, M = kLossTile + 2 * HW;
   const size_t smem = sizeof(float) * (2 * R * R + 5 * R * M + 3 * M * M + 3 * M * kLossTile);
-  if (cudaFuncSetAttribute(loss_kernel<HW>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)))
+  // The shared-memory opt-in is a per-device function attribute: set once per device.
+  static std::mutex mu;
+  static bool ready[64] = {};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
     return GSB_ERR_CUDA;
-  const dim3 grid((a.W + kLossTile - 1) / kLossTile, (a.H + kLossTile - 1) / kLossTile, a.B * a.C);
-  note_launch();
-  loss_kernel<HW><<<grid, kLossThreads, smem, st>>>(a);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  }
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64 || !ready[dev]) {
+      if (cudaFuncSetAttribute(loss_kernel<HW>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem))) {
+        (void)cudaGetLastError();
+        return GSB_ERR_CUDA;
+      }
+      if (dev >= 0 && dev < 64) ready[dev] = true;
+    }
+  }
+  const int64_t planes = int64_t(a.B) * a.C;
+  for (int64_t p0 = 0; p0 < planes; p0 += kMaxGridZ) {
+    LossArgs c = a;
+    c.plane_base = int(p0);
+    const dim3 grid((a.W + kLossTile - 1) / kLossTile, (a.H + kLossTile - 1) / kLossTile,
+                    unsigned(std::min(kMaxGridZ, planes - p0)));
+    note_launch();
+    loss_kernel<HW><<<grid, kLossThreads, smem, st>>>(c);
+  }
+  return launch_status();
 }
 
 gsb_status loss_fwd_bwd(const gsb_loss_options& o, int32_t B, int32_t C, int32_t H, int32_t W, const float* pred,
                         const float* target, float* loss, float* dpred, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (!pred || !target || !loss) return GSB_ERR_ARG;
   if (B <= 0 || C <= 0 || H <= 0 || W <= 0) return GSB_ERR_SHAPE;
+  if (int64_t(B) * C > INT32_MAX || (H + kLossTile - 1) / kLossTile > 65535) return GSB_ERR_SHAPE;
   if (o.type < 0 || o.type > 3) return GSB_ERR_ARG;
   const int ws_size = o.window_size;
   const int half = ws_size / 2;
@@ -395,7 +422,7 @@ gsb_status loss_fwd_bwd(const gsb_loss_options& o, int32_t B, int32_t C, int32_t
     note_launch();
     loss_fixup_kernel<<<grid, 256, 0, st>>>(B, C, H, W, a.c_l1, hit, pred, target, dpred);
   }
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 gsb_status scale_planes(const float* in, const float* scale, float* out, int32_t B, int64_t per, cudaStream_t st) {
@@ -406,7 +433,7 @@ gsb_status scale_planes(const float* in, const float* scale, float* out, int32_t
   const dim3 grid(unsigned(std::min<int64_t>((per / 4 + 255) / 256 + 1, 64)), unsigned(B));
   note_launch();
   scale_planes_kernel<<<grid, 256, 0, st>>>(in, scale, out, per);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 // ---- allocation-free loss entry ----------------------------------------------------------------

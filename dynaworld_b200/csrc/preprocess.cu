@@ -172,13 +172,27 @@ __device__ inline float bank_opacity(float o0, float da) {
   return 1.0f / (1.0f + expf(-(logf(c / (1.0f - c)) + da)));
 }
 
+// Decoder-head activation of the means (GaussianParameterHeads.forward, blocks.py:174-181), each
+// product and sum rounded on its own as torch forms them: (tanh(x) * e, tanh(y) * e,
+// sigmoid(z) * z_extent + z_min).
+__device__ inline float head_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ inline void head_means(const gsb_scene& sc, const float raw[3], float m[3]) {
+  m[0] = __fmul_rn(tanhf(raw[0]), sc.head_xy_extent);
+  m[1] = __fmul_rn(tanhf(raw[1]), sc.head_xy_extent);
+  m[2] = __fadd_rn(__fmul_rn(head_sigmoid(raw[2]), sc.head_z_extent), sc.head_z_min);
+}
+
 // Mean at view time t (velocity) or with the bank offset of basis phi (NULL: none).
 __device__ inline void mean_at(const gsb_scene& sc, size_t pg, float t, const float* phi, float m[3]) {
 #pragma unroll
-  for (int k = 0; k < 3; ++k) {
-    m[k] = sc.means[pg * 3 + k];
-    if (sc.flags & GSB_SCENE_VELOCITY) m[k] = __fadd_rn(m[k], __fmul_rn(t, sc.velocity[pg * 3 + k]));
+  for (int k = 0; k < 3; ++k) m[k] = sc.means[pg * 3 + k];
+  if (sc.flags & GSB_SCENE_HEAD) {
+    const float raw[3] = {m[0], m[1], m[2]};
+    head_means(sc, raw, m);
   }
+#pragma unroll
+  for (int k = 0; k < 3; ++k)
+    if (sc.flags & GSB_SCENE_VELOCITY) m[k] = __fadd_rn(m[k], __fmul_rn(t, sc.velocity[pg * 3 + k]));
   size_t row;
   if (phi && bank_row(sc, pg, row)) {
     float dm[3];
@@ -193,19 +207,20 @@ __device__ inline void mean_at(const gsb_scene& sc, size_t pg, float t, const fl
 __device__ inline GaussParams load_params(const gsb_scene& sc, size_t pg, float t, const float* phi,
                                           BankRotation* rot = nullptr) {
   GaussParams p;
-  const bool raw = sc.flags & GSB_SCENE_RAW;
+  const bool head = sc.flags & GSB_SCENE_HEAD;
+  const bool raw = (sc.flags & GSB_SCENE_RAW) || head;
   mean_at(sc, pg, t, phi, p.m);
 #pragma unroll
   for (int k = 0; k < 3; ++k) {
     const float s = sc.scales[pg * 3 + k];
-    p.s[k] = raw ? expf(s) : s;
+    p.s[k] = raw ? (head ? __fmul_rn(expf(s), sc.head_scale_init) : expf(s)) : s;
   }
   const float4 q4 = reinterpret_cast<const float4*>(sc.quats)[pg];
   p.q[0] = q4.x, p.q[1] = q4.y, p.q[2] = q4.z, p.q[3] = q4.w;
   p.qn_inv = 1.0f;
   if (raw) {
     const float n = sqrtf(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
-    p.qn_inv = 1.0f / n;
+    p.qn_inv = 1.0f / (head ? fmaxf(n, 1e-12f) : n);  // F.normalize's eps (blocks.py:183)
 #pragma unroll
     for (int k = 0; k < 4; ++k) p.q[k] *= p.qn_inv;
   }
@@ -368,6 +383,11 @@ __device__ inline void eval_color(const gsb_scene& sc, size_t pg, const float d[
 }
 
 __device__ inline void load_color(const gsb_scene& sc, size_t pg, const float d[3], float rgb[3]) {
+  if (sc.flags & GSB_SCENE_HEAD) {  // rgb = sigmoid(raw) (blocks.py:185)
+#pragma unroll
+    for (int c = 0; c < 3; ++c) rgb[c] = head_sigmoid(sc.colors[pg * 3 + c]);
+    return;
+  }
   if (!(sc.flags & GSB_SCENE_RAW)) {
     rgb[0] = sc.colors[pg * 3 + 0], rgb[1] = sc.colors[pg * 3 + 1], rgb[2] = sc.colors[pg * 3 + 2];
     return;
@@ -457,7 +477,8 @@ template <bool BANK>
 __global__ void __launch_bounds__(256, 4) preprocess_fwd_kernel(gsb_scene sc, gsb_views vw, RenderConsts rc,
                                                              const int32_t* __restrict__ rank_of,
                                                              float* __restrict__ records, int4* __restrict__ rects,
-                                                             uint32_t* __restrict__ counts, float* __restrict__ cov_out) {
+                                                             uint32_t* __restrict__ counts, float* __restrict__ cov_out,
+                                                             int32_t* __restrict__ status) {
   const size_t G = sc.n_gaussians;
   const size_t total = size_t(vw.n_views) * G;
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
@@ -472,10 +493,24 @@ __global__ void __launch_bounds__(256, 4) preprocess_fwd_kernel(gsb_scene sc, gs
     float rgb[3];
     load_color(sc, pg, P.d, rgb);
 
+    // Non-finite inputs (NaN / inf parameters, overflowing scales) show up as non-finite projected
+    // values: counted here (status word 2), first offender in word 1, GSB_ERR_NONFINITE in word 0.
+    // Such a Gaussian gets no tile and is never blended (the host reports it as the reference's
+    // trainers report a non-finite render).
+    const bool finite = isfinite(P.mx) && isfinite(P.my) && isfinite(P.A) && isfinite(P.B) && isfinite(P.C) &&
+                        isfinite(P.o_eff) && isfinite(P.z) && isfinite(rgb[0]) && isfinite(rgb[1]) &&
+                        isfinite(rgb[2]);
     TileRect rect;
     float tau_f;
     uint32_t count = 0;
-    if (rc.compat) {
+    if (!finite) {
+      if (status) {
+        record_error(status, GSB_ERR_NONFINITE, int(i));
+        atomicAdd(status + 2, 1);
+      }
+      rect = TileRect{1, 1, 0, 0};
+      tau_f = -1.0f;
+    } else if (rc.compat) {
       rect = compat_rect(P.mx, P.my, P.c00, P.c11, P.o_eff, rc.bound_scale, rc.tiled_threshold, vw.height, vw.width,
                          rc.tile);
       count = rect.count();
@@ -684,7 +719,8 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
   static_assert(LPG == 1 || (!BANK && 32 % LPG == 0), "lane groups tile a warp; the bank keeps one lane");
   const size_t G = sc.n_gaussians;
   const size_t total = size_t(sc.n_sets) * G;
-  const bool raw = sc.flags & GSB_SCENE_RAW;
+  const bool head = sc.flags & GSB_SCENE_HEAD;
+  const bool raw = (sc.flags & GSB_SCENE_RAW) || head;
   const bool vel = sc.flags & GSB_SCENE_VELOCITY;
   const bool clamp_sh = sc.flags & GSB_SCENE_SH_CLAMP;
   constexpr int KC = K > 0 ? K : 1;
@@ -827,6 +863,18 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
       }
     }
     if (!valid || sub != 0) continue;
+    if (head && K == 0) {  // the head's view-independent activations, applied to the view sums
+      const float* rm = sc.means + pg * 3;
+      const float tx = tanhf(rm[0]), ty = tanhf(rm[1]), sz = head_sigmoid(rm[2]);
+      am[0] *= sc.head_xy_extent * (1.0f - tx * tx);
+      am[1] *= sc.head_xy_extent * (1.0f - ty * ty);
+      am[2] *= sc.head_z_extent * sz * (1.0f - sz);
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        const float v = head_sigmoid(sc.colors[pg * 3 + c]);
+        acol[c] *= v * (1.0f - v);
+      }
+    }
     if (gr.means)
       for (int k = 0; k < 3; ++k) gr.means[pg * 3 + k] = am[k];
     if (gr.scales)
@@ -988,26 +1036,28 @@ gsb_status launch_depth_keys(const gsb_scene& sc, const gsb_views& vw, uint32_t*
   note_launch();
   if (sc.flags & GSB_SCENE_BANK) depth_key_kernel<true><<<grid, kKeyThreads, 0, st>>>(sc, vw, keys, vals, hist);
   else depth_key_kernel<false><<<grid, kKeyThreads, 0, st>>>(sc, vw, keys, vals, hist);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 gsb_status launch_invert_order(const uint32_t* sorted_vals, int32_t B, int32_t G, int32_t* sorted_ids,
                                int32_t* rank_of, cudaStream_t st) {
   note_launch();
   invert_order_kernel<<<grid_for(size_t(B) * G, 256), 256, 0, st>>>(sorted_vals, B, G, sorted_ids, rank_of);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 gsb_status launch_preprocess_fwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
                                  const int32_t* rank_of, float* records, int4* rects, uint32_t* counts, float* cov,
-                                 cudaStream_t st) {
+                                 cudaStream_t st, int32_t* status) {
   const size_t n = size_t(vw.n_views) * sc.n_gaussians;
   note_launch();
   if (sc.flags & GSB_SCENE_BANK)
-    preprocess_fwd_kernel<true><<<grid_for(n, 256), 256, 0, st>>>(sc, vw, rc, rank_of, records, rects, counts, cov);
+    preprocess_fwd_kernel<true>
+        <<<grid_for(n, 256), 256, 0, st>>>(sc, vw, rc, rank_of, records, rects, counts, cov, status);
   else
-    preprocess_fwd_kernel<false><<<grid_for(n, 256), 256, 0, st>>>(sc, vw, rc, rank_of, records, rects, counts, cov);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+    preprocess_fwd_kernel<false>
+        <<<grid_for(n, 256), 256, 0, st>>>(sc, vw, rc, rank_of, records, rects, counts, cov, status);
+  return launch_status();
 }
 
 template <int K, bool LENS, int LPG>
@@ -1072,7 +1122,7 @@ gsb_status launch_camera_bwd(const gsb_scene& sc, const gsb_views& vw, const Ren
   note_launch();
   if (vw.lens_models) launch_camera_for_degree<true>(deg, grid, sc, vw, rc, rank_of, grad2d, out, st);
   else launch_camera_for_degree<false>(deg, grid, sc, vw, rc, rank_of, grad2d, out, st);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 gsb_status launch_preprocess_bwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
@@ -1086,7 +1136,7 @@ gsb_status launch_preprocess_bwd(const gsb_scene& sc, const gsb_views& vw, const
   note_launch();
   if (vw.lens_models) launch_bwd_for_degree<true>(deg, grid, sc, vw, rc, rank_of, grad2d, gr, st);
   else launch_bwd_for_degree<false>(deg, grid, sc, vw, rc, rank_of, grad2d, gr, st);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 }  // namespace gsb

@@ -680,7 +680,7 @@ gsb_status launch_raster_fwd(const RasterArgs& a, cudaStream_t st) {
   if (a.rc.tile == 16) paired ? fwd_launch<16, 2>(a, st) : fwd_launch<16, 1>(a, st);
   else if (a.rc.tile == 8) paired ? fwd_launch<8, 2>(a, st) : fwd_launch<8, 1>(a, st);
   else return GSB_ERR_ARG;
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 gsb_status launch_raster_bwd(const RasterArgs& a, cudaStream_t st) {
@@ -690,7 +690,7 @@ gsb_status launch_raster_bwd(const RasterArgs& a, cudaStream_t st) {
   if (a.rc.tile == 16) paired ? bwd_launch<16, 2>(a, st) : bwd_launch<16, 1>(a, st);
   else if (a.rc.tile == 8) paired ? bwd_launch<8, 2>(a, st) : bwd_launch<8, 1>(a, st);
   else return GSB_ERR_ARG;
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 int raster_segments(const gsb_views& v, const gsb_options& o) {

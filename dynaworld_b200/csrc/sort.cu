@@ -1,9 +1,9 @@
 // Hand-written LSD radix sort (one-sweep: one read and one write of the keys per 8-bit digit,
 // partition prefixes by decoupled look-back) and a three-phase exclusive prefix scan.
 //
-// Look-back waits are bounded: a partition that waits more than kSpinLimit polls records
-// GSB_ERR_TIMEOUT in the workspace status word and carries on with the prefix it has, so a bug
-// can corrupt the output but never hangs the GPU.  Partitions take their index from an atomic
+// Look-back waits are bounded: a partition that waits more than kSpinLimit polls (or the limit a
+// launch gives in Segments::spin_limit) records GSB_ERR_TIMEOUT in the workspace status word and
+// carries on with the prefix it has, so a bug can corrupt the output but never hangs the GPU.  Partitions take their index from an atomic
 // counter in start order, so a partition only ever waits on partitions that are already running.
 #include <cstring>
 
@@ -112,6 +112,7 @@ struct Segments {
   uint32_t key_stride;         // kSegRuns: the digits are those of (key >> 32) - segment * key_stride
   int32_t* ids_out;            // kSegFixed, last pass (may be NULL): write the values as ids_out[pos]
   int32_t* rank_out;           //   and the inverse rank_out[segment start + value] = pos - segment start
+  uint32_t spin_limit;         // look-back polls before giving up (0: kSpinLimit)
 };
 
 // One LSD pass.  Partitions never straddle a segment and look back only within theirs; with
@@ -229,12 +230,13 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
   uint32_t excl = 0;
   if (part > first_part) {  // partitions of this segment only: first_part's word is inclusive
     int64_t p = int64_t(part) - 1;
-    int spins = 0;
+    const uint32_t spin_limit = sg.spin_limit ? sg.spin_limit : uint32_t(kSpinLimit);
+    uint32_t spins = 0;
     while (p >= 0) {
       const uint32_t w = ld_acquire_u32(lookback + size_t(p) * 256 + tid);
       const uint32_t flag = w & ~kCountMask;
       if (flag == 0u) {
-        if (++spins > kSpinLimit) {
+        if (++spins > spin_limit) {
           record_error(status, GSB_ERR_TIMEOUT, int(part));
           break;
         }
@@ -352,7 +354,7 @@ static gsb_status radix_sort_t(const K* keys_in, K* keys_out, const uint32_t* va
     src_k = dst_k;
     src_v = dst_v;
   }
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 gsb_status radix_sort(const void* keys_in, void* keys_out, const uint32_t* vals_in, uint32_t* vals_out, uint32_t n,
@@ -368,6 +370,39 @@ gsb_status radix_sort(const void* keys_in, void* keys_out, const uint32_t* vals_
     return radix_sort_t<uint64_t>(static_cast<const uint64_t*>(keys_in), static_cast<uint64_t*>(keys_out), vals_in,
                                   vals_out, n, bit_lo, bit_hi, ws, ws_bytes, stream, status, n_dev);
   return GSB_ERR_ARG;
+}
+
+__global__ void set_word_kernel(uint32_t* p, uint32_t v) { *p = v; }
+
+// Test hook for the bounded look-back: one 8-bit pass over n 32-bit keys in which the first
+// partition never runs (the partition counter starts at 1 and the grid has one CTA fewer), so the
+// partition after it waits for a predecessor that never publishes.  Its wait gives up after
+// spin_limit polls and records GSB_ERR_TIMEOUT; the partitions after it wait at most as long.  All
+// writes stay inside keys_out[0, n) (positions are short by the missing partition's counts), and
+// the keys of the first partition are not written.  Workspace: radix_sort_workspace(n, 4, 0).
+gsb_status sort_lookback_timeout_probe(const uint32_t* keys_in, uint32_t* keys_out, uint32_t n, uint32_t spin_limit,
+                                       void* ws, size_t ws_bytes, cudaStream_t stream, int32_t* status) {
+  const uint32_t parts = parts_for(n, 4);
+  if (parts < 2 || n >= (1u << 30)) return GSB_ERR_SHAPE;
+  Carver c(ws, ws_bytes);
+  c.take<WorkspaceHeader>(1);
+  uint32_t* hist = c.take<uint32_t>(size_t(8) * 256);
+  uint32_t* counters = c.take<uint32_t>(8);
+  uint32_t* lookback = c.take<uint32_t>(size_t(8) * parts * 256);
+  if (!c.ok() || !ws) return GSB_ERR_WORKSPACE;
+  const size_t clear_bytes = reinterpret_cast<char*>(lookback + size_t(parts) * 256) - reinterpret_cast<char*>(hist);
+  if (cudaMemsetAsync(hist, 0, clear_bytes, stream)) return launch_status();
+  const int hist_blocks = int(std::min<uint32_t>((n + kSortThreads - 1) / kSortThreads, 148u * 8u));
+  note_launch();
+  radix_hist_kernel<uint32_t><<<hist_blocks, kSortThreads, 0, stream>>>(keys_in, n, 0, 8, 1, hist, nullptr);
+  note_launch();
+  set_word_kernel<<<1, 1, 0, stream>>>(counters, 1u);
+  Segments sg{};
+  sg.spin_limit = spin_limit ? spin_limit : 1u;
+  note_launch();
+  onesweep_kernel<uint32_t, false, kSegNone><<<parts - 1, kSortThreads, 0, stream>>>(
+      keys_in, keys_out, nullptr, nullptr, n, 0, 8, hist, lookback, counters, status, nullptr, sg);
+  return launch_status();
 }
 
 // ---- segmented sort: independent runs of 32-bit keys (the per-view depth order) --------------
@@ -450,7 +485,7 @@ gsb_status segmented_sort_run(const uint32_t* keys_in, uint32_t* keys_out, const
     src_k = dst_k;
     src_v = dst_v;
   }
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 // ---- pair keys: runs of one view each, sorted by tile ------------------------------------------
@@ -598,7 +633,7 @@ gsb_status pair_sort_run(const uint64_t* keys_in, uint64_t* keys_out, uint32_t c
                                                                  status);
     *ranges_done = true;
   }
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 // ---- exclusive prefix scan of uint32 counts (three phases, no inter-block waits) -------------
@@ -704,7 +739,7 @@ gsb_status exclusive_scan(const uint32_t* counts, uint32_t n, uint32_t* offsets,
   scan_blocksums_kernel<<<1, 1024, 0, stream>>>(sums, nb, offsets + n, status);
   note_launch();
   scan_apply_kernel<<<nb, kScanThreads, 0, stream>>>(counts, n, sums, offsets);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 }  // namespace gsb

@@ -169,7 +169,7 @@ gsb_status launch_order_keys_2d(const gsb_splats2d& sp, uint32_t* keys, uint32_t
                   unsigned(sp.n_views));
   note_launch();
   order_keys_2d_kernel<<<grid, kOrderThreads, 0, st>>>(sp.depths, sp.n_gaussians, keys, vals, hist);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 gsb_status launch_preprocess_2d(const gsb_splats2d& sp, int H, int W, const RenderConsts& rc, const int32_t* rank_of,
@@ -177,14 +177,14 @@ gsb_status launch_preprocess_2d(const gsb_splats2d& sp, int H, int W, const Rend
   note_launch();
   preprocess_2d_kernel<<<grid_for(size_t(sp.n_views) * sp.n_gaussians), 256, 0, st>>>(sp, H, W, rc, rank_of, records,
                                                                                        rects, counts);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 gsb_status launch_preprocess_2d_bwd(const gsb_splats2d& sp, const int32_t* rank_of, const float* grad2d,
                                     const gsb_splats2d_grads& gr, cudaStream_t st) {
   note_launch();
   preprocess_2d_bwd_kernel<<<grid_for(size_t(sp.n_views) * sp.n_gaussians), 256, 0, st>>>(sp, rank_of, grad2d, gr);
-  return cudaPeekAtLastError() == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+  return launch_status();
 }
 
 }  // namespace gsb

@@ -56,6 +56,8 @@ class SceneSpec:
     sh_clamp: bool
     bank_basis: int = 0  # dynamic bank: temporal basis functions M (0: no bank)
     bank_first: int = 0  # dynamic bank: Gaussians before this index are static
+    # decoder-head activation (xy_extent, z_min, z_extent, scale_init) of the head's raw outputs, or None
+    head: tuple[float, float, float, float] | None = None
 
 
 @dataclass
@@ -111,14 +113,19 @@ class _Words:
         return self.buf[: self.n].tolist()
 
 
-def read_words(words: list[torch.Tensor]) -> _Words:
+def read_words(words: list[torch.Tensor], own_buffer: bool = False) -> _Words:
     """Queues device->host copies of single int32 words (all on one device) behind that device's
     current stream and returns at once; .wait() blocks until they have landed.  One pinned buffer
-    per host thread (each wait completes before that thread queues its next read)."""
-    buf = getattr(_PINNED, "buf", None)
-    if buf is None or buf.numel() < len(words):
-        buf = torch.empty(max(8, len(words)), dtype=torch.int32, pin_memory=True)
-        _PINNED.buf = buf
+    per host thread (each wait completes before that thread queues its next read), or with
+    ``own_buffer`` a pinned buffer of the read's own (for reads that are waited for later, possibly
+    by another thread)."""
+    if own_buffer:
+        buf = torch.empty(max(4, len(words)), dtype=torch.int32, pin_memory=True)
+    else:
+        buf = getattr(_PINNED, "buf", None)
+        if buf is None or buf.numel() < len(words):
+            buf = torch.empty(max(8, len(words)), dtype=torch.int32, pin_memory=True)
+            _PINNED.buf = buf
     dev = words[0].device
     with torch.cuda.device(dev):
         for i, w in enumerate(words):
@@ -126,6 +133,30 @@ def read_words(words: list[torch.Tensor]) -> _Words:
         ev = torch.cuda.Event()
         ev.record(torch.cuda.current_stream(dev))
     return _Words(buf, len(words), ev)
+
+
+# Status words of stages whose result the host does not wait for (binning's sort and emission):
+# read into pinned memory behind the kernels and checked at the device's next synchronisation
+# point, i.e. when the backward of that frame has been queued or when the next forward waits for
+# its pair count, whichever comes first.  No extra host-device synchronisation.
+_PENDING: dict[int, list[tuple[str, _Words]]] = {}
+_PENDING_LOCK = threading.Lock()
+
+
+def _defer_status(dev: torch.device, name: str, word: torch.Tensor) -> None:
+    words = read_words([word], own_buffer=True)
+    with _PENDING_LOCK:
+        _PENDING.setdefault(dev.index, []).append((name, words))
+
+
+def check_pending(dev: torch.device) -> None:
+    """Waits for the deferred status words of ``dev`` and raises on the first error among them."""
+    with _PENDING_LOCK:
+        pending = _PENDING.pop(dev.index, [])
+    for name, words in pending:
+        code = words.wait()[0]
+        if code != _lib.GSB_OK:
+            raise _lib.GsbError(f"{name} (reported at the next synchronisation point)", code)
 
 
 def _f32(t: torch.Tensor | None) -> torch.Tensor | None:
@@ -141,7 +172,10 @@ def scene_struct(spec: SceneSpec, means, scales, quats, opacities, colors, veloc
     s.n_gaussians = spec.n_gaussians
     s.sh_degree = spec.sh_degree
     flags = 0
-    if spec.raw:
+    if spec.head is not None:
+        flags |= _lib.SCENE_HEAD
+        s.head_xy_extent, s.head_z_min, s.head_z_extent, s.head_scale_init = (float(v) for v in spec.head)
+    elif spec.raw:
         flags |= _lib.SCENE_RAW
         if spec.sh_clamp:
             flags |= _lib.SCENE_SH_CLAMP
@@ -223,7 +257,8 @@ def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, n
     # The one host synchronisation of the forward: the pair count plus the device status words,
     # copied into pinned memory behind the kernels.  Binning reads the count on the device, so with
     # a capacity known from earlier frames of this shape it and the blend are queued first.
-    head = read_words([offsets[-1:], ws1.view(torch.int32)[:1], ws2.view(torch.int32)[:1]])
+    ws2w = ws2.view(torch.int32)
+    head = read_words([offsets[-1:], ws1.view(torch.int32)[:1], ws2w[0:1], ws2w[1:2], ws2w[2:3]])
     n_tiles = -(-H // cfg.tile_size) * -(-W // cfg.tile_size)
     ranges = torch.empty(B * n_tiles * 2, dtype=torch.int32, device=dev)
     order = torch.empty(B * n_tiles, dtype=torch.int32, device=dev)
@@ -253,14 +288,24 @@ def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, n
     if cap is not None:
         keys, ws3 = bin_and_blend(cap)
     head = head.wait()
+    check_pending(dev)  # earlier frames' deferred status words have landed by now
     n_pairs = head[0] & 0xFFFFFFFF
-    for name, code in (("gsb_depth_order", head[1]), ("gsb_preprocess_fwd", head[2])):
-        _lib.check(name, code)
+    _lib.check("gsb_depth_order", head[1])
+    if head[2] == _lib.GSB_ERR_NONFINITE:
+        if cfg.check_finite:
+            first = head[3]
+            raise FloatingPointError(
+                f"Non-finite render input: {head[4]} projected Gaussians are not finite (first: view "
+                f"{first // G}, Gaussian {first % G}).")
+    else:
+        _lib.check("gsb_preprocess_fwd", head[2])
     if cap is None or n_pairs > cap:  # no guess yet, or too small: again with the count
         keys, ws3 = bin_and_blend(n_pairs)
     _PAIR_CAPACITY[shape] = _next_capacity(n_pairs, cap)
     if cfg.check_status:
         _lib.check("gsb_bin", int(ws3.view(torch.int32)[0].item()))
+    else:
+        _defer_status(dev, "gsb_bin", ws3.view(torch.int32)[:1])
     state = FrameState(rank_of, records, keys, ranges, order, pixel_t, pixel_state, n_pairs, ckpt)
     return image, alpha, depth, state
 
@@ -301,6 +346,7 @@ def backward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, 
     with _stage("preprocess_bwd"):
         _lib.check("gsb_preprocess_bwd", L.gsb_preprocess_bwd(scene, views, opts, state.rank_of.data_ptr(),
                                                               grad2d.data_ptr(), g, st))
+    check_pending(dev)  # the forward's binning status, while the GPU runs the kernels just queued
     if camera:
         out["cam_intrinsics"] = torch.empty(B, 4, dtype=torch.float32, device=dev)
         out["cam_camera_to_world"] = torch.empty(B, 4, 4, dtype=torch.float32, device=dev)

@@ -6,8 +6,12 @@
   Gaussians [K,G,C], one camera per frame, image [K,3,H,W] (or [3,H,W]).
 * ``render_b200``: raw parameters (means, log-scales, quaternions, opacity logits, SH, optional
   velocity with per-view times) shared by groups of views; returns image, alpha and depth.
+* ``render_b200_head``: the decoder head's raw outputs (GaussianParameterHeads, src/train/
+  gs_models/blocks.py:172-186) with the head's activation fused into the projection.
 """
 from __future__ import annotations
+
+from dataclasses import dataclass
 
 import torch
 
@@ -172,5 +176,82 @@ def render_b200(
         opacities=opacity_logits.reshape(S, G), colors=sh, velocity=velocity,
         intrinsics=intrinsics.reshape(B, 4), camera_to_world=camera_to_world, times=times,
         lens=lens_tensors(lens_models, distortion, B, means.device),
+    )
+    return image, alpha, (depth if config.depth else None)
+
+
+@dataclass(frozen=True)
+class HeadActivation:
+    """Constants of the decoder head's output activation (GaussianParameterHeads, src/train/
+    gs_models/blocks.py:110-186): xy bound, z range and the scale multiplier."""
+
+    xy_extent: float = 1.5
+    z_min: float = 0.5
+    z_max: float = 2.5
+    scale_init: float = 0.05
+
+    @classmethod
+    def from_heads(cls, heads) -> "HeadActivation":
+        """Reads a GaussianParameterHeads-like module's xy_extent, z_min, z_extent, scale_init."""
+        return cls(float(heads.xy_extent), float(heads.z_min), float(heads.z_min) + float(heads.z_extent),
+                   float(heads.scale_init))
+
+    def constants(self) -> tuple[float, float, float, float]:
+        return (self.xy_extent, self.z_min, self.z_max - self.z_min, self.scale_init)
+
+
+def render_b200_head(
+    xyz_raw: torch.Tensor,
+    scale_raw: torch.Tensor,
+    rot_raw: torch.Tensor,
+    opacity_raw: torch.Tensor,
+    rgb_raw: torch.Tensor,
+    *,
+    head: HeadActivation,
+    intrinsics: torch.Tensor,
+    camera_to_world: torch.Tensor,
+    height: int,
+    width: int,
+    velocity: torch.Tensor | None = None,
+    times: torch.Tensor | None = None,
+    views_per_set: int | None = None,
+    near_plane: float = MIN_RENDER_DEPTH,
+    config: B200RendererConfig | None = None,
+    lens_models=None,
+    distortion=None,
+):
+    """Render straight from the decoder head's raw outputs [S,G,*] (the five head MLPs' reshaped
+    outputs of GaussianParameterHeads.forward, blocks.py:172-186), with the head's activation fused
+    into the projection, so the activated [S,G,*] tensors are never written:
+
+        xyz = (tanh(x) xy_extent, tanh(y) xy_extent, sigmoid(z) (z_max - z_min) + z_min)
+        scales = exp(scale_raw) scale_init, quats = normalize(rot_raw), opacity = sigmoid,
+        rgb = sigmoid(rgb_raw)
+
+    Gradients flow to the five raw tensors (and ``velocity``).  Sets, views, lenses and outputs as
+    render_b200."""
+    config = config or B200RendererConfig()
+    if xyz_raw.ndim == 2:
+        xyz_raw, scale_raw, rot_raw = xyz_raw.unsqueeze(0), scale_raw.unsqueeze(0), rot_raw.unsqueeze(0)
+        opacity_raw, rgb_raw = opacity_raw.unsqueeze(0), rgb_raw.unsqueeze(0)
+        velocity = None if velocity is None else velocity.unsqueeze(0)
+    S, G = int(xyz_raw.shape[0]), int(xyz_raw.shape[1])
+    B = int(camera_to_world.shape[0])
+    if rgb_raw.shape[-1] != 3 or rgb_raw.numel() != S * G * 3:
+        raise ValueError(f"rgb_raw must be [S,G,3], got {tuple(rgb_raw.shape)}")
+    if views_per_set is None:
+        views_per_set = B if S == 1 else B // S
+    if views_per_set <= 0 or (B - 1) // views_per_set >= S:
+        raise ValueError(f"{B} views with views_per_set={views_per_set} need more than {S} sets")
+    if velocity is not None and times is None:
+        raise ValueError("velocity needs per-view times")
+    sspec = SceneSpec(n_sets=S, n_gaussians=G, raw=False, sh_degree=0, velocity=velocity is not None,
+                      sh_clamp=False, head=head.constants())
+    vspec = ViewSpec(n_views=B, views_per_set=views_per_set, height=int(height), width=int(width))
+    image, alpha, depth = render_scene(
+        sspec, vspec, config, near_plane, means=xyz_raw, scales=scale_raw, quats=rot_raw,
+        opacities=opacity_raw.reshape(S, G), colors=rgb_raw.reshape(S, G, 3), velocity=velocity,
+        intrinsics=intrinsics.reshape(B, 4), camera_to_world=camera_to_world, times=times,
+        lens=lens_tensors(lens_models, distortion, B, xyz_raw.device),
     )
     return image, alpha, (depth if config.depth else None)

@@ -22,7 +22,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from .render import FrameState, _stage, _stream, _ws, checkpoint_buffer, read_words
+from .render import FrameState, _defer_status, _stage, _stream, _ws, check_pending, checkpoint_buffer, read_words
 
 CONIC = _lib.SPLATS2D_CONIC
 PACKED = _lib.SPLATS2D_PACKED
@@ -114,6 +114,7 @@ def forward_stages_2d(fmt: int, B: int, G: int, H: int, W: int, opt: Splat2DOpti
     pixel_state = torch.empty(B, H, W, dtype=torch.int32, device=dev)
     ckpt = checkpoint_buffer(frame, opts, dev)
     head = head.wait()
+    check_pending(dev)
     n_pairs = head[0] & 0xFFFFFFFF
     for name, code in (("gsb_splats2d_order", head[1]), ("gsb_splats2d_preprocess", head[2])):
         _lib.check(name, code)
@@ -128,6 +129,7 @@ def forward_stages_2d(fmt: int, B: int, G: int, H: int, W: int, opt: Splat2DOpti
                                                       ranges.data_ptr(), order.data_ptr(), image.data_ptr(),
                                                       alpha.data_ptr(), None, pixel_t.data_ptr(),
                                                       pixel_state.data_ptr(), _lib.ptr(ckpt), st))
+    _defer_status(dev, "gsb_bin", ws3.view(torch.int32)[:1])
     state = FrameState(rank_of, records, keys, ranges, order, pixel_t, pixel_state, n_pairs, ckpt)
     return image, alpha, state
 

@@ -61,6 +61,13 @@ typedef enum gsb_status {
 #define GSB_SCENE_BANK 0x8u     /* dynamic Gaussian bank (activated mode only, no velocity): see
                                    gsb_scene.bank_mu */
 #define GSB_BANK_MAX_BASIS 16   /* temporal basis functions a bank may have */
+#define GSB_SCENE_HEAD 0x10u    /* the decoder head's raw outputs (GaussianParameterHeads.forward,
+                                   gs_models/blocks.py:172-186), activated here:
+                                     means  = (tanh(x) xy_extent, tanh(y) xy_extent,
+                                               sigmoid(z) z_extent + z_min)
+                                     scales = exp(raw) scale_init, quats = raw / max(|raw|, 1e-12),
+                                     opacities = sigmoid(raw), colors = sigmoid(raw) [S,G,3]
+                                   (gsb_scene.head_*; not with RAW or BANK; velocity allowed) */
 
 /* Render flags (gsb_options.flags). */
 #define GSB_RENDER_TILED_COMPAT 0x1u /* tiled.py bounds (bound_scale, 1/255 threshold) and
@@ -96,6 +103,12 @@ typedef struct gsb_scene {
   const float* bank_alpha; /* [S, G - bank_first, M]    opacity-logit offsets */
   int32_t bank_first;      /* 0 <= bank_first <= G */
   int32_t bank_basis;      /* M, 1 .. GSB_BANK_MAX_BASIS */
+  /* Decoder-head constants (GSB_SCENE_HEAD), the GaussianParameterHeads attributes of the same
+     names (blocks.py:120-123): z_extent = z_max - z_min. */
+  float head_xy_extent;
+  float head_z_min;
+  float head_z_extent;
+  float head_scale_init;
 } gsb_scene;
 
 /* Lens models (gsb_views.lens_models), the CameraSpec lens_model values of camera.py:7-31. */
@@ -200,7 +213,11 @@ GSB_API size_t gsb_preprocess_workspace(const gsb_views* views, int32_t n_gaussi
    inv_cov01+inv_cov10, inv_cov11; tau: the q above which alpha < alpha_cutoff).  tile_rects[(b*G + r)*4 ..] = tx0, ty0, tx1, ty1 (inclusive;
    empty when tx0 > tx1).  pair_offsets[B*G + 1]: exclusive prefix of the per-Gaussian pair
    counts; pair_offsets[B*G] is the total (<= 2^30, else GSB_ERR_KEY_OVERFLOW at gsb_bin).
-   cov2d_out ([B*G*3] c00, c01, c11 in depth order) may be NULL. */
+   cov2d_out ([B*G*3] c00, c01, c11 in depth order) may be NULL.  Non-finite projected values
+   (NaN / inf parameters, overflowing scales) are counted on the device: the workspace's first
+   three int32 words then hold GSB_ERR_NONFINITE, the first offending b*G + g, and the count (read
+   them after the stream is synchronised; gsb_read_status gives the first).  Such a Gaussian is
+   never blended. */
 GSB_API gsb_status gsb_preprocess_fwd(const gsb_scene* scene, const gsb_views* views,
                                       const gsb_options* opts, const int32_t* rank_of,
                                       float* records, int32_t* tile_rects, uint32_t* pair_offsets,
@@ -256,9 +273,12 @@ GSB_API gsb_status gsb_loss_fwd_bwd(const gsb_loss_options* lopts, int32_t n_ima
    the process exits.  Limit: n_images <= GSB_LOSS_NOALLOC_MAX_IMAGES, larger batches return
    GSB_ERR_SHAPE before anything is launched.  The first call on each device looks up the array's
    device address with that device current and caches it: make that first call before any stream
-   capture.  Every call uses the same array; each call clears the sums it needs, but calls that
-   overlap on the GPU (several streams or host threads at once) race on it and give wrong results,
-   so order them on one stream. */
+   capture.  The cached address belongs to the device's primary context (the one the CUDA runtime
+   and torch use): it stays valid while that context lives, so do not call this entry after
+   cudaDeviceReset or from a context of your own made current with the driver API.  Every call
+   uses the same array; each call clears the sums it needs, but calls that overlap on the GPU
+   (several streams or host threads at once) race on it and give wrong results, so order them on
+   one stream. */
 #define GSB_LOSS_NOALLOC_MAX_IMAGES 4096
 GSB_API gsb_status gsb_loss_fwd_bwd_noalloc(const gsb_loss_options* lopts, int32_t n_images,
                                             int32_t channels, int32_t height, int32_t width,
@@ -364,6 +384,16 @@ GSB_API gsb_status gsb_radix_sort(const void* keys_in, void* keys_out, const uin
                                   uint32_t* values_out, uint32_t n, int key_bytes, int bit_lo,
                                   int bit_hi, void* workspace, size_t workspace_bytes,
                                   void* stream);
+/* Test hook for the bounded look-back waits of the radix sort (no counterpart in the reference):
+   one 8-bit pass over n (> 2048) uint32 keys in which the first partition never runs, so the
+   partition after it waits for a predecessor that never publishes.  The wait gives up after
+   spin_limit polls (0 means 1) and records GSB_ERR_TIMEOUT (gsb_read_status on the workspace);
+   every kernel returns and nothing is written outside keys_out[0, n).  keys_out is not sorted.
+   Workspace: gsb_radix_sort_workspace(n, 4, 0) bytes. */
+GSB_API gsb_status gsb_debug_sort_lookback_timeout(const uint32_t* keys_in, uint32_t* keys_out,
+                                                   uint32_t n, uint32_t spin_limit,
+                                                   void* workspace, size_t workspace_bytes,
+                                                   void* stream);
 
 #ifdef __cplusplus
 }

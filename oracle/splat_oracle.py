@@ -142,6 +142,17 @@ def activate(
     return means_t, scales, quats, opac, rgb
 
 
+def activate_head(xyz_raw, scale_raw, rot_raw, opacity_raw, rgb_raw, xy_extent, z_min, z_max, scale_init):
+    """GaussianParameterHeads.forward's output activation (src/train/gs_models/blocks.py:172-186)
+    restated: xyz = (tanh(x, y) * xy_extent, sigmoid(z) * (z_max - z_min) + z_min), scales =
+    exp * scale_init, quats = F.normalize, opacity = sigmoid, rgb = sigmoid."""
+    xyz = torch.cat([torch.tanh(xyz_raw[..., :2]) * xy_extent,
+                     torch.sigmoid(xyz_raw[..., 2:]) * (z_max - z_min) + z_min], dim=-1)
+    scales = torch.exp(scale_raw) * scale_init
+    quats = F.normalize(rot_raw, p=2, dim=-1)
+    return xyz, scales, quats, torch.sigmoid(opacity_raw), torch.sigmoid(rgb_raw)
+
+
 def quat_to_rotation(q: torch.Tensor) -> torch.Tensor:
     """Unnormalised-safe rotation formula of common.py:169-179 (q = r,i,j,k)."""
     qr, qi, qj, qk = q.unbind(-1)

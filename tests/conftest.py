@@ -59,6 +59,26 @@ def golden_case(request):
     return request.param, load_golden(request.param)
 
 
+# Per-element gradient tolerance: |g - g_ref| <= GRAD_RTOL * |g_ref| + GRAD_ATOL_FRAC * max|g_ref|.
+# The floor is one part in 1e5 of the tensor's largest entry: entries that are sums of terms
+# cancelling far below the tensor's scale carry float32 rounding of the terms (not of the sum),
+# in the reference's own float32 computation as in this one.
+GRAD_RTOL = 1e-3
+GRAD_ATOL_FRAC = 1e-5
+
+
+def grad_close_elementwise(got: torch.Tensor, ref: torch.Tensor, rtol: float = GRAD_RTOL,
+                           atol_frac: float = GRAD_ATOL_FRAC):
+    """Per-element gradient parity: every |got - ref| <= rtol * |ref| + atol_frac * max |ref|.
+    Returns (ok, worst excess ratio err / bound, the scale max |ref|)."""
+    got = got.detach().double().cpu()
+    ref = ref.detach().double().cpu()
+    scale = ref.abs().max().item()
+    bound = rtol * ref.abs() + atol_frac * max(scale, 1e-30)
+    ratio = ((got - ref).abs() / bound).max().item() if ref.numel() else 0.0
+    return ratio <= 1.0, ratio, scale
+
+
 def grad_close(got: torch.Tensor, ref: torch.Tensor, rel: float = 1e-3):
     """Gradient parity: max |got - ref| <= rel * max |ref| (the tensor's own scale)."""
     got = got.detach().double().cpu()

@@ -1,6 +1,7 @@
 """Generates the golden fixtures of tests/golden/ from the reference implementation itself.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference PATH [--only scenes losses tiled_grads]
+    (or DYNAWORLD_REFERENCE=PATH python tests/golden/make_golden.py)
 
 Imports the reference's src/train modules (renderers.dense, renderers.common, renderers.tiled,
 losses) from a checkout of nbardy/dynaworld and records, for seeded synthetic scenes, what the
@@ -20,6 +21,7 @@ from __future__ import annotations
 
 import argparse
 import math
+import os
 import sys
 from pathlib import Path
 
@@ -186,6 +188,51 @@ def edge_workload() -> syn.Workload:
                         torch.eye(4)[None], torch.zeros(1), 1, 48, 40, target)
 
 
+def tiled_grad_cases(R) -> dict:
+    """Gradients of the reference's tiled renderer (render_pytorch_3dgs_tiled, tiled.py:74-198,
+    one call per view) under the standard_gs loss of all views, for the five golden scenes and tile
+    sizes 8 and 16: with respect to the activated tensors of the render call (independent leaves per
+    view; static64, dynamic128_small and edge) and, through the raw-parameter front end, to the raw
+    parameters (all five)."""
+    out = {}
+    for case, wl in (("static64", syn.static64()), ("dynamic128_small", syn.dynamic128(scale=1 / 16, image_scale=0.5,
+                                                                                        frames=2)),
+                     ("multiview384_small", syn.multiview384(scale=0.01, image_scale=1 / 6, views=2)),
+                     ("clips256_small", syn.clips256(scale=1 / 32, image_scale=0.25, clips=2, frames=2)),
+                     ("edge", edge_workload())):
+        for ts in (8, 16):
+            raw = {k: getattr(wl, k).clone().requires_grad_(True)
+                   for k in ("means", "log_scales", "quats", "opacity_logits", "sh")}
+            vel = wl.velocity.clone().requires_grad_(True) if wl.velocity is not None else None
+            rg = so.RawGaussians(raw["means"], raw["log_scales"], raw["quats"], raw["opacity_logits"], raw["sh"], vel)
+            act = so.activate(rg, wl.times, wl.camera_to_world, wl.views_per_set)
+
+            def render(m, s, q, o, rgb):
+                return torch.stack([R["tiled"](m[b], s[b], q[b], o[b], rgb[b], wl.height, wl.width, float(wl.fx[b]),
+                                               float(wl.fy[b]), float(wl.cx[b]), float(wl.cy[b]), tile_size=ts,
+                                               camera_to_world=wl.camera_to_world[b])
+                                    for b in range(wl.n_views)])
+
+            img = render(*act)
+            loss = R["loss"](img, wl.target, LOSS_CFG)
+            loss.sum().backward()
+            key = f"{case}_t{ts}"
+            out[f"{key}_image"] = img.detach()
+            out[f"{key}_loss"] = loss.detach()
+            for k, v in raw.items():
+                out[f"{key}_grad_{k}"] = v.grad
+            if vel is not None:
+                out[f"{key}_grad_velocity"] = vel.grad
+            if case in ("multiview384_small", "clips256_small"):
+                continue  # activated-input gradients of the three smaller scenes suffice
+            leaves = [t.detach().clone().requires_grad_(True) for t in act]
+            R["loss"](render(*leaves), wl.target, LOSS_CFG).sum().backward()
+            for name, v in zip(("xyz", "scales", "quats", "opacities", "rgbs"), leaves):
+                out[f"{key}_grad_act_{name}"] = v.grad
+            print(f"tiled gradients: {key}", flush=True)
+    return out
+
+
 def loss_cases(R) -> dict:
     g = torch.Generator().manual_seed(5)
     out = {}
@@ -208,33 +255,44 @@ def loss_cases(R) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DYNAWORLD_REFERENCE"),
+                    help="checkout of nbardy/dynaworld (default: $DYNAWORLD_REFERENCE)")
+    ap.add_argument("--only", nargs="*", default=["scenes", "losses", "tiled_grads"],
+                    choices=["scenes", "losses", "tiled_grads"])
     args = ap.parse_args()
+    if not args.reference:
+        raise SystemExit("give the reference checkout with --reference PATH or DYNAWORLD_REFERENCE")
     torch.set_num_threads(8)
     R = ref_modules(Path(args.reference))
 
-    wl = syn.static64()
-    save("static64", wl, render_case(R, wl))
+    if "scenes" in args.only:
+        wl = syn.static64()
+        save("static64", wl, render_case(R, wl))
 
-    wl = syn.dynamic128(scale=1 / 16, image_scale=0.5, frames=2)
-    save("dynamic128_small", wl, render_case(R, wl))
+        wl = syn.dynamic128(scale=1 / 16, image_scale=0.5, frames=2)
+        save("dynamic128_small", wl, render_case(R, wl))
 
-    wl = syn.multiview384(scale=0.01, image_scale=1 / 6, views=2)
-    save("multiview384_small", wl, render_case(R, wl))
+        wl = syn.multiview384(scale=0.01, image_scale=1 / 6, views=2)
+        save("multiview384_small", wl, render_case(R, wl))
 
-    wl = syn.clips256(scale=1 / 32, image_scale=0.25, clips=2, frames=2)
-    save("clips256_small", wl, render_case(R, wl))
+        wl = syn.clips256(scale=1 / 32, image_scale=0.25, clips=2, frames=2)
+        save("clips256_small", wl, render_case(R, wl))
 
-    wl = edge_workload()
-    save("edge", wl, render_case(R, wl))
+        wl = edge_workload()
+        save("edge", wl, render_case(R, wl))
 
-    # full-size dynamic128 (G=32768, 128x128): image of a 32x32 window of frame 5 only
-    wl = syn.dynamic128().views(5, 6)
-    save("dynamic128_crop", wl, render_case(R, wl, crop=(48, 40, 32, 32), with_grads=False, tiles=()),
-         extra={"crop": torch.tensor([48, 40, 32, 32])}, lean=True)
+        # full-size dynamic128 (G=32768, 128x128): image of a 32x32 window of frame 5 only
+        wl = syn.dynamic128().views(5, 6)
+        save("dynamic128_crop", wl, render_case(R, wl, crop=(48, 40, 32, 32), with_grads=False, tiles=()),
+             extra={"crop": torch.tensor([48, 40, 32, 32])}, lean=True)
 
-    np.savez_compressed(HERE / "losses.npz", **to_np(loss_cases(R)))
-    print("wrote losses.npz", flush=True)
+    if "losses" in args.only:
+        np.savez_compressed(HERE / "losses.npz", **to_np(loss_cases(R)))
+        print("wrote losses.npz", flush=True)
+
+    if "tiled_grads" in args.only:
+        np.savez_compressed(HERE / "tiled_grads.npz", **to_np(tiled_grad_cases(R)))
+        print("wrote tiled_grads.npz", flush=True)
 
 
 if __name__ == "__main__":

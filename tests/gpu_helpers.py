@@ -49,6 +49,27 @@ def render_raw(wl, cfg: B200RendererConfig | None = None, *, grads=True, loss=Tr
     return out
 
 
+def render_vjp(wl, cotangent: torch.Tensor, cfg: B200RendererConfig | None = None, device=DEV):
+    """render_b200 on the GPU, then the backward of sum(cotangent * image) ([B,3,H,W] cotangent);
+    returns the image and the raw-parameter gradients as CPU tensors."""
+    cfg = cfg or B200RendererConfig()
+    leaves = {k: getattr(wl, k).to(device).requires_grad_(True) for k in
+              ("means", "log_scales", "quats", "opacity_logits", "sh")}
+    if wl.velocity is not None:
+        leaves["velocity"] = wl.velocity.to(device).requires_grad_(True)
+    image, _alpha, _depth = render_b200(
+        leaves["means"], leaves["log_scales"], leaves["quats"], leaves["opacity_logits"], leaves["sh"],
+        intrinsics=intrinsics_of(wl, device), camera_to_world=wl.camera_to_world.to(device),
+        height=wl.height, width=wl.width, velocity=leaves.get("velocity"), times=wl.times.to(device),
+        views_per_set=wl.views_per_set, config=cfg,
+    )
+    image.backward(cotangent.to(device))
+    out = {"image": image.detach().cpu()}
+    out.update({f"grad_{k}": v.grad.detach().cpu() for k, v in leaves.items()})
+    torch.cuda.synchronize()
+    return out
+
+
 def stages(wl, cfg: B200RendererConfig | None = None, device=DEV, lens=None):
     """Forward stages only; returns the FrameState and the outputs.  ``lens``: the pair
     render.lens_tensors returns (None: pinhole views)."""

@@ -45,7 +45,7 @@ def test_version_and_status_strings(lib):
 def test_struct_sizes_match_header():
     # 4 ints + 9 pointers + 2 ints; 4 ints + 6 pointers; 2 ints + 11 floats (incl. background[3])
     # + 1 int; 9 pointers
-    assert ctypes.sizeof(_lib.Scene) == 16 + 9 * 8 + 8
+    assert ctypes.sizeof(_lib.Scene) == 16 + 9 * 8 + 8 + 4 * 4
     assert ctypes.sizeof(_lib.Views) == 16 + 6 * 8
     assert ctypes.sizeof(_lib.SceneGrads) == 9 * 8
     assert ctypes.sizeof(_lib.Options) == 8 + 11 * 4 + 4

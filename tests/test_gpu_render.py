@@ -1,14 +1,15 @@
 """CUDA render + loss against the reference's outputs (golden fixtures) and the oracle.
 
-Tolerances (the BASELINE parity bar): image and alpha within 1e-4 absolute; gradients within
-1e-3 of each tensor's largest magnitude (max |g - g_ref| <= 1e-3 * max |g_ref|); tile lists and
+Tolerances: image and alpha within 1e-4 absolute; gradients within 1e-3 of each tensor's largest
+magnitude (max |g - g_ref| <= 1e-3 * max |g_ref|) and, per element,
+|g - g_ref| <= 1e-3 * |g_ref| + 1e-5 * max |g_ref| (conftest.grad_close_elementwise); tile lists and
 sorted key order bit-exact.
 """
 import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN_CASES, grad_close, load_golden
+from conftest import GOLDEN_CASES, grad_close, grad_close_elementwise, load_golden
 from dynaworld_b200 import synthetic
 from dynaworld_b200.config import B200RendererConfig
 from dynaworld_b200.renderer import render_b200_3dgs, render_b200_3dgs_batch
@@ -109,6 +110,8 @@ def test_image_loss_and_gradients_match_reference(case):
                                                                           else ()):
         ok, e, s = grad_close(out[f"grad_{k}"], g.t(f"ref_grad_{k}"), GRAD_REL)
         assert ok, f"{case} {k}: max err {e:.3e} vs scale {s:.3e}"
+        ok, ratio, s = grad_close_elementwise(out[f"grad_{k}"], g.t(f"ref_grad_{k}"))
+        assert ok, f"{case} {k}: per-element error {ratio:.2f}x the bound (scale {s:.3e})"
 
 
 @pytest.mark.parametrize("case", ["static64", "dynamic128_small", "edge"])
@@ -211,3 +214,48 @@ def test_ragged_image_sizes():
         img, _, _ = so.render_dense(m, s, q, o, rgb, H, W, wl.fx, wl.fy, wl.cx, wl.cy, wl.camera_to_world,
                                     sort_key=so.camera_depth_fp32(m.float(), wl.camera_to_world))
         assert (out["image"].double() - img).abs().max().item() <= IMAGE_TOL
+
+
+@pytest.mark.parametrize("tile", [8, 16])
+@pytest.mark.parametrize("case", GOLDEN_CASES)
+def test_tiled_compat_gradients_match_reference_tiled(case, tile):
+    """tiled_compat backward (tile-local (1 + eps) products, no power clamp) against autograd
+    through the reference's tiled renderer (tiled.py:74-198) under the standard_gs loss."""
+    g = load_golden(case)
+    t = load_golden("tiled_grads")
+    key = f"{case}_t{tile}"
+    wl = g.workload()
+    out = render_raw(wl, B200RendererConfig(mode="tiled_compat", tile_size=tile))
+    assert (out["image"] - t.t(f"{key}_image")).abs().max().item() <= IMAGE_TOL
+    np.testing.assert_allclose(out["loss"].numpy(), t[f"{key}_loss"], rtol=0, atol=1e-5)
+    for k in ("means", "log_scales", "quats", "opacity_logits", "sh", "velocity"):
+        if f"{key}_grad_{k}" not in t:
+            continue
+        ok, e, s = grad_close(out[f"grad_{k}"], t.t(f"{key}_grad_{k}"), GRAD_REL)
+        assert ok, f"{key} {k}: {e:.3e} vs {s:.3e}"
+        ok, ratio, s = grad_close_elementwise(out[f"grad_{k}"], t.t(f"{key}_grad_{k}"))
+        assert ok, f"{key} {k}: per-element {ratio:.2f}x the bound (scale {s:.3e})"
+
+
+@pytest.mark.parametrize("tile", [8, 16])
+@pytest.mark.parametrize("case", ["static64", "dynamic128_small", "edge"])
+def test_tiled_compat_activated_api_gradients(case, tile):
+    """The drop-in activated payload in tiled_compat mode: gradients w.r.t. the render call's own
+    inputs against the reference's tiled renderer."""
+    from dynaworld_b200.losses import reconstruction_loss_per_image
+
+    g = load_golden(case)
+    t = load_golden("tiled_grads")
+    key = f"{case}_t{tile}"
+    wl = g.workload()
+    act = {k: g.t(f"ref_act_{k}", DEV).requires_grad_(True) for k in ("xyz", "scales", "quats", "opacities",
+                                                                        "rgbs")}
+    img = render_b200_3dgs_batch(act["xyz"], act["scales"], act["quats"], act["opacities"], act["rgbs"],
+                                 wl.height, wl.width, wl.fx.to(DEV), wl.fy.to(DEV), wl.cx.to(DEV), wl.cy.to(DEV),
+                                 camera_to_world=wl.camera_to_world.to(DEV),
+                                 config=B200RendererConfig(mode="tiled_compat", tile_size=tile))
+    assert (img.detach().cpu() - t.t(f"{key}_image")).abs().max().item() <= IMAGE_TOL
+    reconstruction_loss_per_image(img, wl.target.to(DEV)).sum().backward()
+    for k, v in act.items():
+        ok, e, s = grad_close(v.grad, t.t(f"{key}_grad_act_{k}"), GRAD_REL)
+        assert ok, f"{key} {k}: {e:.3e} vs {s:.3e}"

@@ -1,0 +1,121 @@
+"""Gradient parity with the reference at the full sizes of the seeded workloads.
+
+The fixtures (tests/golden/make_golden_crops.py) hold the reference's window vector-Jacobian
+products: for a cotangent c that is zero outside a set of windows, the gradient of sum(c * image)
+with respect to every raw parameter, summed over the reference's backward of each window (pixels
+are independent given the Gaussians, so a window render with a shifted principal point is the full
+render restricted to the window).  Here the CUDA path renders the whole frames with every Gaussian
+of the full-size scene and back-propagates the full-frame cotangent.  For dynamic128 the windows
+tile both frames and c is the reference's loss gradient, so that case is the full loss gradient.
+
+Bars: window images within 1e-4 absolute; every gradient entry within
+1e-3 * |g_ref| + 1e-5 * max |g_ref| of the reference (per element), and also within 1e-3 of the
+tensor's largest magnitude.  The fixtures leave out Gaussians whose reference gradient entries are
+all below 1e-6 of the scale and keep the largest of those (rest_max); there the GPU gradient must
+stay below the floor minus rest_max, which implies the per-element bound whatever the reference
+value was.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import GRAD_ATOL_FRAC, grad_close, grad_close_elementwise, load_golden
+from dynaworld_b200 import synthetic
+from dynaworld_b200.losses import reconstruction_loss_per_image
+from gpu_helpers import DEV, render_raw, render_vjp
+
+pytestmark = pytest.mark.gpu
+
+IMAGE_TOL = 1e-4
+PARAMS = ("means", "log_scales", "quats", "opacity_logits", "sh", "velocity")
+
+
+def workload_of(name):
+    if name == "dynamic128_vjp":
+        return synthetic.dynamic128().views(6, 8)
+    if name == "multiview384_vjp":
+        return synthetic.multiview384().views(3, 5)
+    if name == "large1080_vjp":
+        return synthetic.large1080().views(0, 2)
+    if name == "clips256_vjp":
+        return synthetic.clips256(clips=1)
+    raise KeyError(name)
+
+
+def check_inputs(g, wl):
+    """The regenerated inputs are the ones the fixture was made from (float64 checksums)."""
+    arrays = dict(means=wl.means, log_scales=wl.log_scales, quats=wl.quats, opacity_logits=wl.opacity_logits,
+                  sh=wl.sh, camera_to_world=wl.camera_to_world, times=wl.times, target=wl.target)
+    if wl.velocity is not None:
+        arrays["velocity"] = wl.velocity
+    for k, v in arrays.items():
+        ref = float(g[f"checksum_{k}"])
+        assert abs(v.double().sum().item() - ref) <= 1e-9 * max(1.0, abs(ref)), k
+
+
+def full_cotangent(g, wl):
+    cot = torch.zeros(wl.n_views, 3, wl.height, wl.width)
+    for (v, x, y, w, h), c in zip(g["windows"], g["cotangents"]):
+        cot[v, :, y:y + h, x:x + w] += torch.from_numpy(c)
+    return cot
+
+
+def check_gradients(g, wl, out):
+    idx = torch.from_numpy(g["ref_idx"].astype(np.int64))
+    S, G = wl.n_sets, wl.n_gaussians
+    rest = torch.ones(S * G, dtype=torch.bool)
+    rest[idx] = False
+    for k in PARAMS:
+        if f"ref_grad_{k}" not in g:
+            continue
+        got = out[f"grad_{k}"].reshape(S * G, *out[f"grad_{k}"].shape[2:])
+        ref = g.t(f"ref_grad_{k}")
+        ok, ratio, scale = grad_close_elementwise(got[idx], ref)
+        assert ok, f"{k}: worst per-element error {ratio:.2f}x the bound (scale {scale:.3e})"
+        ok, err, scale = grad_close(got[idx], ref)
+        assert ok, f"{k}: {err:.3e} vs scale {scale:.3e}"
+        stray = got[rest].abs().max().item() if rest.any() else 0.0
+        limit = GRAD_ATOL_FRAC * scale - float(g[f"ref_rest_max_{k}"])
+        assert stray <= limit, f"{k}: gradient {stray:.3e} where the reference's is below {limit:.3e}"
+
+
+def check_windows(g, out):
+    for (v, x, y, w, h), ref in zip(g["windows"], g["ref_windows"]):
+        got = out["image"][v, :, y:y + h, x:x + w]
+        err = (got - torch.from_numpy(ref)).abs().max().item()
+        assert err <= IMAGE_TOL, f"view {v} window ({x},{y}): {err:.3e}"
+
+
+@pytest.mark.parametrize("name", ["multiview384_vjp", "large1080_vjp", "clips256_vjp"])
+def test_window_vjp_matches_reference(name):
+    g = load_golden(name)
+    wl = workload_of(name)
+    check_inputs(g, wl)
+    out = render_vjp(wl, full_cotangent(g, wl))
+    check_windows(g, out)
+    check_gradients(g, wl, out)
+
+
+def test_dynamic128_full_loss_gradient_matches_reference():
+    """Two full 128x128 frames of the 32,768-Gaussian scene: loss and full loss gradient."""
+    g = load_golden("dynamic128_vjp")
+    wl = workload_of("dynamic128_vjp")
+    check_inputs(g, wl)
+    out = render_raw(wl)
+    check_windows(g, out)
+    np.testing.assert_allclose(out["loss"].numpy(), g["ref_loss"], rtol=0, atol=1e-5)
+    check_gradients(g, wl, out)
+
+
+def test_loss_cotangent_route_matches_explicit_cotangent():
+    """The same dynamic128 gradient through an explicit image cotangent (the loss gradient taken
+    on the host) equals the one through the fused loss."""
+    wl = workload_of("dynamic128_vjp")
+    out = render_raw(wl)
+    img = out["image"].clone().requires_grad_(True)
+    (cot,) = torch.autograd.grad(reconstruction_loss_per_image(img.to(DEV), wl.target.to(DEV)).sum(), img)
+    out2 = render_vjp(wl, cot)
+    for k in PARAMS:
+        if f"grad_{k}" in out:
+            ok, err, scale = grad_close(out2[f"grad_{k}"], out[f"grad_{k}"], 1e-5)
+            assert ok, f"{k}: {err:.3e} vs {scale:.3e}"
