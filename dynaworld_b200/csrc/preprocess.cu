@@ -378,7 +378,7 @@ __device__ inline void eval_color(const gsb_scene& sc, size_t pg, const float d[
     float v = 0.5f;
 #pragma unroll
     for (int k = 0; k < K; ++k) v += Y[k] * sh[k * 3 + c];
-    rgb[c] = clamp ? fmaxf(v, 0.0f) : v;
+    rgb[c] = (clamp && v < 0.0f) ? 0.0f : v;  // torch.clamp(min=0): NaN stays NaN
   }
 }
 

@@ -466,6 +466,49 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
         const float4 ct = s_cot[lw][j];
         const float dx = __fsub_rn(fx, g.x);
         const float hB = 0.5f * g.w;  // half the cross coefficient
+#ifdef GSB_BWD_PREDICATED
+        const float4 col = s_col[lw][j];
+#pragma unroll
+        for (int k = 0; k < PX; ++k) {
+          // every pixel runs the same instructions; a pixel that does not take this entry (past
+          // its last blended entry, or alpha below the cutoff) keeps S and rs and adds zeros
+          const bool live = lj < n_proc[k];
+          const float dy = __fsub_rn(fy[k], g.y);
+          const float qk = pair_q(g.z, g.w, ct.x, dx, dy);
+          const float e = decltype(fast)::value ? gauss_falloff_nonpos(qk) : gauss_falloff(qk);
+          const float araw = ct.y * e;
+          const float alpha = fminf(fmaxf(araw, 0.0f), rc.alpha_clamp);
+          const bool on = live && alpha >= rc.alpha_cutoff;
+          const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
+          const float rf = __fdividef(1.0f, f);
+          const float Sb = S[k] * (rc.f0 * rf);  // S before this entry: S_after / (f / F0)
+          S[k] = on ? Sb : S[k];
+          const float T = Sb * ct.w;
+          const float w = on ? T * alpha : 0.0f;
+          float dldw = g0[k] * col.x + g1[k] * col.y + g2c[k] * col.z + gW[k];
+          if (DEPTH) dldw = fmaf(gD[k], col.w, dldw);
+          const float dlda = T * dldw - rs[k] * rf;
+          rs[k] = fmaf(w, dldw, rs[k]);
+          const float dlr = (on && alpha == araw) ? dlda : 0.0f;
+          const float pmask = decltype(fast)::value
+                                  ? kInvFalloffScale
+                                  : (qk < 0.0f ? kInvFalloffScale : (qk == 0.0f ? 0.5f * kInvFalloffScale : 0.0f));
+          const float dpow = dlr * araw * pmask;
+          const float u = dpow * dx, t = dpow * dy;
+          v[0] = fmaf(g.z, u, fmaf(hB, t, v[0]));
+          v[1] = fmaf(ct.x, t, fmaf(hB, u, v[1]));
+          v[2] = fmaf(u, dx, v[2]);
+          v[3] = fmaf(u, dy, v[3]);
+          v[4] = fmaf(t, dy, v[4]);
+          v[5] = fmaf(dlr, e, v[5]);
+          v[6] = fmaf(g0[k], w, v[6]);
+          v[7] = fmaf(g1[k], w, v[7]);
+          v[8] = fmaf(g2c[k], w, v[8]);
+          if (DEPTH) v[9] = fmaf(gD[k], w, v[9]);
+          contrib = contrib || on;
+        }
+      }
+#else
 #pragma unroll
         for (int k = 0; k < PX; ++k) {
           if (!(lj < n_proc[k])) continue;
@@ -507,6 +550,7 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           contrib = true;
         }
       }
+#endif
       const uint32_t cm = __ballot_sync(kFull, contrib);
       if (cm == 0u) continue;
       float* dst = g2 + size_t(s_rank[lw][j]) * GSB_GRAD2D_FLOATS;
@@ -659,26 +703,27 @@ static void bwd_launch(const RasterArgs& a, cudaStream_t st) {
   else bwd_launch_seg<TILE, PX, 1>(a, st);
 }
 
-// GSB200_RASTER_PX=1 or 2 forces the pixels per lane of both stages, GSB200_RASTER_PX_BWD of the
-// backward alone (tests and tuning; results do not depend on them); read at every launch so that
-// a process can switch them between calls.
+// GSB200_RASTER_PX=1, 2 or 4 forces the pixels per lane of both stages, GSB200_RASTER_PX_BWD of
+// the backward alone (tests and tuning; results do not depend on them; 4 applies to 16x16 tiles
+// only); read at every launch so that a process can switch them between calls.
 static int forced_px(const char* name) {
   const char* v = std::getenv(name);
-  if (v && (v[0] == '1' || v[0] == '2') && v[1] == '\0') return v[0] - '0';
+  if (v && (v[0] == '1' || v[0] == '2' || v[0] == '4') && v[1] == '\0') return v[0] - '0';
   return 0;
 }
 
-static bool paired_launch(uint64_t tiles, uint64_t threshold, bool backward) {
+static int lane_pixels(uint64_t tiles, uint64_t threshold, bool backward, int tile) {
   int force = backward ? forced_px("GSB200_RASTER_PX_BWD") : 0;
   if (!force) force = forced_px("GSB200_RASTER_PX");
-  if (force) return force == 2;
-  return tiles >= threshold;
+  if (force == 4 && tile != 16) force = 2;
+  if (force) return force;
+  return tiles >= threshold ? 2 : 1;
 }
 
 gsb_status launch_raster_fwd(const RasterArgs& a, cudaStream_t st) {
-  const bool paired = paired_launch(uint64_t(a.rc.n_tiles) * uint64_t(a.B), kFwdPairedTiles, false);
-  if (a.rc.tile == 16) paired ? fwd_launch<16, 2>(a, st) : fwd_launch<16, 1>(a, st);
-  else if (a.rc.tile == 8) paired ? fwd_launch<8, 2>(a, st) : fwd_launch<8, 1>(a, st);
+  const int px = lane_pixels(uint64_t(a.rc.n_tiles) * uint64_t(a.B), kFwdPairedTiles, false, a.rc.tile);
+  if (a.rc.tile == 16) px == 4 ? fwd_launch<16, 4>(a, st) : px == 2 ? fwd_launch<16, 2>(a, st) : fwd_launch<16, 1>(a, st);
+  else if (a.rc.tile == 8) px == 2 ? fwd_launch<8, 2>(a, st) : fwd_launch<8, 1>(a, st);
   else return GSB_ERR_ARG;
   return launch_status();
 }
@@ -686,9 +731,10 @@ gsb_status launch_raster_fwd(const RasterArgs& a, cudaStream_t st) {
 gsb_status launch_raster_bwd(const RasterArgs& a, cudaStream_t st) {
   if (cudaMemsetAsync(a.grad2d, 0, size_t(a.B) * a.G * GSB_GRAD2D_FLOATS * sizeof(float), st)) return GSB_ERR_CUDA;
   // segmented lists restore the parallelism two pixels per lane gives up: pair them always then
-  const bool paired = paired_launch(uint64_t(a.rc.n_tiles) * uint64_t(a.B), a.nseg > 1 ? 0 : kBwdPairedTiles, true);
-  if (a.rc.tile == 16) paired ? bwd_launch<16, 2>(a, st) : bwd_launch<16, 1>(a, st);
-  else if (a.rc.tile == 8) paired ? bwd_launch<8, 2>(a, st) : bwd_launch<8, 1>(a, st);
+  const int px =
+      lane_pixels(uint64_t(a.rc.n_tiles) * uint64_t(a.B), a.nseg > 1 ? 0 : kBwdPairedTiles, true, a.rc.tile);
+  if (a.rc.tile == 16) px == 4 ? bwd_launch<16, 4>(a, st) : px == 2 ? bwd_launch<16, 2>(a, st) : bwd_launch<16, 1>(a, st);
+  else if (a.rc.tile == 8) px == 2 ? bwd_launch<8, 2>(a, st) : bwd_launch<8, 1>(a, st);
   else return GSB_ERR_ARG;
   return launch_status();
 }

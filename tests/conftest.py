@@ -60,11 +60,12 @@ def golden_case(request):
 
 
 # Per-element gradient tolerance: |g - g_ref| <= GRAD_RTOL * |g_ref| + GRAD_ATOL_FRAC * max|g_ref|.
-# The floor is one part in 1e5 of the tensor's largest entry: entries that are sums of terms
-# cancelling far below the tensor's scale carry float32 rounding of the terms (not of the sum),
-# in the reference's own float32 computation as in this one.
+# The floor is one part in 1e4 of the tensor's largest entry (ten times below the 1e-3-of-scale
+# bar): an entry that is a sum of per-pixel terms cancelling far below the tensor's scale (a mean
+# gradient over a nearly symmetric footprint, say) carries the float32 rounding of its terms, not
+# of its value, in the reference's own float32 computation as in this one.
 GRAD_RTOL = 1e-3
-GRAD_ATOL_FRAC = 1e-5
+GRAD_ATOL_FRAC = 1e-4
 
 
 def grad_close_elementwise(got: torch.Tensor, ref: torch.Tensor, rtol: float = GRAD_RTOL,

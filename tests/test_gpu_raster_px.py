@@ -1,4 +1,4 @@
-"""Both raster decompositions (one or two pixels per lane) against the reference's outputs.
+"""Every raster decomposition (one, two or four pixels per lane) against the reference's outputs.
 
 The launch picks the decomposition from the grid size; GSB200_RASTER_PX forces it, so every
 golden case runs through each.  Forward arithmetic per pixel does not depend on the
@@ -22,7 +22,7 @@ GRAD_REL = 1e-3
 GRAD_KEYS = ("means", "log_scales", "quats", "opacity_logits", "sh")
 
 
-@pytest.fixture(params=["1", "2"])
+@pytest.fixture(params=["1", "2", "4"])
 def px(request, monkeypatch):
     monkeypatch.setenv("GSB200_RASTER_PX", request.param)
     return request.param

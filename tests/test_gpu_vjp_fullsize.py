@@ -9,8 +9,8 @@ of the full-size scene and back-propagates the full-frame cotangent.  For dynami
 tile both frames and c is the reference's loss gradient, so that case is the full loss gradient.
 
 Bars: window images within 1e-4 absolute; every gradient entry within
-1e-3 * |g_ref| + 1e-5 * max |g_ref| of the reference (per element), and also within 1e-3 of the
-tensor's largest magnitude.  The fixtures leave out Gaussians whose reference gradient entries are
+1e-3 * |g_ref| + 1e-4 * max |g_ref| of the reference (per element, conftest.grad_close_elementwise),
+and also within 1e-3 of the tensor's largest magnitude.  The fixtures leave out Gaussians whose reference gradient entries are
 all below 1e-6 of the scale and keep the largest of those (rest_max); there the GPU gradient must
 stay below the floor minus rest_max, which implies the per-element bound whatever the reference
 value was.
