@@ -110,12 +110,17 @@ def workload_config(name, full, shard, world):
 class Step:
     """One render + loss forward/backward of a workload resident on the device."""
 
-    def __init__(self, wl, device, world, tile=None, segments=0):
+    def __init__(self, wl, device, world, tile=None, segments=0, shared_set=True):
         from dynaworld_b200.config import B200RendererConfig
+        from dynaworld_b200.distributed import GradientAllReduce
+        from dynaworld_b200.render import set_gradient_reducer
 
         self.wl = wl
         self.dev = device
         self.world = world
+        # one Gaussian set shared by every rank: the backward sums its gradients over the ranks
+        # (bucketed NCCL all-reduce overlapped with the chain rule); per-clip sets need no exchange
+        set_gradient_reducer(GradientAllReduce() if (world > 1 and shared_set) else None)
         self.cfg = B200RendererConfig(tile_size=tile or 16, backward_segments=segments)
         self.params = {k: getattr(wl, k).to(device).contiguous().requires_grad_(True)
                        for k in ("means", "log_scales", "quats", "opacity_logits", "sh")}
@@ -127,7 +132,6 @@ class Step:
         self.target = wl.target.to(device).contiguous()
 
     def run(self, params=None, intr=None, c2w=None, times=None, target=None):
-        from dynaworld_b200.distributed import allreduce_gradients
         from dynaworld_b200.losses import reconstruction_loss_per_image
         from dynaworld_b200.renderer import render_b200
 
@@ -142,8 +146,6 @@ class Step:
         )
         loss = reconstruction_loss_per_image(image, self.target if target is None else target)
         loss.sum().backward()
-        if self.world > 1:
-            allreduce_gradients([v.grad for v in p.values()])
         return loss
 
 
@@ -434,7 +436,7 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     L = _lib.load()
     full, wl = make_workload(args.workload, rank, world, args.scale, args.image_scale, args.views)
-    step = Step(wl, dev, world, args.tile, args.segments)
+    step = Step(wl, dev, world, args.tile, args.segments, shared_set=full.views_per_set >= full.n_views)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
 
     def barrier():

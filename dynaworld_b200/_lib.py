@@ -126,6 +126,8 @@ SIGNATURES = {
     "gsb_raster_bwd": (C.c_int, [P(Views), P(Options), C.c_int32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                  vp]),
     "gsb_preprocess_bwd": (C.c_int, [P(Scene), P(Views), P(Options), vp, vp, P(SceneGrads), vp]),
+    "gsb_preprocess_bwd_range": (C.c_int, [P(Scene), P(Views), P(Options), vp, vp, P(SceneGrads), C.c_int64,
+                                           C.c_int64, vp]),
     "gsb_camera_bwd": (C.c_int, [P(Scene), P(Views), P(Options), vp, vp, P(CameraGrads), vp]),
     "gsb_splats2d_order_workspace": (C.c_size_t, [P(Splats2D)]),
     "gsb_splats2d_order": (C.c_int, [P(Splats2D), vp, vp, vp, C.c_size_t, vp]),

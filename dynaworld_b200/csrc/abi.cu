@@ -408,6 +408,23 @@ GSB_API gsb_status gsb_preprocess_bwd(const gsb_scene* scene, const gsb_views* v
   return launch_preprocess_bwd(*scene, *views, rc, rank_of, grad2d, *grads, as_stream(stream));
 }
 
+GSB_API gsb_status gsb_preprocess_bwd_range(const gsb_scene* scene, const gsb_views* views, const gsb_options* opts,
+                                            const int32_t* rank_of, const float* grad2d, gsb_scene_grads* grads,
+                                            int64_t first, int64_t count, void* stream) {
+  gsb_status s;
+  if ((s = check_views(views)) != GSB_OK) return s;
+  if ((s = check_scene(scene, views)) != GSB_OK) return s;
+  if ((s = check_opts(opts)) != GSB_OK) return s;
+  if (!rank_of || !grad2d || !grads) return GSB_ERR_ARG;
+  const int64_t total = int64_t(scene->n_sets) * scene->n_gaussians;
+  if (first < 0 || count < 0 || first > total || count > total - first) return GSB_ERR_SHAPE;
+  if (count == 0) return GSB_OK;
+  RenderConsts rc = make_consts(*views, *opts);
+  rc.bwd_first = uint64_t(first);
+  rc.bwd_count = uint64_t(count);
+  return launch_preprocess_bwd(*scene, *views, rc, rank_of, grad2d, *grads, as_stream(stream));
+}
+
 GSB_API gsb_status gsb_camera_bwd(const gsb_scene* scene, const gsb_views* views, const gsb_options* opts,
                                   const int32_t* rank_of, const float* grad2d, gsb_camera_grads* grads, void* stream) {
   gsb_status s;

@@ -81,6 +81,9 @@ struct RenderConsts {
   float bound_scale, tiled_threshold;
   float f0;      // fl32(1 + eps): the transmittance factor of an alpha-0 pair
   float log2_f0; // log2(f0): T_i = F0^pos_i * S_i (pos = depth rank, or list index in compat mode)
+  // preprocess backward: the Gaussians (set * G + index) [bwd_first, bwd_first + bwd_count) it
+  // writes (bwd_count 0: all of them)
+  uint64_t bwd_first, bwd_count;
 };
 
 RenderConsts make_consts(const gsb_views& v, const gsb_options& o);

@@ -46,6 +46,30 @@ __device__ __forceinline__ int reflect_idx(int i, int n) {
   return min(max(i, 0), n - 1);
 }
 
+// SSIM of one window from its five means m = (mu_x, mu_y, E[x^2], E[y^2], E[xy]) (losses.py:29-44,
+// the denominator clamped at 1e-12), and its derivatives with respect to the three window means
+// that depend on the prediction: d / d mu_x (through mu_x and the variances), d / d E[x^2],
+// d / d E[xy].
+__device__ __forceinline__ float ssim_point(const float m[5], float c1, float c2, float& d_mx, float& d_mxx,
+                                            float& d_mxy) {
+  const float mux = m[0], muy = m[1];
+  const float mux2 = mux * mux, muy2 = muy * muy, muxy = mux * muy;
+  const float sxx = m[2] - mux2, syy = m[3] - muy2, sxy = m[4] - muxy;
+  const float A1 = 2.0f * muxy + c1, A2 = 2.0f * sxy + c2;
+  const float B1 = mux2 + muy2 + c1, B2 = sxx + syy + c2;
+  const float Draw = B1 * B2;
+  const float Dc = fmaxf(Draw, 1e-12f);
+  const float s = (A1 * A2) / Dc;
+  const float dsdD = Draw >= 1e-12f ? -s / Dc : 0.0f;
+  const float ds_mu = (2.0f * muy * A2) / Dc + dsdD * (2.0f * mux * B2);  // explicit mu_x
+  const float ds_sxx = dsdD * B1;
+  const float ds_sxy = 2.0f * A1 / Dc;
+  d_mx = ds_mu - 2.0f * mux * ds_sxx - muy * ds_sxy;
+  d_mxx = ds_sxx;
+  d_mxy = ds_sxy;
+  return s;
+}
+
 template <int HW>
 __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
   constexpr int R = kLossTile + 4 * HW;  // input rows/cols held
@@ -136,107 +160,213 @@ __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
     }
     __syncthreads();
     // vertical sums -> SSIM map and its derivatives w.r.t. the three prediction moments
-    for (int i = tid; i < M * M; i += kLossThreads) {
-      const int r = i / M, c = i - r * M;
-      const int gy = y0 - HW + r, gx = x0 - HW + c;
-      float d_mx = 0.0f, d_mxx = 0.0f, d_mxy = 0.0f;
-      if (gy >= 0 && gy < H && gx >= 0 && gx < W) {
-        float m[5] = {0, 0, 0, 0, 0};
+    if (a.box) {
+      // Box window: a thread keeps the five column sums of kRunV consecutive mean rows as running
+      // sums (add the row entering the window, drop the one leaving it).
+      constexpr int kRunV = 6;
+      constexpr int kRunsV = (M + kRunV - 1) / kRunV;
+      const float wk = a.w[0];
+      for (int i = tid; i < M * kRunsV; i += kLossThreads) {
+        const int c = i % M, r0 = (i / M) * kRunV;
+        const int r_end = min(r0 + kRunV, M);
+        float m[5] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int k = -HW; k <= HW; ++k) {
-          const float wk = a.w[k + HW];
-          const int row = (r + HW + k) * M + c;
+        for (int t = 0; t <= 2 * HW; ++t)
 #pragma unroll
-          for (int q = 0; q < 5; ++q) m[q] = fmaf(wk, hs[q * R * M + row], m[q]);
+          for (int q = 0; q < 5; ++q) m[q] += hs[q * R * M + (r0 + t) * M + c];
+        for (int r = r0;; ++r) {
+          const int gy = y0 - HW + r, gx = x0 - HW + c;
+          float d_mx = 0.0f, d_mxx = 0.0f, d_mxy = 0.0f;
+          if (gy >= 0 && gy < H && gx >= 0 && gx < W) {
+            const float mm[5] = {m[0] * wk, m[1] * wk, m[2] * wk, m[3] * wk, m[4] * wk};
+            const float sv = ssim_point(mm, a.c1, a.c2, d_mx, d_mxx, d_mxy);
+            if (r >= HW && r < HW + kLossTile && c >= HW && c < HW + kLossTile) sum_s += double(sv);
+          }
+          const int o = r * M + c;
+          gm[0 * M * M + o] = d_mx;
+          gm[1 * M * M + o] = d_mxx;
+          gm[2 * M * M + o] = d_mxy;
+          if (r + 1 >= r_end) break;
+#pragma unroll
+          for (int q = 0; q < 5; ++q) m[q] += hs[q * R * M + (r + 2 * HW + 1) * M + c] - hs[q * R * M + r * M + c];
         }
-        const float mux = m[0], muy = m[1];
-        const float mux2 = mux * mux, muy2 = muy * muy, muxy = mux * muy;
-        const float sxx = m[2] - mux2, syy = m[3] - muy2, sxy = m[4] - muxy;
-        const float A1 = 2.0f * muxy + a.c1, A2 = 2.0f * sxy + a.c2;
-        const float B1 = mux2 + muy2 + a.c1, B2 = sxx + syy + a.c2;
-        const float Draw = B1 * B2;
-        const float Dc = fmaxf(Draw, 1e-12f);
-        const float s = (A1 * A2) / Dc;
-        const float dsdD = Draw >= 1e-12f ? -s / Dc : 0.0f;
-        const float ds_mu = (2.0f * muy * A2) / Dc + dsdD * (2.0f * mux * B2);  // explicit mu_x
-        const float ds_sxx = dsdD * B1;
-        const float ds_sxy = 2.0f * A1 / Dc;
-        d_mx = ds_mu - 2.0f * mux * ds_sxx - muy * ds_sxy;
-        d_mxx = ds_sxx;
-        d_mxy = ds_sxy;
-        if (r >= HW && r < HW + kLossTile && c >= HW && c < HW + kLossTile) sum_s += double(s);
       }
-      gm[0 * M * M + i] = d_mx;
-      gm[1 * M * M + i] = d_mxx;
-      gm[2 * M * M + i] = d_mxy;
-    }
-    __syncthreads();
-    // horizontal adjoint: rows r in [0,M), output columns cq in [0,kLossTile)
-    for (int i = tid; i < M * kLossTile; i += kLossThreads) {
-      const int r = i / kLossTile, cq = i - r * kLossTile;
-      const int qx = x0 + cq;
-      float acc0 = 0, acc1 = 0, acc2 = 0;
-      if (qx < W) {
-        const int ms[3] = {qx, (qx >= 1 && qx <= HW) ? -qx : INT32_MIN,
-                           (qx >= W - 1 - HW && qx <= W - 2) ? 2 * (W - 1) - qx : INT32_MIN};
-#pragma unroll
-        for (int t = 0; t < 3; ++t) {
-          if (ms[t] == INT32_MIN) continue;
+    } else {
+      for (int i = tid; i < M * M; i += kLossThreads) {
+        const int r = i / M, c = i - r * M;
+        const int gy = y0 - HW + r, gx = x0 - HW + c;
+        float d_mx = 0.0f, d_mxx = 0.0f, d_mxy = 0.0f;
+        if (gy >= 0 && gy < H && gx >= 0 && gx < W) {
+          float m[5] = {0, 0, 0, 0, 0};
 #pragma unroll
           for (int k = -HW; k <= HW; ++k) {
-            const int gi = ms[t] + k;
-            if (gi < 0 || gi >= W) continue;
-            const int col = gi - x0 + HW;
+            const float wk = a.w[k + HW];
+            const int row = (r + HW + k) * M + c;
+#pragma unroll
+            for (int q = 0; q < 5; ++q) m[q] = fmaf(wk, hs[q * R * M + row], m[q]);
+          }
+          const float sv = ssim_point(m, a.c1, a.c2, d_mx, d_mxx, d_mxy);
+          if (r >= HW && r < HW + kLossTile && c >= HW && c < HW + kLossTile) sum_s += double(sv);
+        }
+        gm[0 * M * M + i] = d_mx;
+        gm[1 * M * M + i] = d_mxx;
+        gm[2 * M * M + i] = d_mxy;
+      }
+    }
+    __syncthreads();
+    // horizontal adjoint: rows r in [0,M), output columns cq in [0,kLossTile).  The window operator
+    // of reflect padding folds the zero-padded window sums at the mirrored positions -q and
+    // 2(W-1)-q back onto q; gm is zero off the image, so the direct term needs no bounds and, for
+    // the box window, is a running sum along the row.  The mirrored terms exist only within HW of
+    // the image's left and right edges.
+    auto mirror_h = [&](int r, int qx, float& acc0, float& acc1, float& acc2) {
+      const int ms[2] = {(qx >= 1 && qx <= HW) ? -qx : INT32_MIN,
+                         (qx >= W - 1 - HW && qx <= W - 2) ? 2 * (W - 1) - qx : INT32_MIN};
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (ms[t] == INT32_MIN) continue;
+#pragma unroll
+        for (int k = -HW; k <= HW; ++k) {
+          const int gi = ms[t] + k;
+          if (gi < 0 || gi >= W) continue;
+          const int col = gi - x0 + HW;
+          const float wk = a.w[k + HW];
+          acc0 = fmaf(wk, gm[0 * M * M + r * M + col], acc0);
+          acc1 = fmaf(wk, gm[1 * M * M + r * M + col], acc1);
+          acc2 = fmaf(wk, gm[2 * M * M + r * M + col], acc2);
+        }
+      }
+    };
+    if (a.box) {
+      constexpr int kRunH = 8;
+      constexpr int kRunsH = kLossTile / kRunH;
+      const float wk = a.w[0];
+      for (int i = tid; i < M * kRunsH; i += kLossThreads) {
+        const int r = i / kRunsH, c0 = (i - r * kRunsH) * kRunH;
+        const float* q0 = gm + 0 * M * M + r * M;
+        const float* q1 = gm + 1 * M * M + r * M;
+        const float* q2 = gm + 2 * M * M + r * M;
+        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+        for (int t = 0; t <= 2 * HW; ++t) s0 += q0[c0 + t], s1 += q1[c0 + t], s2 += q2[c0 + t];
+#pragma unroll
+        for (int j = 0; j < kRunH; ++j) {
+          const int cq = c0 + j, qx = x0 + cq;
+          float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f;
+          if (qx < W) {
+            acc0 = s0 * wk, acc1 = s1 * wk, acc2 = s2 * wk;
+            if (qx <= HW || qx >= W - 1 - HW) mirror_h(r, qx, acc0, acc1, acc2);
+          }
+          const int o = r * kLossTile + cq;
+          ha[0 * M * kLossTile + o] = acc0;
+          ha[1 * M * kLossTile + o] = acc1;
+          ha[2 * M * kLossTile + o] = acc2;
+          if (j + 1 < kRunH) {
+            s0 += q0[cq + 2 * HW + 1] - q0[cq];
+            s1 += q1[cq + 2 * HW + 1] - q1[cq];
+            s2 += q2[cq + 2 * HW + 1] - q2[cq];
+          }
+        }
+      }
+    } else {
+      for (int i = tid; i < M * kLossTile; i += kLossThreads) {
+        const int r = i / kLossTile, cq = i - r * kLossTile;
+        const int qx = x0 + cq;
+        float acc0 = 0, acc1 = 0, acc2 = 0;
+        if (qx < W) {
+#pragma unroll
+          for (int k = -HW; k <= HW; ++k) {
+            const int col = cq + HW + k;  // gm is zero off the image
             const float wk = a.w[k + HW];
             acc0 = fmaf(wk, gm[0 * M * M + r * M + col], acc0);
             acc1 = fmaf(wk, gm[1 * M * M + r * M + col], acc1);
             acc2 = fmaf(wk, gm[2 * M * M + r * M + col], acc2);
           }
+          mirror_h(r, qx, acc0, acc1, acc2);
         }
+        ha[0 * M * kLossTile + i] = acc0;
+        ha[1 * M * kLossTile + i] = acc1;
+        ha[2 * M * kLossTile + i] = acc2;
       }
-      ha[0 * M * kLossTile + i] = acc0;
-      ha[1 * M * kLossTile + i] = acc1;
-      ha[2 * M * kLossTile + i] = acc2;
     }
     __syncthreads();
   }
 
-  // vertical adjoint + gradient + L1/L2 sums over the output tile
+  // vertical adjoint + gradient + L1/L2 sums over the output tile: column cq, kRunQ consecutive
+  // output rows per thread (running sums of ha down the column for the box window; ha is zero off
+  // the image; the mirrored terms only within HW of the top and bottom edges)
   double sum_l1 = 0.0, sum_l2 = 0.0;
-  for (int i = tid; i < kLossTile * kLossTile; i += kLossThreads) {
-    const int rq = i / kLossTile, cq = i - rq * kLossTile;
-    const int qy = y0 + rq, qx = x0 + cq;
-    if (qy >= H || qx >= W) continue;
-    const float x = xs[(rq + 2 * HW) * R + cq + 2 * HW];
-    const float y = ys[(rq + 2 * HW) * R + cq + 2 * HW];
-    const float d = x - y;
-    sum_l1 += double(fabsf(d));
-    sum_l2 += double(d * d);
-    if (!a.dpred) continue;
-    const float sgn = d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f);
-    float grad = a.c_l1 * sgn + a.c_mse * 2.0f * d;
-    if (ssim) {
-      float v0 = 0, v1 = 0, v2 = 0;
-      const int ms[3] = {qy, (qy >= 1 && qy <= HW) ? -qy : INT32_MIN,
-                         (qy >= H - 1 - HW && qy <= H - 2) ? 2 * (H - 1) - qy : INT32_MIN};
+  constexpr int kRunQ = 4;
+  for (int i = tid; i < kLossTile * (kLossTile / kRunQ); i += kLossThreads) {
+    const int cq = i % kLossTile, rq0 = (i / kLossTile) * kRunQ;
+    const int qx = x0 + cq;
+    if (qx >= W) continue;
+    const float* h0 = ha + 0 * M * kLossTile + cq;
+    const float* h1 = ha + 1 * M * kLossTile + cq;
+    const float* h2 = ha + 2 * M * kLossTile + cq;
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f;
+    if (ssim && a.box && a.dpred) {
 #pragma unroll
-      for (int t = 0; t < 3; ++t) {
-        if (ms[t] == INT32_MIN) continue;
-#pragma unroll
-        for (int k = -HW; k <= HW; ++k) {
-          const int gi = ms[t] + k;
-          if (gi < 0 || gi >= H) continue;
-          const int row = gi - y0 + HW;
-          const float wk = a.w[k + HW];
-          v0 = fmaf(wk, ha[0 * M * kLossTile + row * kLossTile + cq], v0);
-          v1 = fmaf(wk, ha[1 * M * kLossTile + row * kLossTile + cq], v1);
-          v2 = fmaf(wk, ha[2 * M * kLossTile + row * kLossTile + cq], v2);
-        }
-      }
-      grad += a.c_ssim * (v0 + 2.0f * x * v1 + y * v2);
+      for (int t = 0; t <= 2 * HW; ++t)
+        s0 += h0[(rq0 + t) * kLossTile], s1 += h1[(rq0 + t) * kLossTile], s2 += h2[(rq0 + t) * kLossTile];
     }
-    a.dpred[poff + size_t(qy) * W + qx] = grad;
+#pragma unroll
+    for (int j = 0; j < kRunQ; ++j) {
+      const int rq = rq0 + j, qy = y0 + rq;
+      if (qy >= H) break;
+      const float x = xs[(rq + 2 * HW) * R + cq + 2 * HW];
+      const float y = ys[(rq + 2 * HW) * R + cq + 2 * HW];
+      const float d = x - y;
+      sum_l1 += double(fabsf(d));
+      sum_l2 += double(d * d);
+      if (!a.dpred) continue;
+      const float sgn = d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f);
+      float grad = a.c_l1 * sgn + a.c_mse * 2.0f * d;
+      if (ssim) {
+        float v0 = 0, v1 = 0, v2 = 0;
+        if (a.box) {
+          const float wk = a.w[0];
+          v0 = s0 * wk, v1 = s1 * wk, v2 = s2 * wk;
+          if (j + 1 < kRunQ) {
+            const int in = (rq + 2 * HW + 1) * kLossTile, out = rq * kLossTile;
+            s0 += h0[in] - h0[out];
+            s1 += h1[in] - h1[out];
+            s2 += h2[in] - h2[out];
+          }
+        } else {
+#pragma unroll
+          for (int k = -HW; k <= HW; ++k) {
+            const int row = rq + HW + k;
+            const float wk = a.w[k + HW];
+            v0 = fmaf(wk, h0[row * kLossTile], v0);
+            v1 = fmaf(wk, h1[row * kLossTile], v1);
+            v2 = fmaf(wk, h2[row * kLossTile], v2);
+          }
+        }
+        if (qy <= HW || qy >= H - 1 - HW) {
+          const int ms[2] = {(qy >= 1 && qy <= HW) ? -qy : INT32_MIN,
+                             (qy >= H - 1 - HW && qy <= H - 2) ? 2 * (H - 1) - qy : INT32_MIN};
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (ms[t] == INT32_MIN) continue;
+#pragma unroll
+            for (int k = -HW; k <= HW; ++k) {
+              const int gi = ms[t] + k;
+              if (gi < 0 || gi >= H) continue;
+              const int row = gi - y0 + HW;
+              const float wk = a.w[k + HW];
+              v0 = fmaf(wk, h0[row * kLossTile], v0);
+              v1 = fmaf(wk, h1[row * kLossTile], v1);
+              v2 = fmaf(wk, h2[row * kLossTile], v2);
+            }
+          }
+        }
+        grad += a.c_ssim * (v0 + 2.0f * x * v1 + y * v2);
+      }
+      a.dpred[poff + size_t(qy) * W + qx] = grad;
+    }
   }
+
   // block reduction of the three sums, one double atomic per quantity
   const int lane = tid & 31, warp = tid >> 5;
   double v[3] = {sum_l1, sum_l2, sum_s};

@@ -718,7 +718,8 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
                                                              const float* __restrict__ grad2d, gsb_scene_grads gr) {
   static_assert(LPG == 1 || (!BANK && 32 % LPG == 0), "lane groups tile a warp; the bank keeps one lane");
   const size_t G = sc.n_gaussians;
-  const size_t total = size_t(sc.n_sets) * G;
+  const size_t first = rc.bwd_first;
+  const size_t total = rc.bwd_count ? size_t(rc.bwd_count) : size_t(sc.n_sets) * G - first;
   const bool head = sc.flags & GSB_SCENE_HEAD;
   const bool raw = (sc.flags & GSB_SCENE_RAW) || head;
   const bool vel = sc.flags & GSB_SCENE_VELOCITY;
@@ -731,7 +732,7 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(gsb_scene sc, gsb_v
   for (size_t t0 = blockIdx.x * size_t(blockDim.x); t0 < lanes_total; t0 += size_t(gridDim.x) * blockDim.x) {
     const size_t tix = t0 + threadIdx.x;
     const bool valid = tix < lanes_total;
-    const size_t pg = valid ? tix / LPG : 0;
+    const size_t pg = first + (valid ? tix / LPG : 0);
     const int sub = int(tix % LPG);
     const int s = int(pg / G);
     const size_t g = pg - size_t(s) * G;
@@ -1063,7 +1064,8 @@ gsb_status launch_preprocess_fwd(const gsb_scene& sc, const gsb_views& vw, const
 template <int K, bool LENS, int LPG>
 static void bwd_launch_lpg(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc, const int32_t* rank_of,
                            const float* grad2d, const gsb_scene_grads& gr, cudaStream_t st) {
-  const int grid = grid_for(size_t(sc.n_sets) * sc.n_gaussians * LPG, 128);
+  const size_t n = rc.bwd_count ? size_t(rc.bwd_count) : size_t(sc.n_sets) * sc.n_gaussians;
+  const int grid = grid_for(n * LPG, 128);
   preprocess_bwd_kernel<K, LENS, false, LPG><<<grid, 128, 0, st>>>(sc, vw, rc, rank_of, grad2d, gr);
 }
 
@@ -1128,7 +1130,7 @@ gsb_status launch_camera_bwd(const gsb_scene& sc, const gsb_views& vw, const Ren
 gsb_status launch_preprocess_bwd(const gsb_scene& sc, const gsb_views& vw, const RenderConsts& rc,
                                  const int32_t* rank_of, const float* grad2d, const gsb_scene_grads& gr,
                                  cudaStream_t st) {
-  const size_t n = size_t(sc.n_sets) * sc.n_gaussians;
+  const size_t n = rc.bwd_count ? size_t(rc.bwd_count) : size_t(sc.n_sets) * sc.n_gaussians;
   const int grid = grid_for(n, 128);
   const bool raw = sc.flags & GSB_SCENE_RAW;
   const int deg = raw ? sc.sh_degree : -1;

@@ -408,6 +408,7 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
   const uint32_t hi = uint32_t((uint64_t(seg + 1) * n_list) / NSEG);
   const float* recs = a.records + size_t(view) * a.G * GSB_RECORD_FLOATS;
   float* g2 = a.grad2d + size_t(view) * a.G * GSB_GRAD2D_FLOATS;
+  const float inv_f0 = 1.0f / rc.f0;
   const WarpSlots ws{s_geo[lw], s_cot[lw], s_col[lw], s_rank[lw]};
 
   const size_t HW = size_t(a.H) * a.W;
@@ -480,8 +481,16 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           const float alpha = fminf(fmaxf(araw, 0.0f), rc.alpha_clamp);
           const bool on = live && alpha >= rc.alpha_cutoff;
           const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
+#ifdef GSB_BWD_EXACT_UNBLEND
+          const float qf = f * inv_f0;  // the forward's factor, same rounding
+          float rq = __fdividef(1.0f, qf);
+          rq = fmaf(rq, fmaf(-qf, rq, 1.0f), rq);  // one Newton step
+          const float rf = rq * inv_f0;
+          const float Sb = S[k] * rq;
+#else
           const float rf = __fdividef(1.0f, f);
           const float Sb = S[k] * (rc.f0 * rf);  // S before this entry: S_after / (f / F0)
+#endif
           S[k] = on ? Sb : S[k];
           const float T = Sb * ct.w;
           const float w = on ? T * alpha : 0.0f;
@@ -519,8 +528,16 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           const float alpha = fminf(fmaxf(araw, 0.0f), rc.alpha_clamp);
           if (!(alpha >= rc.alpha_cutoff)) continue;
           const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
+#ifdef GSB_BWD_EXACT_UNBLEND
+          const float qf = f * inv_f0;  // the forward's factor, same rounding
+          float rq = __fdividef(1.0f, qf);
+          rq = fmaf(rq, fmaf(-qf, rq, 1.0f), rq);  // one Newton step
+          const float rf = rq * inv_f0;
+          S[k] = S[k] * rq;
+#else
           const float rf = __fdividef(1.0f, f);
           S[k] = S[k] * (rc.f0 * rf);  // S before this entry: S_after / (f / F0)
+#endif
           const float T = S[k] * ct.w;
           const float4 col = s_col[lw][j];
           const float w = T * alpha;
@@ -621,6 +638,11 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
 // largest grids (32 x 1080p: 66 -> 60 ms; 8 x 384^2: 0.60 -> 0.69 ms).
 constexpr uint64_t kFwdPairedTiles = 32768;
 constexpr uint64_t kBwdPairedTiles = 2048;
+// Four pixels per lane (an 8 x 16 block per warp, two warps per 16x16 tile) halve the per-entry
+// cost of the walk and the gradient reduction once more; the backward takes them on grids this
+// large.  Measured on one B200, 8 x 1920x1080 (65k tiles): backward 31.9 -> 26.9 ms with four; the
+// forward, whose pixels stop early and need no reduction, 11.70 -> 11.94 ms, so it keeps two.
+constexpr uint64_t kBwdQuadTiles = 32768;
 // Below this many tiles the backward cuts every tile's list in four (gsb_options.backward_segments
 // = 0): four times the CTAs and a quarter of the serial walk per tile, which lets it pair pixels
 // per lane at any size, for 72 bytes of checkpoint per pixel.  Measured on one B200, 16 x 128^2
@@ -717,6 +739,7 @@ static int lane_pixels(uint64_t tiles, uint64_t threshold, bool backward, int ti
   if (!force) force = forced_px("GSB200_RASTER_PX");
   if (force == 4 && tile != 16) force = 2;
   if (force) return force;
+  if (backward && tile == 16 && tiles >= kBwdQuadTiles) return 4;
   return tiles >= threshold ? 2 : 1;
 }
 

@@ -140,6 +140,19 @@ def read_words(words: list[torch.Tensor], own_buffer: bool = False) -> _Words:
 # point, i.e. when the backward of that frame has been queued or when the next forward waits for
 # its pair count, whichever comes first.  No extra host-device synchronisation.
 _PENDING: dict[int, list[tuple[str, _Words]]] = {}
+
+# Data-parallel gradient reducer (distributed.GradientAllReduce) the backward hands its parameter
+# gradients to, or None.
+_GRAD_REDUCER = None
+
+
+def set_gradient_reducer(reducer) -> None:
+    """Installs (or, with None, removes) the reducer the render backward sums its parameter
+    gradients over ranks with (distributed.GradientAllReduce): the sum then happens inside the
+    backward, overlapped with the chain-rule kernel, and the returned gradients are already
+    summed.  Scenes with per-clip Gaussian sets or a dynamic bank are not reduced."""
+    global _GRAD_REDUCER
+    _GRAD_REDUCER = reducer
 _PENDING_LOCK = threading.Lock()
 
 
@@ -332,9 +345,15 @@ def backward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, 
                                                       _lib.ptr(state.ckpt),
                                                       d_image.data_ptr(), _lib.ptr(d_alpha), _lib.ptr(d_depth),
                                                       _lib.ptr(view_scale), grad2d.data_ptr(), st))
-    out = {k: torch.empty_like(tensors[k]) for k in ("means", "scales", "quats", "opacities", "colors")}
-    if sspec.velocity:
-        out["velocity"] = torch.empty_like(tensors["velocity"])
+    # every parameter gradient is a view of one flat buffer: a data-parallel sum over ranks is then
+    # one in-place collective (distributed.allreduce_gradients), with no gather or scatter copies
+    names = ["means", "scales", "quats", "opacities", "colors"] + (["velocity"] if sspec.velocity else [])
+    flat = torch.empty(sum(tensors[k].numel() for k in names), dtype=torch.float32, device=dev)
+    out, off = {}, 0
+    for k in names:
+        n = tensors[k].numel()
+        out[k] = flat[off:off + n].view(tensors[k].shape)
+        off += n
     g = _lib.SceneGrads()
     g.means, g.scales, g.quats = out["means"].data_ptr(), out["scales"].data_ptr(), out["quats"].data_ptr()
     g.opacities, g.colors = out["opacities"].data_ptr(), out["colors"].data_ptr()
@@ -343,9 +362,23 @@ def backward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, 
         for k in ("bank_mu", "bank_rot", "bank_alpha"):
             out[k] = torch.empty_like(tensors[k])
         g.bank_mu, g.bank_rot, g.bank_alpha = (out[k].data_ptr() for k in ("bank_mu", "bank_rot", "bank_alpha"))
-    with _stage("preprocess_bwd"):
-        _lib.check("gsb_preprocess_bwd", L.gsb_preprocess_bwd(scene, views, opts, state.rank_of.data_ptr(),
-                                                              grad2d.data_ptr(), g, st))
+    reducer = _GRAD_REDUCER
+    if reducer is not None and sspec.n_sets == 1 and not sspec.bank_basis and reducer.active():
+        # chain rule in ranges of Gaussians; each range's rows are summed over the ranks (on the
+        # collective's stream) while the next range is computed
+        G1 = sspec.n_gaussians
+        with _stage("preprocess_bwd"):
+            for c in range(reducer.buckets):
+                g0, g1 = c * G1 // reducer.buckets, (c + 1) * G1 // reducer.buckets
+                _lib.check("gsb_preprocess_bwd_range",
+                           L.gsb_preprocess_bwd_range(scene, views, opts, state.rank_of.data_ptr(), grad2d.data_ptr(),
+                                                      g, g0, g1 - g0, st))
+                reducer.reduce([out[k].view(G1, -1)[g0:g1] for k in names])
+            reducer.finish()
+    else:
+        with _stage("preprocess_bwd"):
+            _lib.check("gsb_preprocess_bwd", L.gsb_preprocess_bwd(scene, views, opts, state.rank_of.data_ptr(),
+                                                                  grad2d.data_ptr(), g, st))
     check_pending(dev)  # the forward's binning status, while the GPU runs the kernels just queued
     if camera:
         out["cam_intrinsics"] = torch.empty(B, 4, dtype=torch.float32, device=dev)

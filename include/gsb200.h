@@ -309,6 +309,13 @@ GSB_API gsb_status gsb_raster_bwd(const gsb_views* views, const gsb_options* opt
 GSB_API gsb_status gsb_preprocess_bwd(const gsb_scene* scene, const gsb_views* views,
                                       const gsb_options* opts, const int32_t* rank_of,
                                       const float* grad2d, gsb_scene_grads* grads, void* stream);
+/* gsb_preprocess_bwd for the Gaussians (set * G + index) [first, first + count) only: writes
+   their rows of the outputs and nothing else, so the rows can be handed to a collective while the
+   next range is computed (no counterpart in the reference: its autograd has no such split). */
+GSB_API gsb_status gsb_preprocess_bwd_range(const gsb_scene* scene, const gsb_views* views,
+                                            const gsb_options* opts, const int32_t* rank_of,
+                                            const float* grad2d, gsb_scene_grads* grads,
+                                            int64_t first, int64_t count, void* stream);
 
 /* ---- stage 7b: camera gradients (torch autograd through common.py / projection.py into the
    camera tensors, which the implicit-camera models of gs_models/implicit_camera.py:146-262

@@ -8,7 +8,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from dynaworld_b200.distributed import allreduce_gradients, shard_views
+from dynaworld_b200.distributed import GradientAllReduce, allreduce_gradients, shard_views, shared_span
 
 
 def test_shard_views_cover_and_balance():
@@ -45,6 +45,18 @@ def _worker(rank, world, port, mode, results):
             g2 = torch.arange(5, dtype=torch.float32) * (rank + 1)
             allreduce_gradients([g1, None, g2])
             results[rank] = (g1.sum().item(), g2.tolist())
+        elif mode == "span":
+            # views of one flat buffer, as the render backward returns them: reduced in place
+            flat = torch.arange(12, dtype=torch.float32) * (rank + 1)
+            views = [flat[0:3].view(3, 1), flat[3:7], flat[7:12].view(5)]
+            assert shared_span(views) is not None
+            allreduce_gradients(views)
+            red = GradientAllReduce(buckets=2)
+            assert red.active()
+            extra = torch.ones(4) * (rank + 1)
+            red.reduce([extra[:2], extra[2:]])
+            red.finish()
+            results[rank] = (flat.tolist(), extra.tolist())
         elif mode == "rank_dies":
             if rank == 1:
                 raise SystemExit(3)  # leaves between steps, nothing in flight
@@ -69,6 +81,26 @@ def test_allreduce_sums_across_two_ranks():
         assert results[0] == results[1]
         assert results[0][0] == pytest.approx(12 * 3.0)
         assert results[0][1] == pytest.approx([0.0, 3.0, 6.0, 9.0, 12.0])
+
+
+def test_shared_span_detects_one_flat_buffer():
+    flat = torch.zeros(10)
+    assert shared_span([flat[4:10], flat[0:4]]) is not None
+    assert shared_span([flat[0:4], flat[5:10]]) is None  # a gap
+    assert shared_span([flat[0:4], torch.zeros(6)]) is None  # another storage
+    assert shared_span([flat.view(2, 5)[:, :2]]) is None  # not contiguous
+    span = shared_span([flat[2:5], flat[5:9]])
+    assert span.numel() == 7 and span.data_ptr() == flat[2:].data_ptr()
+
+
+def test_allreduce_in_place_on_views_and_reducer():
+    port = _free_port()
+    with mp.get_context("spawn").Manager() as m:
+        results = m.dict()
+        mp.spawn(_worker, args=(2, port, "span", results), nprocs=2, join=True)
+        assert results[0] == results[1]
+        assert results[0][0] == pytest.approx([3.0 * i for i in range(12)])
+        assert results[0][1] == pytest.approx([3.0] * 4)
 
 
 def test_dead_rank_surfaces_as_error_not_hang():

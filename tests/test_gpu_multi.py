@@ -26,7 +26,7 @@ def _grads(wl, device):
     return {k: v for k, v in out.items() if k.startswith("grad_")}, out["loss"]
 
 
-def _rank(rank, world, port, queue):
+def _rank(rank, world, port, queue, mode="explicit"):
     import sys
 
     sys.path.insert(0, os.path.dirname(__file__))
@@ -45,9 +45,18 @@ def _rank(rank, world, port, queue):
         full = synthetic.dynamic128(scale=0.125, image_scale=0.5, frames=FRAMES)
         sh = shard_views(FRAMES, world, rank)
         part = full.views(sh.start, sh.stop)
-        grads, _ = _grads(part, dev)
-        tensors = [grads[k].to(dev) for k in sorted(grads)]
-        allreduce_gradients(tensors)
+        if mode == "reducer":  # summed inside the backward, overlapped with the chain rule
+            from dynaworld_b200.distributed import GradientAllReduce
+            from dynaworld_b200.render import set_gradient_reducer
+
+            set_gradient_reducer(GradientAllReduce(buckets=3))
+            grads, _ = _grads(part, dev)
+            set_gradient_reducer(None)
+            tensors = [grads[k].to(dev) for k in sorted(grads)]
+        else:
+            grads, _ = _grads(part, dev)
+            tensors = [grads[k].to(dev) for k in sorted(grads)]
+            allreduce_gradients(tensors)
         if rank == 0:
             single, _ = _grads(full, dev)
             worst = 0.0
@@ -61,11 +70,12 @@ def _rank(rank, world, port, queue):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_allreduce_matches_single_gpu():
+@pytest.mark.parametrize("mode", ["explicit", "reducer"])
+def test_two_gpu_allreduce_matches_single_gpu(mode):
     ctx = torch.multiprocessing.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, queue)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, queue, mode)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
