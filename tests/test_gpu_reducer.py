@@ -1,10 +1,12 @@
 """The backward's bucketed chain rule (gsb_preprocess_bwd_range, used when a data-parallel
 reducer is installed) on one GPU: a reducer that records the buckets instead of summing over
-ranks must leave the gradients bit-identical to the one-launch chain rule, hand over every
-Gaussian's rows exactly once, and return gradients that are views of one flat buffer."""
+ranks must leave the gradients equal to the one-launch chain rule (up to the order of the
+reverse blend's float atomics, which differs between any two runs), hand over every Gaussian's
+rows exactly once, and return gradients that are views of one flat buffer."""
 import pytest
 import torch
 
+from conftest import grad_close
 from dynaworld_b200 import synthetic
 from dynaworld_b200.distributed import shared_span
 from dynaworld_b200.render import set_gradient_reducer
@@ -40,7 +42,8 @@ def test_bucketed_chain_rule_matches_one_launch(buckets):
         set_gradient_reducer(None)
     assert sum(rec.rows) == wl.n_gaussians and len(rec.rows) == buckets
     for k in ("means", "log_scales", "quats", "opacity_logits", "sh", "velocity"):
-        assert torch.equal(out[f"grad_{k}"], ref[f"grad_{k}"]), k
+        ok, err, scale = grad_close(out[f"grad_{k}"], ref[f"grad_{k}"], 1e-5)
+        assert ok, f"{k}: {err:.3e} vs {scale:.3e}"
 
 
 def test_gradients_are_views_of_one_buffer():

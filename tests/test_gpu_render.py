@@ -15,6 +15,7 @@ from dynaworld_b200.config import B200RendererConfig
 from dynaworld_b200.renderer import render_b200_3dgs, render_b200_3dgs_batch
 from gpu_helpers import DEV, keys_np, records_np, render_raw, sorted_ids_from_rank, stages
 from oracle import splat_oracle as so
+from oracle import tiled_oracle
 from oracle import tiles_oracle as to
 
 pytestmark = pytest.mark.gpu
@@ -65,6 +66,49 @@ def test_exact_mode_lists_bit_exact(case, ellipse):
                                                 wl.width, 16, np.float32(cfg.alpha_cutoff), ellipse_test=ellipse))
     ref = to.sort_pairs(per_view, to.n_tiles_for(wl.height, wl.width, 16))
     np.testing.assert_array_equal(keys_np(st), ref)
+
+
+def _large_splat_scene():
+    """2 views of 192x192 from the multiview384 generator (2000 Gaussians) with a quarter of them
+    grown 4-12x: many Gaussians span more than 32 tiles (the warp-cooperative emission path) next
+    to small ones (the per-thread path)."""
+    wl = synthetic.multiview384(scale=0.01, image_scale=0.5, views=2)
+    g = torch.Generator().manual_seed(17)
+    grow = torch.rand(wl.n_gaussians, generator=g) < 0.25
+    wl.log_scales[:, grow] += torch.log(4.0 + 8.0 * torch.rand(int(grow.sum()), 1, generator=g))
+    return wl
+
+
+@pytest.mark.parametrize("tile", [8, 16])
+@pytest.mark.parametrize("ellipse", [True, False])
+def test_lists_of_large_splats(tile, ellipse):
+    """Keys of Gaussians emitted by a whole warp (more than 32 tiles) equal the numpy restatement."""
+    wl = _large_splat_scene()
+    cfg = B200RendererConfig(tile_size=tile, ellipse_culling=ellipse)
+    _, _, _, st = stages(wl, cfg)
+    rec = records_np(st, wl.n_views, wl.n_gaussians)
+    per_view = [to.exact_pairs_one_view(rec[b][:, 0], rec[b][:, 1], rec[b][:, 2], rec[b][:, 3], rec[b][:, 4],
+                                        rec[b][:, 5], wl.height, wl.width, tile, np.float32(cfg.alpha_cutoff),
+                                        ellipse_test=ellipse) for b in range(wl.n_views)]
+    ref = to.sort_pairs(per_view, to.n_tiles_for(wl.height, wl.width, tile))
+    np.testing.assert_array_equal(keys_np(st), ref)
+    ranks = (ref & np.uint64(0xFFFFFFFF)).astype(np.int64) + (ref >> np.uint64(32)).astype(np.int64) // \
+        to.n_tiles_for(wl.height, wl.width, tile) * wl.n_gaussians
+    assert np.bincount(ranks).max() > 32  # the warp path ran
+
+
+@pytest.mark.parametrize("tile", [8, 16])
+def test_tiled_compat_large_splats_match_tiled_oracle(tile):
+    """tiled_compat lists of large Gaussians (warp emission, edge-clamped rectangles): the image equals
+    the tiled renderer restated (oracle/tiled_oracle.py)."""
+    wl = _large_splat_scene()
+    out = render_raw(wl, B200RendererConfig(mode="tiled_compat", tile_size=tile), grads=False, loss=False)
+    raw = so.RawGaussians(wl.means, wl.log_scales, wl.quats, wl.opacity_logits, wl.sh, wl.velocity)
+    m, s, q, o, rgb = so.activate(raw, wl.times, wl.camera_to_world, wl.views_per_set)
+    for b in range(wl.n_views):
+        ref = tiled_oracle.render_tiled_view(m[b], s[b], q[b], o[b], rgb[b], wl.height, wl.width, wl.fx[b], wl.fy[b],
+                                             wl.cx[b], wl.cy[b], wl.camera_to_world[b], tile_size=tile)
+        assert (out["image"][b] - ref).abs().max().item() <= IMAGE_TOL
 
 
 @pytest.mark.parametrize("case", GOLDEN_CASES)
