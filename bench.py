@@ -390,40 +390,65 @@ def reference_arm(args, rank, world):
 # main GPU arm
 
 
-def ncu_traffic(kernel: str, workload: str):
-    """DRAM bytes (read + write) of one launch of `kernel` from the committed ncu summary
-    profiles/<kernel>_<workload>.md, or None when there is none for this workload."""
+def _profile_rows(kernel: str, workload: str):
+    """Rows `| `metric` | value unit |` of the committed ncu summary profiles/<kernel>_<workload>.md
+    as {metric: (value, unit)}, and its path; (None, None) when there is none."""
     path = ROOT / "profiles" / f"{kernel}_{workload}.md"
     if not path.exists():
         return None, None
-    total = 0.0
-    scale = {"byte": 1.0, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
-    found = 0
+    rows = {}
     for line in path.read_text().splitlines():
-        for metric in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
-            if f"`{metric}`" in line:
-                value, unit = line.split("|")[2].split()
-                total += float(value) * scale.get(unit, 1.0)
-                found += 1
-    return (total if found == 2 else None), str(path.relative_to(ROOT))
+        cells = line.split("|")
+        if len(cells) >= 3 and cells[1].strip().startswith("`"):
+            parts = cells[2].split()
+            try:
+                rows[cells[1].strip().strip("`")] = (float(parts[0]), parts[1] if len(parts) > 1 else "")
+            except (ValueError, IndexError):
+                pass
+    return rows, str(path.relative_to(ROOT))
+
+
+def ncu_traffic(kernel: str, workload: str, n_pairs: int):
+    """DRAM bytes (read + write) of one launch of `kernel` from the committed ncu summary,
+    per launch of this run: a summary of a smaller slice of the workload (its `pairs` row) is
+    scaled by the pair count, which the traffic follows.  (None, None) when there is no summary."""
+    rows, src = _profile_rows(kernel, workload)
+    if rows is None or "dram__bytes_read.sum" not in rows or "dram__bytes_write.sum" not in rows:
+        return None, src
+    scale = {"byte": 1.0, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
+    total = sum(rows[m][0] * scale.get(rows[m][1], 1.0) for m in ("dram__bytes_read.sum", "dram__bytes_write.sum"))
+    if "pairs" in rows and rows["pairs"][0] > 0:
+        total *= n_pairs / rows["pairs"][0]
+    return total, src
+
+
+# FP32 operations one B200 SM can retire per cycle (128 lanes, an FMA counted as two).
+FP32_FLOP_PER_SM_CYCLE = 256
+B200_SMS = 148
 
 
 def ncu_issue(kernel: str, workload: str):
-    """Issue-slot and SM-busy fractions of `kernel` from the same committed ncu summary (the bound
-    the raster kernels actually meet), or None."""
-    path = ROOT / "profiles" / f"{kernel}_{workload}.md"
-    if not path.exists():
+    """The compute-side bound of `kernel` from the same committed ncu summary: issue-slot use,
+    FP32 operations per cycle as a fraction of the SMs' peak, warp instructions per (tile,
+    Gaussian) pair.  None without a summary."""
+    rows, src = _profile_rows(kernel, workload)
+    if rows is None:
         return None
     out = {}
-    for line in path.read_text().splitlines():
-        for metric, key in (("smsp__issue_active.avg.pct_of_peak_sustained_active", "issue_active_pct"),
-                            ("sm__throughput.avg.pct_of_peak_sustained_elapsed", "sm_throughput_pct"),
-                            ("smsp__inst_executed.sum", "warp_instructions")):
-            if f"`{metric}`" in line:
-                out[key] = float(line.split("|")[2].split()[0])
-    if len(out) != 3:
+    for metric, key in (("smsp__issue_active.avg.pct_of_peak_sustained_active", "issue_active_pct"),
+                        ("sm__throughput.avg.pct_of_peak_sustained_elapsed", "sm_throughput_pct"),
+                        ("smsp__inst_executed.sum", "warp_instructions"),
+                        ("sm__pipe_fma_cycles_active.avg.pct_of_peak_sustained_active", "fma_pipe_pct")):
+        if metric in rows:
+            out[key] = rows[metric][0]
+    if "fp32_flop_per_cycle" in rows:
+        out["fp32_flop_per_cycle"] = rows["fp32_flop_per_cycle"][0]
+        out["fp32_frac"] = rows["fp32_flop_per_cycle"][0] / (FP32_FLOP_PER_SM_CYCLE * B200_SMS)
+    if "pairs" in rows and "warp_instructions" in out:
+        out["warp_instructions_per_pair"] = out["warp_instructions"] / rows["pairs"][0]
+    if "issue_active_pct" not in out:
         return None
-    out["source"] = str(path.relative_to(ROOT))
+    out["source"] = src
     return out
 
 
@@ -597,14 +622,17 @@ def main():
     peak, peak_kind = hbm_peak()
     dur_s = means[dominant] / 1e3
     achieved = alg_bytes / dur_s / 1e9
-    traffic, traffic_src = ncu_traffic(dominant, args.workload) if (args.tile is None and args.segments == 0) else (None, None)
+    traffic, traffic_src = (ncu_traffic(dominant, args.workload, n_pairs) if (args.tile is None and args.segments == 0
+                                                                             and not args.views) else (None, None))
     roofline = {"bound": "hbm", "kernel": f"{dominant} (gsb_{dominant})", "achieved": achieved, "peak": peak,
                 "unit": "GB/s", "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_src,
                 "peak_source": peak_kind, "bytes_per_launch": int(alg_bytes), "pairs": int(n_pairs),
                 "pixels": int(px), "launch_ms": means[dominant],
-                "issue": ncu_issue(dominant, args.workload) if (args.tile is None and args.segments == 0) else None,
-                "note": "raster is issue-bound (records re-read from L2, DRAM traffic below the algorithmic "
-                        "bytes): 'issue' gives the ncu issue-slot use of the same kernel; see profiles/"}
+                "issue": (ncu_issue(dominant, args.workload) if (args.tile is None and args.segments == 0
+                                                                 and not args.views) else None),
+                "note": "the raster is issue-bound (records re-read from L2, DRAM traffic below the algorithmic "
+                        "bytes): 'issue' gives the same kernel's ncu issue-slot use, FP32 operations as a "
+                        "fraction of the SMs' FP32 peak and warp instructions per pair (profiles/)"}
     stage_share = {k: round(v / sum(means.values()), 4) for k, v in means.items()} if means else {}
 
     if rank == 0:

@@ -55,17 +55,23 @@ __device__ __forceinline__ float gauss_falloff_nonpos(float qk) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(qk));
   return y;
 }
-// The backward's per-pixel power gradient is kept divided by k (the 1/k rides on the mask of
-// d min(power, 0) / d power), so the mean gradients come out of the k-scaled conic unchanged and the
-// conic gradients -1/2 sum dpow dx^2 (and so on) take the factor -k / 2 when they are flushed.
+// The backward sums d loss / d power times dx and dy over a lane's pixels; the mean gradients take
+// the slots' k-scaled conic coefficients and the factor 1/k once per entry, the conic gradients
+// -1/2 sum dpow dx^2 (and so on) the factor -1/2 when they are flushed.
 constexpr float kInvFalloffScale = -1.38629436111989061883f;  // 1 / k = -2 ln 2
-constexpr float kConicGradScale = 0.36067376022224085184f;    // -k / 2
+constexpr float kConicGradScale = -0.5f;
 
 // q = A dx^2 + B dx dy + C dy^2 with a fixed rounding sequence (forward and backward agree).
 __device__ __forceinline__ float pair_q(float A, float B, float C, float dx, float dy) {
   const float t0 = __fmul_rn(__fmul_rn(A, dx), dx);
   const float t1 = __fmaf_rn(__fmul_rn(B, dx), dy, t0);
   return __fmaf_rn(__fmul_rn(C, dy), dy, t1);
+}
+
+__device__ __forceinline__ uint32_t lane_mask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
 }
 
 // PX pixels per lane, 4 rows apart: the warp block is 8 wide and 4 * PX high.
@@ -115,9 +121,15 @@ struct WarpSlots {
 // negative (qk never positive), the falloff needs no clamp and d min(power, 0) / d power is 1
 // wherever dx or dy is nonzero.  A chunk whose kept entries are all conditioned takes that path;
 // both paths give the same bits for such an entry, so forward and backward agree whichever each takes.
+// One list entry as the walk reads it: the slot contents.
+struct Entry {
+  float4 geo, cot, col;
+  uint32_t rank;
+};
+
 template <int BH, bool FWD>
-__device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* recs, uint32_t idx, uint32_t li,
-                                           float bx0, float by0, const WarpSlots& s, int lane, bool& conditioned) {
+__device__ __forceinline__ bool entry_of(const RasterArgs& a, const float* recs, uint32_t idx, uint32_t li,
+                                         float bx0, float by0, Entry& en, bool& conditioned) {
   conditioned = false;
   const uint32_t r = min(uint32_t(a.keys[idx]), uint32_t(a.G - 1));  // ranks are < G for valid keys
   const float4* rec = reinterpret_cast<const float4*>(recs + size_t(r) * GSB_RECORD_FLOATS);
@@ -125,12 +137,12 @@ __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* rec
   const float pos = a.rc.compat ? float(li) : float(r);
   const float pw = exp2f(pos * a.rc.log2_f0);
   const float A = r0.z, B = r0.w, C = r1.x, tau = r1.w;
-  s.geo[lane] = make_float4(r0.x, r0.y, A * kFalloffScale, B * kFalloffScale);
+  en.geo = make_float4(r0.x, r0.y, A * kFalloffScale, B * kFalloffScale);
   // T after an entry = S after it * F0 * F0^pos: the forward compares S with the bound
-  s.cot[lane] = make_float4(C * kFalloffScale, FWD ? fmaxf(r1.y, 0.0f) : r1.y,
-                            FWD ? __fdividef(a.rc.t_threshold, a.rc.f0 * pw) : 0.0f, pw);
-  s.col[lane] = make_float4(r2.x, r2.y, r2.z, r1.z);
-  if (s.rank) s.rank[lane] = r;
+  en.cot = make_float4(C * kFalloffScale, FWD ? fmaxf(r1.y, 0.0f) : r1.y,
+                       FWD ? __fdividef(a.rc.t_threshold, a.rc.f0 * pw) : 0.0f, pw);
+  en.col = make_float4(r2.x, r2.y, r2.z, r1.z);
+  en.rank = r;
   if (!(tau >= 0.0f)) return false;
   // half extents of the ellipse (cull_extents: sqrt(tau (A^-1)_ii), +inf for a degenerate conic)
   const float ex = r3.x, ey = r3.y;
@@ -157,6 +169,22 @@ __device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* rec
   return q <= tau * 1.0001f + 0.01f;
 }
 
+__device__ __forceinline__ void store_entry(const WarpSlots& s, int slot, const Entry& en) {
+  s.geo[slot] = en.geo;
+  s.cot[slot] = en.cot;
+  s.col[slot] = en.col;
+  if (s.rank) s.rank[slot] = en.rank;
+}
+
+template <int BH, bool FWD>
+__device__ __forceinline__ bool load_entry(const RasterArgs& a, const float* recs, uint32_t idx, uint32_t li,
+                                           float bx0, float by0, const WarpSlots& s, int lane, bool& conditioned) {
+  Entry en;
+  const bool keep = entry_of<BH, FWD>(a, recs, idx, li, bx0, by0, en, conditioned);
+  store_entry(s, lane, en);
+  return keep;
+}
+
 // Floats a checkpoint slot holds per pixel: S, then the suffix sums of r, g, b, weight, depth.
 constexpr int kCkptFloats = 6;
 
@@ -170,6 +198,9 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
   static_assert(SPLIT * CW == NW, "CTAs must hold whole warp blocks of one tile");
   constexpr int NB = NSEG > 1 ? NSEG - 1 : 1;  // checkpoint slots (boundaries between segments)
   __shared__ float4 s_geo[CW][32], s_cot[CW][32], s_col[CW][32];
+#ifdef GSB_FWD_V2
+  __shared__ uint32_t s_li[CW][32];  // chunk position (lane) of each compacted slot
+#endif
   const RenderConsts& rc = a.rc;
   const uint32_t cta = blockIdx.y * uint32_t(rc.n_tiles) * SPLIT + blockIdx.x;
   const uint32_t slot = cta / SPLIT;
@@ -270,6 +301,78 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
       blend(c, j, fast);
     }
   };
+#ifdef GSB_FWD_V2
+  // The kept entries of a chunk sit in consecutive slots; every lane runs every slot, a pixel that
+  // has stopped or whose alpha is below the cutoff taking alpha 0 with its state kept unchanged
+  // (the same bits as skipping it), so the walk has no per-pixel branches.
+  auto blend2 = [&](uint32_t c, int j, auto fast) {
+    const float4 g = s_geo[lw][j];
+    const float4 ct = s_cot[lw][j];
+    const float4 col = s_col[lw][j];
+    const float dx = __fsub_rn(fx, g.x);
+#pragma unroll
+    for (int k = 0; k < PX; ++k) {
+      const float dy = __fsub_rn(fy[k], g.y);
+      const float qk = pair_q(g.z, g.w, ct.x, dx, dy);
+      const float e = decltype(fast)::value ? gauss_falloff_nonpos(qk) : gauss_falloff(qk);
+      const float a0 = fminf(ct.y * e, rc.alpha_clamp);  // ct.y >= 0
+      const bool take = !done[k] && a0 >= rc.alpha_cutoff;
+      const float alpha = take ? a0 : 0.0f;
+      const float T = S[k] * ct.w;
+      const float w = T * alpha;
+      C0[k] = fmaf(w, col.x, C0[k]);
+      C1[k] = fmaf(w, col.y, C1[k]);
+      C2[k] = fmaf(w, col.z, C2[k]);
+      Ws[k] += w;
+      if (DEPTH) D[k] = fmaf(w, col.w, D[k]);
+      const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
+      const float Sn = S[k] * (f * inv_f0);
+      S[k] = take ? Sn : S[k];
+      if (take && Sn < ct.z) {  // T after this entry below the threshold
+        done[k] = true;
+        n_proc[k] = c - start + s_li[lw][j] + 1u;
+      }
+    }
+  };
+  auto walk2 = [&](uint32_t c, uint32_t m, auto fast) {
+    const int nk = __popc(m);
+    int j = 0;
+    if (NSEG > 1) {
+#pragma unroll
+      for (int s = 0; s < NB; ++s) {
+        if (next == s && bnd[s] < c + 32u) {
+          const uint32_t cut = bnd[s] > c ? bnd[s] - c : 0u;  // chunk positions < cut lie before it
+          const int jb = __popc(m & ((1u << cut) - 1u));
+          for (; j < jb; ++j) blend2(c, j, fast);
+          snapshot(s);
+          next = s + 1;
+        }
+      }
+    }
+    for (; j < nk; ++j) {
+      blend2(c, j, fast);
+      if ((j & 7) == 7 && __all_sync(kFull, all_of(done))) break;
+    }
+  };
+  for (uint32_t c = start; c < end; c += 32) {
+    if (__all_sync(kFull, all_of(done))) break;
+    const uint32_t idx = c + lane;
+    bool cond = false;
+    Entry en;
+    const bool keep = idx < end && entry_of<block_h<PX>(), true>(a, recs, idx, idx - start, bx0, by0, en, cond);
+    const uint32_t m = __ballot_sync(kFull, keep);
+    const bool fast = __all_sync(kFull, cond || !keep);
+    if (keep) {
+      const int pos = __popc(m & lane_mask_lt());
+      store_entry(ws, pos, en);
+      s_li[lw][pos] = uint32_t(lane);
+    }
+    __syncwarp();
+    if (fast) walk2(c, m, std::true_type{});
+    else walk2(c, m, std::false_type{});
+    __syncwarp();  // slots are rewritten by the next chunk
+  }
+#else
   for (uint32_t c = start; c < end; c += 32) {
     if (__all_sync(kFull, all_of(done))) break;
     const uint32_t idx = c + lane;
@@ -283,6 +386,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
     else walk(c, m, std::false_type{});
     __syncwarp();  // slots are rewritten by the next chunk
   }
+#endif
   if (NSEG > 1) {
     // boundaries the pixel never reached (stopped early, or no later entry) hold the final state
 #pragma unroll
@@ -387,6 +491,9 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
   static_assert(SPLIT * CW == NW, "CTAs must hold whole warp blocks of one tile");
   __shared__ float4 s_geo[CW][32], s_cot[CW][32], s_col[CW][32];
   __shared__ uint32_t s_rank[CW][32];
+#ifdef GSB_BWD_V2
+  __shared__ uint32_t s_li[CW][32];  // chunk position (lane) of each compacted slot
+#endif
   const RenderConsts& rc = a.rc;
   const uint32_t cta = blockIdx.y * uint32_t(rc.n_tiles) * (NSEG * SPLIT) + blockIdx.x;
   const uint32_t slot = cta / (NSEG * SPLIT);
@@ -408,7 +515,6 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
   const uint32_t hi = uint32_t((uint64_t(seg + 1) * n_list) / NSEG);
   const float* recs = a.records + size_t(view) * a.G * GSB_RECORD_FLOATS;
   float* g2 = a.grad2d + size_t(view) * a.G * GSB_GRAD2D_FLOATS;
-  const float inv_f0 = 1.0f / rc.f0;
   const WarpSlots ws{s_geo[lw], s_cot[lw], s_col[lw], s_rank[lw]};
 
   const size_t HW = size_t(a.H) * a.W;
@@ -454,70 +560,24 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
 
   // the kept entries m of the chunk at list index cb, last first; fast as in the forward
   auto walk = [&](int64_t cb, uint32_t m, auto fast) {
+#ifdef GSB_BWD_V2
+    for (int j = __popc(m) - 1; j >= 0; --j) {  // compacted slots, last entry first
+      const uint32_t lj = uint32_t(cb) + s_li[lw][j];
+#else
     while (m) {
       const int j = 31 - __clz(m);
       m &= ~(1u << j);
+      const uint32_t lj = uint32_t(cb) + uint32_t(j);
+#endif
       float v[12];
 #pragma unroll
       for (int k = 0; k < 12; ++k) v[k] = 0.0f;
       bool contrib = false;
-      const uint32_t lj = uint32_t(cb) + uint32_t(j);
       if (lj < max_of(n_proc)) {
         const float4 g = s_geo[lw][j];
         const float4 ct = s_cot[lw][j];
         const float dx = __fsub_rn(fx, g.x);
         const float hB = 0.5f * g.w;  // half the cross coefficient
-#ifdef GSB_BWD_PREDICATED
-        const float4 col = s_col[lw][j];
-#pragma unroll
-        for (int k = 0; k < PX; ++k) {
-          // every pixel runs the same instructions; a pixel that does not take this entry (past
-          // its last blended entry, or alpha below the cutoff) keeps S and rs and adds zeros
-          const bool live = lj < n_proc[k];
-          const float dy = __fsub_rn(fy[k], g.y);
-          const float qk = pair_q(g.z, g.w, ct.x, dx, dy);
-          const float e = decltype(fast)::value ? gauss_falloff_nonpos(qk) : gauss_falloff(qk);
-          const float araw = ct.y * e;
-          const float alpha = fminf(fmaxf(araw, 0.0f), rc.alpha_clamp);
-          const bool on = live && alpha >= rc.alpha_cutoff;
-          const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
-#ifdef GSB_BWD_EXACT_UNBLEND
-          const float qf = f * inv_f0;  // the forward's factor, same rounding
-          float rq = __fdividef(1.0f, qf);
-          rq = fmaf(rq, fmaf(-qf, rq, 1.0f), rq);  // one Newton step
-          const float rf = rq * inv_f0;
-          const float Sb = S[k] * rq;
-#else
-          const float rf = __fdividef(1.0f, f);
-          const float Sb = S[k] * (rc.f0 * rf);  // S before this entry: S_after / (f / F0)
-#endif
-          S[k] = on ? Sb : S[k];
-          const float T = Sb * ct.w;
-          const float w = on ? T * alpha : 0.0f;
-          float dldw = g0[k] * col.x + g1[k] * col.y + g2c[k] * col.z + gW[k];
-          if (DEPTH) dldw = fmaf(gD[k], col.w, dldw);
-          const float dlda = T * dldw - rs[k] * rf;
-          rs[k] = fmaf(w, dldw, rs[k]);
-          const float dlr = (on && alpha == araw) ? dlda : 0.0f;
-          const float pmask = decltype(fast)::value
-                                  ? kInvFalloffScale
-                                  : (qk < 0.0f ? kInvFalloffScale : (qk == 0.0f ? 0.5f * kInvFalloffScale : 0.0f));
-          const float dpow = dlr * araw * pmask;
-          const float u = dpow * dx, t = dpow * dy;
-          v[0] = fmaf(g.z, u, fmaf(hB, t, v[0]));
-          v[1] = fmaf(ct.x, t, fmaf(hB, u, v[1]));
-          v[2] = fmaf(u, dx, v[2]);
-          v[3] = fmaf(u, dy, v[3]);
-          v[4] = fmaf(t, dy, v[4]);
-          v[5] = fmaf(dlr, e, v[5]);
-          v[6] = fmaf(g0[k], w, v[6]);
-          v[7] = fmaf(g1[k], w, v[7]);
-          v[8] = fmaf(g2c[k], w, v[8]);
-          if (DEPTH) v[9] = fmaf(gD[k], w, v[9]);
-          contrib = contrib || on;
-        }
-      }
-#else
 #pragma unroll
         for (int k = 0; k < PX; ++k) {
           if (!(lj < n_proc[k])) continue;
@@ -528,16 +588,8 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           const float alpha = fminf(fmaxf(araw, 0.0f), rc.alpha_clamp);
           if (!(alpha >= rc.alpha_cutoff)) continue;
           const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
-#ifdef GSB_BWD_EXACT_UNBLEND
-          const float qf = f * inv_f0;  // the forward's factor, same rounding
-          float rq = __fdividef(1.0f, qf);
-          rq = fmaf(rq, fmaf(-qf, rq, 1.0f), rq);  // one Newton step
-          const float rf = rq * inv_f0;
-          S[k] = S[k] * rq;
-#else
           const float rf = __fdividef(1.0f, f);
           S[k] = S[k] * (rc.f0 * rf);  // S before this entry: S_after / (f / F0)
-#endif
           const float T = S[k] * ct.w;
           const float4 col = s_col[lw][j];
           const float w = T * alpha;
@@ -546,17 +598,16 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           const float dlda = T * dldw - rs[k] * rf;
           rs[k] = fmaf(w, dldw, rs[k]);
           const float dlr = alpha == araw ? dlda : 0.0f;  // the clamp to [0, alpha_clamp] is inactive
-          // d min(power, 0) / d power, power = -q / 2 (torch splits a tie at 0 evenly), divided by k;
-          // q > 0 where qk < 0.  A conditioned entry has q = 0 only at dx = dy = 0, where the mask
-          // multiplies zeros.
-          const float pmask = decltype(fast)::value
-                                  ? kInvFalloffScale
-                                  : (qk < 0.0f ? kInvFalloffScale : (qk == 0.0f ? 0.5f * kInvFalloffScale : 0.0f));
-          const float dpow = dlr * araw * pmask;
+          // d loss / d power, power = -q / 2, through d min(power, 0) / d power (torch splits a tie
+          // at 0 evenly); q > 0 where qk < 0.  A conditioned entry has q = 0 only at dx = dy = 0,
+          // where the mask multiplies zeros.
+          const float dpow = decltype(fast)::value
+                                 ? dlr * araw
+                                 : dlr * araw * (qk < 0.0f ? 1.0f : (qk == 0.0f ? 0.5f : 0.0f));
           const float u = dpow * dx, t = dpow * dy;
-          v[0] = fmaf(g.z, u, fmaf(hB, t, v[0]));
-          v[1] = fmaf(ct.x, t, fmaf(hB, u, v[1]));
-          v[2] = fmaf(u, dx, v[2]);  // conic gradients: times -k/2 once the pixels are summed
+          v[0] += u;  // the mean gradients are linear in these sums: formed once the pixels are summed
+          v[1] += t;
+          v[2] = fmaf(u, dx, v[2]);  // conic gradients: times -1/2 once the pixels are summed
           v[3] = fmaf(u, dy, v[3]);
           v[4] = fmaf(t, dy, v[4]);
           v[5] = fmaf(dlr, e, v[5]);
@@ -566,8 +617,12 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           if (DEPTH) v[9] = fmaf(gD[k], w, v[9]);
           contrib = true;
         }
+        // d loss / d mean = sum dpow (A dx + B/2 dy, C dy + B/2 dx) with the unscaled conic, i.e.
+        // (1/k) times the k-scaled slots' coefficients applied to the sums of u and t
+        const float su = v[0], st = v[1];
+        v[0] = kInvFalloffScale * fmaf(g.z, su, hB * st);
+        v[1] = kInvFalloffScale * fmaf(ct.x, st, hB * su);
       }
-#endif
       const uint32_t cm = __ballot_sync(kFull, contrib);
       if (cm == 0u) continue;
       float* dst = g2 + size_t(s_rank[lw][j]) * GSB_GRAD2D_FLOATS;
@@ -619,10 +674,23 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
   for (int64_t cb = wmax > lo ? int64_t((wmax - 1) / 32) * 32 : -32; cb >= cb_lo; cb -= 32) {
     const uint32_t li = uint32_t(cb) + lane;
     bool cond = false;
+#ifdef GSB_BWD_V2
+    Entry en;
+    const bool keep = li >= lo && li < wmax &&
+                      entry_of<block_h<PX>(), false>(a, recs, start + li, li, bx0, by0, en, cond);
+    const uint32_t m = __ballot_sync(kFull, keep);
+    const bool fast = __all_sync(kFull, cond || !keep);
+    if (keep) {
+      const int pos = __popc(m & lane_mask_lt());
+      store_entry(ws, pos, en);
+      s_li[lw][pos] = uint32_t(lane);
+    }
+#else
     const bool keep = li >= lo && li < wmax &&
                       load_entry<block_h<PX>(), false>(a, recs, start + li, li, bx0, by0, ws, lane, cond);
     const uint32_t m = __ballot_sync(kFull, keep);
     const bool fast = __all_sync(kFull, cond || !keep);
+#endif
     __syncwarp();
     if (fast) walk(cb, m, std::true_type{});
     else walk(cb, m, std::false_type{});
