@@ -38,7 +38,7 @@ PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 1024 * 1024
 
-# Algorithmic bytes of one raster launch (see DESIGN.md "raster roofline"):
+# Algorithmic bytes of one raster launch:
 #   backward: per (tile, Gaussian) pair an 8 B key + a 48 B projected record read and a 40 B
 #   gradient record read-modify-written (80 B); per pixel 4 B transmittance + 4 B state + 12 B
 #   image gradient read.   forward: per pair key + record (56 B); per pixel 24 B written.

@@ -1,6 +1,6 @@
 """Generates the golden fixtures of tests/golden/ from the reference implementation itself.
 
-    python tests/golden/make_golden.py --reference PATH [--only scenes losses tiled_grads]
+    python tests/golden/make_golden.py --reference PATH [--only scenes losses tiled_grads overlap]
     (or DYNAWORLD_REFERENCE=PATH python tests/golden/make_golden.py)
 
 Imports the reference's src/train modules (renderers.dense, renderers.common, renderers.tiled,
@@ -233,6 +233,44 @@ def tiled_grad_cases(R) -> dict:
     return out
 
 
+def overlap_cases(reference: Path) -> dict:
+    """Per-splat tile counts of the reference's exact-conic overlap statistic
+    (exact_conic_overlap_stats, renderers/overlap_metrics.py:286-408: tiles whose pixel-centre box,
+    centres at +0.5, meets the ellipse q <= -2 ln(threshold / opacity)) for the projected Gaussians of
+    view 0 of the five golden scenes, threshold 1/255, tiles of 8 and 16.  The statistic returns
+    totals only, so each splat is counted by its own call."""
+    from renderers.overlap_metrics import exact_conic_overlap_stats  # noqa: E402
+
+    R = ref_modules(reference)
+    out = {}
+    for case, wl in (("static64", syn.static64()), ("dynamic128_small", syn.dynamic128(scale=1 / 16, image_scale=0.5,
+                                                                                        frames=2)),
+                     ("multiview384_small", syn.multiview384(scale=0.01, image_scale=1 / 6, views=2)),
+                     ("clips256_small", syn.clips256(scale=1 / 32, image_scale=0.25, clips=2, frames=2)),
+                     ("edge", edge_workload())):
+        rg = so.RawGaussians(wl.means, wl.log_scales, wl.quats, wl.opacity_logits, wl.sh, wl.velocity)
+        m, s, q, o, rgb = so.activate(rg, wl.times, wl.camera_to_world, wl.views_per_set)
+        with torch.no_grad():
+            m2, inv, _cov, op, _rgb = R["project_batch"](m, s, q, o, rgb, wl.fx, wl.fy, wl.cx, wl.cy,
+                                                          camera_to_world=wl.camera_to_world)
+        means2d = m2[0].float()
+        conics = torch.stack([inv[0, :, 0, 0], 0.5 * (inv[0, :, 0, 1] + inv[0, :, 1, 0]), inv[0, :, 1, 1]], -1).float()
+        opac = op[0, :, 0].float()
+        out[f"{case}_means2d"], out[f"{case}_conics"], out[f"{case}_opacities"] = means2d, conics, opac
+        out[f"{case}_size"] = torch.tensor([wl.height, wl.width])
+        for ts in (8, 16):
+            counts = [int(exact_conic_overlap_stats(means2d[g:g + 1], conics[g:g + 1], opac[g:g + 1],
+                                                    (wl.height, wl.width), tile_size=ts,
+                                                    alpha_threshold=1.0 / 255.0)["total_overlap_keys"])
+                      for g in range(means2d.shape[0])]
+            out[f"{case}_t{ts}_counts"] = torch.tensor(counts, dtype=torch.int64)
+            total = exact_conic_overlap_stats(means2d, conics, opac, (wl.height, wl.width), tile_size=ts,
+                                              alpha_threshold=1.0 / 255.0)["total_overlap_keys"]
+            assert int(total) == sum(counts)
+        print(f"overlap counts: {case}", flush=True)
+    return out
+
+
 def loss_cases(R) -> dict:
     g = torch.Generator().manual_seed(5)
     out = {}
@@ -257,8 +295,8 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("DYNAWORLD_REFERENCE"),
                     help="checkout of nbardy/dynaworld (default: $DYNAWORLD_REFERENCE)")
-    ap.add_argument("--only", nargs="*", default=["scenes", "losses", "tiled_grads"],
-                    choices=["scenes", "losses", "tiled_grads"])
+    ap.add_argument("--only", nargs="*", default=["scenes", "losses", "tiled_grads", "overlap"],
+                    choices=["scenes", "losses", "tiled_grads", "overlap"])
     args = ap.parse_args()
     if not args.reference:
         raise SystemExit("give the reference checkout with --reference PATH or DYNAWORLD_REFERENCE")
@@ -293,6 +331,10 @@ def main() -> None:
     if "tiled_grads" in args.only:
         np.savez_compressed(HERE / "tiled_grads.npz", **to_np(tiled_grad_cases(R)))
         print("wrote tiled_grads.npz", flush=True)
+
+    if "overlap" in args.only:
+        np.savez_compressed(HERE / "overlap.npz", **to_np(overlap_cases(Path(args.reference))))
+        print("wrote overlap.npz", flush=True)
 
 
 if __name__ == "__main__":

@@ -1,6 +1,6 @@
 """Generates tests/golden/splats2d_accuracy.npz from the reference's own 2-D accuracy harness.
 
-    python tests/golden/make_golden_2d.py [--reference /root/reference]
+    python tests/golden/make_golden_2d.py --reference PATH   (or DYNAWORLD_REFERENCE=PATH)
 
 Imports src/benchmarks/splat_renderer_accuracy.py from a checkout of nbardy/dynaworld and, for
 each case, records what the reference computes: the inputs of make_accuracy_case (:190-238; its
@@ -19,6 +19,7 @@ and is all the tests read.
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -33,9 +34,12 @@ EXTRA_CASES = [(48, 64, 64, 2), (96, 80, 160, 1), (128, 128, 400, 1)]
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DYNAWORLD_REFERENCE"),
+                    help="checkout of nbardy/dynaworld (default: $DYNAWORLD_REFERENCE)")
     ap.add_argument("--out", default=str(HERE / "splats2d_accuracy.npz"))
     args = ap.parse_args()
+    if not args.reference:
+        raise SystemExit("give the reference checkout with --reference PATH or DYNAWORLD_REFERENCE")
     sys.path.insert(0, str(Path(args.reference) / "src" / "benchmarks"))
     import splat_renderer_accuracy as acc  # noqa: E402
 

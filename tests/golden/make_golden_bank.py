@@ -1,6 +1,6 @@
 """Generates tests/golden/bank.npz: the reference's dynamic-bank frames, image, loss and gradients.
 
-    python tests/golden/make_golden_bank.py [--reference /root/reference]
+    python tests/golden/make_golden_bank.py --reference PATH   (or DYNAWORLD_REFERENCE=PATH)
 
 For seeded banks this runs the reference's own evaluation
 (gs_models/dynamic_video_token_gs_implicit_camera.py:1206-1224, _eval_dynamic_bank, with the
@@ -21,6 +21,7 @@ Needs the reference checkout; the .npz it writes is committed and is all the tes
 from __future__ import annotations
 
 import argparse
+import os
 import math
 import sys
 from pathlib import Path
@@ -104,8 +105,11 @@ def case_arrays(R, bank: dict, static: dict | None, wl: syn.Workload) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DYNAWORLD_REFERENCE"),
+                    help="checkout of nbardy/dynaworld (default: $DYNAWORLD_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        raise SystemExit("give the reference checkout with --reference PATH or DYNAWORLD_REFERENCE")
     sys.path.insert(0, str(Path(args.reference) / "src" / "train"))
     from gs_models.dynamic_video_token_gs_implicit_camera import (  # noqa: E402
         DynamicGaussianBank,

@@ -1,6 +1,6 @@
 """Generates tests/golden/camera_grads.npz: gradients w.r.t. the cameras from the reference.
 
-    python tests/golden/make_golden_camera.py [--reference /root/reference]
+    python tests/golden/make_golden_camera.py --reference PATH   (or DYNAWORLD_REFERENCE=PATH)
 
 The reference's implicit-camera models predict fx, fy, cx, cy, camera_to_world and lens
 distortion with networks (gs_models/implicit_camera.py:146-262) and train them through the render
@@ -18,6 +18,7 @@ Needs the reference checkout; the .npz it writes is committed and is all the tes
 from __future__ import annotations
 
 import argparse
+import os
 import math
 import sys
 from pathlib import Path
@@ -87,8 +88,11 @@ def case_arrays(R, CameraSpec, wl: syn.Workload, lenses) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DYNAWORLD_REFERENCE"),
+                    help="checkout of nbardy/dynaworld (default: $DYNAWORLD_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        raise SystemExit("give the reference checkout with --reference PATH or DYNAWORLD_REFERENCE")
     sys.path.insert(0, str(Path(args.reference) / "src" / "train"))
     from camera import CameraSpec  # noqa: E402
     from losses import reconstruction_loss_per_image  # noqa: E402

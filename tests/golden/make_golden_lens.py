@@ -1,6 +1,6 @@
 """Generates tests/golden/lens_*.npz: the reference's camera_model rendering with distorted lenses.
 
-    python tests/golden/make_golden_lens.py [--reference /root/reference]
+    python tests/golden/make_golden_lens.py --reference PATH   (or DYNAWORLD_REFERENCE=PATH)
 
 Imports the reference's src/train modules and records, for seeded synthetic scenes seen through
 radial-tangential, OpenCV-fisheye and pinhole CameraSpec values (camera.py:11-31) in one batch,
@@ -16,6 +16,7 @@ committed and are all the tests read.
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -93,8 +94,11 @@ def render_case(R, CameraSpec, wl: syn.Workload, lenses) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DYNAWORLD_REFERENCE"),
+                    help="checkout of nbardy/dynaworld (default: $DYNAWORLD_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        raise SystemExit("give the reference checkout with --reference PATH or DYNAWORLD_REFERENCE")
     sys.path.insert(0, str(Path(args.reference) / "src" / "train"))
     from camera import CameraSpec  # noqa: E402
     from losses import reconstruction_loss_per_image  # noqa: E402
