@@ -14,11 +14,12 @@
 namespace gsb {
 
 constexpr int kMaxTilePasses = 4;
-constexpr int kWarpEmit = 32;  // pairs above which a Gaussian's keys are emitted by the whole warp
 
 // One thread per (view blockIdx.y, depth rank): the Gaussian's keys in its slot of the pair array,
 // and the block's counts of the tile digits its written keys carry (the per-view histograms of
-// the pair sort's passes).
+// the pair sort's passes).  (Emitting the keys of a Gaussian with more than 32 tiles by the whole
+// warp -- a thread per tile row, a warp scan, coalesced stores -- was measured slower on
+// 2 x 1920x1080: 0.53 -> 0.60 ms, the extra registers costing more than the balance gains.)
 __global__ void __launch_bounds__(256) emit_keys_kernel(int32_t G, RenderConsts rc, int H, int W,
                                                         const float* __restrict__ records,
                                                         const int4* __restrict__ rects,
@@ -36,23 +37,18 @@ __global__ void __launch_bounds__(256) emit_keys_kernel(int32_t G, RenderConsts 
   const uint32_t start = r < uint32_t(G) ? offsets[i] : 0u;
   const uint32_t end = r < uint32_t(G) ? offsets[i + 1] : 0u;
   const uint64_t view_base = uint64_t(b) * rc.n_tiles;
-  const bool exact = !rc.compat && rc.ellipse;
-  auto put_at = [&](uint32_t k, uint32_t end_k, int tx, int ty, uint32_t rank) {
-    if (k < end_k && k < n_pairs) {
+  uint32_t k = start;
+  auto put = [&](int tx, int ty) {
+    if (k < end && k < n_pairs) {
       const uint32_t t = uint32_t(ty * rc.tiles_x + tx);
-      keys[k] = ((view_base + t) << 32) | rank;
+      keys[k] = ((view_base + t) << 32) | r;
       for (int p = 0; p < passes; ++p) atomicAdd(&s_hist[p][(t >> (8 * p)) & 0xffu], 1u);
     }
+    ++k;
   };
-  // A Gaussian with more than kWarpEmit pairs is emitted by the whole warp below: one thread per
-  // tile row for its ellipse intervals, a warp scan for the row offsets, and one lane per key for
-  // the stores (coalesced).  Smaller ones are emitted by their own thread.  Both write the same
-  // keys at the same positions (rows in order, tiles in order within a row).
-  const bool big = end - start > uint32_t(kWarpEmit);
-  if (start != end && !big) {
-    uint32_t k = start;
+  if (start != end) {
     const int4 rc4 = rects[i];
-    if (exact) {
+    if (!rc.compat && rc.ellipse) {
       const float4* rec = reinterpret_cast<const float4*>(records + i * GSB_RECORD_FLOATS);
       const float4 r0 = rec[0], r1 = rec[1];
       ExactShape es;
@@ -60,63 +56,20 @@ __global__ void __launch_bounds__(256) emit_keys_kernel(int32_t G, RenderConsts 
         for (int ty = rc4.y; ty <= rc4.w; ++ty) {
           int tx0, tx1;
           if (!exact_row_pairs(es, ty, rc.tile, rc.pixel_center, &tx0, &tx1)) continue;
-          for (int tx = tx0; tx <= tx1; ++tx) put_at(k++, end, tx, ty, r);
+          for (int tx = tx0; tx <= tx1; ++tx) put(tx, ty);
         }
       }
     } else {
       for (int ty = rc4.y; ty <= rc4.w; ++ty)
-        for (int tx = rc4.x; tx <= rc4.z; ++tx) put_at(k++, end, tx, ty, r);
+        for (int tx = rc4.x; tx <= rc4.z; ++tx) put(tx, ty);
     }
     if (k != end) record_error(status, GSB_ERR_KEY_OVERFLOW, int(i));
-  }
-  const int lane = threadIdx.x & 31;
-  uint32_t bigs = __ballot_sync(0xffffffffu, big);
-  while (bigs) {
-    const int src = __ffs(bigs) - 1;
-    bigs &= bigs - 1;
-    const uint32_t rb = __shfl_sync(0xffffffffu, r, src);
-    const size_t ib = size_t(b) * G + rb;
-    const uint32_t sb = __shfl_sync(0xffffffffu, start, src), eb = __shfl_sync(0xffffffffu, end, src);
-    const int4 rc4 = rects[ib];  // same address in every lane: one broadcast load
-    ExactShape es;
-    bool shaped = true;
-    if (exact) {
-      const float4* rec = reinterpret_cast<const float4*>(records + ib * GSB_RECORD_FLOATS);
-      const float4 r0 = rec[0], r1 = rec[1];
-      shaped = exact_shape(r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, rc.alpha_cutoff, H, W, rc.pixel_center, &es);
-    }
-    uint32_t kb = sb;
-    if (shaped) {
-      for (int base = rc4.y; base <= rc4.w; base += 32) {
-        const int ty = base + lane;
-        int tx0 = rc4.x, tx1 = rc4.z;
-        bool row = ty <= rc4.w;
-        if (row && exact) row = exact_row_pairs(es, ty, rc.tile, rc.pixel_center, &tx0, &tx1);
-        const uint32_t n = row ? uint32_t(tx1 - tx0 + 1) : 0u;
-        uint32_t incl = n;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += v;
-        }
-        const uint32_t excl = incl - n;
-        uint32_t rows = __ballot_sync(0xffffffffu, n > 0u);
-        while (rows) {
-          const int rl = __ffs(rows) - 1;
-          rows &= rows - 1;
-          const int rtx0 = __shfl_sync(0xffffffffu, tx0, rl);
-          const uint32_t rn = __shfl_sync(0xffffffffu, n, rl), roff = __shfl_sync(0xffffffffu, excl, rl);
-          for (uint32_t t = lane; t < rn; t += 32) put_at(kb + roff + t, eb, rtx0 + int(t), base + rl, rb);
-        }
-        kb += __shfl_sync(0xffffffffu, incl, 31);
-      }
-    }
-    if (kb != eb && lane == 0) record_error(status, GSB_ERR_KEY_OVERFLOW, int(ib));
   }
   // The last warp to finish adds the block's counts to the view's histograms: no block barrier, so
   // warps done with short Gaussians do not wait for the block's longest one.
   __syncwarp();
   __threadfence_block();
+  const int lane = threadIdx.x & 31;
   uint32_t done = 0u;
   if (lane == 0) done = atomicAdd(&s_done, 1u);
   done = __shfl_sync(0xffffffffu, done, 0);

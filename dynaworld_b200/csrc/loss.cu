@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
       // Box window: a thread keeps running sums along kBoxRun columns of one row (the sum at
       // column c + 1 is the one at c plus input column c + 2 HW + 1 minus input column c), scaled
       // by the tap when stored; about a third of the per-tap loop's instructions.
-      constexpr int kBoxRun = 5;
+      constexpr int kBoxRun = 6;
       constexpr int kRuns = (M + kBoxRun - 1) / kBoxRun;
       const float wk = a.w[0];
       for (int i = tid; i < R * kRuns; i += kLossThreads) {
@@ -162,9 +162,10 @@ __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
     // vertical sums -> SSIM map and its derivatives w.r.t. the three prediction moments
     if (a.box) {
       // Box window: a thread keeps the five column sums of kRunV consecutive mean rows as running
-      // sums (add the row entering the window, drop the one leaving it).  The run lengths of the
-      // passes (5, 4, 4, 2) give each pass about one item per thread of the CTA.
-      constexpr int kRunV = 4;
+      // sums (add the row entering the window, drop the one leaving it).  (Shorter runs, 5 / 4 / 4 / 2
+      // in the four passes for about one item per thread, were measured slower: 8 x 1920x1080
+      // loss 1.94 -> 2.02 ms.)
+      constexpr int kRunV = 6;
       constexpr int kRunsV = (M + kRunV - 1) / kRunV;
       const float wk = a.w[0];
       for (int i = tid; i < M * kRunsV; i += kLossThreads) {
@@ -239,7 +240,7 @@ __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
       }
     };
     if (a.box) {
-      constexpr int kRunH = 4;
+      constexpr int kRunH = 8;
       constexpr int kRunsH = kLossTile / kRunH;
       const float wk = a.w[0];
       for (int i = tid; i < M * kRunsH; i += kLossThreads) {
@@ -297,7 +298,7 @@ __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
   // output rows per thread (running sums of ha down the column for the box window; ha is zero off
   // the image; the mirrored terms only within HW of the top and bottom edges)
   double sum_l1 = 0.0, sum_l2 = 0.0;
-  constexpr int kRunQ = 2;
+  constexpr int kRunQ = 4;
   for (int i = tid; i < kLossTile * (kLossTile / kRunQ); i += kLossThreads) {
     const int cq = i % kLossTile, rq0 = (i / kLossTile) * kRunQ;
     const int qx = x0 + cq;

@@ -55,11 +55,13 @@ __device__ __forceinline__ float gauss_falloff_nonpos(float qk) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(qk));
   return y;
 }
-// The backward sums d loss / d power times dx and dy over a lane's pixels; the mean gradients take
-// the slots' k-scaled conic coefficients and the factor 1/k once per entry, the conic gradients
-// -1/2 sum dpow dx^2 (and so on) the factor -1/2 when they are flushed.
+// The backward's per-pixel power gradient is kept divided by k (the 1/k rides on the mask of
+// d min(power, 0) / d power), so the mean gradients come out of the k-scaled conic unchanged and the
+// conic gradients -1/2 sum dpow dx^2 (and so on) take the factor -k / 2 when they are flushed.
+// (Applying the conic coefficients and 1/k once per entry to per-lane sums instead was measured
+// slower: 8 x 1920x1080 backward 26.9 -> 28.1 ms.)
 constexpr float kInvFalloffScale = -1.38629436111989061883f;  // 1 / k = -2 ln 2
-constexpr float kConicGradScale = -0.5f;
+constexpr float kConicGradScale = 0.36067376022224085184f;    // -k / 2
 
 // q = A dx^2 + B dx dy + C dy^2 with a fixed rounding sequence (forward and backward agree).
 __device__ __forceinline__ float pair_q(float A, float B, float C, float dx, float dy) {
@@ -198,9 +200,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
   static_assert(SPLIT * CW == NW, "CTAs must hold whole warp blocks of one tile");
   constexpr int NB = NSEG > 1 ? NSEG - 1 : 1;  // checkpoint slots (boundaries between segments)
   __shared__ float4 s_geo[CW][32], s_cot[CW][32], s_col[CW][32];
-#ifdef GSB_FWD_V2
-  __shared__ uint32_t s_li[CW][32];  // chunk position (lane) of each compacted slot
-#endif
+  __shared__ uint32_t s_li[CW][32];  // chunk position (lane) of each compacted slot (kCompact)
   const RenderConsts& rc = a.rc;
   const uint32_t cta = blockIdx.y * uint32_t(rc.n_tiles) * SPLIT + blockIdx.x;
   const uint32_t slot = cta / SPLIT;
@@ -301,7 +301,14 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
       blend(c, j, fast);
     }
   };
-#ifdef GSB_FWD_V2
+  // Two walks of a chunk's kept entries.  Compact (two or more pixels per lane): the kept entries
+  // sit in consecutive slots and every lane runs every slot, a pixel that has stopped or whose
+  // alpha is below the cutoff taking alpha 0 with its state kept unchanged (the same bits as
+  // skipping it), so the walk has no per-pixel branches; measured on one B200, 8 x 1920x1080
+  // forward 11.63 -> 11.09 ms.  With one pixel per lane the lane's own early exit pays more
+  // (16 x 128^2: 0.332 ms, 0.351 compact), so it walks the set bits of the keep mask.
+  constexpr bool kCompact = PX >= 2;
+  if constexpr (kCompact) {
   // The kept entries of a chunk sit in consecutive slots; every lane runs every slot, a pixel that
   // has stopped or whose alpha is below the cutoff taking alpha 0 with its state kept unchanged
   // (the same bits as skipping it), so the walk has no per-pixel branches.
@@ -372,7 +379,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
     else walk2(c, m, std::false_type{});
     __syncwarp();  // slots are rewritten by the next chunk
   }
-#else
+  } else {
   for (uint32_t c = start; c < end; c += 32) {
     if (__all_sync(kFull, all_of(done))) break;
     const uint32_t idx = c + lane;
@@ -386,7 +393,8 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
     else walk(c, m, std::false_type{});
     __syncwarp();  // slots are rewritten by the next chunk
   }
-#endif
+  }
+
   if (NSEG > 1) {
     // boundaries the pixel never reached (stopped early, or no later entry) hold the final state
 #pragma unroll
@@ -491,9 +499,6 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
   static_assert(SPLIT * CW == NW, "CTAs must hold whole warp blocks of one tile");
   __shared__ float4 s_geo[CW][32], s_cot[CW][32], s_col[CW][32];
   __shared__ uint32_t s_rank[CW][32];
-#ifdef GSB_BWD_V2
-  __shared__ uint32_t s_li[CW][32];  // chunk position (lane) of each compacted slot
-#endif
   const RenderConsts& rc = a.rc;
   const uint32_t cta = blockIdx.y * uint32_t(rc.n_tiles) * (NSEG * SPLIT) + blockIdx.x;
   const uint32_t slot = cta / (NSEG * SPLIT);
@@ -560,15 +565,10 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
 
   // the kept entries m of the chunk at list index cb, last first; fast as in the forward
   auto walk = [&](int64_t cb, uint32_t m, auto fast) {
-#ifdef GSB_BWD_V2
-    for (int j = __popc(m) - 1; j >= 0; --j) {  // compacted slots, last entry first
-      const uint32_t lj = uint32_t(cb) + s_li[lw][j];
-#else
     while (m) {
       const int j = 31 - __clz(m);
       m &= ~(1u << j);
       const uint32_t lj = uint32_t(cb) + uint32_t(j);
-#endif
       float v[12];
 #pragma unroll
       for (int k = 0; k < 12; ++k) v[k] = 0.0f;
@@ -598,16 +598,17 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           const float dlda = T * dldw - rs[k] * rf;
           rs[k] = fmaf(w, dldw, rs[k]);
           const float dlr = alpha == araw ? dlda : 0.0f;  // the clamp to [0, alpha_clamp] is inactive
-          // d loss / d power, power = -q / 2, through d min(power, 0) / d power (torch splits a tie
-          // at 0 evenly); q > 0 where qk < 0.  A conditioned entry has q = 0 only at dx = dy = 0,
-          // where the mask multiplies zeros.
-          const float dpow = decltype(fast)::value
-                                 ? dlr * araw
-                                 : dlr * araw * (qk < 0.0f ? 1.0f : (qk == 0.0f ? 0.5f : 0.0f));
+          // d min(power, 0) / d power, power = -q / 2 (torch splits a tie at 0 evenly), divided by k;
+          // q > 0 where qk < 0.  A conditioned entry has q = 0 only at dx = dy = 0, where the mask
+          // multiplies zeros.
+          const float pmask = decltype(fast)::value
+                                  ? kInvFalloffScale
+                                  : (qk < 0.0f ? kInvFalloffScale : (qk == 0.0f ? 0.5f * kInvFalloffScale : 0.0f));
+          const float dpow = dlr * araw * pmask;
           const float u = dpow * dx, t = dpow * dy;
-          v[0] += u;  // the mean gradients are linear in these sums: formed once the pixels are summed
-          v[1] += t;
-          v[2] = fmaf(u, dx, v[2]);  // conic gradients: times -1/2 once the pixels are summed
+          v[0] = fmaf(g.z, u, fmaf(hB, t, v[0]));
+          v[1] = fmaf(ct.x, t, fmaf(hB, u, v[1]));
+          v[2] = fmaf(u, dx, v[2]);  // conic gradients: times -k/2 once the pixels are summed
           v[3] = fmaf(u, dy, v[3]);
           v[4] = fmaf(t, dy, v[4]);
           v[5] = fmaf(dlr, e, v[5]);
@@ -617,11 +618,6 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           if (DEPTH) v[9] = fmaf(gD[k], w, v[9]);
           contrib = true;
         }
-        // d loss / d mean = sum dpow (A dx + B/2 dy, C dy + B/2 dx) with the unscaled conic, i.e.
-        // (1/k) times the k-scaled slots' coefficients applied to the sums of u and t
-        const float su = v[0], st = v[1];
-        v[0] = kInvFalloffScale * fmaf(g.z, su, hB * st);
-        v[1] = kInvFalloffScale * fmaf(ct.x, st, hB * su);
       }
       const uint32_t cm = __ballot_sync(kFull, contrib);
       if (cm == 0u) continue;
@@ -674,23 +670,10 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
   for (int64_t cb = wmax > lo ? int64_t((wmax - 1) / 32) * 32 : -32; cb >= cb_lo; cb -= 32) {
     const uint32_t li = uint32_t(cb) + lane;
     bool cond = false;
-#ifdef GSB_BWD_V2
-    Entry en;
-    const bool keep = li >= lo && li < wmax &&
-                      entry_of<block_h<PX>(), false>(a, recs, start + li, li, bx0, by0, en, cond);
-    const uint32_t m = __ballot_sync(kFull, keep);
-    const bool fast = __all_sync(kFull, cond || !keep);
-    if (keep) {
-      const int pos = __popc(m & lane_mask_lt());
-      store_entry(ws, pos, en);
-      s_li[lw][pos] = uint32_t(lane);
-    }
-#else
     const bool keep = li >= lo && li < wmax &&
                       load_entry<block_h<PX>(), false>(a, recs, start + li, li, bx0, by0, ws, lane, cond);
     const uint32_t m = __ballot_sync(kFull, keep);
     const bool fast = __all_sync(kFull, cond || !keep);
-#endif
     __syncwarp();
     if (fast) walk(cb, m, std::true_type{});
     else walk(cb, m, std::false_type{});

@@ -357,8 +357,16 @@ def blend_dense(
     background=(1.0, 1.0, 1.0),
     x0: int = 0,
     y0: int = 0,
+    flip_wsum: torch.Tensor | None = None,
+    flip_image: torch.Tensor | None = None,
+    return_pre: bool = False,
 ):
     """All-pairs blend of dense.py:208-233 for a window [y0,y0+H) x [x0,x0+W).
+
+    ``flip_wsum`` [B,H,W] / ``flip_image`` [B,3,H,W] (bool, optional): pixels where the clamp of
+    the weight sum (dense.py:232) / of the image (:233) takes the other side of its kink, for
+    values within rounding of 0 or 1 (see flip_clamp); the default is torch.clamp's.
+    ``return_pre``: also return the image before its clamp [B,3,H,W].
 
     Returns image [B,3,H,W] (clamped to [0,1]), alpha = sum of weights
     [B,H,W] (before the clamp dense.py:232 applies), depth = sum of
@@ -386,18 +394,36 @@ def blend_dense(
     color = (w.unsqueeze(-1) * rgbs[:, :, None, None, :]).sum(dim=1)  # [B,H,W,3]
     wsum = w.sum(dim=1)
     bg = torch.as_tensor(background, dtype=dtype)
-    out = color + (1.0 - wsum.clamp(0, 1)).unsqueeze(-1) * bg
-    out = out.clamp(0.0, 1.0).permute(0, 3, 1, 2)
+    ws_c = wsum.clamp(0, 1)
+    if flip_wsum is not None:  # the other side of the clamp's kink at these pixels
+        ws_c = torch.where(flip_wsum, flip_clamp(wsum, ws_c), ws_c)
+    out = color + (1.0 - ws_c).unsqueeze(-1) * bg
+    out_c = out.clamp(0.0, 1.0)
+    if flip_image is not None:
+        out_c = torch.where(flip_image.permute(0, 2, 3, 1), flip_clamp(out, out_c), out_c)
+    pre = out.permute(0, 3, 1, 2)
+    out = out_c.permute(0, 3, 1, 2)
     d = None
     if depth is not None:
         d = (w * depth[:, :, None, None]).sum(dim=1)
+    if return_pre:
+        return out, wsum, d, pre
     return out, wsum, d
+
+
+def flip_clamp(x: torch.Tensor, clamped: torch.Tensor) -> torch.Tensor:
+    """The clamp of ``x`` to [0, 1] from the other side of its kink: where torch.clamp passes the
+    gradient (0 <= x <= 1) the value is kept and the gradient blocked; where it blocks it, x itself
+    (within rounding of the bound at the pixels this is used for) passes it."""
+    inside = (x >= 0) & (x <= 1)
+    return torch.where(inside, clamped.detach(), x)
 
 
 def render_dense(
     means, scales, quats, opacities, rgbs, H, W, fx, fy, cx, cy, camera_to_world,
     *, near_plane=MIN_RENDER_DEPTH, pixel_center=0.0, eps=1e-6, alpha_clamp=0.99,
     background=(1.0, 1.0, 1.0), sort_key=None, x0=0, y0=0, lens_models=None, distortion=None,
+    flip_wsum=None, flip_image=None, return_pre=False,
 ):
     """Projection + dense blend: render_pytorch_3dgs_batch restated (dense.py:170-236)."""
     m2, inv, _cov, op, rgb, z, _order = project_batch(
@@ -407,6 +433,7 @@ def render_dense(
     return blend_dense(
         m2, inv, op, rgb, z, H, W, pixel_center=pixel_center, eps=eps,
         alpha_clamp=alpha_clamp, background=background, x0=x0, y0=y0,
+        flip_wsum=flip_wsum, flip_image=flip_image, return_pre=return_pre,
     )
 
 

@@ -20,7 +20,7 @@ from __future__ import annotations
 
 import torch
 
-from .splat_oracle import MIN_RENDER_DEPTH, project_batch
+from .splat_oracle import MIN_RENDER_DEPTH, flip_clamp, project_batch
 
 
 def gaussian_bounds(means2d, cov2d, opacities, H, W, bound_scale=3.0, alpha_threshold=1.0 / 255.0):
@@ -82,8 +82,11 @@ def project_view(means, scales, quats, opacities, rgbs, fx, fy, cx, cy, camera_t
     return m2[0], inv[0], cov[0], op[0], rgb[0]
 
 
-def blend_tile(m2, inv, op, rgb, ids, ox: int, oy: int, tile_size: int, eps=1e-6, alpha_clamp=0.99):
-    """tiled.py:178-194 for one tile: [tile, tile, 3] before the image clamp."""
+def blend_tile(m2, inv, op, rgb, ids, ox: int, oy: int, tile_size: int, eps=1e-6, alpha_clamp=0.99, flip=None,
+               with_wsum=False):
+    """tiled.py:178-194 for one tile: [tile, tile, 3] before the image clamp.  ``flip`` [tile, tile]
+    (bool, optional): pixels where the clamp of the weight sum takes the other side of its kink.
+    ``with_wsum``: return (colour, weight sum)."""
     dtype = m2.dtype
     ly, lx = torch.meshgrid(torch.arange(tile_size, dtype=dtype), torch.arange(tile_size, dtype=dtype),
                             indexing="ij")
@@ -96,13 +99,22 @@ def blend_tile(m2, inv, op, rgb, ids, ox: int, oy: int, tile_size: int, eps=1e-6
     T = torch.cat([alpha.new_ones((1, tile_size, tile_size)), torch.cumprod(1.0 - alpha[:-1] + eps, dim=0)], 0)
     w = T * alpha
     col = (w.unsqueeze(-1) * rgb[ids][:, None, None, :]).sum(0)
-    return col + (1.0 - w.sum(0).unsqueeze(-1).clamp(0, 1))
+    ws = w.sum(0)
+    ws_c = ws.clamp(0, 1)
+    if flip is not None:
+        ws_c = torch.where(flip, flip_clamp(ws, ws_c), ws_c)
+    if with_wsum:
+        return col + (1.0 - ws_c.unsqueeze(-1)), ws
+    return col + (1.0 - ws_c.unsqueeze(-1))
 
 
 def render_tiled_view(means, scales, quats, opacities, rgbs, H, W, fx, fy, cx, cy, camera_to_world, *,
                       tile_size=8, bound_scale=3.0, alpha_threshold=1.0 / 255.0, near_plane=MIN_RENDER_DEPTH,
-                      eps=1e-6, alpha_clamp=0.99):
-    """One view ([G,*] activated tensors, scalar intrinsics, [4,4] camera) -> image [3,H,W]."""
+                      eps=1e-6, alpha_clamp=0.99, flip_wsum=None, flip_image=None, return_pre=False):
+    """One view ([G,*] activated tensors, scalar intrinsics, [4,4] camera) -> image [3,H,W].
+    ``flip_wsum`` [H,W] / ``flip_image`` [3,H,W] (bool, optional): pixels whose weight-sum / image
+    clamp takes the other side of its kink (splat_oracle.flip_clamp).  ``return_pre``: return
+    (image, weight sum [H,W], image before its clamp [3,H,W])."""
     m2, inv, cov, op, rgb = project_view(means, scales, quats, opacities, rgbs, fx, fy, cx, cy, camera_to_world,
                                          near_plane)
     bounds = gaussian_bounds(m2.detach(), cov.detach(), op.detach(), H, W, bound_scale, alpha_threshold)
@@ -110,10 +122,30 @@ def render_tiled_view(means, scales, quats, opacities, rgbs, H, W, fx, fy, cx, c
     lists = tile_lists(*bounds, tile_size, tiles_x)
     Hp = -(-H // tile_size) * tile_size
     Wp = -(-W // tile_size) * tile_size
-    canvas = {tid: blend_tile(m2, inv, op, rgb, ids, (tid % tiles_x) * tile_size, (tid // tiles_x) * tile_size,
-                              tile_size, eps, alpha_clamp) for tid, ids in lists.items()}
+    fw = None
+    if flip_wsum is not None:
+        fw = torch.zeros(Hp, Wp, dtype=torch.bool)
+        fw[:H, :W] = flip_wsum
+
+    def flip_of(tid):
+        if fw is None:
+            return None
+        ox, oy = (tid % tiles_x) * tile_size, (tid // tiles_x) * tile_size
+        return fw[oy:oy + tile_size, ox:ox + tile_size]
+
+    parts = {tid: blend_tile(m2, inv, op, rgb, ids, (tid % tiles_x) * tile_size, (tid // tiles_x) * tile_size,
+                             tile_size, eps, alpha_clamp, flip_of(tid), with_wsum=True) for tid, ids in lists.items()}
     blank = torch.ones(tile_size, tile_size, 3, dtype=m2.dtype)  # tiled.py:190, unlisted tiles
-    rows = [torch.cat([canvas.get(ty * tiles_x + tx, blank) for tx in range(Wp // tile_size)], 1)
-            for ty in range(Hp // tile_size)]
+    zero = torch.zeros(tile_size, tile_size, dtype=m2.dtype)
+    rows = [torch.cat([parts[ty * tiles_x + tx][0] if ty * tiles_x + tx in parts else blank
+                       for tx in range(Wp // tile_size)], 1) for ty in range(Hp // tile_size)]
     img = torch.cat(rows, 0)[:H, :W]
-    return img.clamp(0.0, 1.0).permute(2, 0, 1)
+    wrows = [torch.cat([parts[ty * tiles_x + tx][1] if ty * tiles_x + tx in parts else zero
+                        for tx in range(Wp // tile_size)], 1) for ty in range(Hp // tile_size)]
+    wsum = torch.cat(wrows, 0)[:H, :W]
+    img_c = img.clamp(0.0, 1.0)
+    if flip_image is not None:
+        img_c = torch.where(flip_image.permute(1, 2, 0), flip_clamp(img, img_c), img_c)
+    if return_pre:
+        return img_c.permute(2, 0, 1), wsum, img.permute(2, 0, 1)
+    return img_c.permute(2, 0, 1)

@@ -157,3 +157,27 @@ def test_activated_input_gradients_match_reference(case):
     for k, v in act.items():
         ok, err, scale = grad_close(v.grad, g.t(f"ref_grad_act_{k}"))
         assert ok, f"{k}: {err:.3e} vs {scale:.3e}"
+
+
+def test_flip_clamp_takes_the_other_side_of_the_kink():
+    x = torch.tensor([0.5, 1.0 + 1e-7, 1.0 - 1e-7, -1e-7], dtype=torch.float64, requires_grad=True)
+    c = x.clamp(0, 1)
+    f = so.flip_clamp(x, c)
+    torch.testing.assert_close(f[[0, 2]], c[[0, 2]])
+    f.sum().backward()
+    # torch.clamp passes the gradient at 0.5 and 1 - 1e-7 and blocks it outside; flipped, the reverse
+    assert x.grad.tolist() == [0.0, 1.0, 0.0, 1.0]
+
+
+def test_clips256_small_has_a_weight_sum_at_the_kink():
+    """The golden clips256_small scene holds pixels whose weight sum is within 3e-7 of 1, where the
+    reference's gradient jumps with the last bit of that sum (tests/kinks.py)."""
+    g = load_golden("clips256_small")
+    wl = g.workload()
+    raw = so.RawGaussians(*(getattr(wl, k).double() for k in ("means", "log_scales", "quats", "opacity_logits",
+                                                             "sh")), wl.velocity.double())
+    m, s, q, o, rgb = so.activate(raw, wl.times.double(), wl.camera_to_world, wl.views_per_set)
+    key = so.camera_depth_fp32(m.float(), wl.camera_to_world)
+    _img, wsum, _ = so.render_dense(m, s, q, o, rgb, wl.height, wl.width, wl.fx, wl.fy, wl.cx, wl.cy,
+                                    wl.camera_to_world, sort_key=key)
+    assert (wsum - 1.0).abs().min().item() < 3e-7
