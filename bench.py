@@ -259,11 +259,12 @@ def cpu_window(name: str, wl) -> int:
 
 
 def cpu_baseline(name, wl, reps: int = 2):
-    """Dense line: the centre window of frame 0, one warm-up on a 4x4 window, median of ``reps``."""
+    """Dense line: the centre window of frame 0, one warm-up on an 8x8 window (the SSIM window's
+    reflect padding needs at least 6 pixels a side), median of ``reps``."""
     torch.set_num_threads(os.cpu_count() or 1)
     cores = torch.get_num_threads()
     window = cpu_window(name, wl)
-    cpu_sample_time(wl, 4)
+    cpu_sample_time(wl, min(8, window))
     t = statistics.median(cpu_sample_time(wl, window) for _ in range(reps))
     return {
         "value": (window * window) / t / 1e6,
