@@ -22,16 +22,25 @@ MIN_RENDER_DEPTH = 1e-4  # src/train/renderers/common.py:3
 # of stage names, or None for all) limits which stages are bracketed.
 STAGE_EVENTS: list | None = None
 STAGE_FILTER: set | None = None
+# NVTX ranges "gsb:<stage>" around every C-ABI stage call (diagnostics.nvtx).
+NVTX = False
+# When a list, every forward appends the lists it built (diagnostics.collect / FrameLists).
+STATS_FRAMES: list | None = None
 
 
 class _stage:
-    """Brackets one C-ABI call with CUDA events when STAGE_EVENTS is enabled."""
+    """Brackets one C-ABI call with CUDA events when STAGE_EVENTS is enabled, and with an NVTX
+    range when NVTX is."""
 
     def __init__(self, name: str):
         self.name = name
         self.ev = None
+        self.nvtx = False
 
     def __enter__(self):
+        if NVTX:
+            torch.cuda.nvtx.range_push("gsb:" + self.name)
+            self.nvtx = True
         if STAGE_EVENTS is not None and (STAGE_FILTER is None or self.name in STAGE_FILTER):
             self.ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             self.ev[0].record()
@@ -41,6 +50,8 @@ class _stage:
         if self.ev is not None:
             self.ev[1].record()
             STAGE_EVENTS.append((self.name, *self.ev))
+        if self.nvtx:
+            torch.cuda.nvtx.range_pop()
         return False
 
 
@@ -320,6 +331,10 @@ def forward_stages(sspec: SceneSpec, vspec: ViewSpec, cfg: B200RendererConfig, n
     else:
         _defer_status(dev, "gsb_bin", ws3.view(torch.int32)[:1])
     state = FrameState(rank_of, records, keys, ranges, order, pixel_t, pixel_state, n_pairs, ckpt)
+    if STATS_FRAMES is not None:
+        from .diagnostics import FrameLists
+
+        STATS_FRAMES.append(FrameLists(B, G, n_tiles, cfg.tile_size, cfg.mode, offsets, ranges))
     return image, alpha, depth, state
 
 

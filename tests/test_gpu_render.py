@@ -71,8 +71,8 @@ def test_exact_mode_lists_bit_exact(case, ellipse):
 
 def _large_splat_scene():
     """2 views of 192x192 from the multiview384 generator (2000 Gaussians) with a quarter of them
-    grown 4-12x: many Gaussians span more than 32 tiles (the warp-cooperative emission path) next
-    to small ones (the per-thread path)."""
+    grown 4-12x: many Gaussians span more than 32 tiles (long emission runs, many rows) next to
+    small ones."""
     wl = synthetic.multiview384(scale=0.01, image_scale=0.5, views=2)
     g = torch.Generator().manual_seed(17)
     grow = torch.rand(wl.n_gaussians, generator=g) < 0.25
@@ -83,7 +83,7 @@ def _large_splat_scene():
 @pytest.mark.parametrize("tile", [8, 16])
 @pytest.mark.parametrize("ellipse", [True, False])
 def test_lists_of_large_splats(tile, ellipse):
-    """Keys of Gaussians emitted by a whole warp (more than 32 tiles) equal the numpy restatement."""
+    """Keys of Gaussians listed in more than 32 tiles equal the numpy restatement."""
     wl = _large_splat_scene()
     cfg = B200RendererConfig(tile_size=tile, ellipse_culling=ellipse)
     _, _, _, st = stages(wl, cfg)
@@ -95,12 +95,12 @@ def test_lists_of_large_splats(tile, ellipse):
     np.testing.assert_array_equal(keys_np(st), ref)
     ranks = (ref & np.uint64(0xFFFFFFFF)).astype(np.int64) + (ref >> np.uint64(32)).astype(np.int64) // \
         to.n_tiles_for(wl.height, wl.width, tile) * wl.n_gaussians
-    assert np.bincount(ranks).max() > 32  # the warp path ran
+    assert np.bincount(ranks).max() > 32  # some Gaussians span more than 32 tiles
 
 
 @pytest.mark.parametrize("tile", [8, 16])
 def test_tiled_compat_large_splats_match_tiled_oracle(tile):
-    """tiled_compat lists of large Gaussians (warp emission, edge-clamped rectangles): the image equals
+    """tiled_compat lists of large Gaussians (long emission runs, edge-clamped rectangles): the image equals
     the tiled renderer restated (oracle/tiled_oracle.py)."""
     wl = _large_splat_scene()
     out = render_raw(wl, B200RendererConfig(mode="tiled_compat", tile_size=tile), grads=False, loss=False)
