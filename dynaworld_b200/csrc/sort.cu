@@ -24,22 +24,41 @@ struct SortTraits;
 // Keys per thread of a partition.  32-bit keys (the depth order, the tile launch order): 8, measured
 // on one B200 against 16 / 12 (depth order, 8 x 200k keys: 0.188 / 0.179 ms -> 0.180 ms; 16 x 32768
 // keys: 0.084 / 0.090 -> 0.084): twice the partitions fill the GPU at these sizes.
+#ifndef GSB_SORT_ITEMS32
+#define GSB_SORT_ITEMS32 8
+#endif
+#ifndef GSB_SORT_ITEMS64
+#define GSB_SORT_ITEMS64 12
+#endif
 template <>
 struct SortTraits<uint32_t> {
-  static constexpr int kItems = 8;
+  static constexpr int kItems = GSB_SORT_ITEMS32;
+  static constexpr int kItemsVals = GSB_SORT_ITEMS32;
 };
 template <>
 struct SortTraits<uint64_t> {
-  static constexpr int kItems = 12;
+  static constexpr int kItems = GSB_SORT_ITEMS64;
+  static constexpr int kItemsVals = 12;  // 12 B per item staged: the static shared-memory limit
 };
+template <typename K, bool kVals>
+__host__ __device__ constexpr int items_of() {
+  return kVals ? SortTraits<K>::kItemsVals : SortTraits<K>::kItems;
+}
+#ifndef GSB_SORT_WINDOW
+#define GSB_SORT_WINDOW 16
+#endif
+constexpr int kLookbackWindow = GSB_SORT_WINDOW;
 
-__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+// Look-back words hold a partition's flag and digit count in one 32-bit word, so a reader needs
+// no ordering with any other data: relaxed gpu-scope accesses suffice, and a thread can keep a
+// whole window of predecessors' words in flight at once.
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
   return v;
 }
-__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t lanemask_lt() {
   uint32_t m;
@@ -123,7 +142,7 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
     uint32_t* __restrict__ vals_out, uint32_t n, int shift, int nbits, const uint32_t* __restrict__ hist,
     uint32_t* __restrict__ lookback, uint32_t* __restrict__ part_counter, int32_t* __restrict__ status,
     const uint32_t* __restrict__ n_dev, Segments sg) {
-  constexpr int kItems = SortTraits<K>::kItems;
+  constexpr int kItems = items_of<K, kVals>();
   if (kSeg == kSegNone && n_dev) n = min(n, *n_dev);  // partitions past the count find no key, write nothing
   constexpr uint32_t kPart = kSortThreads * kItems;
   __shared__ uint32_t s_part, s_seg;
@@ -183,6 +202,7 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
     hi = lo < n ? min(lo + kPart, n) : lo;
   }
 
+  const uint32_t hist_word = hist[tid];  // this digit's count over the segment (read early)
   // Warp-striped load: warp w owns keys [lo + w*32*kItems, +32*kItems), item j of lane l is key
   // base + 32*j + l, so (j, lane) order is input order: the ranking below is stable.
   const uint32_t base = lo + warp * 32 * kItems + lane;
@@ -220,40 +240,12 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
     s_warp_hist[w][tid] = total;
     total += c;
   }
-  // Publish this partition's digit count, then look back for the exclusive prefix.
+  // Publish this partition's digit count at once; its successors look back while it stages keys.
   uint32_t* my = lookback + size_t(part) * 256 + tid;
-  if (part == first_part) {
-    st_release_u32(my, kFlagIncl | total);
-  } else {
-    st_release_u32(my, kFlagAgg | total);
-  }
-  uint32_t excl = 0;
-  if (part > first_part) {  // partitions of this segment only: first_part's word is inclusive
-    int64_t p = int64_t(part) - 1;
-    const uint32_t spin_limit = sg.spin_limit ? sg.spin_limit : uint32_t(kSpinLimit);
-    uint32_t spins = 0;
-    while (p >= 0) {
-      const uint32_t w = ld_acquire_u32(lookback + size_t(p) * 256 + tid);
-      const uint32_t flag = w & ~kCountMask;
-      if (flag == 0u) {
-        if (++spins > spin_limit) {
-          record_error(status, GSB_ERR_TIMEOUT, int(part));
-          break;
-        }
-        continue;
-      }
-      excl += w & kCountMask;
-      if (flag == kFlagIncl) break;
-      --p;
-    }
-    st_release_u32(my, kFlagIncl | ((excl + total) & kCountMask));
-  }
-  // Digit runs of this partition: local start of each digit, global start of its run.
+  st_relaxed_u32(my, (part == first_part ? kFlagIncl : kFlagAgg) | total);
+  // Stage the partition in (digit, input) order (local positions need no global prefix).
   s_local[tid] = block_excl_scan_256(total, s_tmp, nullptr);
-  const uint32_t digit_start = block_excl_scan_256(hist[tid], s_tmp, nullptr);
-  s_base[tid] = seg_lo + digit_start + excl;
   __syncthreads();
-  // Stage the partition in (digit, input) order, then write each digit's run contiguously.
 #pragma unroll
   for (int j = 0; j < kItems; ++j) {
     const uint32_t d = dig[j];
@@ -262,6 +254,46 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
     s_keys[lpos] = k[j];
     if (kVals) s_vals[lpos] = v[j];
   }
+  const uint32_t digit_start = block_excl_scan_256(hist_word, s_tmp, nullptr);
+  // Look back for the exclusive prefix: a window of predecessors' words per read (the wait for a
+  // predecessor's inclusive count then ends after about one memory round trip, not one per
+  // partition between this one and the last inclusive one), summing counts up to the nearest
+  // inclusive word; a word not yet published is read again.
+  uint32_t excl = 0;
+  if (part > first_part) {  // partitions of this segment only: first_part's word is inclusive
+    const uint32_t spin_limit = sg.spin_limit ? sg.spin_limit : uint32_t(kSpinLimit);
+    uint32_t spins = 0;
+    uint32_t p = part;  // the next window reads p - 1, p - 2, ...
+    for (;;) {
+      uint32_t w[kLookbackWindow];
+#pragma unroll
+      for (int i = 0; i < kLookbackWindow; ++i)
+        w[i] = p >= first_part + 1u + uint32_t(i) ? ld_relaxed_u32(lookback + size_t(p - 1u - uint32_t(i)) * 256 + tid)
+                                                   : kFlagIncl;
+      uint32_t used = 0;
+      bool found = false, waiting = false;
+#pragma unroll
+      for (int i = 0; i < kLookbackWindow; ++i) {
+        if (found || waiting) continue;
+        const uint32_t flag = w[i] & ~kCountMask;
+        if (flag == 0u) {
+          waiting = true;
+          continue;
+        }
+        excl += w[i] & kCountMask;
+        ++used;
+        found = flag == kFlagIncl;
+      }
+      if (found) break;
+      p -= used;
+      if (waiting && ++spins > spin_limit) {
+        record_error(status, GSB_ERR_TIMEOUT, int(part));
+        break;
+      }
+    }
+    st_relaxed_u32(my, kFlagIncl | ((excl + total) & kCountMask));
+  }
+  s_base[tid] = seg_lo + digit_start + excl;
   __syncthreads();
   const uint32_t n_valid = hi - lo;
   for (uint32_t i = tid; i < n_valid; i += kSortThreads) {
@@ -285,14 +317,16 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_kernel(
 
 // ---- host driver ---------------------------------------------------------------------------
 
-static uint32_t parts_for(uint32_t n, int key_bytes) {
-  const uint32_t part = kSortThreads * (key_bytes == 8 ? SortTraits<uint64_t>::kItems : SortTraits<uint32_t>::kItems);
+static uint32_t parts_for(uint32_t n, int key_bytes, bool with_values) {
+  const int items = key_bytes == 8 ? (with_values ? items_of<uint64_t, true>() : items_of<uint64_t, false>())
+                                   : (with_values ? items_of<uint32_t, true>() : items_of<uint32_t, false>());
+  const uint32_t part = kSortThreads * uint32_t(items);
   return (n + part - 1) / part;
 }
 
 size_t radix_sort_workspace(uint32_t n, int key_bytes, int with_values) {
   const int passes = 8;  // worst case (64-bit keys)
-  const uint32_t parts = parts_for(n, key_bytes);
+  const uint32_t parts = parts_for(n, key_bytes, with_values != 0);
   Carver c(nullptr, 0);
   c.take<WorkspaceHeader>(1);
   c.take<uint32_t>(size_t(passes) * 256);          // histograms
@@ -315,7 +349,7 @@ static gsb_status radix_sort_t(const K* keys_in, K* keys_out, const uint32_t* va
     if (with_vals && cudaMemcpyAsync(vals_out, vals_in, size_t(n) * 4, cudaMemcpyDeviceToDevice, stream)) return GSB_ERR_CUDA;
     return GSB_OK;
   }
-  const uint32_t parts = parts_for(n, sizeof(K));
+  const uint32_t parts = parts_for(n, sizeof(K), with_vals);
   Carver c(ws, ws_bytes);
   c.take<WorkspaceHeader>(1);
   uint32_t* hist = c.take<uint32_t>(size_t(8) * 256);
@@ -382,7 +416,7 @@ __global__ void set_word_kernel(uint32_t* p, uint32_t v) { *p = v; }
 // the keys of the first partition are not written.  Workspace: radix_sort_workspace(n, 4, 0).
 gsb_status sort_lookback_timeout_probe(const uint32_t* keys_in, uint32_t* keys_out, uint32_t n, uint32_t spin_limit,
                                        void* ws, size_t ws_bytes, cudaStream_t stream, int32_t* status) {
-  const uint32_t parts = parts_for(n, 4);
+  const uint32_t parts = parts_for(n, 4, false);
   if (parts < 2 || n >= (1u << 30)) return GSB_ERR_SHAPE;
   Carver c(ws, ws_bytes);
   c.take<WorkspaceHeader>(1);
@@ -415,7 +449,7 @@ gsb_status sort_lookback_timeout_probe(const uint32_t* keys_in, uint32_t* keys_o
 constexpr int kSegPasses = 4;
 
 static uint32_t seg_parts(uint32_t seg_len) {
-  const uint32_t part = kSortThreads * SortTraits<uint32_t>::kItems;
+  const uint32_t part = kSortThreads * items_of<uint32_t, true>();
   return (seg_len + part - 1) / part;
 }
 
@@ -497,7 +531,7 @@ gsb_status segmented_sort_run(const uint32_t* keys_in, uint32_t* keys_out, const
 // (clipped to the keys' capacity), so the grid is sized for the worst case and spare partitions
 // return at once.
 
-constexpr uint32_t kPairPart = kSortThreads * SortTraits<uint64_t>::kItems;
+constexpr uint32_t kPairPart = kSortThreads * items_of<uint64_t, false>();
 
 static int pair_passes(uint32_t n_tiles) { return (bits_for(n_tiles) + 7) / 8; }
 int pair_sort_passes(uint32_t n_tiles) { return pair_passes(n_tiles); }

@@ -32,6 +32,7 @@ struct ExactShape {
   int px0, px1, py0, py1;  // pixel rectangle (inclusive), clipped to the image
   double ul;               // row offset b ex / (2c) of the leftmost point (exact_row's one division
                            // that does not depend on the row, formed once)
+  double inv_two_a;        // 1 / (2a): the rows' boundary offsets take a product, not a quotient
 };
 
 __device__ inline double dmul(double x, double y) { return __dmul_rn(x, y); }
@@ -60,15 +61,16 @@ __device__ inline bool exact_shape(float mxf, float myf, float af, float bf, flo
   s->mx = mx, s->my = my, s->a = a, s->b = b, s->c = c, s->det = det, s->L = L, s->ex = ex, s->ey = ey;
   s->px0 = int(px0), s->px1 = int(px1), s->py0 = int(py0), s->py1 = int(py1);
   s->ul = ddiv(dmul(b, ex), dmul(2.0, c));
+  s->inv_two_a = ddiv(1.0, dmul(2.0, a));
   return true;
 }
 
-// x offset of the ellipse boundary at row offset u: (-(b u) -/+ sqrt(4 a L - 4 det u^2)) / (2 a).
+// x offset of the ellipse boundary at row offset u: (-(b u) -/+ sqrt(4 a L - 4 det u^2)) (1 / (2 a)).
 __device__ inline double ellipse_x(const ExactShape& s, double u, bool right) {
   const double disc = fmax(dsub(dmul(dmul(4.0, s.a), s.L), dmul(dmul(4.0, s.det), dmul(u, u))), 0.0);
   const double r = __dsqrt_rn(disc);
   const double nb = -dmul(s.b, u);
-  return ddiv(right ? dadd(nb, r) : dsub(nb, r), dmul(2.0, s.a));
+  return dmul(right ? dadd(nb, r) : dsub(nb, r), s.inv_two_a);
 }
 
 // Tile-column range [tx0, tx1] of tile row ty (false if the row has no tile).
@@ -106,15 +108,15 @@ __device__ inline bool exact_row_pairs(const ExactShape& s, int ty, int tile, fl
   const bool at_l = u0 <= ul && ul <= u1, at_r = u0 <= ur && ur <= u1;
   double xl = -s.ex, xr = s.ex;
   if (!at_l || !at_r) {
-    const double four_aL = dmul(dmul(4.0, s.a), s.L), four_det = dmul(4.0, s.det), two_a = dmul(2.0, s.a);
+    const double four_aL = dmul(dmul(4.0, s.a), s.L), four_det = dmul(4.0, s.det);
     double l[2], r[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const double u = e ? u1 : u0;
       const double root = __dsqrt_rn(fmax(dsub(four_aL, dmul(four_det, dmul(u, u))), 0.0));
       const double nb = -dmul(s.b, u);
-      l[e] = ddiv(dsub(nb, root), two_a);
-      r[e] = ddiv(dadd(nb, root), two_a);
+      l[e] = dmul(dsub(nb, root), s.inv_two_a);
+      r[e] = dmul(dadd(nb, root), s.inv_two_a);
     }
     if (!at_l) xl = fmin(l[0], l[1]);
     if (!at_r) xr = fmax(r[0], r[1]);

@@ -78,11 +78,11 @@ def tile_rects_from_pixel_bounds(min_x, max_x, min_y, max_y, valid, tile_size):
 
 
 def _ellipse_x(a, b, det, L, u, right):
-    """x offset of the ellipse boundary at row offset u: (-(b u) -/+ sqrt(4 a L - 4 det u^2)) / (2 a)."""
+    """x offset of the ellipse boundary at row offset u: (-(b u) -/+ sqrt(4 a L - 4 det u^2)) (1 / (2 a))."""
     disc = max((4.0 * a) * L - (4.0 * det) * (u * u), 0.0)
     r = math.sqrt(disc)
     nb = -(b * u)
-    return ((nb + r) if right else (nb - r)) / (2.0 * a)
+    return ((nb + r) if right else (nb - r)) * (1.0 / (2.0 * a))
 
 
 def exact_pairs_one_view(mx, my, a, b, c, o, H, W, tile_size, alpha_cutoff, pixel_center=0.0, ellipse_test=True):
