@@ -17,6 +17,31 @@ int bits_for(uint64_t count) {
   return b;
 }
 
+// The float nearest 1 / f0 (searched within four ulp) whose float product with f0 is exactly 1;
+// *found = 0 and plain 1 / f0 when there is none.  With it the blend multiplies S by f * inv_f0
+// for a skipped pair (alpha 0, f = f0) and keeps S to the bit.
+static float unit_inverse(float f0, int* found) {
+  volatile float num = 1.0f;
+  const float inv = num / f0;
+  float cand[9] = {inv};
+  float up = inv, down = inv;
+  for (int d = 0; d < 4; ++d) {
+    up = std::nextafter(up, 2.0f);
+    down = std::nextafter(down, 0.0f);
+    cand[1 + 2 * d] = up;
+    cand[2 + 2 * d] = down;
+  }
+  for (float c : cand) {
+    volatile float prod = f0 * c;
+    if (prod == 1.0f) {
+      *found = 1;
+      return c;
+    }
+  }
+  *found = 0;
+  return inv;
+}
+
 RenderConsts make_consts(const gsb_views& v, const gsb_options& o) {
   RenderConsts rc{};
   rc.tile = o.tile_size;
@@ -40,6 +65,7 @@ RenderConsts make_consts(const gsb_views& v, const gsb_options& o) {
   rc.f0 = one + o.eps;  // fl32(1 + eps)
   // T_i = F0^pos_i * S_i in both modes; pos is the depth rank (exact) or the list index (compat)
   rc.log2_f0 = float(std::log2(double(rc.f0)));
+  rc.inv_f0 = unit_inverse(rc.f0, &rc.unit_inv);
   return rc;
 }
 
@@ -232,6 +258,10 @@ GSB_API gsb_status gsb_preprocess_fwd(const gsb_scene* scene, const gsb_views* v
   const RenderConsts rc = make_consts(*views, *opts);
   if ((s = launch_preprocess_fwd(*scene, *views, rc, rank_of, records, reinterpret_cast<int4*>(tile_rects), counts,
                                  cov2d_out, st, status)) != GSB_OK)
+    return s;
+  if (!rc.compat && rc.ellipse &&
+      (s = launch_count_pairs(views->n_views, scene->n_gaussians, rc, views->height, views->width, records,
+                              reinterpret_cast<const int4*>(tile_rects), counts, status, st)) != GSB_OK)
     return s;
   return exclusive_scan(counts, n, pair_offsets, scan_ws, scan_bytes, st, status);
 }
@@ -506,6 +536,9 @@ GSB_API gsb_status gsb_splats2d_preprocess(const gsb_splats2d* splats, int32_t h
   const RenderConsts rc = make_consts(frame, *opts);
   if ((s = launch_preprocess_2d(*splats, height, width, rc, rank_of, records, reinterpret_cast<int4*>(tile_rects),
                                 counts, st)) != GSB_OK)
+    return s;
+  if (rc.ellipse && (s = launch_count_pairs(B, G, rc, height, width, records,
+                                            reinterpret_cast<const int4*>(tile_rects), counts, status, st)) != GSB_OK)
     return s;
   return exclusive_scan(counts, n, pair_offsets, scan_ws, scan_bytes, st, status);
 }

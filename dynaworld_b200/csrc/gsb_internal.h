@@ -80,6 +80,8 @@ struct RenderConsts {
   float bg[3];
   float bound_scale, tiled_threshold;
   float f0;      // fl32(1 + eps): the transmittance factor of an alpha-0 pair
+  float inv_f0;  // a float within a few ulp of 1 / f0 whose product with f0 rounds to exactly 1
+  int unit_inv;  // such a float exists (every eps up to 0.5): S * (f0 * inv_f0) == S
   float log2_f0; // log2(f0): T_i = F0^pos_i * S_i (pos = depth rank, or list index in compat mode)
   // preprocess backward: the Gaussians (set * G + index) [bwd_first, bwd_first + bwd_count) it
   // writes (bwd_count 0: all of them)
@@ -139,6 +141,9 @@ gsb_status launch_preprocess_2d_bwd(const gsb_splats2d& sp, const int32_t* rank_
 
 // Binning (bin.cu).
 // Pair keys in (view, rank) order; hist [B][passes][256] gets the counts of their tile digits.
+// Exact-mode pair count of every (view, depth rank) from the records and tile rects (rank order).
+gsb_status launch_count_pairs(int32_t B, int32_t G, const RenderConsts& rc, int H, int W, const float* records,
+                              const int4* rects, uint32_t* counts, int32_t* status, cudaStream_t st);
 gsb_status launch_emit(int32_t B, int32_t G, const RenderConsts& rc, int H, int W, const float* records,
                        const int4* rects, const uint32_t* offsets, uint32_t n_pairs, uint64_t* keys, uint32_t* hist,
                        int passes, int32_t* status, cudaStream_t st);

@@ -59,11 +59,12 @@ __device__ __forceinline__ float ssim_point(const float m[5], float c1, float c2
   const float B1 = mux2 + muy2 + c1, B2 = sxx + syy + c2;
   const float Draw = B1 * B2;
   const float Dc = fmaxf(Draw, 1e-12f);
-  const float s = (A1 * A2) / Dc;
-  const float dsdD = Draw >= 1e-12f ? -s / Dc : 0.0f;
-  const float ds_mu = (2.0f * muy * A2) / Dc + dsdD * (2.0f * mux * B2);  // explicit mu_x
+  const float rD = 1.0f / Dc;  // one division; the quotients below are products with it
+  const float s = (A1 * A2) * rD;
+  const float dsdD = Draw >= 1e-12f ? -s * rD : 0.0f;
+  const float ds_mu = (2.0f * muy * A2) * rD + dsdD * (2.0f * mux * B2);  // explicit mu_x
   const float ds_sxx = dsdD * B1;
-  const float ds_sxy = 2.0f * A1 / Dc;
+  const float ds_sxy = 2.0f * A1 * rD;
   d_mx = ds_mu - 2.0f * mux * ds_sxx - muy * ds_sxy;
   d_mxx = ds_sxx;
   d_mxy = ds_sxy;
@@ -97,7 +98,7 @@ __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
   }
   __syncthreads();
 
-  double sum_s = 0.0;
+  float sum_s = 0.0f;  // a thread's few values in float; the block sums them in double
   if (ssim) {
     // horizontal window sums for input rows r in [0,R), mean columns c in [0,M)
     if (a.box) {
@@ -182,7 +183,7 @@ __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
           if (gy >= 0 && gy < H && gx >= 0 && gx < W) {
             const float mm[5] = {m[0] * wk, m[1] * wk, m[2] * wk, m[3] * wk, m[4] * wk};
             const float sv = ssim_point(mm, a.c1, a.c2, d_mx, d_mxx, d_mxy);
-            if (r >= HW && r < HW + kLossTile && c >= HW && c < HW + kLossTile) sum_s += double(sv);
+            if (r >= HW && r < HW + kLossTile && c >= HW && c < HW + kLossTile) sum_s += sv;
           }
           const int o = r * M + c;
           gm[0 * M * M + o] = d_mx;
@@ -208,7 +209,7 @@ __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
             for (int q = 0; q < 5; ++q) m[q] = fmaf(wk, hs[q * R * M + row], m[q]);
           }
           const float sv = ssim_point(m, a.c1, a.c2, d_mx, d_mxx, d_mxy);
-          if (r >= HW && r < HW + kLossTile && c >= HW && c < HW + kLossTile) sum_s += double(sv);
+          if (r >= HW && r < HW + kLossTile && c >= HW && c < HW + kLossTile) sum_s += sv;
         }
         gm[0 * M * M + i] = d_mx;
         gm[1 * M * M + i] = d_mxx;
@@ -297,7 +298,7 @@ __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
   // vertical adjoint + gradient + L1/L2 sums over the output tile: column cq, kRunQ consecutive
   // output rows per thread (running sums of ha down the column for the box window; ha is zero off
   // the image; the mirrored terms only within HW of the top and bottom edges)
-  double sum_l1 = 0.0, sum_l2 = 0.0;
+  float sum_l1 = 0.0f, sum_l2 = 0.0f;
   constexpr int kRunQ = 4;
   for (int i = tid; i < kLossTile * (kLossTile / kRunQ); i += kLossThreads) {
     const int cq = i % kLossTile, rq0 = (i / kLossTile) * kRunQ;
@@ -319,8 +320,8 @@ __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
       const float x = xs[(rq + 2 * HW) * R + cq + 2 * HW];
       const float y = ys[(rq + 2 * HW) * R + cq + 2 * HW];
       const float d = x - y;
-      sum_l1 += double(fabsf(d));
-      sum_l2 += double(d * d);
+      sum_l1 += fabsf(d);
+      sum_l2 += d * d;
       if (!a.dpred) continue;
       const float sgn = d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f);
       float grad = a.c_l1 * sgn + a.c_mse * 2.0f * d;
@@ -371,7 +372,7 @@ __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
 
   // block reduction of the three sums, one double atomic per quantity
   const int lane = tid & 31, warp = tid >> 5;
-  double v[3] = {sum_l1, sum_l2, sum_s};
+  double v[3] = {double(sum_l1), double(sum_l2), double(sum_s)};
 #pragma unroll
   for (int q = 0; q < 3; ++q) {
     for (int o = 16; o > 0; o >>= 1) v[q] += __shfl_down_sync(0xffffffffu, v[q], o);

@@ -521,14 +521,9 @@ __global__ void __launch_bounds__(256, 4) preprocess_fwd_kernel(gsb_scene sc, gs
       if (exact_shape(P.mx, P.my, P.A, P.B, P.C, P.o_eff, rc.alpha_cutoff, vw.height, vw.width, rc.pixel_center,
                       &es)) {
         rect = exact_rect_of(es, rc.tile);
-        if (rc.ellipse) {
-          for (int ty = rect.ty0; ty <= rect.ty1; ++ty) {
-            int tx0, tx1;
-            if (exact_row(es, ty, rc.tile, rc.pixel_center, &tx0, &tx1)) count += uint32_t(tx1 - tx0 + 1);
-          }
-        } else {
-          count = rect.count();
-        }
+        // with the ellipse rows the pairs are counted afterwards in rank order (pairs_kernel: the
+        // rows of a block's Gaussians spread over its lanes)
+        if (!rc.ellipse) count = rect.count();
         tau_f = __double2float_ru(es.L);
       } else {
         tau_f = -1.0f;  // never blended

@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
   const size_t rb = (size_t(view) * rc.n_tiles + tile) * 2;
   const uint32_t start = a.ranges[rb], end = a.ranges[rb + 1];
   const float* recs = a.records + size_t(view) * a.G * GSB_RECORD_FLOATS;
-  const float inv_f0 = 1.0f / rc.f0;
+  const float inv_f0 = rc.inv_f0;
   const WarpSlots ws{s_geo[lw], s_cot[lw], s_col[lw], nullptr};
 
   int py[PX];
@@ -303,15 +303,24 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
   };
   // Two walks of a chunk's kept entries.  Compact (two or more pixels per lane): the kept entries
   // sit in consecutive slots and every lane runs every slot, a pixel that has stopped or whose
-  // alpha is below the cutoff taking alpha 0 with its state kept unchanged (the same bits as
-  // skipping it), so the walk has no per-pixel branches; measured on one B200, 8 x 1920x1080
-  // forward 11.63 -> 11.09 ms.  With one pixel per lane the lane's own early exit pays more
-  // (16 x 128^2: 0.332 ms, 0.351 compact), so it walks the set bits of the keep mask.
+  // alpha is below the cutoff taking alpha 0, so the walk has no per-pixel branches.  With alpha 0
+  // the factor is f = F0 and S * (f * inv_f0) is S to the bit (inv_f0 is chosen so that
+  // F0 * inv_f0 rounds to 1), so a skipped entry changes nothing; a stopped pixel's cutoff is
+  // +inf.  Measured on one B200, 8 x 1920x1080 forward 11.63 -> 11.09 ms against the set-bit walk.
+  // With one pixel per lane the lane's own early exit pays more (16 x 128^2: 0.332 ms, 0.351
+  // compact), so it walks the set bits of the keep mask.
   constexpr bool kCompact = PX >= 2;
   if constexpr (kCompact) {
-  // The kept entries of a chunk sit in consecutive slots; every lane runs every slot, a pixel that
-  // has stopped or whose alpha is below the cutoff taking alpha 0 with its state kept unchanged
-  // (the same bits as skipping it), so the walk has no per-pixel branches.
+  const float kInf = __int_as_float(0x7f800000);
+  float cut[PX];
+#pragma unroll
+  for (int k = 0; k < PX; ++k) cut[k] = done[k] ? kInf : rc.alpha_cutoff;
+  auto stopped = [&]() {
+    bool r = true;
+#pragma unroll
+    for (int k = 0; k < PX; ++k) r = r && cut[k] == kInf;
+    return r;
+  };
   auto blend2 = [&](uint32_t c, int j, auto fast) {
     const float4 g = s_geo[lw][j];
     const float4 ct = s_cot[lw][j];
@@ -323,7 +332,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
       const float qk = pair_q(g.z, g.w, ct.x, dx, dy);
       const float e = decltype(fast)::value ? gauss_falloff_nonpos(qk) : gauss_falloff(qk);
       const float a0 = fminf(ct.y * e, rc.alpha_clamp);  // ct.y >= 0
-      const bool take = !done[k] && a0 >= rc.alpha_cutoff;
+      const bool take = a0 >= cut[k];
       const float alpha = take ? a0 : 0.0f;
       const float T = S[k] * ct.w;
       const float w = T * alpha;
@@ -333,10 +342,9 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
       Ws[k] += w;
       if (DEPTH) D[k] = fmaf(w, col.w, D[k]);
       const float f = __fadd_rn(__fsub_rn(1.0f, alpha), rc.eps);
-      const float Sn = S[k] * (f * inv_f0);
-      S[k] = take ? Sn : S[k];
-      if (take && Sn < ct.z) {  // T after this entry below the threshold
-        done[k] = true;
+      S[k] = S[k] * (f * inv_f0);
+      if (take && S[k] < ct.z) {  // T after this entry below the threshold
+        cut[k] = kInf;
         n_proc[k] = c - start + s_li[lw][j] + 1u;
       }
     }
@@ -348,8 +356,8 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
 #pragma unroll
       for (int s = 0; s < NB; ++s) {
         if (next == s && bnd[s] < c + 32u) {
-          const uint32_t cut = bnd[s] > c ? bnd[s] - c : 0u;  // chunk positions < cut lie before it
-          const int jb = __popc(m & ((1u << cut) - 1u));
+          const uint32_t cut_at = bnd[s] > c ? bnd[s] - c : 0u;  // chunk positions < cut_at lie before it
+          const int jb = __popc(m & ((1u << cut_at) - 1u));
           for (; j < jb; ++j) blend2(c, j, fast);
           snapshot(s);
           next = s + 1;
@@ -358,11 +366,11 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
     }
     for (; j < nk; ++j) {
       blend2(c, j, fast);
-      if ((j & 7) == 7 && __all_sync(kFull, all_of(done))) break;
+      if ((j & 7) == 7 && __all_sync(kFull, stopped())) break;
     }
   };
   for (uint32_t c = start; c < end; c += 32) {
-    if (__all_sync(kFull, all_of(done))) break;
+    if (__all_sync(kFull, stopped())) break;
     const uint32_t idx = c + lane;
     bool cond = false;
     Entry en;
@@ -492,6 +500,8 @@ constexpr int kPartialContributors = 18;
 // [s n / NSEG, (s + 1) n / NSEG), each walked by its own CTA (adjacent in launch order), starting
 // from the forward's checkpoint of its upper boundary (the last segment from the final state).
 // CW: warps per CTA, as in the forward.
+// (Register caps measured on 8 x 1920x1080, four pixels per lane, 80 registers uncapped: 26.9 ms;
+// capped at 72: 29.8 ms, at 64: 30.7 ms.)
 template <int TILE, int PX, bool DEPTH, int NSEG, int CW>
 __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
   constexpr int NW = TILE * TILE / (32 * PX);
@@ -693,6 +703,8 @@ constexpr uint64_t kBwdPairedTiles = 2048;
 // cost of the walk and the gradient reduction once more; the backward takes them on grids this
 // large.  Measured on one B200, 8 x 1920x1080 (65k tiles): backward 31.9 -> 26.9 ms with four; the
 // forward, whose pixels stop early and need no reduction, 11.70 -> 11.94 ms, so it keeps two.
+// (Eight per lane, one warp walking and reducing a whole tile, was measured slower: 26.9 -> 30.7 ms,
+// 117 registers; 4% fewer instructions but fewer warps in flight and more idle lanes.)
 constexpr uint64_t kBwdQuadTiles = 32768;
 // Below this many tiles the backward cuts every tile's list in four (gsb_options.backward_segments
 // = 0): four times the CTAs and a quarter of the serial walk per tile, which lets it pair pixels
@@ -795,7 +807,10 @@ static int lane_pixels(uint64_t tiles, uint64_t threshold, bool backward, int ti
 }
 
 gsb_status launch_raster_fwd(const RasterArgs& a, cudaStream_t st) {
-  const int px = lane_pixels(uint64_t(a.rc.n_tiles) * uint64_t(a.B), kFwdPairedTiles, false, a.rc.tile);
+  // the compact walk (two or more pixels per lane) needs an inverse of F0 with F0 * inv_f0 == 1
+  const int px = a.rc.unit_inv ? lane_pixels(uint64_t(a.rc.n_tiles) * uint64_t(a.B), kFwdPairedTiles, false,
+                                             a.rc.tile)
+                               : 1;
   if (a.rc.tile == 16) px == 4 ? fwd_launch<16, 4>(a, st) : px == 2 ? fwd_launch<16, 2>(a, st) : fwd_launch<16, 1>(a, st);
   else if (a.rc.tile == 8) px == 2 ? fwd_launch<8, 2>(a, st) : fwd_launch<8, 1>(a, st);
   else return GSB_ERR_ARG;

@@ -96,10 +96,7 @@ __global__ void __launch_bounds__(256) preprocess_2d_kernel(gsb_splats2d sp, int
     float tau_f = -1.0f;
     if (visible && exact_shape(g.mx, g.my, g.A, g.B, g.C, g.o, rc.alpha_cutoff, H, W, rc.pixel_center, &es)) {
       rect = exact_rect_of(es, rc.tile);
-      for (int ty = rect.ty0; ty <= rect.ty1; ++ty) {
-        int tx0, tx1;
-        if (exact_row(es, ty, rc.tile, rc.pixel_center, &tx0, &tx1)) count += uint32_t(tx1 - tx0 + 1);
-      }
+      if (!rc.ellipse) count = uint32_t(rect.count());  // else counted afterwards (pairs_kernel)
       tau_f = __double2float_ru(es.L);
     }
     const size_t slot = b * G + size_t(rank_of[i]);
