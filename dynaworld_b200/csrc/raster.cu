@@ -55,13 +55,14 @@ __device__ __forceinline__ float gauss_falloff_nonpos(float qk) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(qk));
   return y;
 }
-// The backward's per-pixel power gradient is kept divided by k (the 1/k rides on the mask of
-// d min(power, 0) / d power), so the mean gradients come out of the k-scaled conic unchanged and the
-// conic gradients -1/2 sum dpow dx^2 (and so on) take the factor -k / 2 when they are flushed.
-// (Applying the conic coefficients and 1/k once per entry to per-lane sums instead was measured
-// slower: 8 x 1920x1080 backward 26.9 -> 28.1 ms.)
+// The backward accumulates the per-pixel power gradient without the 1/k that relates the k-scaled
+// conic to q (dpow = d loss / d power times k, where power = -q / 2 and the slots hold k A, k B,
+// k C), so a conditioned chunk multiplies nothing per pixel for it; the factors come in once per
+// entry when the sums are flushed: 1/k on the mean gradients, -1/2 (= 1/k times -k/2) on the conic
+// gradients -1/2 sum dpow dx^2 (and so on).  (Applying the conic coefficients once per entry to
+// per-lane sums as well was measured slower: 8 x 1920x1080 backward 26.9 -> 28.1 ms.)
 constexpr float kInvFalloffScale = -1.38629436111989061883f;  // 1 / k = -2 ln 2
-constexpr float kConicGradScale = 0.36067376022224085184f;    // -k / 2
+constexpr float kConicFlushScale = -0.5f;                     // (1 / k) (-k / 2)
 
 // q = A dx^2 + B dx dy + C dy^2 with a fixed rounding sequence (forward and backward agree).
 __device__ __forceinline__ float pair_q(float A, float B, float C, float dx, float dy) {
@@ -97,6 +98,14 @@ __device__ __forceinline__ bool all_of(const bool (&v)[PX]) {
 }
 
 template <int PX>
+__device__ __forceinline__ uint32_t min_of(const uint32_t (&v)[PX]) {
+  uint32_t r = 0xffffffffu;
+#pragma unroll
+  for (int k = 0; k < PX; ++k) r = min(r, v[k]);
+  return r;
+}
+
+template <int PX>
 __device__ __forceinline__ uint32_t max_of(const uint32_t (&v)[PX]) {
   uint32_t r = 0;
 #pragma unroll
@@ -118,11 +127,14 @@ struct WarpSlots {
 // max(o, 0) e equals max(o e, 0) exactly, so the forward skips the lower clamp.
 //
 // conditioned: the entry is kept with finite extents and a finite conic with A, C > 0 and
-// B^2 <= 4 A C (1 - 2^-8).  Then |B dx dy| <= 0.999 (A dx^2 + C dy^2), so q >= 0.001 (A dx^2 +
-// C dy^2) while the rounding of pair_q stays below 8 ulp of that sum: the computed q is never
-// negative (qk never positive), the falloff needs no clamp and d min(power, 0) / d power is 1
-// wherever dx or dy is nonzero.  A chunk whose kept entries are all conditioned takes that path;
-// both paths give the same bits for such an entry, so forward and backward agree whichever each takes.
+// B^2 <= 4 A C (1 - 2^-8) (and, in the forward, an opacity in [0, alpha_clamp]).  Then |B dx dy| <=
+// 0.999 (A dx^2 + C dy^2), so q >= 0.001 (A dx^2 + C dy^2) while the rounding of pair_q stays below
+// 8 ulp of that sum: the computed q is never negative (qk never positive), the falloff needs no clamp
+// and d min(power, 0) / d power is 1 wherever dx or dy is nonzero; with e <= 1 the forward's alpha
+// = o e needs no clamp either (the rounded product is at most o).  A chunk whose kept entries are
+// all conditioned takes that path; both paths give the same bits for such an entry, so forward and
+// backward agree whichever each takes.  (Skipping the alpha clamps in the backward too raised its
+// registers at four pixels per lane from 80 to 100 and was slower: 8 x 1920x1080 26.9 -> 31.7 ms.)
 // One list entry as the walk reads it: the slot contents.
 struct Entry {
   float4 geo, cot, col;
@@ -153,7 +165,7 @@ __device__ __forceinline__ bool entry_of(const RasterArgs& a, const float* recs,
   if (!((r0.x + ex >= bx0) && (r0.x - ex <= bx0 + 7.0f) && (r0.y + ey >= by0) && (r0.y - ey <= by0 + kH)))
     return false;
   conditioned = A > 0.0f && C > 0.0f && A < 1e30f && C < 1e30f && fabsf(B) < 1e30f &&
-                B * B <= 4.0f * A * C * (1.0f - 1.0f / 256.0f);
+                B * B <= 4.0f * A * C * (1.0f - 1.0f / 256.0f) && (!FWD || (r1.y >= 0.0f && r1.y <= a.rc.alpha_clamp));
   // exact: the minimum of q over the block's pixel-centre box (on an edge unless the mean is inside)
   const float X0 = bx0 - r0.x, X1 = bx0 + 7.0f - r0.x, Y0 = by0 - r0.y, Y1 = by0 + kH - r0.y;
   if (X0 <= 0.0f && X1 >= 0.0f && Y0 <= 0.0f && Y1 >= 0.0f) return true;
@@ -257,7 +269,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
       const float dy = __fsub_rn(fy[k], g.y);
       const float qk = pair_q(g.z, g.w, ct.x, dx, dy);
       const float e = decltype(fast)::value ? gauss_falloff_nonpos(qk) : gauss_falloff(qk);
-      const float alpha = fminf(ct.y * e, rc.alpha_clamp);  // ct.y >= 0
+      const float alpha = decltype(fast)::value ? ct.y * e : fminf(ct.y * e, rc.alpha_clamp);  // ct.y >= 0
       if (!(alpha >= rc.alpha_cutoff)) continue;
       const float4 col = s_col[lw][j];
       const float T = S[k] * ct.w;
@@ -331,7 +343,7 @@ __global__ void __launch_bounds__(32 * CW) raster_fwd_kernel(RasterArgs a) {
       const float dy = __fsub_rn(fy[k], g.y);
       const float qk = pair_q(g.z, g.w, ct.x, dx, dy);
       const float e = decltype(fast)::value ? gauss_falloff_nonpos(qk) : gauss_falloff(qk);
-      const float a0 = fminf(ct.y * e, rc.alpha_clamp);  // ct.y >= 0
+      const float a0 = decltype(fast)::value ? ct.y * e : fminf(ct.y * e, rc.alpha_clamp);  // ct.y >= 0
       const bool take = a0 >= cut[k];
       const float alpha = take ? a0 : 0.0f;
       const float T = S[k] * ct.w;
@@ -569,12 +581,14 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
       }
     }
   }
-  // list range [lo, wmax) this warp has to revisit
+  // list range [lo, wmax) this warp has to revisit; below wmin every pixel of the warp blended
   const uint32_t wmax = __reduce_max_sync(kFull, max_of(n_proc));
+  const uint32_t wmin = __reduce_min_sync(kFull, min_of(n_proc));
   const int64_t cb_lo = int64_t(lo / 32) * 32;
 
-  // the kept entries m of the chunk at list index cb, last first; fast as in the forward
-  auto walk = [&](int64_t cb, uint32_t m, auto fast) {
+  // the kept entries m of the chunk at list index cb, last first; fast as in the forward; live:
+  // every entry of the chunk lies below every pixel's count, so no pixel tests it
+  auto walk = [&](int64_t cb, uint32_t m, auto fast, auto live) {
     while (m) {
       const int j = 31 - __clz(m);
       m &= ~(1u << j);
@@ -583,14 +597,14 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
 #pragma unroll
       for (int k = 0; k < 12; ++k) v[k] = 0.0f;
       bool contrib = false;
-      if (lj < max_of(n_proc)) {
+      if (decltype(live)::value || lj < max_of(n_proc)) {
         const float4 g = s_geo[lw][j];
         const float4 ct = s_cot[lw][j];
         const float dx = __fsub_rn(fx, g.x);
         const float hB = 0.5f * g.w;  // half the cross coefficient
 #pragma unroll
         for (int k = 0; k < PX; ++k) {
-          if (!(lj < n_proc[k])) continue;
+          if (!decltype(live)::value && !(lj < n_proc[k])) continue;
           const float dy = __fsub_rn(fy[k], g.y);
           const float qk = pair_q(g.z, g.w, ct.x, dx, dy);
           const float e = decltype(fast)::value ? gauss_falloff_nonpos(qk) : gauss_falloff(qk);
@@ -611,14 +625,12 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           // d min(power, 0) / d power, power = -q / 2 (torch splits a tie at 0 evenly), divided by k;
           // q > 0 where qk < 0.  A conditioned entry has q = 0 only at dx = dy = 0, where the mask
           // multiplies zeros.
-          const float pmask = decltype(fast)::value
-                                  ? kInvFalloffScale
-                                  : (qk < 0.0f ? kInvFalloffScale : (qk == 0.0f ? 0.5f * kInvFalloffScale : 0.0f));
+          const float pmask = decltype(fast)::value ? 1.0f : (qk < 0.0f ? 1.0f : (qk == 0.0f ? 0.5f : 0.0f));
           const float dpow = dlr * araw * pmask;
           const float u = dpow * dx, t = dpow * dy;
           v[0] = fmaf(g.z, u, fmaf(hB, t, v[0]));
           v[1] = fmaf(ct.x, t, fmaf(hB, u, v[1]));
-          v[2] = fmaf(u, dx, v[2]);  // conic gradients: times -k/2 once the pixels are summed
+          v[2] = fmaf(u, dx, v[2]);  // conic gradients: times -1/2 once the pixels are summed
           v[3] = fmaf(u, dy, v[3]);
           v[4] = fmaf(t, dy, v[4]);
           v[5] = fmaf(dlr, e, v[5]);
@@ -635,9 +647,9 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
       if (__popc(cm) <= kSparseContributors) {
         if (contrib) {
           float2* d2 = reinterpret_cast<float2*>(dst);
-          atomicAdd(d2 + 0, make_float2(v[0], v[1]));
-          atomicAdd(d2 + 1, make_float2(kConicGradScale * v[2], kConicGradScale * v[3]));
-          atomicAdd(d2 + 2, make_float2(kConicGradScale * v[4], v[5]));
+          atomicAdd(d2 + 0, make_float2(kInvFalloffScale * v[0], kInvFalloffScale * v[1]));
+          atomicAdd(d2 + 1, make_float2(kConicFlushScale * v[2], kConicFlushScale * v[3]));
+          atomicAdd(d2 + 2, make_float2(kConicFlushScale * v[4], v[5]));
           atomicAdd(d2 + 3, make_float2(v[6], v[7]));
           if (DEPTH) atomicAdd(d2 + 4, make_float2(v[8], v[9]));
           else atomicAdd(dst + 8, v[8]);
@@ -663,8 +675,10 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
         float2 pv;
         float sv;
         int p2, p1;
-        if (grp == 0) pv = make_float2(v[0], v[1]), p2 = 0, sv = kConicGradScale * v[2], p1 = 2;
-        else if (grp == 1) pv = make_float2(kConicGradScale * v[1], v[2]), p2 = 4, sv = kConicGradScale * v[0], p1 = 3;
+        if (grp == 0)
+          pv = make_float2(kInvFalloffScale * v[0], kInvFalloffScale * v[1]), p2 = 0, sv = kConicFlushScale * v[2], p1 = 2;
+        else if (grp == 1)
+          pv = make_float2(kConicFlushScale * v[1], v[2]), p2 = 4, sv = kConicFlushScale * v[0], p1 = 3;
         else if (grp == 2) pv = make_float2(v[0], v[1]), p2 = 6, sv = v[2], p1 = 8;
         else pv = make_float2(0.0f, 0.0f), p2 = 0, sv = DEPTH ? v[0] : 0.0f, p1 = 9;
         if (pv.x != 0.0f || pv.y != 0.0f) atomicAdd(reinterpret_cast<float2*>(dst + p2), pv);
@@ -672,7 +686,7 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
       } else {
         int k;
         float s = warp_sum10(v, lane, &k);
-        if (k >= 2 && k <= 4) s *= kConicGradScale;
+        s *= k <= 1 ? kInvFalloffScale : (k <= 4 ? kConicFlushScale : 1.0f);
         if ((lane & 1) == 0 && k < GSB_GRAD2D_FLOATS && s != 0.0f) atomicAdd(dst + k, s);
       }
     }
@@ -684,9 +698,16 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
                       load_entry<block_h<PX>(), false>(a, recs, start + li, li, bx0, by0, ws, lane, cond);
     const uint32_t m = __ballot_sync(kFull, keep);
     const bool fast = __all_sync(kFull, cond || !keep);
+    // (at four pixels per lane the live walk took 95 registers instead of 80 and was slower)
+    const bool live = PX <= 2 && cb + 32 <= int64_t(wmin);
     __syncwarp();
-    if (fast) walk(cb, m, std::true_type{});
-    else walk(cb, m, std::false_type{});
+    if (fast) {
+      if (live) walk(cb, m, std::true_type{}, std::true_type{});
+      else walk(cb, m, std::true_type{}, std::false_type{});
+    } else {
+      if (live) walk(cb, m, std::false_type{}, std::true_type{});
+      else walk(cb, m, std::false_type{}, std::false_type{});
+    }
     __syncwarp();  // slots are rewritten by the next chunk
   }
 }
@@ -702,10 +723,11 @@ constexpr uint64_t kBwdPairedTiles = 2048;
 // Four pixels per lane (an 8 x 16 block per warp, two warps per 16x16 tile) halve the per-entry
 // cost of the walk and the gradient reduction once more; the backward takes them on grids this
 // large.  Measured on one B200, 8 x 1920x1080 (65k tiles): backward 31.9 -> 26.9 ms with four; the
-// forward, whose pixels stop early and need no reduction, 11.70 -> 11.94 ms, so it keeps two.
+// forward 11.70 -> 11.94 ms with the set-bit walk, and with the compact walk 10.60 -> 10.36 ms, so
+// it takes four on these grids as well.
 // (Eight per lane, one warp walking and reducing a whole tile, was measured slower: 26.9 -> 30.7 ms,
 // 117 registers; 4% fewer instructions but fewer warps in flight and more idle lanes.)
-constexpr uint64_t kBwdQuadTiles = 32768;
+constexpr uint64_t kQuadTiles = 32768;
 // Below this many tiles the backward cuts every tile's list in four (gsb_options.backward_segments
 // = 0): four times the CTAs and a quarter of the serial walk per tile, which lets it pair pixels
 // per lane at any size, for 72 bytes of checkpoint per pixel.  Measured on one B200, 16 x 128^2
@@ -802,7 +824,7 @@ static int lane_pixels(uint64_t tiles, uint64_t threshold, bool backward, int ti
   if (!force) force = forced_px("GSB200_RASTER_PX");
   if (force == 4 && tile != 16) force = 2;
   if (force) return force;
-  if (backward && tile == 16 && tiles >= kBwdQuadTiles) return 4;
+  if (tile == 16 && tiles >= kQuadTiles) return 4;
   return tiles >= threshold ? 2 : 1;
 }
 
