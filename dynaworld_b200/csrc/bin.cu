@@ -186,20 +186,48 @@ __global__ void __launch_bounds__(kEmitThreads) pairs_kernel(int32_t G, RenderCo
   }
 }
 
+// Run boundaries of the sorted keys: thread j reads keys 2j and 2j + 1 (one 16-byte load when the
+// array is 16-byte aligned) and
+// takes its neighbours' tiles from the adjacent lanes (lanes 0 and 31 read the one key beyond the
+// warp), so every key is read once.  The loop bound is uniform over a block: every lane reaches the
+// shuffles.
 __global__ void tile_ranges_kernel(const uint64_t* __restrict__ keys, uint32_t cap,
                                    const uint32_t* __restrict__ n_dev, uint32_t* __restrict__ ranges,
-                                   size_t n_ranges, int32_t* __restrict__ status) {
+                                   size_t n_ranges, int32_t* __restrict__ status, int aligned16) {
   uint32_t n = cap;
   if (n_dev) {
     const uint32_t count = *n_dev;
     if (count > cap && blockIdx.x == 0 && threadIdx.x == 0) record_error(status, GSB_ERR_CAPACITY, int(cap));
     n = min(cap, count);
   }
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const uint32_t t = uint32_t(keys[i] >> 32);
-    if (t >= n_ranges) continue;
-    if (i == 0 || uint32_t(keys[i - 1] >> 32) != t) ranges[size_t(t) * 2] = i;
-    if (i + 1 == n || uint32_t(keys[i + 1] >> 32) != t) ranges[size_t(t) * 2 + 1] = i + 1;
+  constexpr uint32_t kNone = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const uint32_t n2 = (n + 1u) / 2u;
+  for (uint32_t base = blockIdx.x * blockDim.x; base < n2; base += gridDim.x * blockDim.x) {
+    const uint32_t i = 2u * (base + threadIdx.x);
+    uint32_t t0 = kNone, t1 = kNone;
+    if (i + 1u < n) {
+      if (aligned16) {
+        const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(keys + i);
+        t0 = uint32_t(v.x >> 32), t1 = uint32_t(v.y >> 32);
+      } else {
+        t0 = uint32_t(keys[i] >> 32), t1 = uint32_t(keys[i + 1u] >> 32);
+      }
+    } else if (i < n) {
+      t0 = uint32_t(keys[i] >> 32);
+    }
+    uint32_t prev = __shfl_up_sync(0xffffffffu, t1, 1);    // tile of key i - 1
+    uint32_t next = __shfl_down_sync(0xffffffffu, t0, 1);  // tile of key i + 2
+    if (lane == 0 && i > 0u && i < n) prev = uint32_t(keys[i - 1u] >> 32);
+    if (lane == 31 && i + 2u < n) next = uint32_t(keys[i + 2u] >> 32);
+    if (i < n && t0 < n_ranges) {
+      if (i == 0u || prev != t0) ranges[size_t(t0) * 2] = i;
+      if (i + 1u == n || t1 != t0) ranges[size_t(t0) * 2 + 1] = i + 1u;
+    }
+    if (i + 1u < n && t1 < n_ranges) {
+      if (t0 != t1) ranges[size_t(t1) * 2] = i + 1u;
+      if (i + 2u == n || next != t1) ranges[size_t(t1) * 2 + 1] = i + 2u;
+    }
   }
 }
 
@@ -249,7 +277,8 @@ gsb_status launch_tile_ranges(const uint64_t* keys, uint32_t n, const uint32_t* 
   if (n == 0 && !n_dev) return GSB_OK;
   const int grid = int(std::min<uint32_t>(std::max<uint32_t>((n + 255) / 256, 1u), 148u * 32u));
   note_launch();
-  tile_ranges_kernel<<<grid, 256, 0, st>>>(keys, n, n_dev, ranges, n_ranges, status);
+  tile_ranges_kernel<<<grid, 256, 0, st>>>(keys, n, n_dev, ranges, n_ranges, status,
+                                           int(reinterpret_cast<uintptr_t>(keys) % 16 == 0));
   return launch_status();
 }
 
