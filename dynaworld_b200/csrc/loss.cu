@@ -21,10 +21,14 @@
 namespace gsb {
 
 constexpr int kLossTile = 32;
-// 512 threads: the ~100 KB of shared memory per tile allows two CTAs per SM, so the CTA size sets
-// the warps in flight.  Measured on one B200 (ms, 16 x 128^2 / 8 x 384^2): 256 threads 0.068 /
-// 0.216, 512 0.062 / 0.192, 1024 0.064 / 0.201.
-constexpr int kLossThreads = 512;
+// 384 threads, three CTAs per SM: with its two regions reused (65 KB of shared memory per tile) and
+// at most 56 registers a thread, three tiles share an SM and one's barriers overlap the others'
+// work.  Measured on one B200, 8 x 1920x1080 loss: 100 KB and 512 threads (two CTAs per SM) 1.81 ms;
+// 65 KB, 512 threads, two CTAs 1.85; three CTAs of 512 (40 registers) 1.63; three of 384 1.60.
+// (Earlier, at 100 KB: 16 x 128^2 / 8 x 384^2, 256 threads 0.068 / 0.216 ms, 512 0.062 / 0.192,
+// 1024 0.064 / 0.201.)
+constexpr int kLossThreads = 384;
+constexpr int kLossCtasPerSm = 3;
 
 struct LossArgs {
   int B, C, H, W;
@@ -71,16 +75,32 @@ __device__ __forceinline__ float ssim_point(const float m[5], float c1, float c2
   return s;
 }
 
+// Shared-memory floats of the loss kernel's two regions (see loss_kernel).
 template <int HW>
-__global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
+__host__ __device__ constexpr int loss_region_a() {
+  constexpr int R = kLossTile + 4 * HW, M = kLossTile + 2 * HW;
+  return 2 * R * R > 3 * M * M ? 2 * R * R : 3 * M * M;
+}
+template <int HW>
+__host__ __device__ constexpr int loss_region_b() {
+  constexpr int R = kLossTile + 4 * HW, M = kLossTile + 2 * HW;
+  return 5 * R * M > 3 * M * kLossTile ? 5 * R * M : 3 * M * kLossTile;
+}
+
+template <int HW>
+__global__ void __launch_bounds__(kLossThreads, kLossCtasPerSm) loss_kernel(LossArgs a) {
   constexpr int R = kLossTile + 4 * HW;  // input rows/cols held
   constexpr int M = kLossTile + 2 * HW;  // window-mean rows/cols computed
+  // Two regions, each reused once its first tenant is dead: the inputs (read by the horizontal
+  // pass only; the last pass reads its pixels from global memory) give way to the derivative maps
+  // the vertical pass writes, the horizontal sums (read by the vertical pass only) to the
+  // horizontal adjoint.
   extern __shared__ float smem[];
-  float* xs = smem;                 // [R][R]
-  float* ys = xs + R * R;           // [R][R]
-  float* hs = ys + R * R;           // [5][R][M]
-  float* gm = hs + 5 * R * M;       // [3][M][M]
-  float* ha = gm + 3 * M * M;       // [3][M][kLossTile]
+  float* xs = smem;                               // [R][R]
+  float* ys = xs + R * R;                         // [R][R]
+  float* gm = smem;                               // [3][M][M], after the horizontal pass
+  float* hs = smem + loss_region_a<HW>();         // [5][R][M]
+  float* ha = hs;                                 // [3][M][kLossTile], after the vertical pass
   __shared__ double s_red[3][kLossThreads / 32];
 
   const int plane = a.plane_base + int(blockIdx.z), b = plane / a.C;
@@ -317,8 +337,8 @@ __global__ void __launch_bounds__(kLossThreads) loss_kernel(LossArgs a) {
     for (int j = 0; j < kRunQ; ++j) {
       const int rq = rq0 + j, qy = y0 + rq;
       if (qy >= H) break;
-      const float x = xs[(rq + 2 * HW) * R + cq + 2 * HW];
-      const float y = ys[(rq + 2 * HW) * R + cq + 2 * HW];
+      const float x = a.pred[poff + size_t(qy) * W + qx];
+      const float y = a.target[poff + size_t(qy) * W + qx];
       const float d = x - y;
       sum_l1 += fabsf(d);
       sum_l2 += d * d;
@@ -466,8 +486,7 @@ constexpr int64_t kMaxGridZ = 65535;
 
 template <int HW>
 static gsb_status launch_loss_t(const LossArgs& a, cudaStream_t st) {
-  constexpr int R = kLossTile + 4 * HW, M = kLossTile + 2 * HW;
-  const size_t smem = sizeof(float) * (2 * R * R + 5 * R * M + 3 * M * M + 3 * M * kLossTile);
+  const size_t smem = sizeof(float) * size_t(loss_region_a<HW>() + loss_region_b<HW>());
   // The shared-memory opt-in is a per-device function attribute: set once per device.
   static std::mutex mu;
   static bool ready[64] = {};
