@@ -725,9 +725,12 @@ constexpr uint64_t kBwdPairedTiles = 2048;
 // large.  Measured on one B200, 8 x 1920x1080 (65k tiles): backward 31.9 -> 26.9 ms with four; the
 // forward 11.70 -> 11.94 ms with the set-bit walk, and with the compact walk 10.60 -> 10.36 ms, so
 // it takes four on these grids as well.
+// At 4 x 1920x1080 (32,640 tiles, one GPU's share of the 32 views at 8 GPUs): four in both stages
+// 22.48 ms a step, two in both 24.08 (backward 14.98 -> 13.49 ms, forward 5.33 -> 5.21); grids
+// between the segmented ones (below 8192 tiles) and 16k tiles were not measured.
 // (Eight per lane, one warp walking and reducing a whole tile, was measured slower: 26.9 -> 30.7 ms,
 // 117 registers; 4% fewer instructions but fewer warps in flight and more idle lanes.)
-constexpr uint64_t kQuadTiles = 32768;
+constexpr uint64_t kQuadTiles = 16384;
 // Below this many tiles the backward cuts every tile's list in four (gsb_options.backward_segments
 // = 0): four times the CTAs and a quarter of the serial walk per tile, which lets it pair pixels
 // per lane at any size, for 72 bytes of checkpoint per pixel.  Measured on one B200, 16 x 128^2
