@@ -496,7 +496,7 @@ __device__ __forceinline__ float warp_sum10(float v[12], int lane, int* index) {
 
 // Lanes contributing to one entry at or below this count add their own values atomically, as five
 // 8-byte vector reductions (red.global.add.v2.f32; a gradient slot is 40 bytes, so every pair of
-// floats is 8-byte aligned); up to kPartialContributors the warp first sums each pixel column's four
+// floats is 8-byte aligned); up to partial_contributors the warp first sums each pixel column's four
 // rows (two transpose steps, three values per lane, two reductions per lane); above that it sums
 // over the whole warp (warp_sum10).  Measured on one B200 (backward ms, 16 x 128^2 / 8 x 384^2):
 // scalar atomics, one per nonzero value, up to 12: 0.730 / 1.433; vector pairs up to 12: 0.667 /
@@ -505,8 +505,15 @@ __device__ __forceinline__ float warp_sum10(float v[12], int lane, int* index) {
 // the warp): 0.893 / 1.714.  Then, with pairs up to 16, column sums up to 18: 0.625 / 1.135, 20:
 // 0.627 / 1.139, 22: 0.629 / 1.143, 24: 0.631 / 1.147, 28: 0.635 / 1.152, 32: 0.646 / 1.262, none:
 // 0.630 / 1.233; pairs up to 12 or 14 with column sums up to 20: 0.637 / 1.164, 0.632 / 1.152.
-constexpr int kSparseContributors = 16;
-constexpr int kPartialContributors = 18;
+// At four pixels per lane (a lane's four pixels share a column, so fewer lanes carry more of an
+// entry's gradient) the per-lane atomics pay up to 24 contributors, and the column sums no longer:
+// measured on 8 x 1920x1080 (backward ms, atomics / column sums up to): 16 / 18 26.85, 12 / 18 27.10,
+// 20 / 20 26.65, 24 / 24 26.56, 16 / 24 26.94, 16 / 16 26.80 (8 x 384^2 at two pixels per lane:
+// 16 / 18 1.120, 20 / 20 1.112, 24 / 24 1.217).
+template <int PX>
+__host__ __device__ constexpr int sparse_contributors() { return PX == 4 ? 24 : 16; }
+template <int PX>
+__host__ __device__ constexpr int partial_contributors() { return PX == 4 ? 24 : 18; }
 
 // DEPTH: a depth gradient is given.  NSEG: the tile's list is cut into NSEG segments
 // [s n / NSEG, (s + 1) n / NSEG), each walked by its own CTA (adjacent in launch order), starting
@@ -644,7 +651,7 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
       const uint32_t cm = __ballot_sync(kFull, contrib);
       if (cm == 0u) continue;
       float* dst = g2 + size_t(s_rank[lw][j]) * GSB_GRAD2D_FLOATS;
-      if (__popc(cm) <= kSparseContributors) {
+      if (__popc(cm) <= sparse_contributors<PX>()) {
         if (contrib) {
           float2* d2 = reinterpret_cast<float2*>(dst);
           atomicAdd(d2 + 0, make_float2(kInvFalloffScale * v[0], kInvFalloffScale * v[1]));
@@ -654,7 +661,7 @@ __global__ void __launch_bounds__(32 * CW) raster_bwd_kernel(RasterArgs a) {
           if (DEPTH) atomicAdd(d2 + 4, make_float2(v[8], v[9]));
           else atomicAdd(dst + 8, v[8]);
         }
-      } else if (__popc(cm) <= kPartialContributors) {
+      } else if (__popc(cm) <= partial_contributors<PX>()) {
         // column sums: lane l keeps values 3 grp + (0, 1, 2), grp = 2 b4 + b3, summed over l ^ {8, 16, 24}
 #pragma unroll
         for (int k = 0; k < 6; ++k) {
