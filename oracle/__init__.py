@@ -2,7 +2,8 @@
 
 TEST INFRASTRUCTURE ONLY.  Nothing in ``dynaworld_b200`` imports this package;
 only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
-``bench.py`` use it, and only as the checker or as the timed CPU port.
+``bench.py`` use it, and only as the reference the CUDA results are compared with or as
+the timed CPU port.
 
 Modules:
   splat_oracle  torch restatement (float32/float64) of the reference's

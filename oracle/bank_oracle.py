@@ -1,7 +1,7 @@
 """Torch restatement of the reference's dynamic Gaussian bank evaluation.
 
-TEST INFRASTRUCTURE ONLY (see oracle/__init__.py): the checker for the bank path of the CUDA
-preprocess, never imported by the product.  Differentiable through torch autograd, usable in
+TEST INFRASTRUCTURE ONLY (see oracle/__init__.py): the tests compare the bank path of the CUDA
+preprocess with it; never imported by the product.  Differentiable through torch autograd, usable in
 float32 or float64.  Citations are to src/train/gs_models/dynamic_video_token_gs_implicit_camera.py
 of nbardy/dynaworld:
 

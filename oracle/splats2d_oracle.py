@@ -1,6 +1,6 @@
 """NumPy float64 restatement of the reference's 2-D (already-projected) Gaussian rasterizers.
 
-TEST INFRASTRUCTURE ONLY (see oracle/__init__.py): the checker of the CUDA 2-D entry, never a
+TEST INFRASTRUCTURE ONLY (see oracle/__init__.py): what the tests compare the CUDA 2-D entry with, never a
 compute path.  Citations are to files of nbardy/dynaworld.
 
 Restated:

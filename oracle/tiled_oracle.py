@@ -13,8 +13,8 @@ render_pytorch_3dgs_tiled (src/train/renderers/tiled.py:74-198) for the pinhole 
     tile-local T = prod (1 - alpha + 1e-6) over the tile's list only, white background where no
     tile is listed, the whole image clamped to [0, 1].
 
-Used as a checker for the CUDA path's tiled_compat mode and, in bench.py, as the timed CPU
-baseline of the reference's faster CPU renderer.
+The tests compare the CUDA path's tiled_compat mode with it; bench.py times it as the CPU baseline
+of the reference's faster CPU renderer.
 """
 from __future__ import annotations
 
